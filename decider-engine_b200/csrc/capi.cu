@@ -1,0 +1,380 @@
+// extern "C" boundary of libdecider_gpu (declared in include/decider_gpu.h).
+#include <atomic>
+#include <cmath>
+#include <cstring>
+
+#include "../../include/decider_gpu.h"
+#include "engine.h"
+
+namespace dg {
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launch_count() { return g_launches.load(); }
+void note_launch() { g_launches.fetch_add(1); }
+}  // namespace dg
+
+struct dg_engine {
+  std::unique_ptr<dg::Engine> e;
+};
+struct dg_prefix {
+  std::unique_ptr<dg::Prefix> p;
+  const dg_engine* owner;
+};
+
+// The isolated INT8 projection of BASELINE config 1.
+struct dg_linear {
+  int device = 0, n = 0, k = 0, n_pad = 0, rank = 0;
+  float scale = 0.0f;
+  bool exact = true;
+  cudaStream_t stream = nullptr;
+  dg::DevBuf wq, ws_t, lora_a, lora_b, chunk_pid, status;
+  CUtensorMap map_b{};
+  int cap_m = 0, ldxs = 0;
+  dg::DevBuf x, xq, xs, mid, y;
+};
+
+namespace {
+thread_local std::string g_error;
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& ex) {
+    g_error = ex.what();
+    return 1;
+  } catch (...) {
+    g_error = "unknown error";
+    return 1;
+  }
+}
+
+dg::Config to_config(const dg_model_config* c) {
+  dg::Config k;
+  k.hidden = c->hidden_size;
+  k.intermediate = c->intermediate_size;
+  k.layers = c->num_hidden_layers;
+  k.vocab = c->vocab_size;
+  k.heads = c->num_attention_heads;
+  k.kv_heads = c->num_key_value_heads;
+  k.head_dim = c->head_dim;
+  k.conv_kernel = c->linear_conv_kernel_dim;
+  k.dk = c->linear_key_head_dim;
+  k.dv = c->linear_value_head_dim;
+  k.key_heads = c->linear_num_key_heads;
+  k.value_heads = c->linear_num_value_heads;
+  k.eps = c->rms_norm_eps;
+  k.rope_theta = c->rope_theta;
+  k.partial_rotary = c->partial_rotary_factor;
+  if (c->num_hidden_layers > 0 && !c->layer_types) throw std::runtime_error("layer_types is required");
+  k.layer_types.assign(c->layer_types, c->layer_types + std::max(0, c->num_hidden_layers));
+  k.rank = c->lora_rank;
+  k.lora_scale = c->lora_scale;
+  k.pointer_dim = c->pointer_dim;
+  return k;
+}
+
+void check_engine(const dg_engine* e) {
+  if (!e || !e->e) throw std::runtime_error("null engine");
+}
+
+void linear_reserve(dg_linear* l, int m) {
+  if (m <= l->cap_m) return;
+  const int cap = (m + 127) / 128 * 128;
+  l->ldxs = cap;
+  l->x = dg::DevBuf(size_t(cap) * l->k * 4);
+  l->xq = dg::DevBuf(size_t(cap) * l->k);
+  l->xs = dg::DevBuf(size_t(l->k / 64) * cap * 4);
+  DG_CUDA(cudaMemset(l->xs.ptr, 0, l->xs.bytes));
+  l->mid = dg::DevBuf(size_t(cap) * 32 * 4);
+  l->y = dg::DevBuf(size_t(cap) * l->n_pad * 4);
+  l->cap_m = cap;
+}
+
+void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* dots) {
+  using namespace dg;
+  if (m <= 0) throw std::runtime_error("dg_linear: need at least one row");
+  DG_CUDA(cudaSetDevice(l->device));
+  linear_reserve(l, m);
+  DG_CUDA(cudaMemsetAsync(l->status.ptr, 0, sizeof(DeviceStatus), l->stream));
+  DeviceStatus* st = l->status.as<DeviceStatus>();
+  launch_norm_quant(x_dev, l->k, m, l->k, nullptr, 0.0f, nullptr, 0, l->xq.as<int8_t>(), l->xs.as<float>(), l->ldxs, st,
+                    l->stream);
+  note_launch();
+  if (l->rank) {
+    launch_lora_a(x_dev, l->k, m, l->k, l->lora_a.as<float>(), l->rank, l->mid.as<float>(), 32, l->exact, l->stream);
+    note_launch();
+  }
+  CUtensorMap map_a;
+  make_tmap_i8_2d(&map_a, l->xq.ptr, uint64_t(l->k), uint64_t(m), gemm::BK, gemm::BM);
+  GemmArgs a{};
+  a.M = m;
+  a.N = l->n_pad;
+  a.K = l->k;
+  a.xs = l->xs.as<float>();
+  a.ldxs = l->ldxs;
+  a.ws = l->ws_t.as<float>();
+  a.lora_mid = l->mid.as<float>();
+  a.ld_mid = 32;
+  a.lora_b = l->lora_b.as<float>();
+  a.chunk_pid = l->chunk_pid.as<int>();
+  a.lora_scale = l->scale;
+  const bool direct = l->n_pad == l->n && dots == nullptr;
+  a.out = direct ? y_dev : l->y.as<float>();
+  a.ldo = direct ? l->n : l->n_pad;
+  a.status = st;
+  int32_t* dump = nullptr;
+  if (dots) {
+    if (l->n_pad != l->n) throw std::runtime_error("dg_linear: group-dot dump needs n % 256 == 0");
+    dump = dots;
+  }
+  a.dots = dump;
+  launch_gemm_i8(map_a, l->map_b, a, l->rank, kEpiWrite, l->exact, l->stream);
+  note_launch();
+  if (!direct)
+    DG_CUDA(cudaMemcpy2DAsync(y_dev, size_t(l->n) * 4, l->y.ptr, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
+                              cudaMemcpyDeviceToDevice, l->stream));
+  DeviceStatus h{};
+  DG_CUDA(cudaMemcpyAsync(&h, l->status.ptr, sizeof(h), cudaMemcpyDeviceToHost, l->stream));
+  DG_CUDA(cudaStreamSynchronize(l->stream));
+  if (h.code == kNonFinite) throw std::runtime_error("non-finite projection input");
+  if (h.code) throw std::runtime_error("device error code " + std::to_string(h.code) + " at " + std::to_string(h.where));
+}
+}  // namespace
+
+extern "C" {
+
+const char* dg_last_error(void) { return g_error.c_str(); }
+uint64_t dg_launch_count(void) { return dg::launch_count(); }
+
+int dg_engine_create(const dg_model_config* cfg, int precision, int device, int max_tokens, dg_engine** out) {
+  return guarded([&] {
+    if (!cfg || !out) throw std::runtime_error("null argument");
+    auto* e = new dg_engine();
+    try {
+      e->e.reset(new dg::Engine(to_config(cfg), precision, device, max_tokens));
+    } catch (...) {
+      delete e;
+      throw;
+    }
+    *out = e;
+  });
+}
+
+int dg_engine_set_tensor(dg_engine* e, const char* name, int dtype, const int64_t* shape, int ndim, const void* data) {
+  return guarded([&] {
+    check_engine(e);
+    if (!name || (ndim > 0 && !shape) || ndim < 0 || ndim > 8) throw std::runtime_error("bad tensor arguments");
+    std::vector<int64_t> s(shape, shape + ndim);
+    size_t n = 1;
+    for (auto d : s) n *= size_t(d < 0 ? 0 : d);
+    if (n && !data) throw std::runtime_error("null tensor data");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->set_tensor(name, dtype, s, data);
+  });
+}
+
+int dg_engine_fill_synthetic(dg_engine* e, uint64_t seed, float stddev) {
+  return guarded([&] {
+    check_engine(e);
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->fill_synthetic(seed, stddev);
+  });
+}
+
+int dg_engine_finalize(dg_engine* e) {
+  return guarded([&] {
+    check_engine(e);
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->finalize();
+  });
+}
+
+int dg_engine_fast_path(const dg_engine* e) { return e && e->e && e->e->fast_path() ? 1 : 0; }
+
+int dg_engine_set_exact(dg_engine* e, int exact) {
+  return guarded([&] {
+    check_engine(e);
+    e->e->exact = exact != 0;
+  });
+}
+
+void dg_engine_free(dg_engine* e) { delete e; }
+
+void* dg_engine_stream(const dg_engine* e) { return e && e->e ? static_cast<void*>(e->e->stream()) : nullptr; }
+
+float dg_engine_last_forward_ms(const dg_engine* e) { return e && e->e ? e->e->last_forward_ms : -1.0f; }
+
+int dg_engine_last_launches(const dg_engine* e) { return e && e->e ? e->e->last_launches : -1; }
+
+int dg_forward_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, float* hidden_out) {
+  return guarded([&] {
+    check_engine(e);
+    if (past && past->owner != e) throw std::runtime_error("prefix belongs to another engine");
+    if (n && !ids) throw std::runtime_error("null ids");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->forward(ids, int(std::min<size_t>(n, 1u << 30)), past ? past->p.get() : nullptr, false, hidden_out, nullptr);
+  });
+}
+
+int dg_prefill(dg_engine* e, const uint32_t* ids, size_t n, dg_prefix** out) {
+  return guarded([&] {
+    check_engine(e);
+    if (!out || (n && !ids)) throw std::runtime_error("null argument");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    std::unique_ptr<dg::Prefix> p;
+    e->e->forward(ids, int(std::min<size_t>(n, 1u << 30)), nullptr, true, nullptr, &p);
+    auto* h = new dg_prefix();
+    h->p = std::move(p);
+    h->owner = e;
+    *out = h;
+  });
+}
+
+size_t dg_prefix_len(const dg_prefix* p) { return p && p->p ? size_t(p->p->len) : 0; }
+void dg_prefix_free(dg_prefix* p) { delete p; }
+
+int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, const size_t* opt_pos, size_t n_opt,
+              float* logits_out) {
+  return guarded([&] {
+    check_engine(e);
+    if (past && past->owner != e) throw std::runtime_error("prefix belongs to another engine");
+    if (!ids || !opt_pos || !logits_out || n == 0 || n_opt == 0)
+      throw std::runtime_error("invalid encoding positions or window");
+    for (size_t i = 0; i < n_opt; ++i)
+      if (opt_pos[i] + 1 >= n) throw std::runtime_error("invalid encoding positions or window");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->forward(ids, int(std::min<size_t>(n, 1u << 30)), past ? past->p.get() : nullptr, false, nullptr, nullptr);
+    e->e->head_logits(int(n), opt_pos, int(n_opt), logits_out);
+  });
+}
+
+int dg_linear_create(const float* w, int n, int k, const float* lora_a, const float* lora_b, int rank, float lora_scale,
+                     int device, dg_linear** out) {
+  return guarded([&] {
+    using namespace dg;
+    if (!w || !out || n <= 0 || k <= 0) throw std::runtime_error("bad dg_linear arguments");
+    if (k % 128) throw std::runtime_error("dg_linear: k must be a multiple of 128");
+    if (rank != 0 && rank != 32) throw std::runtime_error("dg_linear: LoRA rank must be 0 or 32");
+    if (rank && (!lora_a || !lora_b)) throw std::runtime_error("dg_linear: LoRA weights missing");
+    DG_CUDA(cudaSetDevice(device));
+    std::unique_ptr<dg_linear> l(new dg_linear());
+    l->device = device;
+    l->n = n;
+    l->k = k;
+    l->rank = rank;
+    l->scale = lora_scale;
+    l->n_pad = (n + gemm::BN - 1) / gemm::BN * gemm::BN;
+    const int G = k / 64, N = l->n_pad;
+    std::vector<float> wf(w, w + size_t(n) * k);
+    std::vector<uint8_t> q;
+    std::vector<float> sc;
+    quantize_host(wf, size_t(n), size_t(k), 8, q, sc);
+    std::vector<uint8_t> wq(size_t(N) * k, 0);
+    std::memcpy(wq.data(), q.data(), q.size());
+    std::vector<float> ws(size_t(G) * N, 1.0f);
+    for (int r = 0; r < n; ++r)
+      for (int g = 0; g < G; ++g) ws[size_t(g) * N + r] = sc[size_t(r) * G + g];
+    auto up = [](const void* src, size_t bytes) {
+      DevBuf b(bytes);
+      DG_CUDA(cudaMemcpy(b.ptr, src, bytes, cudaMemcpyHostToDevice));
+      return b;
+    };
+    l->wq = up(wq.data(), wq.size());
+    l->ws_t = up(ws.data(), ws.size() * 4);
+    std::vector<int> pid(N / 32, 0);
+    l->chunk_pid = up(pid.data(), pid.size() * 4);
+    if (rank) {
+      std::vector<float> lb(size_t(N) * rank, 0.0f);
+      std::memcpy(lb.data(), lora_b, size_t(n) * rank * 4);
+      l->lora_b = up(lb.data(), lb.size() * 4);
+      l->lora_a = up(lora_a, size_t(rank) * k * 4);
+    }
+    l->status = DevBuf(sizeof(DeviceStatus));
+    make_tmap_i8_2d(&l->map_b, l->wq.ptr, uint64_t(k), uint64_t(N), gemm::BK, gemm::BN);
+    DG_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
+    *out = l.release();
+  });
+}
+
+int dg_linear_forward(dg_linear* l, const float* x, int m, float* y) {
+  return guarded([&] {
+    if (!l || !x || !y) throw std::runtime_error("null argument");
+    DG_CUDA(cudaSetDevice(l->device));
+    linear_reserve(l, m);
+    DG_CUDA(cudaMemcpyAsync(l->x.ptr, x, size_t(m) * l->k * 4, cudaMemcpyHostToDevice, l->stream));
+    dg::DevBuf out(size_t(m) * l->n * 4);
+    linear_run(l, l->x.as<float>(), m, out.as<float>(), nullptr);
+    DG_CUDA(cudaMemcpyAsync(y, out.ptr, size_t(m) * l->n * 4, cudaMemcpyDeviceToHost, l->stream));
+    DG_CUDA(cudaStreamSynchronize(l->stream));
+  });
+}
+
+int dg_linear_forward_device(dg_linear* l, const float* x_device, int m, float* y_device, int32_t* group_dots_device) {
+  return guarded([&] {
+    if (!l || !x_device || !y_device) throw std::runtime_error("null argument");
+    linear_run(l, x_device, m, y_device, group_dots_device);
+  });
+}
+
+int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs) {
+  return guarded([&] {
+    if (!l || m <= 0 || m > l->cap_m) throw std::runtime_error("no quantized rows of that size");
+    DG_CUDA(cudaSetDevice(l->device));
+    DG_CUDA(cudaMemcpy(xq, l->xq.ptr, size_t(m) * l->k, cudaMemcpyDeviceToHost));
+    for (int g = 0; g < l->k / 64; ++g)
+      DG_CUDA(cudaMemcpy(xs + size_t(g) * m, l->xs.as<float>() + size_t(g) * l->ldxs, size_t(m) * 4,
+                         cudaMemcpyDeviceToHost));
+  });
+}
+
+void* dg_linear_stream(const dg_linear* l) { return l ? static_cast<void*>(l->stream) : nullptr; }
+
+int dg_linear_set_exact(dg_linear* l, int exact) {
+  return guarded([&] {
+    if (!l) throw std::runtime_error("null argument");
+    l->exact = exact != 0;
+  });
+}
+
+void dg_linear_free(dg_linear* l) {
+  if (!l) return;
+  cudaSetDevice(l->device);
+  if (l->stream) {
+    cudaStreamSynchronize(l->stream);
+    cudaStreamDestroy(l->stream);
+  }
+  delete l;
+}
+
+int dg_gated_delta_rule_device(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                               int batch, int t, int heads, float* state, float* o, void* stream) {
+  return guarded([&] {
+    if (!q || !k || !v || !g || !beta || !state || !o) throw std::runtime_error("null argument");
+    if (batch <= 0 || t <= 0 || heads <= 0) throw std::runtime_error("bad gated delta rule shape");
+    dg::DeltaArgs a{};
+    const size_t row = size_t(heads) * 128;
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.ld_qk = a.ld_v = int(row);
+    a.bs_qkv = size_t(t) * row;
+    a.decay = g;
+    a.beta = beta;
+    a.log_decay = 1;
+    a.ld_gb = heads;
+    a.bs_gb = size_t(t) * heads;
+    a.n = t;
+    a.key_heads = a.value_heads = heads;
+    a.dv = 128;
+    a.state = state;
+    a.bs_state = size_t(heads) * 128 * 128;
+    a.o = o;
+    a.ldo = int(row);
+    a.bs_o = size_t(t) * row;
+    dg::launch_delta_rec128(a, batch, static_cast<cudaStream_t>(stream));
+    dg::note_launch();
+  });
+}
+
+}  // extern "C"

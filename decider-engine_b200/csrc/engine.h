@@ -1,0 +1,167 @@
+// Device-resident Qwen3.5 decider torso + pointer head: the executor behind
+// the C ABI. One engine = one GPU, one stream, weights resident in HBM.
+//
+// Replaces qwen::Model (src/qwen.rs:280-505) and Head (src/lib.rs:87-131).
+#pragma once
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemm_i8.cuh"
+#include "launch.h"
+
+namespace dg {
+
+enum Precision { kCheckpoint = 0, kInt8 = 1, kInt8Compute = 2, kInt4 = 3 };
+
+struct Config {
+  int hidden = 0, intermediate = 0, layers = 0, vocab = 0, heads = 0, kv_heads = 0, head_dim = 0;
+  int conv_kernel = 0, dk = 0, dv = 0, key_heads = 0, value_heads = 0;
+  float eps = 1e-6f, rope_theta = 1e7f, partial_rotary = 0.25f;
+  std::vector<int> layer_types;  // 1 = full_attention, 0 = linear_attention
+  int rank = 0;
+  float lora_scale = 0.0f;
+  int pointer_dim = 0;           // 0: no pointer head
+  int rotary_dim() const { return int(float(head_dim) * partial_rotary); }
+  int kd() const { return key_heads * dk; }
+  int vd() const { return value_heads * dv; }
+  int conv_width() const { return 2 * kd() + vd(); }
+  int qw() const { return heads * head_dim; }
+  int kw() const { return kv_heads * head_dim; }
+  void validate() const;
+};
+
+// Device buffer with RAII.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  explicit DevBuf(size_t n);
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes) { o.ptr = nullptr; o.bytes = 0; }
+  DevBuf& operator=(DevBuf&& o) noexcept;
+  ~DevBuf();
+  template <class T> T* as() const { return static_cast<T*>(ptr); }
+};
+
+// Host-side staged tensor (FP32, or already quantized projection weights).
+struct HostTensor {
+  std::vector<int64_t> shape;
+  std::vector<float> f32;
+  bool quantized = false;
+  int bits = 0;
+  std::vector<uint8_t> q;      // bits 8: [rows][width]; bits 4: packed as the reference
+  std::vector<float> scales;   // [rows][ceil(width/64)]
+};
+
+// Data::quantize (src/weights.rs:98-146) of an F32 [rows][width] tensor:
+// bits 8 -> one byte per value, bits 4 -> nibbles packed as the reference.
+void quantize_host(const std::vector<float>& w, size_t rows, size_t width, int bits, std::vector<uint8_t>& q,
+                   std::vector<float>& scales);
+
+// One (possibly fused) projection on the device.
+struct DevProj {
+  int in = 0, out = 0, out_pad = 0;
+  // tcgen05 path (int8-compute, aligned shapes)
+  DevBuf wq, ws_t, lora_a, lora_b, chunk_pid;
+  CUtensorMap map_b{};
+  int lora_rows = 0;             // rows of lora_a (= projections sharing the input x rank)
+  std::vector<int> part_off;     // output column of each fused part
+  // generic path
+  GenericProj g{};
+  DevBuf w_f32, scale_rows, bias;
+};
+
+struct Layer {
+  bool full = false;
+  DevBuf input_norm, post_norm;
+  // fast path: fused input projection and single output projection
+  DevProj in_proj, out_proj, mlp_in, down;
+  // generic path: separate projections in reference order
+  std::vector<DevProj> parts;    // DeltaNet: qkv,z,a,b,out ; attention: q,k,v,o ; then gate,up,down
+  DevBuf q_norm, k_norm;          // attention
+  DevBuf conv, dt, decay_rate, norm;  // DeltaNet (conv tap-major)
+};
+
+struct Prefix {
+  int len = 0;
+  struct LayerState {
+    bool full = false;
+    DevBuf k, v;          // [len][kw]
+    DevBuf tail, state;   // [rows][W], [H][dk][dv]
+    int tail_rows = 0;
+  };
+  std::vector<LayerState> layers;
+};
+
+class Engine {
+ public:
+  Engine(const Config& c, int precision, int device, int max_tokens);
+  ~Engine();
+  void set_tensor(const std::string& name, int dtype, const std::vector<int64_t>& shape, const void* data);
+  void fill_synthetic(uint64_t seed, float stddev);
+  void finalize();
+  // Model::run: hidden [n][hidden] to host (nullable); capture -> new prefix.
+  void forward(const uint32_t* ids, int n, const Prefix* past, bool capture, float* hidden_out,
+               std::unique_ptr<Prefix>* captured);
+  // Head::logits on the last forward's hidden rows (device-resident).
+  void head_logits(int rows, const size_t* positions, int n_pos, float* logits_out);
+  const Config& config() const { return c_; }
+  bool fast_path() const { return fast_; }
+  int device() const { return device_; }
+  cudaStream_t stream() const { return stream_; }
+  std::mutex mu;
+  // Exact FP32 promotion order in the tcgen05 projections (reference order).
+  bool exact = true;
+  // Device launches issued by the last forward (kernels only).
+  int last_launches = 0;
+  // Device time of the last forward's kernels (after the id upload, before
+  // the hidden-state download), from CUDA events on the engine stream.
+  float last_forward_ms = 0.0f;
+
+ private:
+  struct Expected {
+    std::vector<int64_t> shape;
+    bool projection;
+  };
+  std::map<std::string, Expected> expected_names() const;
+  void stage(const std::string& name, std::vector<int64_t> shape, std::vector<float>&& f32);
+  HostTensor take(const std::string& name);
+  DevBuf upload_f32(const std::vector<float>& v);
+  void build_fast_layer(int i, Layer& L);
+  void build_generic_layer(int i, Layer& L);
+  DevProj build_generic_proj(const std::string& key, int in, int out, bool lora, bool bias);
+  DevProj build_fused(const std::vector<std::string>& keys, const std::vector<int>& outs, int in, bool interleave_mlp);
+  void run_proj_fast(const DevProj& p, int M, const float* mid, float* out, int ldo, int epi);
+  void run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi);
+  void layer_fast(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap);
+  void layer_generic(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap);
+  void mixer_tail(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap,
+                  const float* raw, int ldr);
+  void check_status();
+
+  Config c_;
+  int precision_, device_, max_tokens_;
+  bool fast_ = false, finalized_ = false;
+  cudaStream_t stream_ = nullptr;
+  std::map<std::string, HostTensor> staged_;
+  std::vector<Layer> layers_;
+  DevBuf embedding_, final_norm_, rope_;
+  int rope_half_ = 0;
+  // pointer head
+  DevBuf head_norm_w_, head_norm_b_;
+  DevProj head_q_, head_k_;
+  // workspace
+  int ldxs_ = 0, ld_proj_ = 0;
+  DevBuf ids_, x_, n_, xq_, xs_, mid_, proj_, conv_, decay_, beta_, o_, ofin_, h_, qbuf_, att_;
+  DevBuf hrows_, hnorm_, hq_, hk_, hlogits_, hrow_idx_;
+  std::vector<DevBuf> kcache_, vcache_, state_;
+  DevBuf status_;
+  cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
+  DeviceStatus* status() const { return status_.as<DeviceStatus>(); }
+};
+
+}  // namespace dg

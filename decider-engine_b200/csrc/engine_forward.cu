@@ -1,0 +1,300 @@
+// Engine::forward: Model::run (src/qwen.rs:426-504) on the device, plus the
+// pointer head (src/lib.rs:116-131).
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <utility>
+
+#include "engine.h"
+
+namespace dg {
+
+struct DgError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+// Activation tensor maps, cached per (buffer, K, rows): the rows extent makes
+// TMA fill rows past the sequence with zeros.
+static const CUtensorMap& act_map(const void* base, int K, int rows) {
+  static thread_local std::map<std::tuple<const void*, int, int>, CUtensorMap> cache;
+  auto key = std::make_tuple(base, K, rows);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  CUtensorMap m;
+  make_tmap_i8_2d(&m, base, uint64_t(K), uint64_t(rows), gemm::BK, gemm::BM);
+  return cache.emplace(key, m).first->second;
+}
+
+void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out, int ldo, int epi) {
+  GemmArgs a{};
+  a.M = M;
+  a.N = p.out_pad;
+  a.K = p.in;
+  a.xs = xs_.as<float>();
+  a.ldxs = ldxs_;
+  a.ws = p.ws_t.as<float>();
+  a.lora_mid = mid;
+  a.ld_mid = 128;
+  a.lora_b = p.lora_b.as<float>();
+  a.chunk_pid = p.chunk_pid.as<int>();
+  a.lora_scale = c_.lora_scale;
+  a.out = out;
+  a.ldo = ldo;
+  a.status = status();
+  launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.map_b, a, 32, epi, exact, stream_);
+  note_launch();
+}
+
+void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi) {
+  if (p.lora_rows) {
+    launch_lora_a(x, ldx, M, p.in, p.lora_a.as<float>(), p.lora_rows, mid_.as<float>(), 128, true, stream_);
+    note_launch();
+  }
+  launch_proj_generic(p.g, x, ldx, xq_.as<int8_t>(), xs_.as<float>(), ldxs_, mid_.as<float>(), 128, M, out, ldo, epi,
+                      stream_);
+  note_launch();
+}
+
+// DeltaNet mixer after the input projections (src/qwen.rs:667-693): conv with
+// the prefix tail, recurrence from the prefix state, gated norm; captures the
+// next tail and state when prefilling.
+void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap,
+                        const float* raw, int ldr) {
+  const Config& c = c_;
+  const Layer& L = layers_[i];
+  const int W = c.conv_width(), k = c.conv_kernel, H = c.value_heads;
+  const float* tail = past ? past->tail.as<float>() : nullptr;
+  const int tail_rows = past ? past->tail_rows : 0;
+  if (tail_rows != std::min(start, k - 1)) throw DgError("prefix cache does not match the layer types");
+  const int* off = L.in_proj.part_off.data();
+  float* base = proj_.as<float>();
+  launch_conv_silu(raw, ldr, n, tail, tail_rows, start, W, k, L.conv.as<float>(), conv_.as<float>(), stream_);
+  launch_delta_prep(conv_.as<float>(), W, n, c.key_heads, c.dk, H, base + off[2], base + off[3], ldr,
+                    L.decay_rate.as<float>(), L.dt.as<float>(), decay_.as<float>(), beta_.as<float>(), stream_);
+  const size_t sbytes = size_t(H) * c.dk * c.dv * 4;
+  if (past)
+    DG_CUDA(cudaMemcpyAsync(state_[i].ptr, past->state.ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
+  else
+    DG_CUDA(cudaMemsetAsync(state_[i].ptr, 0, sbytes, stream_));
+  launch_delta_recurrence(conv_.as<float>(), n, c.key_heads, c.dk, H, c.dv, decay_.as<float>(), beta_.as<float>(),
+                          state_[i].as<float>(), o_.as<float>(), stream_);
+  const bool q = precision_ == kInt8Compute;
+  launch_gated_norm_quant(o_.as<float>(), base + off[1], ldr, n, H, c.dv, L.norm.as<float>(), c.eps, ofin_.as<float>(),
+                          xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);
+  for (int j = 0; j < 5; ++j) note_launch();
+  if (cap) {
+    cap->full = false;
+    cap->state = DevBuf(sbytes);
+    DG_CUDA(cudaMemcpyAsync(cap->state.ptr, state_[i].ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
+    const int keep = std::min(start + n, k - 1), from_tail = std::max(0, keep - n), from_raw = keep - from_tail;
+    cap->tail_rows = keep;
+    cap->tail = DevBuf(size_t(std::max(keep, 1)) * W * 4);
+    if (from_tail)
+      DG_CUDA(cudaMemcpyAsync(cap->tail.ptr, tail + size_t(tail_rows - from_tail) * W, size_t(from_tail) * W * 4,
+                              cudaMemcpyDeviceToDevice, stream_));
+    if (from_raw)
+      DG_CUDA(cudaMemcpy2DAsync(cap->tail.as<float>() + size_t(from_tail) * W, size_t(W) * 4,
+                                raw + size_t(n - from_raw) * ldr, size_t(ldr) * 4, size_t(W) * 4, from_raw,
+                                cudaMemcpyDeviceToDevice, stream_));
+  }
+}
+
+void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap) {
+  const Config& c = c_;
+  const Layer& L = layers_[i];
+  const int H = c.hidden, I = c.intermediate;
+  float* x = x_.as<float>();
+  float* nb = n_.as<float>();
+  float* mid = mid_.as<float>();
+  float* proj = proj_.as<float>();
+  launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
+                    status(), stream_);
+  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_);
+  note_launch();
+  note_launch();
+  run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
+  const float* mixed_in;
+  int kin;
+  if (L.full) {
+    const int d = c.head_dim, kw = c.kw();
+    if (past) {
+      DG_CUDA(cudaMemcpyAsync(kcache_[i].ptr, past->k.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+      DG_CUDA(cudaMemcpyAsync(vcache_[i].ptr, past->v.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+    }
+    launch_qk_norm_rope(proj, ld_proj_, n, c.heads, c.kv_heads, d, L.q_norm.as<float>(), L.k_norm.as<float>(), c.eps,
+                        rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
+                        vcache_[i].as<float>(), stream_);
+    launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
+                     c.heads, c.kv_heads, d, att_.as<float>(), stream_);
+    launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(),
+                      xs_.as<float>(), ldxs_, status(), stream_);
+    for (int j = 0; j < 3; ++j) note_launch();
+    if (cap) {
+      cap->full = true;
+      cap->k = DevBuf(size_t(start + n) * kw * 4);
+      cap->v = DevBuf(size_t(start + n) * kw * 4);
+      DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
+      DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
+    }
+    mixed_in = att_.as<float>();
+    kin = c.qw();
+  } else {
+    mixer_tail(i, n, start, past, cap, proj, ld_proj_);
+    mixed_in = ofin_.as<float>();
+    kin = c.vd();
+  }
+  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_);
+  note_launch();
+  run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
+  launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
+                    status(), stream_);
+  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_);
+  note_launch();
+  note_launch();
+  run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
+  launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
+                    status(), stream_);
+  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_);
+  note_launch();
+  note_launch();
+  run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
+}
+
+void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap) {
+  const Config& c = c_;
+  const Layer& L = layers_[i];
+  const int H = c.hidden, I = c.intermediate;
+  const bool q = precision_ == kInt8Compute;
+  float* x = x_.as<float>();
+  float* nb = n_.as<float>();
+  float* proj = proj_.as<float>();
+  int8_t* xq = q ? xq_.as<int8_t>() : nullptr;
+  launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq, xs_.as<float>(), ldxs_, status(), stream_);
+  note_launch();
+  const int* off = L.in_proj.part_off.data();
+  int mlp = 0;
+  if (L.full) {
+    for (int p = 0; p < 3; ++p) run_proj_generic(L.parts[p], nb, H, n, proj + off[p], ld_proj_, kEpiWrite);
+    const int d = c.head_dim, kw = c.kw();
+    if (past) {
+      DG_CUDA(cudaMemcpyAsync(kcache_[i].ptr, past->k.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+      DG_CUDA(cudaMemcpyAsync(vcache_[i].ptr, past->v.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+    }
+    launch_qk_norm_rope(proj, ld_proj_, n, c.heads, c.kv_heads, d, L.q_norm.as<float>(), L.k_norm.as<float>(), c.eps,
+                        rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
+                        vcache_[i].as<float>(), stream_);
+    launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
+                     c.heads, c.kv_heads, d, att_.as<float>(), stream_);
+    note_launch();
+    note_launch();
+    if (q) {
+      launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq, xs_.as<float>(), ldxs_,
+                        status(), stream_);
+      note_launch();
+    }
+    if (cap) {
+      cap->full = true;
+      cap->k = DevBuf(size_t(start + n) * kw * 4);
+      cap->v = DevBuf(size_t(start + n) * kw * 4);
+      DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
+      DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
+    }
+    run_proj_generic(L.parts[3], att_.as<float>(), c.qw(), n, x, H, kEpiAdd);
+    mlp = 4;
+  } else {
+    for (int p = 0; p < 4; ++p) run_proj_generic(L.parts[p], nb, H, n, proj + off[p], ld_proj_, kEpiWrite);
+    mixer_tail(i, n, start, past, cap, proj, ld_proj_);
+    run_proj_generic(L.parts[4], ofin_.as<float>(), c.vd(), n, x, H, kEpiAdd);
+    mlp = 5;
+  }
+  launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq, xs_.as<float>(), ldxs_, status(), stream_);
+  note_launch();
+  run_proj_generic(L.parts[mlp], nb, H, n, h_.as<float>(), I, kEpiWrite);
+  run_proj_generic(L.parts[mlp + 1], nb, H, n, h_.as<float>(), I, kEpiSwiGlu);
+  if (q) {
+    launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq, xs_.as<float>(), ldxs_, status(),
+                      stream_);
+    note_launch();
+  }
+  run_proj_generic(L.parts[mlp + 2], h_.as<float>(), I, n, x, H, kEpiAdd);
+}
+
+void Engine::check_status() {
+  DeviceStatus st{};
+  DG_CUDA(cudaMemcpyAsync(&st, status_.ptr, sizeof(st), cudaMemcpyDeviceToHost, stream_));
+  DG_CUDA(cudaStreamSynchronize(stream_));
+  if (st.code == kNonFinite) throw DgError("non-finite Qwen hidden states");
+  if (st.code == kWaitTimeout)
+    throw DgError("device pipeline wait timed out (location " + std::to_string(st.where) + ")");
+  if (st.code) throw DgError("device error code " + std::to_string(st.code));
+}
+
+void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool capture, float* hidden_out,
+                     std::unique_ptr<Prefix>* captured) {
+  if (!finalized_) throw DgError("engine is not finalized");
+  const int start = past ? past->len : 0;
+  if (n <= 0 || start + n > 4096) throw DgError("token sequence must contain 1\xe2\x80\x93" "4096 tokens");
+  if (n > max_tokens_) throw DgError("token sequence exceeds the engine's max_tokens workspace");
+  for (int t = 0; t < n; ++t)
+    if (ids[t] >= uint32_t(c_.vocab)) throw DgError("token " + std::to_string(ids[t]) + " outside vocabulary");
+  if (past && int(past->layers.size()) != c_.layers) throw DgError("prefix cache does not match the layer types");
+  if (past)
+    for (int i = 0; i < c_.layers; ++i)
+      if (past->layers[i].full != layers_[i].full) throw DgError("prefix cache does not match the layer types");
+  DG_CUDA(cudaSetDevice(device_));
+  const uint64_t launches0 = launch_count();
+  std::unique_ptr<Prefix> cap;
+  if (capture) {
+    cap.reset(new Prefix());
+    cap->len = start + n;
+    cap->layers.resize(c_.layers);
+  }
+  DG_CUDA(cudaMemcpyAsync(ids_.ptr, ids, size_t(n) * 4, cudaMemcpyHostToDevice, stream_));
+  DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
+  DG_CUDA(cudaEventRecord(ev0_, stream_));
+  launch_embed(embedding_.ptr, 0, c_.hidden, ids_.as<uint32_t>(), n, x_.as<float>(), stream_);
+  note_launch();
+  for (int i = 0; i < c_.layers; ++i) {
+    const Prefix::LayerState* lp = past ? &past->layers[i] : nullptr;
+    Prefix::LayerState* lc = cap ? &cap->layers[i] : nullptr;
+    if (fast_)
+      layer_fast(i, n, start, lp, lc);
+    else
+      layer_generic(i, n, start, lp, lc);
+  }
+  launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
+  note_launch();
+  DG_CUDA(cudaEventRecord(ev1_, stream_));
+  if (hidden_out)
+    DG_CUDA(cudaMemcpyAsync(hidden_out, x_.ptr, size_t(n) * c_.hidden * 4, cudaMemcpyDeviceToHost, stream_));
+  check_status();
+  DG_CUDA(cudaEventElapsedTime(&last_forward_ms, ev0_, ev1_));
+  last_launches = int(launch_count() - launches0);
+  if (capture) *captured = std::move(cap);
+}
+
+void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* logits_out) {
+  if (c_.pointer_dim <= 0) throw DgError("engine has no pointer head");
+  if (n_pos <= 0 || n_pos + 1 > 512) throw DgError("invalid encoding positions or window");
+  std::vector<int> idx(n_pos + 1);
+  idx[0] = rows - 1;
+  for (int i = 0; i < n_pos; ++i) {
+    if (positions[i] >= size_t(rows)) throw DgError("invalid encoding positions or window");
+    idx[i + 1] = int(positions[i]);
+  }
+  const int H = c_.hidden, P = c_.pointer_dim;
+  DG_CUDA(cudaMemcpyAsync(hrow_idx_.ptr, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, stream_));
+  launch_head_norm(x_.as<float>(), H, hrow_idx_.as<int>(), n_pos + 1, head_norm_w_.as<float>(),
+                   head_norm_b_.as<float>(), hnorm_.as<float>(), stream_);
+  launch_proj_generic(head_q_.g, hnorm_.as<float>(), H, nullptr, nullptr, 0, nullptr, 0, 1, hq_.as<float>(), P,
+                      kEpiWrite, stream_);
+  launch_proj_generic(head_k_.g, hnorm_.as<float>() + H, H, nullptr, nullptr, 0, nullptr, 0, n_pos, hk_.as<float>(), P,
+                      kEpiWrite, stream_);
+  launch_head_dot(hq_.as<float>(), hk_.as<float>(), n_pos, P, 1.0f / std::sqrt(float(P)), hlogits_.as<float>(),
+                  stream_);
+  for (int j = 0; j < 4; ++j) note_launch();
+  DG_CUDA(cudaMemcpyAsync(logits_out, hlogits_.ptr, size_t(n_pos) * 4, cudaMemcpyDeviceToHost, stream_));
+  DG_CUDA(cudaStreamSynchronize(stream_));
+}
+
+}  // namespace dg

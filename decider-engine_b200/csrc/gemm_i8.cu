@@ -1,0 +1,79 @@
+// Launchers and instantiations of the tcgen05 INT8 projection.
+#include <mutex>
+
+#include "gemm_i8.cuh"
+#include "launch.h"
+
+namespace dg {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) throw CudaError("cuTensorMapEncodeTiled is unavailable");
+  return fn;
+}
+
+// Row-major int8 matrix [outer][inner] (inner contiguous), 128-byte swizzled boxes.
+void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                     uint32_t box_outer) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || inner % 16)
+    throw CudaError("TMA operand must be 16-byte aligned with a 16-byte multiple row stride");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+}
+
+size_t gemm_i8_smem_bytes(int rank) { return size_t(gemm::smem_bytes(rank)); }
+
+template <int R, int EPI, bool EXACT>
+static void launch_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+  auto kern = gemm_i8_g64_kernel<R, EPI, EXACT>;
+  const int smem = gemm::smem_bytes(R);
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((args.M + gemm::BM - 1) / gemm::BM, args.N / gemm::BN);
+  kern<<<grid, gemm::NUM_THREADS, smem, s>>>(a, b, args);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_gemm_i8(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi, bool exact,
+                    cudaStream_t s) {
+  if (args.M <= 0) return;
+  if (args.N % gemm::BN || args.K % gemm::BK || args.K <= 0)
+    throw CudaError("gemm_i8: N must be a multiple of 256 and K a positive multiple of 128");
+  if (args.ldxs % gemm::BM || args.ldxs < ((args.M + gemm::BM - 1) / gemm::BM) * gemm::BM)
+    throw CudaError("gemm_i8: activation-scale stride must cover whole 128-row tiles");
+  if (rank != 0 && rank != 32) throw CudaError("gemm_i8: LoRA rank must be 0 or 32");
+  if (rank && (args.ld_mid % 4 || !args.lora_mid || !args.lora_b || !args.chunk_pid))
+    throw CudaError("gemm_i8: bad LoRA operands");
+  if (epi == kEpiSwiGlu ? (args.ldo % 4) : (args.ldo % 4 || args.ldo < args.N))
+    throw CudaError("gemm_i8: output stride must be a multiple of 4 covering the tile");
+#define DG_GEMM_CASE(R_, E_, X_) \
+  if (rank == R_ && epi == E_ && exact == X_) return launch_impl<R_, E_, X_>(a, b, args, s);
+  DG_GEMM_CASE(32, kEpiWrite, true) DG_GEMM_CASE(32, kEpiAdd, true) DG_GEMM_CASE(32, kEpiSwiGlu, true)
+  DG_GEMM_CASE(32, kEpiWrite, false) DG_GEMM_CASE(32, kEpiAdd, false) DG_GEMM_CASE(32, kEpiSwiGlu, false)
+  DG_GEMM_CASE(0, kEpiWrite, true) DG_GEMM_CASE(0, kEpiWrite, false)
+#undef DG_GEMM_CASE
+  throw CudaError("gemm_i8: unsupported rank/epilogue combination");
+}
+
+}  // namespace dg

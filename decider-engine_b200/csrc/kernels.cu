@@ -1,0 +1,308 @@
+// Normalisation, quantisation, LoRA-A, generic projection and embedding kernels.
+// Compiled with -fmad=false (see common.cuh): reference-order arithmetic by default.
+#include <cfloat>
+
+#include "launch.h"
+
+namespace dg {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+// Block-wide sum for blockDim.x == 256 (8 warps); all threads get the result.
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = l < 8 ? red[l] : 0.0f;
+  t = warp_sum(t);
+  return t;
+}
+
+// QuantizedInputs::new per 64-wide group (src/tensor.rs:328-339): scale =
+// max|v|/127 (at least FLT_MIN; 1.0 for an all-zero group), q = round(v/scale)
+// clamped to +-127. `vals` points at the group in shared memory; one warp
+// quantises one group of `len` <= 64 values.
+__device__ __forceinline__ void quantize_group_warp(const float* vals, int len, int8_t* q_out, float* scale_out,
+                                                    bool* nonfinite) {
+  const int l = threadIdx.x % 32;
+  float a = l < len ? vals[l] : 0.0f, b = l + 32 < len ? vals[l + 32] : 0.0f;
+  bool bad = !isfinite(a) || !isfinite(b);
+  if (__any_sync(0xffffffffu, bad)) *nonfinite = true;
+  float mx = warp_max(fmaxf(fabsf(a), fabsf(b)));
+  float scale = mx == 0.0f ? 1.0f : fmaxf(mx / 127.0f, FLT_MIN);
+  if (l < len) q_out[l] = int8_t(fminf(fmaxf(roundf(a / scale), -127.0f), 127.0f));
+  if (l + 32 < len) q_out[l + 32] = int8_t(fminf(fmaxf(roundf(b / scale), -127.0f), 127.0f));
+  if (l == 0) *scale_out = scale;
+}
+
+// One 256-thread CTA per row.
+__global__ void norm_quant_kernel(const float* __restrict__ x, int ldx, int K, const float* __restrict__ gamma,
+                                  float eps, float* __restrict__ n_out, int ldn, int8_t* __restrict__ xq,
+                                  float* __restrict__ xs, int ldxs, DeviceStatus* st) {
+  extern __shared__ float row[];
+  __shared__ float red[8];
+  const int m = blockIdx.x;
+  const float* xr = x + size_t(m) * ldx;
+  float ss = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = xr[k];
+    row[k] = v;
+    ss = __fmaf_rn(v, v, ss);
+  }
+  if (gamma) {
+    // rms, src/qwen.rs:208-217: v * (inv * (1 + g)), inv = 1/sqrt(mean(v^2) + eps).
+    const float total = block_sum_256(ss, red);
+    const float inv = 1.0f / sqrtf(total / float(K) + eps);
+    for (int k = threadIdx.x; k < K; k += 256) row[k] = row[k] * (inv * (1.0f + gamma[k]));
+  }
+  __syncthreads();
+  if (n_out)
+    for (int k = threadIdx.x; k < K; k += 256) n_out[size_t(m) * ldn + k] = row[k];
+  if (xq) {
+    __shared__ bool nonfinite;
+    if (threadIdx.x == 0) nonfinite = false;
+    __syncthreads();
+    const int G = (K + 63) / 64;
+    for (int g = threadIdx.x / 32; g < G; g += 8) {
+      const int len = min(64, K - g * 64);
+      quantize_group_warp(row + g * 64, len, xq + size_t(m) * K + g * 64, xs + size_t(g) * ldxs + m, &nonfinite);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && nonfinite) report(st, kNonFinite, 1);
+  }
+}
+
+// Recurrence::head's output step (src/qwen.rs:867-873): per value head,
+// o = rms(o, w) (non-centred weight) then o *= silu(z). One CTA per token.
+__global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float* __restrict__ z, int ldz, int heads,
+                                        int dv, const float* __restrict__ w, float eps, float* __restrict__ out,
+                                        int8_t* __restrict__ xq, float* __restrict__ xs, int ldxs, int quantize,
+                                        DeviceStatus* st) {
+  extern __shared__ float row[];
+  const int m = blockIdx.x, K = heads * dv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int h = warp; h < heads; h += 8) {
+    const float* oh = o + size_t(m) * K + h * dv;
+    float ss = 0.0f;
+    for (int j = lane; j < dv; j += 32) ss = __fmaf_rn(oh[j], oh[j], ss);
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(dv) + eps);
+    for (int j = lane; j < dv; j += 32) {
+      const float v = oh[j] * (inv * w[j]);
+      row[h * dv + j] = v * silu_f(z[size_t(m) * ldz + h * dv + j]);
+    }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < K; k += 256) out[size_t(m) * K + k] = row[k];
+  if (quantize) {
+    __shared__ bool nonfinite;
+    if (threadIdx.x == 0) nonfinite = false;
+    __syncthreads();
+    const int G = (K + 63) / 64;
+    for (int g = warp; g < G; g += 8)
+      quantize_group_warp(row + g * 64, min(64, K - g * 64), xq + size_t(m) * K + g * 64, xs + size_t(g) * ldxs + m,
+                          &nonfinite);
+    __syncthreads();
+    if (threadIdx.x == 0 && nonfinite) report(st, kNonFinite, 2);
+  }
+}
+
+// LoRA A: mid[m][r] = dot_scores(x[m], A[r]) (src/tensor.rs:6-25 order when
+// EXACT: eight lanes over k % 8, each mul-then-add, lanes summed from -0.0,
+// then the tail). Tile: 16 rows x 32 outputs per 256-thread CTA, 64-wide K chunks.
+template <bool EXACT>
+__global__ void lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K, const float* __restrict__ A, int R,
+                              float* __restrict__ mid, int ldm) {
+  constexpr int TM = 16, TR = 32, KC = 64;
+  __shared__ float xs_[TM][KC + 1];
+  __shared__ float as_[TR][KC + 1];
+  const int r_local = threadIdx.x % 32, m_local0 = (threadIdx.x / 32) * 2;
+  const int m_base = blockIdx.x * TM, r_base = blockIdx.y * TR;
+  const int r = r_base + r_local;
+  float lanes[2][8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int l = 0; l < 8; ++l) lanes[i][l] = 0.0f;
+  const int kfull = (K / 8) * 8;  // lane-ordered part; the tail is added afterwards
+  for (int k0 = 0; k0 < kfull; k0 += KC) {
+    for (int i = threadIdx.x; i < TM * KC; i += 256) {
+      const int mm = i / KC, kk = i % KC, m = m_base + mm, k = k0 + kk;
+      xs_[mm][kk] = (m < M && k < kfull) ? x[size_t(m) * ldx + k] : 0.0f;
+    }
+    for (int i = threadIdx.x; i < TR * KC; i += 256) {
+      const int rr = i / KC, kk = i % KC, rg = r_base + rr, k = k0 + kk;
+      as_[rr][kk] = (rg < R && k < kfull) ? A[size_t(rg) * K + k] : 0.0f;
+    }
+    __syncthreads();
+    const int kc = min(KC, kfull - k0);
+    for (int kk = 0; kk < kc; kk += 8) {
+#pragma unroll
+      for (int l = 0; l < 8; ++l) {
+        const float a = as_[r_local][kk + l];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float xv = xs_[m_local0 + i][kk + l];
+          if (EXACT)
+            lanes[i][l] = __fadd_rn(lanes[i][l], __fmul_rn(xv, a));
+          else
+            lanes[i][l] = __fmaf_rn(xv, a, lanes[i][l]);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (r >= R) return;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = m_base + m_local0 + i;
+    if (m >= M) continue;
+    float s = -0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, lanes[i][l]);
+    for (int k = kfull; k < K; ++k) s = __fadd_rn(s, __fmul_rn(x[size_t(m) * ldx + k], A[size_t(r) * K + k]));
+    mid[size_t(m) * ldm + r] = s;
+  }
+}
+
+__device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale, int precision, int n, int k, int K) {
+  const int G = (K + 63) / 64;
+  const float sc = wscale[size_t(n) * G + k / 64];
+  if (precision == 3) {
+    const size_t i = size_t(n) * K + k;
+    const int nib = (wq[i / 2] >> (4 * (i % 2))) & 15;
+    return (float(nib) - 8.0f) * sc;
+  }
+  return float(int8_t(wq[size_t(n) * K + k])) * sc;
+}
+
+// Generic projection: one thread per output (m, n), reference arithmetic
+// (linear_int8 scaled dots or dot_scores over expanded weights, + bias or 0.0,
+// Adapter::combine, Epilogue::store).
+__global__ void proj_generic_kernel(GenericProj p, const float* __restrict__ x, int ldx, const int8_t* __restrict__ xq,
+                                    const float* __restrict__ xs, int ldxs, const float* __restrict__ mid, int ldm,
+                                    int M, float* __restrict__ out, int ldo, int epi) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+  if (n >= p.out || m >= M) return;
+  const int K = p.in;
+  float base;
+  if (p.precision == 2) {
+    const int G = (K + 63) / 64;
+    float sum = 0.0f;
+    for (int g = 0; g < G; ++g) {
+      int dot = 0;
+      const int len = min(64, K - g * 64);
+      for (int k = 0; k < len; ++k)
+        dot += int(xq[size_t(m) * K + g * 64 + k]) * int(int8_t(p.wq[size_t(n) * K + g * 64 + k]));
+      sum = sum + float(dot) * (xs[size_t(g) * ldxs + m] * p.wscale[size_t(n) * G + g]);
+    }
+    base = sum;
+  } else {
+    float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int kfull = (K / 8) * 8;
+    const float* xr = x + size_t(m) * ldx;
+    for (int k = 0; k < kfull; ++k) {
+      const float w = p.precision == 0 ? p.w[size_t(n) * K + k] : dequant(p.wq, p.wscale, p.precision, n, k, K);
+      lanes[k & 7] = lanes[k & 7] + xr[k] * w;
+    }
+    float s = -0.0f;
+    for (int l = 0; l < 8; ++l) s = s + lanes[l];
+    for (int k = kfull; k < K; ++k) {
+      const float w = p.precision == 0 ? p.w[size_t(n) * K + k] : dequant(p.wq, p.wscale, p.precision, n, k, K);
+      s = s + xr[k] * w;
+    }
+    base = s;
+  }
+  base = base + (p.bias ? p.bias[n] : 0.0f);
+  float v = base;
+  if (p.lora_b) {
+    const float* mr = mid + size_t(m) * ldm;
+    const float* br = p.lora_b + size_t(n) * p.rank;
+    float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int rfull = (p.rank / 8) * 8;
+    for (int r = 0; r < rfull; ++r) lanes[r & 7] = lanes[r & 7] + mr[r] * br[r];
+    float d = -0.0f;
+    for (int l = 0; l < 8; ++l) d = d + lanes[l];
+    for (int r = rfull; r < p.rank; ++r) d = d + mr[r] * br[r];
+    d = d + 0.0f;
+    v = base + p.lora_scale * d;
+  }
+  float* o = out + size_t(m) * ldo + n;
+  if (epi == kEpiWrite)
+    *o = v;
+  else if (epi == kEpiAdd)
+    *o = *o + v;
+  else
+    *o = silu_f(*o) * v;
+}
+
+__global__ void embed_kernel(const void* table, int dtype, int hidden, const uint32_t* ids, float* x) {
+  const int t = blockIdx.x;
+  const size_t row = size_t(ids[t]) * hidden;
+  for (int k = threadIdx.x; k < hidden; k += blockDim.x) {
+    float v;
+    if (dtype == 0)
+      v = static_cast<const float*>(table)[row + k];
+    else
+      v = __uint_as_float(uint32_t(static_cast<const uint16_t*>(table)[row + k]) << 16);
+    x[size_t(t) * hidden + k] = v;
+  }
+}
+
+}  // namespace
+
+void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma, float eps, float* n_out, int ldn,
+                       int8_t* xq, float* xs, int ldxs, DeviceStatus* st, cudaStream_t s) {
+  if (M <= 0) return;
+  if (K > 12288) throw CudaError("norm_quant: row too wide");
+  norm_quant_kernel<<<M, 256, K * sizeof(float), s>>>(x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int heads, int dv, const float* w,
+                             float eps, float* out, int8_t* xq, float* xs, int ldxs, bool quantize, DeviceStatus* st,
+                             cudaStream_t s) {
+  if (M <= 0) return;
+  gated_norm_quant_kernel<<<M, 256, heads * dv * sizeof(float), s>>>(o, z, ldz, heads, dv, w, eps, out, xq, xs, ldxs,
+                                                                      quantize ? 1 : 0, st);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
+                   cudaStream_t s) {
+  if (M <= 0 || R <= 0) return;
+  dim3 grid((M + 15) / 16, (R + 31) / 32);
+  if (exact)
+    lora_a_kernel<true><<<grid, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  else
+    lora_a_kernel<false><<<grid, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const int8_t* xq, const float* xs, int ldxs,
+                         const float* mid, int ldm, int M, float* out, int ldo, int epi, cudaStream_t s) {
+  if (M <= 0) return;
+  dim3 grid((p.out + 127) / 128, M);
+  proj_generic_kernel<<<grid, 128, 0, s>>>(p, x, ldx, xq, xs, ldxs, mid, ldm, M, out, ldo, epi);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids, int n, float* x, cudaStream_t s) {
+  if (n <= 0) return;
+  embed_kernel<<<n, 256, 0, s>>>(table, dtype, hidden, ids, x);
+  DG_CUDA(cudaGetLastError());
+}
+
+}  // namespace dg

@@ -1,0 +1,341 @@
+// Gated GQA attention with partial RoPE and the shared-prefix KV cache, the
+// final norm, and the pointer head (src/qwen.rs:530-643, src/lib.rs:106-131).
+#include <cfloat>
+
+#include "launch.h"
+
+namespace dg {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Full::forward's pre-attention steps (src/qwen.rs:542-566): split q|gate per
+// head, centred RMSNorm of q and k per head (eps), partial RoPE on pairs
+// (i, i + half) from the table rope[pos][i] = (sin, cos), and append the
+// normalised, rotated k and the raw v at position start + t. One warp per
+// vector (heads q vectors + kv_heads k vectors + kv_heads v vectors per token).
+__global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int ldq, int heads, int kv_heads, int d,
+                                    const float* __restrict__ qn, const float* __restrict__ kn, float eps,
+                                    const float* __restrict__ rope, int half, int start, float* __restrict__ q_out,
+                                    float* __restrict__ kcache, float* __restrict__ vcache) {
+  extern __shared__ float buf[];  // [warps][d]
+  const int t = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  float* x = buf + warp * d;
+  const float* row = qkv + size_t(t) * ldq;
+  const int pos = start + t, kw = kv_heads * d;
+  for (int v = warp; v < heads + 2 * kv_heads; v += nw) {
+    const float* src;
+    const float* g = nullptr;
+    float* dst;
+    if (v < heads) {
+      src = row + size_t(v) * 2 * d;
+      g = qn;
+      dst = q_out + (size_t(t) * heads + v) * d;
+    } else if (v < heads + kv_heads) {
+      const int kh = v - heads;
+      src = row + size_t(heads) * 2 * d + kh * d;
+      g = kn;
+      dst = kcache + size_t(pos) * kw + kh * d;
+    } else {
+      const int kh = v - heads - kv_heads;
+      src = row + size_t(heads) * 2 * d + kw + kh * d;
+      dst = vcache + size_t(pos) * kw + kh * d;
+    }
+    float ss = 0.0f;
+    for (int i = lane; i < d; i += 32) {
+      const float a = src[i];
+      x[i] = a;
+      ss = __fmaf_rn(a, a, ss);
+    }
+    __syncwarp();
+    if (g) {
+      ss = warp_sum(ss);
+      const float inv = 1.0f / sqrtf(ss / float(d) + eps);
+      for (int i = lane; i < d; i += 32) x[i] = x[i] * (inv * (1.0f + g[i]));
+      __syncwarp();
+      const float* ang = rope + size_t(pos) * half * 2;
+      for (int i = lane; i < half; i += 32) {
+        const float sn = ang[2 * i], cs = ang[2 * i + 1];
+        const float a = x[i], b = x[i + half];
+        x[i] = a * cs - b * sn;
+        x[i + half] = b * cs + a * sn;
+      }
+      __syncwarp();
+    }
+    for (int i = lane; i < d; i += 32) dst[i] = x[i];
+    __syncwarp();
+  }
+}
+
+// Flash-style causal attention for head_dim 256, FP32 throughout. CTA: 16
+// query rows of one head (4 warps x 4 rows); key blocks of 32 in shared memory
+// (K transposed so lane = key reads conflict-free); online softmax; output
+// multiplied by sigmoid(gate) (src/qwen.rs:581-583).
+constexpr int AD = 256, ABQ = 16, ABK = 32;
+__global__ void __launch_bounds__(128) attention256_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                                           const float* __restrict__ vc,
+                                                           const float* __restrict__ gate_src, int ld_gate, int n,
+                                                           int offset, int heads, int kv_heads,
+                                                           float* __restrict__ out) {
+  extern __shared__ float sm[];
+  float* Qs = sm;                       // [ABQ][AD]
+  float* Kt = Qs + ABQ * AD;            // [AD][ABK + 1]
+  float* Vs = Kt + AD * (ABK + 1);      // [ABK][AD]
+  const int h = blockIdx.y, kh = h / (heads / kv_heads), t0 = blockIdx.x * ABQ;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kw = kv_heads * AD;
+  const float scale = 1.0f / sqrtf(float(AD));
+  for (int i = threadIdx.x; i < ABQ * AD; i += 128) {
+    const int r = i / AD, c = i % AD, t = t0 + r;
+    Qs[i] = t < n ? q[(size_t(t) * heads + h) * AD + c] : 0.0f;
+  }
+  float o[4][AD / 32];
+  float mrow[4], lrow[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    mrow[r] = -INFINITY;
+    lrow[r] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < AD / 32; ++e) o[r][e] = 0.0f;
+  }
+  const int L = offset + n;
+  const int last_key = min(L - 1, offset + t0 + ABQ - 1);
+  for (int kb = 0; kb <= last_key; kb += ABK) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < ABK * AD; i += 128) {
+      const int key = i / AD, c = i % AD, s = kb + key;
+      const bool ok = s < L;
+      Kt[c * (ABK + 1) + key] = ok ? kc[size_t(s) * kw + kh * AD + c] : 0.0f;
+      Vs[key * AD + c] = ok ? vc[size_t(s) * kw + kh * AD + c] : 0.0f;
+    }
+    __syncthreads();
+    float sc[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sc[r] = 0.0f;
+    const float* qrow = Qs + (warp * 4) * AD;
+#pragma unroll 8
+    for (int c = 0; c < AD; ++c) {
+      const float kv = Kt[c * (ABK + 1) + lane];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) sc[r] = __fmaf_rn(qrow[r * AD + c], kv, sc[r]);
+    }
+    const int key = kb + lane;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int t = t0 + warp * 4 + r;
+      float s = sc[r] * scale;
+      if (key > offset + t || key >= L) s = -INFINITY;
+      const float mx = warp_max(s);
+      const float mnew = fmaxf(mrow[r], mx);
+      const float p = s == -INFINITY ? 0.0f : expf(s - mnew);
+      const float corr = mrow[r] == -INFINITY ? 0.0f : expf(mrow[r] - mnew);
+      lrow[r] = lrow[r] * corr + warp_sum(p);
+      mrow[r] = mnew;
+#pragma unroll
+      for (int e = 0; e < AD / 32; ++e) o[r][e] = o[r][e] * corr;
+      sc[r] = p;
+    }
+#pragma unroll 4
+    for (int k2 = 0; k2 < ABK; ++k2) {
+      float pk[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) pk[r] = __shfl_sync(0xffffffffu, sc[r], k2);
+#pragma unroll
+      for (int e = 0; e < AD / 32; ++e) {
+        const float v = Vs[k2 * AD + lane + 32 * e];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) o[r][e] = __fmaf_rn(pk[r], v, o[r][e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int t = t0 + warp * 4 + r;
+    if (t >= n) continue;
+    const float inv = 1.0f / lrow[r];
+#pragma unroll
+    for (int e = 0; e < AD / 32; ++e) {
+      const int c = lane + 32 * e;
+      const float g = gate_src[size_t(t) * ld_gate + size_t(h) * 2 * AD + AD + c];
+      out[size_t(t) * heads * AD + h * AD + c] = (o[r][e] * inv) * sigmoid_f(g);
+    }
+  }
+}
+
+// Generic causal attention (any head_dim): one thread per (token, head),
+// reference order (causal_attention, src/qwen.rs:610-629) with the scores
+// recomputed per pass instead of buffered.
+__global__ void attention_generic_kernel(const float* __restrict__ q, const float* __restrict__ kc,
+                                         const float* __restrict__ vc, const float* __restrict__ gate_src, int ld_gate,
+                                         int n, int offset, int heads, int kv_heads, int d, float* __restrict__ out) {
+  const int id = blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= n * heads) return;
+  const int t = id / heads, h = id % heads, kh = h / (heads / kv_heads), kw = kv_heads * d;
+  const float scale = 1.0f / sqrtf(float(d));
+  const float* qr = q + (size_t(t) * heads + h) * d;
+  auto score = [&](int s) {
+    const float* kr = kc + size_t(s) * kw + kh * d;
+    float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const int full = (d / 8) * 8;
+    for (int i = 0; i < full; ++i) lanes[i & 7] = lanes[i & 7] + qr[i] * kr[i];
+    float sum = -0.0f;
+    for (int i = 0; i < 8; ++i) sum = sum + lanes[i];
+    for (int i = full; i < d; ++i) sum = sum + qr[i] * kr[i];
+    return sum * scale;
+  };
+  float mx = -INFINITY;
+  for (int s = 0; s <= offset + t; ++s) mx = fmaxf(mx, score(s));
+  float total = 0.0f;
+  for (int s = 0; s <= offset + t; ++s) total = total + expf(score(s) - mx);
+  float* dst = out + size_t(t) * heads * d + h * d;
+  for (int i = 0; i < d; ++i) dst[i] = 0.0f;
+  for (int s = 0; s <= offset + t; ++s) {
+    float p = expf(score(s) - mx);
+    if (total > 0.0f) p = p / total;
+    const float* vr = vc + size_t(s) * kw + kh * d;
+    for (int i = 0; i < d; ++i) dst[i] = dst[i] + p * vr[i];
+  }
+  for (int i = 0; i < d; ++i)
+    dst[i] = dst[i] * sigmoid_f(gate_src[size_t(t) * ld_gate + size_t(h) * 2 * d + d + i]);
+}
+
+// rms (centred) in place, src/qwen.rs:495, plus the non-finite hidden-state
+// check of src/qwen.rs:496-498. One 256-thread CTA per row.
+__global__ void final_norm_kernel(float* __restrict__ x, int K, const float* __restrict__ g, float eps,
+                                  DeviceStatus* st) {
+  __shared__ float red[8];
+  __shared__ int bad;
+  float* r = x + size_t(blockIdx.x) * K;
+  if (threadIdx.x == 0) bad = 0;
+  float ss = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) ss = __fmaf_rn(r[k], r[k], ss);
+  ss = warp_sum(ss);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  float tot = threadIdx.x < 8 ? red[threadIdx.x] : 0.0f;
+  if (threadIdx.x < 32) tot = warp_sum(tot);
+  __syncthreads();
+  if (threadIdx.x == 0) red[0] = tot;
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(red[0] / float(K) + eps);
+  int local_bad = 0;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float v = r[k] * (inv * (1.0f + g[k]));
+    r[k] = v;
+    local_bad |= !isfinite(v);
+  }
+  if (local_bad) bad = 1;
+  __syncthreads();
+  if (threadIdx.x == 0 && bad) report(st, kNonFinite, 3);
+}
+
+// Head::normalize, src/lib.rs:106-115: mean, biased variance, eps 1e-5.
+__global__ void head_norm_kernel(const float* __restrict__ hidden, int K, const int* __restrict__ rows,
+                                 const float* __restrict__ w, const float* __restrict__ b, float* __restrict__ out) {
+  __shared__ float red[8];
+  __shared__ float bc;
+  const float* x = hidden + size_t(rows[blockIdx.x]) * K;
+  auto block_sum = [&](float v) {
+    v = warp_sum(v);
+    __syncthreads();
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < 8 ? red[threadIdx.x] : 0.0f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) bc = t;
+    }
+    __syncthreads();
+    return bc;
+  };
+  float s = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) s += x[k];
+  const float mean = block_sum(s) / float(K);
+  float v2 = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) {
+    const float d = x[k] - mean;
+    v2 = __fmaf_rn(d, d, v2);
+  }
+  const float var = block_sum(v2) / float(K);
+  const float inv = 1.0f / sqrtf(var + 1e-5f);
+  for (int k = threadIdx.x; k < K; k += 256)
+    out[size_t(blockIdx.x) * K + k] = (x[k] - mean) * inv * w[k] + b[k];
+}
+
+// logits[i] = dot_scores(q, k_i) * scale (src/lib.rs:128).
+__global__ void head_dot_kernel(const float* __restrict__ q, const float* __restrict__ k, int n_keys, int dim,
+                                float scale, float* __restrict__ logits) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_keys) return;
+  const float* kr = k + size_t(i) * dim;
+  float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const int full = (dim / 8) * 8;
+  for (int j = 0; j < full; ++j) lanes[j & 7] = lanes[j & 7] + q[j] * kr[j];
+  float s = -0.0f;
+  for (int l = 0; l < 8; ++l) s = s + lanes[l];
+  for (int j = full; j < dim; ++j) s = s + q[j] * kr[j];
+  logits[i] = s * scale;
+}
+
+}  // namespace
+
+void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_heads, int d, const float* qn,
+                         const float* kn, float eps, const float* rope, int half, int start, float* q_out,
+                         float* kcache, float* vcache, cudaStream_t s) {
+  if (n <= 0) return;
+  qk_norm_rope_kernel<<<n, 256, 8 * d * sizeof(float), s>>>(qkv, ldq, heads, kv_heads, d, qn, kn, eps, rope, half,
+                                                            start, q_out, kcache, vcache);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src, int ld_gate,
+                      int n, int offset, int heads, int kv_heads, int d, float* out, cudaStream_t s) {
+  if (n <= 0) return;
+  if (d == AD) {
+    const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
+    static bool configured = false;
+    if (!configured) {
+      DG_CUDA(cudaFuncSetAttribute(attention256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      configured = true;
+    }
+    dim3 grid((n + ABQ - 1) / ABQ, heads);
+    attention256_kernel<<<grid, 128, smem, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out);
+  } else {
+    const int threads = n * heads;
+    attention_generic_kernel<<<(threads + 127) / 128, 128, 0, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset,
+                                                                   heads, kv_heads, d, out);
+  }
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, DeviceStatus* st, cudaStream_t s) {
+  if (M <= 0) return;
+  final_norm_kernel<<<M, 256, 0, s>>>(x, K, gamma, eps, st);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, const float* w, const float* b,
+                      float* out, cudaStream_t s) {
+  if (n_rows <= 0) return;
+  head_norm_kernel<<<n_rows, 256, 0, s>>>(hidden, K, rows, w, b, out);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, float* logits,
+                     cudaStream_t s) {
+  if (n_keys <= 0) return;
+  head_dot_kernel<<<(n_keys + 127) / 128, 128, 0, s>>>(q, k, n_keys, dim, scale, logits);
+  DG_CUDA(cudaGetLastError());
+}
+
+}  // namespace dg

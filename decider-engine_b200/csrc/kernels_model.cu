@@ -1,0 +1,240 @@
+// Mixer kernels of the Qwen3.5 torso: DeltaNet conv / recurrence, gated GQA
+// attention with partial RoPE, final norm and the pointer head.
+#include <cfloat>
+
+#include "launch.h"
+
+namespace dg {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+// convolve, src/qwen.rs:712-756: per channel, taps in order from a zero sum,
+// skipping taps before the sequence start, then SiLU.
+__global__ void conv_silu_kernel(const float* __restrict__ raw, int ldr, const float* __restrict__ tail, int tail_rows,
+                                 int start, int W, int kernel, const float* __restrict__ taps, float* __restrict__ out) {
+  const int t = blockIdx.x, position = start + t;
+  for (int c = threadIdx.x; c < W; c += blockDim.x) {
+    float sum = 0.0f;
+    for (int j = 0; j < kernel; ++j) {
+      if (position + j + 1 < kernel) continue;
+      const int source = position + j + 1 - kernel;
+      const float in = source >= start ? raw[size_t(source - start) * ldr + c]
+                                       : tail[size_t(source + tail_rows - start) * W + c];
+      sum = sum + in * taps[size_t(j) * W + c];
+    }
+    out[size_t(t) * W + c] = silu_f(sum);
+  }
+}
+
+// Recurrence::head prologue (src/qwen.rs:832-845) for one token: L2 norms of
+// q (then / sqrt(dk)) and k per key head, in place; decay and beta per value head.
+__global__ void delta_prep_kernel(float* __restrict__ conv, int W, int key_heads, int dk, int value_heads,
+                                  const float* __restrict__ a, const float* __restrict__ b, int ldab,
+                                  const float* __restrict__ rate, const float* __restrict__ dt, float* __restrict__ decay,
+                                  float* __restrict__ beta) {
+  const int t = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
+  float* row = conv + size_t(t) * W;
+  const float rdk = sqrtf(float(dk));
+  for (int v = warp; v < 2 * key_heads; v += nwarps) {
+    float* x = row + v * dk;  // v < key_heads: q of head v; else k of head v - key_heads
+    float ss = 0.0f;
+    for (int i = lane; i < dk; i += 32) ss = __fmaf_rn(x[i], x[i], ss);
+    ss = warp_sum(ss);
+    float norm = 1.0f / sqrtf(ss + 1e-6f);
+    if (v < key_heads) norm = norm / rdk;
+    for (int i = lane; i < dk; i += 32) x[i] = x[i] * norm;
+  }
+  for (int h = threadIdx.x; h < value_heads; h += blockDim.x) {
+    decay[size_t(t) * value_heads + h] = expf(rate[h] * softplus_f(a[size_t(t) * ldab + h] + dt[h]));
+    beta[size_t(t) * value_heads + h] = sigmoid_f(b[size_t(t) * ldab + h]);
+  }
+}
+
+// Gated delta rule, generic shapes: one thread per (value head, value column),
+// the reference's per-column arithmetic order (src/qwen.rs:846-866).
+__global__ void delta_rec_generic_kernel(const float* __restrict__ conv, int n, int W, int key_heads, int dk,
+                                         int value_heads, int dv, const float* __restrict__ decay,
+                                         const float* __restrict__ beta, float* __restrict__ state,
+                                         float* __restrict__ o) {
+  const int id = blockIdx.x * blockDim.x + threadIdx.x;
+  if (id >= value_heads * dv) return;
+  const int h = id / dv, j = id % dv, kh = h / (value_heads / key_heads), kd = key_heads * dk;
+  float* S = state + size_t(h) * dk * dv;
+  for (int t = 0; t < n; ++t) {
+    const float* q = conv + size_t(t) * W + kh * dk;
+    const float* k = conv + size_t(t) * W + kd + kh * dk;
+    const float v = conv[size_t(t) * W + 2 * kd + h * dv + j];
+    const float dec = decay[size_t(t) * value_heads + h], be = beta[size_t(t) * value_heads + h];
+    float delta = 0.0f;
+    for (int i = 0; i < dk; ++i) {
+      const float s = S[size_t(i) * dv + j] * dec;
+      S[size_t(i) * dv + j] = s;
+      delta = delta + k[i] * s;
+    }
+    delta = (v - delta) * be;
+    float out = 0.0f;
+    for (int i = 0; i < dk; ++i) {
+      const float s = S[size_t(i) * dv + j] + k[i] * delta;
+      S[size_t(i) * dv + j] = s;
+      out = out + q[i] * s;
+    }
+    o[size_t(t) * value_heads * dv + h * dv + j] = out;
+  }
+}
+
+// Gated delta rule for dk == 128: one warp owns 4 value columns of one head
+// of one sequence; lane l holds state rows 4l..4l+3 of those columns in
+// registers. Per token: decay, k^T S (warp reduction), delta, rank-1 update,
+// q^T S (reduction). Operands are strided so the same kernel serves the model
+// (q|k|v rows of the conv output) and the isolated batched recurrence.
+__global__ void __launch_bounds__(128) delta_rec128_kernel(DeltaArgs a) {
+  constexpr int DK = 128;
+  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  const int groups = a.dv / 4;
+  if (wid >= a.value_heads * groups) return;
+  const size_t bi = blockIdx.y;
+  const int h = wid / groups, j0 = (wid % groups) * 4, kh = h / (a.value_heads / a.key_heads);
+  const float* qb = a.q + bi * a.bs_qkv + kh * DK + lane * 4;
+  const float* kb = a.k + bi * a.bs_qkv + kh * DK + lane * 4;
+  const float* vb = a.v + bi * a.bs_qkv + h * a.dv + j0;
+  const float* db = a.decay + bi * a.bs_gb + h;
+  const float* bb = a.beta + bi * a.bs_gb + h;
+  float* ob = a.o + bi * a.bs_o + h * a.dv + j0;
+  float* S = a.state + bi * a.bs_state + size_t(h) * DK * a.dv;
+  const int dv = a.dv, n = a.n;
+  float s[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const float4 v = *reinterpret_cast<const float4*>(S + size_t(lane * 4 + r) * dv + j0);
+    s[r][0] = v.x; s[r][1] = v.y; s[r][2] = v.z; s[r][3] = v.w;
+  }
+  float4 kq = make_float4(0, 0, 0, 0), qq = kq, vv = kq;
+  float dec = 0.0f, be = 0.0f;
+  if (n > 0) {
+    kq = *reinterpret_cast<const float4*>(kb);
+    qq = *reinterpret_cast<const float4*>(qb);
+    vv = *reinterpret_cast<const float4*>(vb);
+    dec = a.log_decay ? expf(db[0]) : db[0];
+    be = bb[0];
+  }
+  for (int t = 0; t < n; ++t) {
+    const float kk[4] = {kq.x, kq.y, kq.z, kq.w}, qv[4] = {qq.x, qq.y, qq.z, qq.w}, v[4] = {vv.x, vv.y, vv.z, vv.w};
+    const float d0 = dec, b0 = be;
+    if (t + 1 < n) {  // prefetch the next token's inputs
+      kq = *reinterpret_cast<const float4*>(kb + size_t(t + 1) * a.ld_qk);
+      qq = *reinterpret_cast<const float4*>(qb + size_t(t + 1) * a.ld_qk);
+      vv = *reinterpret_cast<const float4*>(vb + size_t(t + 1) * a.ld_v);
+      dec = db[size_t(t + 1) * a.ld_gb];
+      if (a.log_decay) dec = expf(dec);
+      be = bb[size_t(t + 1) * a.ld_gb];
+    }
+    float p[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        s[r][c] = s[r][c] * d0;
+        acc = __fmaf_rn(kk[r], s[r][c], acc);
+      }
+      p[c] = acc;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) p[c] += __shfl_xor_sync(0xffffffffu, p[c], off);
+    float out[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float delta = (v[c] - p[c]) * b0;
+      float acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        s[r][c] = __fmaf_rn(kk[r], delta, s[r][c]);
+        acc = __fmaf_rn(qv[r], s[r][c], acc);
+      }
+      out[c] = acc;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) out[c] += __shfl_xor_sync(0xffffffffu, out[c], off);
+    if (lane == 0) *reinterpret_cast<float4*>(ob + size_t(t) * a.ldo) = make_float4(out[0], out[1], out[2], out[3]);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    *reinterpret_cast<float4*>(S + size_t(lane * 4 + r) * dv + j0) = make_float4(s[r][0], s[r][1], s[r][2], s[r][3]);
+}
+
+__global__ void exp_kernel(const float* __restrict__ g, float* __restrict__ out, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    out[i] = expf(g[i]);
+}
+
+}  // namespace
+
+void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W, int kernel,
+                      const float* taps, float* out, cudaStream_t s) {
+  if (n <= 0) return;
+  conv_silu_kernel<<<n, 256, 0, s>>>(raw, ldr, tail, tail_rows, start, W, kernel, taps, out);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_delta_prep(float* conv, int W, int n, int key_heads, int dk, int value_heads, const float* a,
+                       const float* b, int ldab, const float* decay_rate, const float* dt, float* decay, float* beta,
+                       cudaStream_t s) {
+  if (n <= 0) return;
+  delta_prep_kernel<<<n, 256, 0, s>>>(conv, W, key_heads, dk, value_heads, a, b, ldab, decay_rate, dt, decay, beta);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, int value_heads, int dv,
+                             const float* decay, const float* beta, float* state, float* o, cudaStream_t s) {
+  if (n <= 0) return;
+  const int W = 2 * key_heads * dk + value_heads * dv;
+  if (dk == 128 && dv % 4 == 0) {
+    DeltaArgs a{};
+    a.q = conv;
+    a.k = conv + key_heads * dk;
+    a.v = conv + 2 * key_heads * dk;
+    a.ld_qk = a.ld_v = W;
+    a.decay = decay;
+    a.beta = beta;
+    a.ld_gb = value_heads;
+    a.n = n;
+    a.key_heads = key_heads;
+    a.value_heads = value_heads;
+    a.dv = dv;
+    a.state = state;
+    a.o = o;
+    a.ldo = value_heads * dv;
+    launch_delta_rec128(a, 1, s);
+  } else {
+    const int threads = value_heads * dv;
+    delta_rec_generic_kernel<<<(threads + 127) / 128, 128, 0, s>>>(conv, n, W, key_heads, dk, value_heads, dv, decay,
+                                                                   beta, state, o);
+    DG_CUDA(cudaGetLastError());
+  }
+}
+
+void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s) {
+  if (a.n <= 0 || batch <= 0) return;
+  const int warps = a.value_heads * (a.dv / 4);
+  dim3 grid((warps * 32 + 127) / 128, batch);
+  delta_rec128_kernel<<<grid, 128, 0, s>>>(a);
+  DG_CUDA(cudaGetLastError());
+}
+
+void launch_exp(const float* g, float* out, size_t n, cudaStream_t s) {
+  if (!n) return;
+  exp_kernel<<<592, 256, 0, s>>>(g, out, n);
+  DG_CUDA(cudaGetLastError());
+}
+
+
+}  // namespace dg

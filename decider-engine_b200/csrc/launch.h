@@ -1,0 +1,105 @@
+// Host-side launchers of the decider GPU kernels (all on the given stream).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace dg {
+
+struct GemmArgs;
+
+// ---- tensor maps (driver entry point resolved at run time; no -lcuda)
+void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                     uint32_t box_inner, uint32_t box_outer);
+
+// ---- INT8 tensor-core projection (tcgen05), gemm_i8.cu
+// rank: 0 or 32. epi: kEpiWrite/kEpiAdd/kEpiSwiGlu. exact: reference FP32 order.
+void launch_gemm_i8(const CUtensorMap& map_a, const CUtensorMap& map_b, const GemmArgs& args, int rank,
+                    int epi, bool exact, cudaStream_t stream);
+size_t gemm_i8_smem_bytes(int rank);
+
+// ---- elementwise / normalisation / quantisation, kernels.cu
+// Row-wise: optional centred RMSNorm (gamma != nullptr: x * (inv * (1 + g))),
+// optional FP32 output, optional group-64 quantisation into xq [M][K] and
+// xs [G][ldxs]. Non-finite quantisation inputs are reported.
+void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma, float eps, float* n_out,
+                       int ldn, int8_t* xq, float* xs, int ldxs, DeviceStatus* st, cudaStream_t s);
+// DeltaNet gated norm fused with quantisation: per value head, o = rms(o, w)
+// (non-centred) * silu(z); writes FP32 and the group-64 quantisation.
+void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int heads, int dv,
+                             const float* w, float eps, float* out, int8_t* xq, float* xs, int ldxs,
+                             bool quantize, DeviceStatus* st, cudaStream_t s);
+// mid[m][r] = dot_scores(x[m], A[r]) for r < R (reference lane order when exact).
+void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
+                   bool exact, cudaStream_t s);
+// Generic SIMT projection for any shape and precision (reference order):
+// precision 0: w f32; 1: int8 weight-only; 2: int8-compute; 3: int4.
+struct GenericProj {
+  int precision, in, out;
+  const float* w;        // precision 0
+  const uint8_t* wq;     // precision 1-3 (int4 packed as the reference)
+  const float* wscale;   // [out][G]
+  const float* bias;     // nullable
+  const float* lora_b;   // [out][rank], nullable
+  int rank;
+  float lora_scale;
+};
+void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const int8_t* xq, const float* xs,
+                         int ldxs, const float* mid, int ldm, int M, float* out, int ldo, int epi,
+                         cudaStream_t s);
+void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids, int n, float* x,
+                  cudaStream_t s);
+// Causal depthwise conv (tap-major weights [k][W]) + SiLU, continuing from a
+// tail of `tail_rows` raw rows that precede position `start`.
+void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W,
+                      int kernel, const float* taps, float* out, cudaStream_t s);
+// Per token: q/k L2 norms (q also / sqrt(dk)), decay = exp(rate * softplus(a + dt)),
+// beta = sigmoid(b). Normalises conv[:, :2kd] in place.
+void launch_delta_prep(float* conv, int W, int n, int key_heads, int dk, int value_heads, const float* a,
+                       const float* b, int ldab, const float* decay_rate, const float* dt, float* decay,
+                       float* beta, cudaStream_t s);
+// Gated delta rule over n tokens for every value head, state [H][dk][dv]
+// updated in place; o [n][H*dv] receives q^T S per token (before the norm).
+void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, int value_heads, int dv,
+                             const float* decay, const float* beta, float* state, float* o,
+                             cudaStream_t s);
+// Strided operands of the dk == 128 recurrence kernel; blockIdx.y indexes
+// independent sequences (batch strides in floats).
+struct DeltaArgs {
+  const float *q, *k, *v;
+  int ld_qk, ld_v;
+  size_t bs_qkv;
+  const float *decay, *beta;   // decay is exp(g) already, or g itself when log_decay != 0
+  int log_decay;
+  int ld_gb;
+  size_t bs_gb;
+  int n, key_heads, value_heads, dv;
+  float* state;
+  size_t bs_state;
+  float* o;
+  int ldo;
+  size_t bs_o;
+};
+void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s);
+void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
+// Split q|gate per head, centred RMSNorm of q and k, partial RoPE from the
+// precomputed table, append k/v to the cache at `start`.
+void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_heads, int d, const float* qn,
+                         const float* kn, float eps, const float* rope, int half, int start, float* q_out,
+                         float* kcache, float* vcache, cudaStream_t s);
+void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src,
+                      int ld_gate, int n, int offset, int heads, int kv_heads, int d, float* out,
+                      cudaStream_t s);
+// Centred RMSNorm over rows, in place, plus a non-finite check.
+void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, DeviceStatus* st,
+                       cudaStream_t s);
+// Pointer-head LayerNorm (eps 1e-5, weight and bias) of selected rows.
+void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, const float* w, const float* b,
+                      float* out, cudaStream_t s);
+// logits[i] = dot_scores(q, k_i) * scale.
+void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, float* logits,
+                     cudaStream_t s);
+
+}  // namespace dg

@@ -1,0 +1,219 @@
+"""Python host mirror of the reference's model seam over the C ABI.
+
+`GpuModel` stands where qwen::Model + Head stand in the reference
+(src/qwen.rs:291-424, src/lib.rs:87-131): `forward`, `prefill`,
+`forward_after` and `logits` run on the B200 through libdecider_gpu.so.
+`Linear` is the isolated INT8 projection and
+`gated_delta_rule` the isolated recurrence (config 3).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import struct
+
+import numpy as np
+
+from ._lib import GpuError, ModelConfig, check, load
+
+PRECISIONS = {"checkpoint": 0, "int8": 1, "int8-compute": 2, "int4": 3}
+_DT = {"F32": (np.float32, 0), "BF16": (np.uint16, 1), "F16": (np.uint16, 2)}
+
+
+def _u32(a):
+    a = np.ascontiguousarray(a, np.uint32)
+    return a, a.ctypes.data
+
+
+def read_safetensors(path: str) -> dict:
+    """Safetensors reader (header bound and length check as read_tensors,
+    src/weights.rs:305-318): {name: (dtype_code, shape, ndarray)}."""
+    size = os.path.getsize(path)
+    with open(path, "rb") as f:
+        raw = f.read()
+    n = struct.unpack("<Q", raw[:8])[0]
+    if n > 16 * 1024 * 1024 or n + 8 > size:
+        raise GpuError("invalid or oversized safetensors header")
+    header = json.loads(raw[8:8 + n])
+    out, base, data_len = {}, 8 + n, 0
+    for name, info in header.items():
+        if name == "__metadata__":
+            continue
+        if info["dtype"] not in _DT:
+            raise GpuError(f"{name}: unsupported weight dtype {info['dtype']}")
+        np_dt, code = _DT[info["dtype"]]
+        lo, hi = info["data_offsets"]
+        data_len = max(data_len, hi)
+        out[name] = (code, list(info["shape"]), np.frombuffer(raw[base + lo:base + hi], dtype=np_dt))
+    if base + data_len != size:
+        raise GpuError("safetensors file length does not match metadata")
+    return out
+
+
+def text_config_to_struct(cfg: dict, rank: int, scale: float, pointer_dim: int):
+    lt = (C.c_int32 * len(cfg["layer_types"]))(
+        *[1 if t == "full_attention" else 0 for t in cfg["layer_types"]])
+    rp = cfg["rope_parameters"]
+    s = ModelConfig(
+        cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"], cfg["vocab_size"],
+        cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"],
+        cfg["linear_conv_kernel_dim"], cfg["linear_key_head_dim"], cfg["linear_value_head_dim"],
+        cfg["linear_num_key_heads"], cfg["linear_num_value_heads"], cfg["rms_norm_eps"],
+        rp["rope_theta"], rp["partial_rotary_factor"], C.cast(lt, C.POINTER(C.c_int32)),
+        rank, scale, pointer_dim)
+    return s, lt
+
+
+class GpuPrefix:
+    """Device-resident, immutable prefix cache (Prefix, src/qwen.rs:509-526)."""
+
+    def __init__(self, model: "GpuModel", handle: int):
+        self._model = model
+        self.h = handle
+
+    def __len__(self):
+        return int(load().dg_prefix_len(self.h))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            load().dg_prefix_free(self.h)
+            self.h = None
+
+
+class GpuModel:
+    """Qwen3.5 torso + pointer head resident on one B200."""
+
+    def __init__(self, text_config: dict, precision: str = "int8-compute", rank: int = 32,
+                 lora_scale: float = 2.0, pointer_dim: int = 0, device: int = 0, max_tokens: int = 4096):
+        L = load()
+        self.config = dict(text_config)
+        self.precision = precision
+        self.pointer_dim = pointer_dim
+        s, self._lt = text_config_to_struct(text_config, rank, lora_scale, pointer_dim)
+        h = C.c_void_p()
+        check(L.dg_engine_create(C.byref(s), PRECISIONS[precision], device, max_tokens, C.byref(h)))
+        self.h = h.value
+        self.hidden = text_config["hidden_size"]
+
+    def set_tensor(self, name: str, dtype: int, shape, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data)
+        shp = (C.c_int64 * len(shape))(*shape)
+        check(load().dg_engine_set_tensor(self.h, name.encode(), dtype, shp, len(shape), data.ctypes.data))
+
+    def set_tensors(self, tensors: dict) -> None:
+        for name, (code, shape, arr) in tensors.items():
+            self.set_tensor(name, code, shape, arr)
+
+    def fill_synthetic(self, seed: int = 0, stddev: float = 0.02) -> None:
+        check(load().dg_engine_fill_synthetic(self.h, seed, stddev))
+
+    def finalize(self) -> "GpuModel":
+        check(load().dg_engine_finalize(self.h))
+        return self
+
+    @property
+    def fast_path(self) -> bool:
+        return bool(load().dg_engine_fast_path(self.h))
+
+    def set_exact(self, exact: bool) -> None:
+        check(load().dg_engine_set_exact(self.h, int(exact)))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            load().dg_engine_free(self.h)
+            self.h = None
+
+    # ---- Model::forward / prefill / forward_after
+    def forward(self, ids, prefix: GpuPrefix | None = None) -> np.ndarray:
+        ids, p = _u32(ids)
+        out = np.zeros((len(ids), self.hidden), np.float32)
+        check(load().dg_forward_hidden(self.h, None if prefix is None else prefix.h, p, len(ids),
+                                       out.ctypes.data))
+        return out
+
+    def prefill(self, ids) -> GpuPrefix:
+        ids, p = _u32(ids)
+        h = C.c_void_p()
+        check(load().dg_prefill(self.h, p, len(ids), C.byref(h)))
+        return GpuPrefix(self, h.value)
+
+    def forward_after(self, prefix: GpuPrefix, ids) -> np.ndarray:
+        return self.forward(ids, prefix)
+
+    # ---- NativeEngine::logits (src/lib.rs:400-419)
+    def logits(self, ids, positions, prefix: GpuPrefix | None = None) -> np.ndarray:
+        ids, p = _u32(ids)
+        pos = np.ascontiguousarray(positions, np.uint64)
+        out = np.zeros(len(pos), np.float32)
+        check(load().dg_logits(self.h, None if prefix is None else prefix.h, p, len(ids), pos.ctypes.data,
+                               len(pos), out.ctypes.data))
+        return out
+
+    @classmethod
+    def from_dir(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096):
+        """Model::load + Head::load from a checkpoint directory in the
+        reference's layout (src/lib.rs:287-367): base/config.json,
+        base/model.safetensors, lora/adapter_config.json,
+        lora/adapter_model.safetensors, head.safetensors and
+        strands_decider_config.json."""
+        from .host import read_decider_config, read_lora_config, read_text_config
+        dc = read_decider_config(d)
+        cfg = read_text_config(d)
+        rank, scale = read_lora_config(d)
+        m = cls(cfg, precision, rank, scale, dc["pointer_dim"], device, max_tokens)
+        prefix = "model.language_model."
+        base = read_safetensors(os.path.join(d, "base", "model.safetensors"))
+        m.set_tensors({k[len(prefix):]: v for k, v in base.items() if k.startswith(prefix)})
+        adapter = read_safetensors(os.path.join(d, "lora", "adapter_model.safetensors"))
+        if not adapter:
+            raise GpuError("empty LoRA adapter")
+        m.set_tensors(adapter)
+        m.set_tensors({"head." + k: v for k, v in read_safetensors(os.path.join(d, "head.safetensors")).items()})
+        return m.finalize()
+
+
+class Linear:
+    """Isolated group-64 INT8 projection with optional rank-32 LoRA (config 1)."""
+
+    def __init__(self, w: np.ndarray, lora_a=None, lora_b=None, lora_scale: float = 0.0, device: int = 0):
+        w = np.ascontiguousarray(w, np.float32)
+        self.n, self.k = w.shape
+        la = None if lora_a is None else np.ascontiguousarray(lora_a, np.float32)
+        lb = None if lora_b is None else np.ascontiguousarray(lora_b, np.float32)
+        rank = 0 if la is None else la.shape[0]
+        h = C.c_void_p()
+        check(load().dg_linear_create(w.ctypes.data, self.n, self.k, None if la is None else la.ctypes.data,
+                                      None if lb is None else lb.ctypes.data, rank, lora_scale, device,
+                                      C.byref(h)))
+        self.h = h.value
+
+    def set_exact(self, exact: bool) -> None:
+        check(load().dg_linear_set_exact(self.h, int(exact)))
+
+    def __call__(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros((x.shape[0], self.n), np.float32)
+        check(load().dg_linear_forward(self.h, x.ctypes.data, x.shape[0], y.ctypes.data))
+        return y
+
+    def forward_device(self, x_ptr: int, m: int, y_ptr: int, dots_ptr: int | None = None) -> None:
+        check(load().dg_linear_forward_device(self.h, x_ptr, m, y_ptr, dots_ptr))
+
+    def last_quantized(self, m: int):
+        xq = np.zeros((m, self.k), np.int8)
+        xs = np.zeros((self.k // 64, m), np.float32)
+        check(load().dg_linear_last_quantized(self.h, m, xq.ctypes.data, xs.ctypes.data))
+        return xq, xs
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            load().dg_linear_free(self.h)
+            self.h = None
+
+
+def gated_delta_rule(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads, state_ptr, o_ptr, stream=0):
+    """Isolated gated delta rule on device buffers (config 3); see
+    dg_gated_delta_rule_device in include/decider_gpu.h."""
+    check(load().dg_gated_delta_rule_device(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads, state_ptr,
+                                            o_ptr, stream))

@@ -1,0 +1,128 @@
+/*
+ * decider_gpu.h — C ABI of the B200 (sm_100a) prefill engine for the Strands
+ * Decider 2B classifier. Drop-in device backend for decider-engine's model
+ * seam: qwen::Model (load / forward / prefill / forward_after,
+ * src/qwen.rs:291-424) and Head::logits (src/lib.rs:116-131). Host logic
+ * (prompting, tokenizer, limits, schema, readout) stays with the caller.
+ *
+ * Conventions: every function returns 0 on success or a nonzero status, with
+ * the message in dg_last_error() (thread-local). All pointers are HOST
+ * pointers unless a name says `_device`; callers own every buffer they pass.
+ * No call keeps a pointer to caller memory after it returns.
+ */
+#ifndef DECIDER_GPU_H
+#define DECIDER_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct dg_engine dg_engine;
+typedef struct dg_prefix dg_prefix;
+typedef struct dg_linear dg_linear;
+
+/* Precision switch, Precision (src/lib.rs:48-66). */
+enum { DG_CHECKPOINT = 0, DG_INT8 = 1, DG_INT8_COMPUTE = 2, DG_INT4 = 3 };
+/* Tensor dtypes accepted by dg_engine_set_tensor (safetensors F32/BF16/F16,
+ * Data::read, src/weights.rs:147-194). */
+enum { DG_F32 = 0, DG_BF16 = 1, DG_F16 = 2 };
+
+/* Qwen3.5 text_config fields read by the forward pass (Config,
+ * src/qwen.rs:8-34), the LoRA rank and alpha/r scale (src/lib.rs:300-358) and
+ * the pointer-head width (src/lib.rs:72-86; 0 = no head). */
+typedef struct dg_model_config {
+  int32_t hidden_size, intermediate_size, num_hidden_layers, vocab_size;
+  int32_t num_attention_heads, num_key_value_heads, head_dim;
+  int32_t linear_conv_kernel_dim, linear_key_head_dim, linear_value_head_dim;
+  int32_t linear_num_key_heads, linear_num_value_heads;
+  float rms_norm_eps, rope_theta, partial_rotary_factor;
+  const int32_t* layer_types; /* num_hidden_layers entries: 1 full_attention, 0 linear_attention */
+  int32_t lora_rank;
+  float lora_scale;
+  int32_t pointer_dim;
+} dg_model_config;
+
+/* Last error message of this thread ("" if none). */
+const char* dg_last_error(void);
+/* Number of kernel launches this library has issued in this process. */
+uint64_t dg_launch_count(void);
+
+/* ---- engine lifecycle: replaces Model::load + Head::load
+ * (src/qwen.rs:291-406, src/lib.rs:94-105). Tensors use the checkpoint names
+ * without the "model.language_model." prefix; adapter tensors keep
+ * "base_model.model."; pointer-head tensors are "head.<name>". Projection
+ * weights ("layers.*_proj.weight") are quantised at staging per `precision`
+ * exactly as Data::quantize (src/weights.rs:98-146). max_tokens bounds the
+ * rows of one forward call (1..4096). */
+int dg_engine_create(const dg_model_config* cfg, int precision, int device, int max_tokens, dg_engine** out);
+int dg_engine_set_tensor(dg_engine* e, const char* name, int dtype, const int64_t* shape, int ndim,
+                         const void* data);
+/* Fills every tensor not yet set with seeded N(0, stddev^2) values (norm
+ * weights 1, biases 0): synthetic checkpoints of a given architecture. */
+int dg_engine_fill_synthetic(dg_engine* e, uint64_t seed, float stddev);
+int dg_engine_finalize(dg_engine* e);
+/* 1 when the tcgen05 INT8 path serves the projections, 0 for the generic kernels. */
+int dg_engine_fast_path(const dg_engine* e);
+/* 1: tcgen05 promotion in the reference's FP32 order (default); 0: fused multiply-add. */
+int dg_engine_set_exact(dg_engine* e, int exact);
+void dg_engine_free(dg_engine* e);
+/* The engine's CUDA stream (cudaStream_t) for callers that time or order work. */
+void* dg_engine_stream(const dg_engine* e);
+/* Device time (ms) of the last forward's kernels, between the id upload and
+ * the result download; and the number of kernels that forward launched. */
+float dg_engine_last_forward_ms(const dg_engine* e);
+int dg_engine_last_launches(const dg_engine* e);
+
+/* ---- forward passes: Model::forward / prefill / forward_after
+ * (src/qwen.rs:407-424). `past` may be NULL. hidden_out (nullable) receives
+ * [n][hidden_size] FP32. Errors mirror the reference's messages:
+ * "token sequence must contain 1–4096 tokens", "token {id} outside
+ * vocabulary", "non-finite Qwen hidden states", "prefix cache does not match
+ * the layer types". */
+int dg_forward_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, float* hidden_out);
+int dg_prefill(dg_engine* e, const uint32_t* ids, size_t n, dg_prefix** out);
+size_t dg_prefix_len(const dg_prefix* p);
+void dg_prefix_free(dg_prefix* p);
+
+/* ---- pointer logits: NativeEngine::logits (src/lib.rs:400-419) =
+ * forward(_after) + Head::logits. opt_pos are positions inside `ids` (already
+ * relative to the prefix when `past` is given); logits_out has n_opt floats.
+ * The answer row is the last token. */
+int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, const size_t* opt_pos,
+              size_t n_opt, float* logits_out);
+
+/* ---- isolated INT8 projection: the reference's
+ * linear_int8 + Adapter::combine (src/tensor.rs:379-456,109-117) with
+ * load-time weight quantisation (src/weights.rs:98-146). w: [n][k] FP32;
+ * lora_a [rank][k], lora_b [n][rank] (nullable when rank == 0; rank 0 or 32);
+ * k % 128 == 0. */
+int dg_linear_create(const float* w, int n, int k, const float* lora_a, const float* lora_b, int rank,
+                     float lora_scale, int device, dg_linear** out);
+/* y[m][n] = projection of x[m][k] (host buffers; copies inside). */
+int dg_linear_forward(dg_linear* l, const float* x, int m, float* y);
+/* Same on device buffers; group_dots_device (nullable) receives the exact
+ * int32 group dots [k/64][m][n] the tensor cores produced. */
+int dg_linear_forward_device(dg_linear* l, const float* x_device, int m, float* y_device, int32_t* group_dots_device);
+/* Quantised activations of the last call: xq [m][k] int8 and scales [k/64][m] (host). */
+int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs);
+int dg_linear_set_exact(dg_linear* l, int exact);
+/* The CUDA stream the projection runs on (cudaStream_t). */
+void* dg_linear_stream(const dg_linear* l);
+void dg_linear_free(dg_linear* l);
+
+/* ---- isolated gated delta rule: Recurrence::head's
+ * state update (src/qwen.rs:846-866) for `batch` sequences x `heads` heads of
+ * `t` tokens, dk = dv = 128, q and k already L2-normalised (q also scaled by
+ * 1/sqrt(dk)). Device buffers: q, k, v [batch][t][heads][128]; g, beta
+ * [batch][t][heads] with decay = exp(g); state [batch][heads][128][128] is
+ * read as the initial state and left as the final one; o receives q^T S. */
+int dg_gated_delta_rule_device(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                               int batch, int t, int heads, float* state, float* o, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DECIDER_GPU_H */

@@ -20,4 +20,5 @@ def pytest_configure(config):
 def oracle_mod():
     from oracle import oracle as O
     O.build()
+    O.set_threads(os.cpu_count() or 1)
     return O

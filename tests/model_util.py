@@ -1,0 +1,89 @@
+"""Seeded synthetic Qwen3.5 decider checkpoints for parity tests (shared by
+the oracle and the GPU engine)."""
+import numpy as np
+
+
+def small_config(hidden=256, intermediate=512, layer_types=("linear_attention",) * 3 + ("full_attention",),
+                 heads=2, kv_heads=1, head_dim=256, key_heads=2, value_heads=2, dk=128, vocab=1000):
+    return {
+        "hidden_size": hidden, "intermediate_size": intermediate, "num_hidden_layers": len(layer_types),
+        "vocab_size": vocab, "layer_types": list(layer_types), "num_attention_heads": heads,
+        "num_key_value_heads": kv_heads, "head_dim": head_dim, "rms_norm_eps": 1e-6,
+        "linear_conv_kernel_dim": 4, "linear_key_head_dim": dk, "linear_value_head_dim": dk,
+        "linear_num_key_heads": key_heads, "linear_num_value_heads": value_heads,
+        "rope_parameters": {"rope_theta": 1e7, "partial_rotary_factor": 0.25, "rope_type": "default"},
+        "attention_bias": False, "attn_output_gate": True, "hidden_act": "silu",
+    }
+
+
+def expected_shapes(c, rank, pointer_dim):
+    H, I = c["hidden_size"], c["intermediate_size"]
+    qw, kw = c["num_attention_heads"] * c["head_dim"], c["num_key_value_heads"] * c["head_dim"]
+    kd = c["linear_num_key_heads"] * c["linear_key_head_dim"]
+    vd = c["linear_num_value_heads"] * c["linear_value_head_dim"]
+    W, VH = 2 * kd + vd, c["linear_num_value_heads"]
+    shapes, projections = {}, []
+
+    def proj(key, i, o):
+        shapes[key + ".weight"] = [o, i]
+        projections.append(key)
+        shapes["base_model.model." + key + ".lora_A.weight"] = [rank, i]
+        shapes["base_model.model." + key + ".lora_B.weight"] = [o, rank]
+
+    for li, t in enumerate(c["layer_types"]):
+        p = f"layers.{li}."
+        if t == "full_attention":
+            proj(p + "self_attn.q_proj", H, 2 * qw)
+            proj(p + "self_attn.k_proj", H, kw)
+            proj(p + "self_attn.v_proj", H, kw)
+            proj(p + "self_attn.o_proj", qw, H)
+            shapes[p + "self_attn.q_norm.weight"] = [c["head_dim"]]
+            shapes[p + "self_attn.k_norm.weight"] = [c["head_dim"]]
+        else:
+            proj(p + "linear_attn.in_proj_qkv", H, W)
+            proj(p + "linear_attn.in_proj_z", H, vd)
+            proj(p + "linear_attn.in_proj_a", H, VH)
+            proj(p + "linear_attn.in_proj_b", H, VH)
+            proj(p + "linear_attn.out_proj", vd, H)
+            shapes[p + "linear_attn.conv1d.weight"] = [W, 1, c["linear_conv_kernel_dim"]]
+            shapes[p + "linear_attn.dt_bias"] = [VH]
+            shapes[p + "linear_attn.A_log"] = [VH]
+            shapes[p + "linear_attn.norm.weight"] = [c["linear_value_head_dim"]]
+        proj(p + "mlp.gate_proj", H, I)
+        proj(p + "mlp.up_proj", H, I)
+        proj(p + "mlp.down_proj", I, H)
+        shapes[p + "input_layernorm.weight"] = [H]
+        shapes[p + "post_attention_layernorm.weight"] = [H]
+    shapes["embed_tokens.weight"] = [c["vocab_size"], H]
+    shapes["norm.weight"] = [H]
+    if pointer_dim:
+        shapes.update({"head.norm.weight": [H], "head.norm.bias": [H], "head.q.weight": [pointer_dim, H],
+                       "head.q.bias": [pointer_dim], "head.k.weight": [pointer_dim, H],
+                       "head.k.bias": [pointer_dim]})
+    return shapes
+
+
+def random_tensors(c, rank=32, pointer_dim=64, seed=0, std=0.02, norm_jitter=0.1):
+    """{name: (0 (F32), shape, array)}: N(0, std^2) weights, norms 1 + jitter."""
+    rng = np.random.default_rng(seed)
+    out = {}
+    for name, shape in expected_shapes(c, rank, pointer_dim).items():
+        if "norm" in name and name.endswith(".weight"):
+            arr = (1.0 + norm_jitter * rng.standard_normal(shape)).astype(np.float32)
+        elif name.endswith(".bias"):
+            arr = (0.1 * rng.standard_normal(shape)).astype(np.float32)
+        elif name.endswith("embed_tokens.weight"):
+            arr = rng.standard_normal(shape).astype(np.float32)
+        else:
+            s = std
+            if "lora_B" in name or "lora_A" in name:
+                s = 0.05
+            arr = (s * rng.standard_normal(shape)).astype(np.float32)
+        out[name] = (0, list(shape), arr)
+    return out
+
+
+def rel_err(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))

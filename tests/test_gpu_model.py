@@ -1,0 +1,131 @@
+"""Whole-forward parity of the device engine.
+
+- Tiny reference checkpoint (generic kernels): hidden states and pointer
+  logits against the reference's PyTorch golden vectors at its own tolerances
+  (2e-5, 1e-5; src/lib.rs:705-732), and against the oracle in every precision.
+- Small 2B-shaped model (tcgen05 path: head_dim 256, DeltaNet 128-wide heads,
+  rank-32 LoRA): hidden states against the oracle, normwise relative error
+  below 1e-3 after 4 layers (int8 rounding flips compound layer by layer; a
+  single teacher-forced layer is checked at 1e-4).
+- Prefix continuation equals the full forward bit for bit (src/lib.rs:796-832).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import TINY
+from model_util import random_tensors, rel_err, small_config
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny(precision):
+    from decider_gpu import GpuModel
+    return GpuModel.from_dir(TINY, precision)
+
+
+def test_tiny_checkpoint_matches_pytorch_golden():
+    m = _tiny("checkpoint")
+    assert not m.fast_path
+    for case in json.load(open(os.path.join(TINY, "raw-reference.json"))):
+        enc = case["encoding"]
+        hidden = m.forward(enc["input_ids"])
+        assert np.abs(hidden - np.array(case["hidden"], np.float32)).max() < 2e-5
+        logits = m.logits(enc["input_ids"], enc["option_positions"])
+        assert np.abs(logits - np.array(case["logits"])).max() < 1e-5
+
+
+def test_tiny_request_probes_match_upstream_logits():
+    m = _tiny("checkpoint")
+    ref = json.load(open(os.path.join(TINY, "reference.json")))
+    for name, probe in ref["probes"].items():
+        e = probe["encoding"]
+        logits = m.logits(e["input_ids"], e["option_positions"])
+        assert np.abs(logits - np.array(probe["logits"])).max() < 1e-5, name
+
+
+@pytest.mark.parametrize("precision", ["checkpoint", "int8", "int8-compute", "int4"])
+def test_tiny_all_precisions_match_oracle(oracle_mod, precision):
+    m = _tiny(precision)
+    o = oracle_mod.OracleModel.from_dir(TINY, precision)
+    ids = [(i * 7 + i // 5) % 32 for i in range(140)]
+    got, exp = m.forward(ids), o.forward(ids)
+    assert rel_err(got, exp) < 1e-5, rel_err(got, exp)
+
+
+@pytest.mark.parametrize("precision", ["checkpoint", "int8-compute"])
+def test_tiny_prefix_cache_reproduces_full_forward_rows_exactly(precision):
+    m = _tiny(precision)
+    ids = [(i * 7 + i // 5) % 32 for i in range(140)]
+    for total, split in [(2, 1), (7, 2), (6, 5), (40, 3), (75, 70), (75, 10), (140, 64)]:
+        full = m.forward(ids[:total])
+        prefix = m.prefill(ids[:split])
+        assert len(prefix) == split
+        rest = m.forward_after(prefix, ids[split:total])
+        assert np.array_equal(rest, full[split:]), (split, total)
+        assert np.array_equal(m.forward_after(prefix, ids[split:total]), rest)
+
+
+def test_tiny_errors_mirror_the_reference():
+    from decider_gpu import GpuError
+    m = _tiny("checkpoint")
+    with pytest.raises(GpuError, match="outside vocabulary"):
+        m.forward([100])
+    with pytest.raises(GpuError, match="4096 tokens"):
+        m.forward([])
+
+
+@pytest.fixture(scope="module")
+def small():
+    cfg = small_config()
+    tensors = random_tensors(cfg, rank=32, pointer_dim=64, seed=1)
+    return cfg, tensors
+
+
+def _gpu_small(cfg, tensors, precision="int8-compute"):
+    from decider_gpu import GpuModel
+    m = GpuModel(cfg, precision, 32, 2.0, 64, 0, 1024)
+    m.set_tensors(tensors)
+    return m.finalize()
+
+
+def test_small_model_takes_the_tcgen05_path_and_matches_oracle(oracle_mod, small):
+    cfg, tensors = small
+    m = _gpu_small(cfg, tensors)
+    assert m.fast_path
+    o = oracle_mod.OracleModel(cfg, tensors, "int8-compute", 32, 2.0)
+    rng = np.random.default_rng(3)
+    ids = rng.integers(0, cfg["vocab_size"], 300)
+    got, exp = m.forward(ids), o.forward(ids)
+    err = rel_err(got, exp)
+    print("small model normwise relative error", err)
+    assert err < 1e-3, err
+    pos = [10, 150, 290]
+    lg, lo = m.logits(ids, pos), o.head_logits(exp, pos)
+    assert np.abs(lg - lo).max() < 1e-3 * max(1.0, np.abs(lo).max())
+
+
+def test_small_model_single_layer_within_1e4(oracle_mod, small):
+    """One DeltaNet layer + one attention layer each as a 1-layer model: the
+    per-layer FP32 tolerance of 1e-4 (normwise)."""
+    cfg, tensors = small
+    for lt in ("linear_attention", "full_attention"):
+        c1 = small_config(layer_types=(lt,))
+        t1 = random_tensors(c1, rank=32, pointer_dim=64, seed=11)
+        m = _gpu_small(c1, t1)
+        o = oracle_mod.OracleModel(c1, t1, "int8-compute", 32, 2.0)
+        ids = np.random.default_rng(4).integers(0, c1["vocab_size"], 257)
+        err = rel_err(m.forward(ids), o.forward(ids))
+        assert err < 1e-4, (lt, err)
+
+
+def test_small_model_prefix_continuation_is_bit_exact(small):
+    cfg, tensors = small
+    m = _gpu_small(cfg, tensors)
+    ids = np.random.default_rng(5).integers(0, cfg["vocab_size"], 400)
+    full = m.forward(ids)
+    for split in (1, 3, 130, 399):
+        p = m.prefill(ids[:split])
+        assert np.array_equal(m.forward_after(p, ids[split:]), full[split:]), split
