@@ -6,15 +6,18 @@
 //   out[m,n] = EPI( Σ_g float(dot_g(xq[m], wq[n])) * (xs[m,g] * ws[n,g])  + 0.0
 //                   + lora_scale * (dot_scores(mid[m, pid(n)], lora_b[n]) + 0.0) )
 //
-// One CTA owns a 128 x 256 output tile. Warp roles:
+// One CTA owns a 128 x 256 output tile; 12 warps (3 warpgroups):
 //   warp 0      TMA producer: int8 A/B tiles (128-byte swizzle) plus the two
 //               groups' activation and weight scales, 3-stage ring;
 //   warp 1      TMEM allocator and single-thread MMA issuer: per 64-wide K group,
 //               two tcgen05.mma kind::i8 (K=32) into a fresh int32 accumulator,
 //               double-buffered in TMEM (2 x 256 columns);
-//   warps 2-9   promotion/epilogue: per group, tcgen05.ld the exact int32 dots,
-//               scale them in FP32 in group order (reference order when EXACT),
-//               then LoRA-B, the epilogue and the store.
+//   warps 2-3   no role (the block is sized in whole warpgroups);
+//   warps 4-11  promotion/epilogue: per group, tcgen05.ld the exact int32 dots,
+//               scale them in FP32 in group order (reference order when EXACT).
+//               After the last group the FP32 sums move to shared memory (the
+//               drained stage ring), and each thread finishes its row: LoRA-B,
+//               the epilogue and the store.
 // Every wait is bounded (mbar_wait_bounded); a stall records kWaitTimeout.
 #pragma once
 #include "common.cuh"
@@ -46,17 +49,23 @@ constexpr int XS_OFF = WS_OFF + 2 * BN * 4;          // [2][BM] floats
 constexpr int STAGE_BYTES = XS_OFF + 2 * BM * 4;     // 52224 = 51 KiB
 constexpr int STAGE_TX = STAGE_BYTES;
 constexpr int LORA_OFF = STAGES * STAGE_BYTES;
-constexpr int NUM_THREADS = 320;
-constexpr int EPI_WARPS = 8;
+constexpr int NUM_THREADS = 384;
+constexpr int EPI_WARP0 = 4, EPI_WARPS = 8;
+constexpr int ACC_LD = BN + 1;                       // padded row stride of the FP32 sums in smem
 constexpr uint32_t TMEM_COLS = 512;
 static_assert(STAGE_BYTES % 1024 == 0, "stages must keep 1024-byte alignment for SWIZZLE_128B");
+static_assert(BM * ACC_LD * 4 <= STAGES * STAGE_BYTES, "FP32 sums must fit in the drained stage ring");
 __host__ __device__ constexpr int lora_bytes(int R) { return BN * R * 4; }
 __host__ __device__ constexpr int bar_off(int R) { return LORA_OFF + lora_bytes(R); }
 __host__ __device__ constexpr int smem_bytes(int R) { return bar_off(R) + 128 + 1024; }
 }  // namespace gemm
 
+__device__ __forceinline__ void epi_bar_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(gemm::EPI_WARPS * 32) : "memory");
+}
+
 template <int R, int EPI, bool EXACT>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(gemm::NUM_THREADS, 1)
     gemm_i8_g64_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        GemmArgs p) {
   using namespace gemm;
@@ -94,11 +103,11 @@ __global__ void __maxnreg__(200)
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
-  if (R > 0 && warp >= 2) {
+  if (R > 0 && warp >= EPI_WARP0) {
     // Stage this tile's LoRA-B rows [BN][R] (contiguous in global memory).
     const float4* src = reinterpret_cast<const float4*>(p.lora_b + size_t(n0) * R);
     float4* dst = reinterpret_cast<float4*>(lora_smem);
-    for (int i = threadIdx.x - 64; i < BN * R / 4; i += EPI_WARPS * 32) dst[i] = src[i];
+    for (int i = threadIdx.x - EPI_WARP0 * 32; i < BN * R / 4; i += EPI_WARPS * 32) dst[i] = src[i];
   }
   tc_fence_before();
   __syncthreads();
@@ -153,10 +162,10 @@ __global__ void __maxnreg__(200)
       mma_commit(mma_done);
       mbar_wait_bounded(mma_done, 0, p.status, 220, nullptr);
     }
-  } else {
-    // ---------------- promotion + epilogue (warps 2..9)
-    const int q = warp & 3;              // TMEM lane quarter this warp may read
-    const int half = (warp - 2) >> 2;    // which 128 columns of the tile
+  } else if (warp >= EPI_WARP0) {
+    // ---------------- promotion (warps 4..11)
+    const int q = warp & 3;                       // TMEM lane quarter this warp may read
+    const int half = (warp - EPI_WARP0) >> 2;     // which 128 columns of the tile
     const int row = q * 32 + lane;
     const int m = m0 + row;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
@@ -174,19 +183,19 @@ __global__ void __maxnreg__(200)
       const float xsg = reinterpret_cast<const float*>(st + XS_OFF)[(g & 1) * BM + row];
       const float* wsg = reinterpret_cast<const float*>(st + WS_OFF) + (g & 1) * BN + half * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t d[32];
-        tmem_ld_32x32b_x32(lane_addr + uint32_t(b * BN + half * 128 + c * 32), d);
+      for (int c = 0; c < 8; ++c) {
+        uint32_t d[16];
+        tmem_ld_32x32b_x16(lane_addr + uint32_t(b * BN + half * 128 + c * 16), d);
         tmem_wait_ld();
         if (p.dots != nullptr && m < p.M) {
-          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * 128 + c * 32);
+          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * 128 + c * 16);
 #pragma unroll
-          for (int j4 = 0; j4 < 8; ++j4)
+          for (int j4 = 0; j4 < 4; ++j4)
             dd[j4] = make_int4(int(d[j4 * 4]), int(d[j4 * 4 + 1]), int(d[j4 * 4 + 2]), int(d[j4 * 4 + 3]));
         }
 #pragma unroll
-        for (int j4 = 0; j4 < 8; ++j4) {
-          const float4 w4 = reinterpret_cast<const float4*>(wsg + c * 32)[j4];
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 w4 = reinterpret_cast<const float4*>(wsg + c * 16)[j4];
           const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -194,9 +203,9 @@ __global__ void __maxnreg__(200)
             const float sc = xsg * wv[e];
             const float fd = i32_to_f32_small(int32_t(d[j]));
             if (EXACT)
-              acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __fmul_rn(fd, sc));
+              acc[c * 16 + j] = __fadd_rn(acc[c * 16 + j], __fmul_rn(fd, sc));
             else
-              acc[c * 32 + j] = __fmaf_rn(fd, sc, acc[c * 32 + j]);
+              acc[c * 16 + j] = __fmaf_rn(fd, sc, acc[c * 16 + j]);
           }
         }
       }
@@ -207,32 +216,35 @@ __global__ void __maxnreg__(200)
         if (g & 1) mbar_arrive(&empty[s]);
       }
     }
+    // ---------------- epilogue: sums to shared memory, then per-row finish.
+    // All stages are drained once every promotion warp has left the loop.
+    epi_bar_sync();
+    float* accs = reinterpret_cast<float*>(smem) + size_t(row) * ACC_LD + half * 128;
     if (ok) {
-      const bool row_ok = m < p.M;
       // Bias-free projections add 0.0 as the reference does (src/tensor.rs:437).
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = __fadd_rn(acc[j], 0.0f);
-      if (R > 0) {
+      for (int j = 0; j < 128; ++j) accs[j] = __fadd_rn(acc[j], 0.0f);
+    }
+    __syncwarp();
+    if (ok && m < p.M) {
+      float vals[32];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const int col0 = half * 128 + c * 32;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int col0 = half * 128 + c * 32;
+        for (int j = 0; j < 32; ++j) vals[j] = accs[c * 32 + j];
+        if (R > 0) {
           const int pid = p.chunk_pid[(n0 + col0) >> 5];
           float mid[R > 0 ? R : 1];
-          if (row_ok) {
-            const float4* mp = reinterpret_cast<const float4*>(p.lora_mid + size_t(m) * p.ld_mid + pid * R);
+          const float4* mp = reinterpret_cast<const float4*>(p.lora_mid + size_t(m) * p.ld_mid + pid * R);
 #pragma unroll
-            for (int r4 = 0; r4 < R / 4; ++r4) {
-              const float4 v = mp[r4];
-              mid[r4 * 4] = v.x; mid[r4 * 4 + 1] = v.y; mid[r4 * 4 + 2] = v.z; mid[r4 * 4 + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int r = 0; r < R; ++r) mid[r] = 0.0f;
+          for (int r4 = 0; r4 < R / 4; ++r4) {
+            const float4 v = mp[r4];
+            mid[r4 * 4] = v.x; mid[r4 * 4 + 1] = v.y; mid[r4 * 4 + 2] = v.z; mid[r4 * 4 + 3] = v.w;
           }
-#pragma unroll
+#pragma unroll 4
           for (int j = 0; j < 32; ++j) {
             const float4* bl = reinterpret_cast<const float4*>(lora_smem + (col0 + j) * R);
-            float delta;
             if (EXACT) {
               // dot_scores order (src/tensor.rs:6-25): eight lanes, then their sum.
               float lanes[8];
@@ -248,13 +260,13 @@ __global__ void __maxnreg__(200)
                   lanes[r & 7] = __fadd_rn(lanes[r & 7], __fmul_rn(mid[r], wv[e]));
                 }
               }
-              delta = -0.0f;
+              float delta = -0.0f;
 #pragma unroll
               for (int i = 0; i < 8; ++i) delta = __fadd_rn(delta, lanes[i]);
               delta = __fadd_rn(delta, 0.0f);
-              acc[c * 32 + j] = __fadd_rn(acc[c * 32 + j], __fmul_rn(p.lora_scale, delta));
+              vals[j] = __fadd_rn(vals[j], __fmul_rn(p.lora_scale, delta));
             } else {
-              delta = 0.0f;
+              float delta = 0.0f;
 #pragma unroll
               for (int r4 = 0; r4 < R / 4; ++r4) {
                 const float4 w = bl[r4];
@@ -263,29 +275,33 @@ __global__ void __maxnreg__(200)
                 delta = __fmaf_rn(mid[r4 * 4 + 2], w.z, delta);
                 delta = __fmaf_rn(mid[r4 * 4 + 3], w.w, delta);
               }
-              acc[c * 32 + j] = __fmaf_rn(p.lora_scale, delta, acc[c * 32 + j]);
+              vals[j] = __fmaf_rn(p.lora_scale, delta, vals[j]);
             }
           }
         }
-      }
-      if (row_ok) {
         if (EPI == kEpiSwiGlu) {
-          // Columns [0,64) of this half hold gate, [64,128) the matching up values.
-          float* o = p.out + size_t(m) * p.ldo + (n0 >> 1) + half * 64;
+          // Columns [0,64) of this half hold gate, [64,128) the matching up
+          // values: keep the gate chunks in shared memory, combine on up chunks.
+          if (c < 2) {
 #pragma unroll
-          for (int j4 = 0; j4 < 16; ++j4) {
-            float4 v;
-            v.x = silu_f(acc[j4 * 4 + 0]) * acc[64 + j4 * 4 + 0];
-            v.y = silu_f(acc[j4 * 4 + 1]) * acc[64 + j4 * 4 + 1];
-            v.z = silu_f(acc[j4 * 4 + 2]) * acc[64 + j4 * 4 + 2];
-            v.w = silu_f(acc[j4 * 4 + 3]) * acc[64 + j4 * 4 + 3];
-            reinterpret_cast<float4*>(o)[j4] = v;
+            for (int j = 0; j < 32; ++j) accs[c * 32 + j] = vals[j];
+          } else {
+            float* o = p.out + size_t(m) * p.ldo + (n0 >> 1) + half * 64 + (c - 2) * 32;
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              float4 v;
+              v.x = silu_f(accs[(c - 2) * 32 + j4 * 4 + 0]) * vals[j4 * 4 + 0];
+              v.y = silu_f(accs[(c - 2) * 32 + j4 * 4 + 1]) * vals[j4 * 4 + 1];
+              v.z = silu_f(accs[(c - 2) * 32 + j4 * 4 + 2]) * vals[j4 * 4 + 2];
+              v.w = silu_f(accs[(c - 2) * 32 + j4 * 4 + 3]) * vals[j4 * 4 + 3];
+              reinterpret_cast<float4*>(o)[j4] = v;
+            }
           }
         } else {
-          float4* o = reinterpret_cast<float4*>(p.out + size_t(m) * p.ldo + n0 + half * 128);
+          float4* o = reinterpret_cast<float4*>(p.out + size_t(m) * p.ldo + n0 + col0);
 #pragma unroll
-          for (int j4 = 0; j4 < 32; ++j4) {
-            float4 v = make_float4(acc[j4 * 4], acc[j4 * 4 + 1], acc[j4 * 4 + 2], acc[j4 * 4 + 3]);
+          for (int j4 = 0; j4 < 8; ++j4) {
+            float4 v = make_float4(vals[j4 * 4], vals[j4 * 4 + 1], vals[j4 * 4 + 2], vals[j4 * 4 + 3]);
             if (EPI == kEpiAdd) {
               const float4 old = o[j4];
               v.x = __fadd_rn(old.x, v.x); v.y = __fadd_rn(old.y, v.y);
