@@ -119,60 +119,40 @@ __global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float
   }
 }
 
-// LoRA A: mid[m][r] = dot_scores(x[m], A[r]) (src/tensor.rs:6-25 order when
-// EXACT: eight lanes over k % 8, each mul-then-add, lanes summed from -0.0,
-// then the tail). Tile: 16 rows x 32 outputs per 256-thread CTA, 64-wide K chunks.
+// LoRA A: mid[m][r] = dot_scores(x[m], A[r]) in the reference's order
+// (src/tensor.rs:6-25): eight lanes over k % 8, each a sequential
+// multiply-then-add chain, the lanes summed from -0.0 in order, then the tail.
+// One thread per (row, output, lane): the eight lanes of an output are eight
+// consecutive threads, so each chain reads 32 contiguous bytes per step.
 template <bool EXACT>
-__global__ void lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K, const float* __restrict__ A, int R,
-                              float* __restrict__ mid, int ldm) {
-  constexpr int TM = 16, TR = 32, KC = 64;
-  __shared__ float xs_[TM][KC + 1];
-  __shared__ float as_[TR][KC + 1];
-  const int r_local = threadIdx.x % 32, m_local0 = (threadIdx.x / 32) * 2;
-  const int m_base = blockIdx.x * TM, r_base = blockIdx.y * TR;
-  const int r = r_base + r_local;
-  float lanes[2][8];
-#pragma unroll
-  for (int i = 0; i < 2; ++i)
-#pragma unroll
-    for (int l = 0; l < 8; ++l) lanes[i][l] = 0.0f;
-  const int kfull = (K / 8) * 8;  // lane-ordered part; the tail is added afterwards
-  for (int k0 = 0; k0 < kfull; k0 += KC) {
-    for (int i = threadIdx.x; i < TM * KC; i += 256) {
-      const int mm = i / KC, kk = i % KC, m = m_base + mm, k = k0 + kk;
-      xs_[mm][kk] = (m < M && k < kfull) ? x[size_t(m) * ldx + k] : 0.0f;
+__global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                     const float* __restrict__ A, int R, float* __restrict__ mid,
+                                                     int ldm) {
+  const long gid = long(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int lane8 = int(gid & 7);
+  const long out = gid >> 3;
+  const int m = int(out / R), r = int(out % R);
+  const bool active = m < M;
+  const float* xr = x + size_t(active ? m : 0) * ldx;
+  const float* ar = A + size_t(r) * K;
+  const int kfull = (K / 8) * 8;
+  float acc = 0.0f;
+  if (active) {
+    int k = lane8;
+#pragma unroll 4
+    for (; k < kfull; k += 8) {
+      if (EXACT)
+        acc = __fadd_rn(acc, __fmul_rn(__ldg(xr + k), __ldg(ar + k)));
+      else
+        acc = __fmaf_rn(__ldg(xr + k), __ldg(ar + k), acc);
     }
-    for (int i = threadIdx.x; i < TR * KC; i += 256) {
-      const int rr = i / KC, kk = i % KC, rg = r_base + rr, k = k0 + kk;
-      as_[rr][kk] = (rg < R && k < kfull) ? A[size_t(rg) * K + k] : 0.0f;
-    }
-    __syncthreads();
-    const int kc = min(KC, kfull - k0);
-    for (int kk = 0; kk < kc; kk += 8) {
-#pragma unroll
-      for (int l = 0; l < 8; ++l) {
-        const float a = as_[r_local][kk + l];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-          const float xv = xs_[m_local0 + i][kk + l];
-          if (EXACT)
-            lanes[i][l] = __fadd_rn(lanes[i][l], __fmul_rn(xv, a));
-          else
-            lanes[i][l] = __fmaf_rn(xv, a, lanes[i][l]);
-        }
-      }
-    }
-    __syncthreads();
   }
-  if (r >= R) return;
+  // Gather the eight lanes into the group's first thread, summed in order.
+  float s = -0.0f;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int m = m_base + m_local0 + i;
-    if (m >= M) continue;
-    float s = -0.0f;
-#pragma unroll
-    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, lanes[i][l]);
-    for (int k = kfull; k < K; ++k) s = __fadd_rn(s, __fmul_rn(x[size_t(m) * ldx + k], A[size_t(r) * K + k]));
+  for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, (threadIdx.x & ~7) + l));
+  if (active && lane8 == 0) {
+    for (int k = kfull; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], ar[k]));
     mid[size_t(m) * ldm + r] = s;
   }
 }
@@ -283,11 +263,12 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
                    cudaStream_t s) {
   if (M <= 0 || R <= 0) return;
-  dim3 grid((M + 15) / 16, (R + 31) / 32);
+  const long threads = long(M) * R * 8;
+  const int blocks = int((threads + 255) / 256);
   if (exact)
-    lora_a_kernel<true><<<grid, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
   else
-    lora_a_kernel<false><<<grid, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    lora_a_kernel<false><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
   DG_CUDA(cudaGetLastError());
 }
 

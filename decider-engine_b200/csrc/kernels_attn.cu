@@ -112,11 +112,32 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
   const int last_key = min(L - 1, offset + t0 + ABQ - 1);
   for (int kb = 0; kb <= last_key; kb += ABK) {
     __syncthreads();
-    for (int i = threadIdx.x; i < ABK * AD; i += 128) {
-      const int key = i / AD, c = i % AD, s = kb + key;
-      const bool ok = s < L;
-      Kt[c * (ABK + 1) + key] = ok ? kc[size_t(s) * kw + kh * AD + c] : 0.0f;
-      Vs[key * AD + c] = ok ? vc[size_t(s) * kw + kh * AD + c] : 0.0f;
+    // 32 keys x 256 dims = 2048 float4 per matrix, 16 per thread: issue all
+    // loads of a batch before any shared-memory store so their latency overlaps.
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float4 kr[8], vr[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = (half * 8 + u) * 128 + threadIdx.x;
+        const int key = i / (AD / 4), c = (i % (AD / 4)) * 4, s = kb + key;
+        if (s < L) {
+          kr[u] = __ldg(reinterpret_cast<const float4*>(kc + size_t(s) * kw + kh * AD + c));
+          vr[u] = __ldg(reinterpret_cast<const float4*>(vc + size_t(s) * kw + kh * AD + c));
+        } else {
+          kr[u] = vr[u] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = (half * 8 + u) * 128 + threadIdx.x;
+        const int key = i / (AD / 4), c = (i % (AD / 4)) * 4;
+        Kt[(c + 0) * (ABK + 1) + key] = kr[u].x;
+        Kt[(c + 1) * (ABK + 1) + key] = kr[u].y;
+        Kt[(c + 2) * (ABK + 1) + key] = kr[u].z;
+        Kt[(c + 3) * (ABK + 1) + key] = kr[u].w;
+        *reinterpret_cast<float4*>(&Vs[key * AD + c]) = vr[u];
+      }
     }
     __syncthreads();
     float sc[4];

@@ -87,84 +87,121 @@ __global__ void delta_rec_generic_kernel(const float* __restrict__ conv, int n, 
   }
 }
 
-// Gated delta rule for dk == 128: one warp owns 4 value columns of one head
-// of one sequence; lane l holds state rows 4l..4l+3 of those columns in
-// registers. Per token: decay, k^T S (warp reduction), delta, rank-1 update,
-// q^T S (reduction). Operands are strided so the same kernel serves the model
-// (q|k|v rows of the conv output) and the isolated batched recurrence.
+// Gated delta rule for dk == 128. A CTA of 4 warps owns 16 value columns of
+// one head of one sequence; each warp owns 4 columns and lane l holds state
+// rows 4l..4l+3 of them in registers. Tokens are staged through shared memory
+// in chunks of 32 with cp.async, double-buffered, so the serial per-token
+// chain (decay, k^T S reduction, delta, rank-1 update, q^T S reduction) never
+// waits on global memory. Operands are strided so the same kernel serves the
+// model (q|k|v rows of the conv output) and the isolated batched recurrence.
+constexpr int REC_T = 32, REC_COLS = 16;
+struct RecStage {
+  float q[REC_T][128];
+  float k[REC_T][128];
+  float v[REC_T][REC_COLS];
+  float decay[REC_T];
+  float beta[REC_T];
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 __global__ void __launch_bounds__(128) delta_rec128_kernel(DeltaArgs a) {
   constexpr int DK = 128;
-  const int wid = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
-  const int groups = a.dv / 4;
-  if (wid >= a.value_heads * groups) return;
+  extern __shared__ __align__(16) uint8_t rec_smem[];
+  RecStage* st = reinterpret_cast<RecStage*>(rec_smem);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int groups16 = a.dv / REC_COLS;
   const size_t bi = blockIdx.y;
-  const int h = wid / groups, j0 = (wid % groups) * 4, kh = h / (a.value_heads / a.key_heads);
-  const float* qb = a.q + bi * a.bs_qkv + kh * DK + lane * 4;
-  const float* kb = a.k + bi * a.bs_qkv + kh * DK + lane * 4;
-  const float* vb = a.v + bi * a.bs_qkv + h * a.dv + j0;
+  const int h = blockIdx.x / groups16, c0 = (blockIdx.x % groups16) * REC_COLS;
+  const int kh = h / (a.value_heads / a.key_heads), j0 = c0 + warp * 4;
+  const float* qb = a.q + bi * a.bs_qkv + kh * DK;
+  const float* kb = a.k + bi * a.bs_qkv + kh * DK;
+  const float* vb = a.v + bi * a.bs_qkv + h * a.dv + c0;
   const float* db = a.decay + bi * a.bs_gb + h;
   const float* bb = a.beta + bi * a.bs_gb + h;
   float* ob = a.o + bi * a.bs_o + h * a.dv + j0;
   float* S = a.state + bi * a.bs_state + size_t(h) * DK * a.dv;
   const int dv = a.dv, n = a.n;
+  const int chunks = (n + REC_T - 1) / REC_T;
+
+  auto stage = [&](int chunk, int buf) {
+    const int t0 = chunk * REC_T, tn = min(REC_T, n - t0);
+    RecStage& sg = st[buf];
+    for (int i = threadIdx.x; i < tn * 32; i += 128) {  // q and k: 32 float4 per token each
+      const int t = i / 32, c = (i % 32) * 4;
+      cp_async16(&sg.q[t][c], qb + size_t(t0 + t) * a.ld_qk + c);
+      cp_async16(&sg.k[t][c], kb + size_t(t0 + t) * a.ld_qk + c);
+    }
+    for (int i = threadIdx.x; i < tn * (REC_COLS / 4); i += 128) {
+      const int t = i / (REC_COLS / 4), c = (i % (REC_COLS / 4)) * 4;
+      cp_async16(&sg.v[t][c], vb + size_t(t0 + t) * a.ld_v + c);
+    }
+    cp_async_commit();
+    for (int t = threadIdx.x; t < tn; t += 128) {
+      const float d = db[size_t(t0 + t) * a.ld_gb];
+      sg.decay[t] = a.log_decay ? expf(d) : d;
+      sg.beta[t] = bb[size_t(t0 + t) * a.ld_gb];
+    }
+  };
+
   float s[4][4];
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
     const float4 v = *reinterpret_cast<const float4*>(S + size_t(lane * 4 + r) * dv + j0);
     s[r][0] = v.x; s[r][1] = v.y; s[r][2] = v.z; s[r][3] = v.w;
   }
-  float4 kq = make_float4(0, 0, 0, 0), qq = kq, vv = kq;
-  float dec = 0.0f, be = 0.0f;
-  if (n > 0) {
-    kq = *reinterpret_cast<const float4*>(kb);
-    qq = *reinterpret_cast<const float4*>(qb);
-    vv = *reinterpret_cast<const float4*>(vb);
-    dec = a.log_decay ? expf(db[0]) : db[0];
-    be = bb[0];
-  }
-  for (int t = 0; t < n; ++t) {
-    const float kk[4] = {kq.x, kq.y, kq.z, kq.w}, qv[4] = {qq.x, qq.y, qq.z, qq.w}, v[4] = {vv.x, vv.y, vv.z, vv.w};
-    const float d0 = dec, b0 = be;
-    if (t + 1 < n) {  // prefetch the next token's inputs
-      kq = *reinterpret_cast<const float4*>(kb + size_t(t + 1) * a.ld_qk);
-      qq = *reinterpret_cast<const float4*>(qb + size_t(t + 1) * a.ld_qk);
-      vv = *reinterpret_cast<const float4*>(vb + size_t(t + 1) * a.ld_v);
-      dec = db[size_t(t + 1) * a.ld_gb];
-      if (a.log_decay) dec = expf(dec);
-      be = bb[size_t(t + 1) * a.ld_gb];
-    }
-    float p[4];
+  if (chunks > 0) stage(0, 0);
+  for (int ch = 0; ch < chunks; ++ch) {
+    cp_async_wait_all();
+    __syncthreads();  // chunk ch is resident; the other buffer is free
+    if (ch + 1 < chunks) stage(ch + 1, (ch + 1) & 1);
+    const RecStage& sg = st[ch & 1];
+    const int t0 = ch * REC_T, tn = min(REC_T, n - t0);
+    for (int t = 0; t < tn; ++t) {
+      const float4 kq4 = *reinterpret_cast<const float4*>(&sg.k[t][lane * 4]);
+      const float4 qq4 = *reinterpret_cast<const float4*>(&sg.q[t][lane * 4]);
+      const float4 vv4 = *reinterpret_cast<const float4*>(&sg.v[t][warp * 4]);
+      const float kk[4] = {kq4.x, kq4.y, kq4.z, kq4.w}, qv[4] = {qq4.x, qq4.y, qq4.z, qq4.w};
+      const float v[4] = {vv4.x, vv4.y, vv4.z, vv4.w};
+      const float d0 = sg.decay[t], b0 = sg.beta[t];
+      float p[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      float acc = 0.0f;
+      for (int c = 0; c < 4; ++c) {
+        float acc = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        s[r][c] = s[r][c] * d0;
-        acc = __fmaf_rn(kk[r], s[r][c], acc);
+        for (int r = 0; r < 4; ++r) {
+          s[r][c] = s[r][c] * d0;
+          acc = __fmaf_rn(kk[r], s[r][c], acc);
+        }
+        p[c] = acc;
       }
-      p[c] = acc;
-    }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
+      for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) p[c] += __shfl_xor_sync(0xffffffffu, p[c], off);
-    float out[4];
+        for (int c = 0; c < 4; ++c) p[c] += __shfl_xor_sync(0xffffffffu, p[c], off);
+      float out[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float delta = (v[c] - p[c]) * b0;
-      float acc = 0.0f;
+      for (int c = 0; c < 4; ++c) {
+        const float delta = (v[c] - p[c]) * b0;
+        float acc = 0.0f;
 #pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        s[r][c] = __fmaf_rn(kk[r], delta, s[r][c]);
-        acc = __fmaf_rn(qv[r], s[r][c], acc);
+        for (int r = 0; r < 4; ++r) {
+          s[r][c] = __fmaf_rn(kk[r], delta, s[r][c]);
+          acc = __fmaf_rn(qv[r], s[r][c], acc);
+        }
+        out[c] = acc;
       }
-      out[c] = acc;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) out[c] += __shfl_xor_sync(0xffffffffu, out[c], off);
+      if (lane == 0)
+        *reinterpret_cast<float4*>(ob + size_t(t0 + t) * a.ldo) = make_float4(out[0], out[1], out[2], out[3]);
     }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) out[c] += __shfl_xor_sync(0xffffffffu, out[c], off);
-    if (lane == 0) *reinterpret_cast<float4*>(ob + size_t(t) * a.ldo) = make_float4(out[0], out[1], out[2], out[3]);
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r)
@@ -197,7 +234,7 @@ void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, in
                              const float* decay, const float* beta, float* state, float* o, cudaStream_t s) {
   if (n <= 0) return;
   const int W = 2 * key_heads * dk + value_heads * dv;
-  if (dk == 128 && dv % 4 == 0) {
+  if (dk == 128 && dv % REC_COLS == 0) {
     DeltaArgs a{};
     a.q = conv;
     a.k = conv + key_heads * dk;
@@ -224,9 +261,15 @@ void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, in
 
 void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s) {
   if (a.n <= 0 || batch <= 0) return;
-  const int warps = a.value_heads * (a.dv / 4);
-  dim3 grid((warps * 32 + 127) / 128, batch);
-  delta_rec128_kernel<<<grid, 128, 0, s>>>(a);
+  if (a.dv % REC_COLS) throw CudaError("delta_rec128: value width must be a multiple of 16");
+  static bool configured = false;
+  const int smem = 2 * sizeof(RecStage);
+  if (!configured) {
+    DG_CUDA(cudaFuncSetAttribute(delta_rec128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid(a.value_heads * (a.dv / REC_COLS), batch);
+  delta_rec128_kernel<<<grid, 128, smem, s>>>(a);
   DG_CUDA(cudaGetLastError());
 }
 
