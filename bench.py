@@ -196,6 +196,7 @@ def run_ours(args, world, rank, local, dist):
     model.fill_synthetic(seed=0, stddev=0.02)
     model.finalize()
     assert model.fast_path
+    model.set_exact(args.exact)
     setup_s = time.time() - t0
     rng = np.random.default_rng(1000 + rank)
     ids = rng.integers(0, cfg["vocab_size"], TOKENS).astype(np.uint32)
@@ -239,6 +240,7 @@ def run_ours(args, world, rank, local, dist):
     lin = Linear((0.02 * g.standard_normal((N, K))).astype(np.float32),
                  (0.02 * g.standard_normal((32, K))).astype(np.float32),
                  (0.02 * g.standard_normal((N, 32))).astype(np.float32), 2.0, local)
+    lin.set_exact(args.exact)
     xd = torch.randn((M, K), device=f"cuda:{local}")
     yd = torch.empty((M, N), device=f"cuda:{local}")
     for _ in range(3):
@@ -266,7 +268,8 @@ def run_ours(args, world, rank, local, dist):
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)", "data": "synthetic",
+        "vs_baseline": None, "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)",
+        "promotion": "reference-order" if args.exact else "fma", "data": "synthetic",
         "config": {"workload": "cfg2: 2B decider forward (24 layers, LoRA r32) over a 512-token prompt + "
                                "pointer head, int8-compute", "tokens_per_step": TOKENS, "parallelism": f"dp{world}",
                    "l2": "not flushed: each step streams 1.4 GB of int8 weights, > 126 MB L2",
@@ -293,6 +296,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--exact", action="store_true",
+                    help="reference-order FP32 promotion instead of fused multiply-add")
     args = ap.parse_args()
     world, rank, local, dist = dist_setup()
     try:

@@ -27,7 +27,7 @@ struct dg_linear {
   bool exact = true;
   cudaStream_t stream = nullptr;
   dg::DevBuf wq, ws_t, lora_a, lora_b, chunk_pid, status;
-  CUtensorMap map_b{};
+  CUtensorMap map_b{}, map_b64{};
   int cap_m = 0, ldxs = 0;
   dg::DevBuf x, xq, xs, mid, y;
 };
@@ -106,7 +106,7 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
     note_launch();
   }
   CUtensorMap map_a;
-  make_tmap_i8_2d(&map_a, l->xq.ptr, uint64_t(l->k), uint64_t(m), gemm::BK, gemm::BM);
+  make_tmap_i8_2d(&map_a, l->xq.ptr, uint64_t(l->k), uint64_t(m), 128, 128);
   GemmArgs a{};
   a.M = m;
   a.N = l->n_pad;
@@ -129,7 +129,7 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
     dump = dots;
   }
   a.dots = dump;
-  launch_gemm_i8(map_a, l->map_b, a, l->rank, kEpiWrite, l->exact, l->stream);
+  launch_gemm_i8(map_a, l->map_b, &l->map_b64, a, l->rank, kEpiWrite, l->exact, l->stream);
   note_launch();
   if (!direct)
     DG_CUDA(cudaMemcpy2DAsync(y_dev, size_t(l->n) * 4, l->y.ptr, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
@@ -264,7 +264,7 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
     l->k = k;
     l->rank = rank;
     l->scale = lora_scale;
-    l->n_pad = (n + gemm::BN - 1) / gemm::BN * gemm::BN;
+    l->n_pad = (n + 255) / 256 * 256;
     const int G = k / 64, N = l->n_pad;
     std::vector<float> wf(w, w + size_t(n) * k);
     std::vector<uint8_t> q;
@@ -291,7 +291,8 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
       l->lora_a = up(lora_a, size_t(rank) * k * 4);
     }
     l->status = DevBuf(sizeof(DeviceStatus));
-    make_tmap_i8_2d(&l->map_b, l->wq.ptr, uint64_t(k), uint64_t(N), gemm::BK, gemm::BN);
+    make_tmap_i8_2d(&l->map_b, l->wq.ptr, uint64_t(k), uint64_t(N), 128, 256);
+    make_tmap_i8_2d(&l->map_b64, l->wq.ptr, uint64_t(k), uint64_t(N), 128, 64);
     DG_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
     *out = l.release();
   });

@@ -38,7 +38,7 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
       total = round_up(total + outs[p], 32);
     }
   }
-  const int N = round_up(total, gemm::BN);
+  const int N = round_up(total, 256);
   d.out = total;
   d.out_pad = N;
   d.part_off = off;
@@ -71,7 +71,8 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
   d.lora_a = upload(la);
   d.lora_b = upload(lb);
   d.chunk_pid = upload(pid);
-  make_tmap_i8_2d(&d.map_b, d.wq.ptr, uint64_t(in), uint64_t(N), gemm::BK, gemm::BN);
+  make_tmap_i8_2d(&d.map_b, d.wq.ptr, uint64_t(in), uint64_t(N), 128, 256);
+  make_tmap_i8_2d(&d.map_b64, d.wq.ptr, uint64_t(in), uint64_t(N), 128, 64);
   return d;
 }
 

@@ -21,7 +21,7 @@ static const CUtensorMap& act_map(const void* base, int K, int rows) {
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
   CUtensorMap m;
-  make_tmap_i8_2d(&m, base, uint64_t(K), uint64_t(rows), gemm::BK, gemm::BM);
+  make_tmap_i8_2d(&m, base, uint64_t(K), uint64_t(rows), 128, 128);
   return cache.emplace(key, m).first->second;
 }
 
@@ -41,7 +41,7 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.out = out;
   a.ldo = ldo;
   a.status = status();
-  launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.map_b, a, 32, epi, exact, stream_);
+  launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.map_b, &p.map_b64, a, 32, epi, exact, stream_);
   note_launch();
 }
 

@@ -1,8 +1,8 @@
-// Launchers and instantiations of the tcgen05 INT8 projection.
+// Tensor maps, tile-width choice and launch of the tcgen05 INT8 projection.
+// The kernel instantiations live in gemm_i8_bn256.cu and gemm_i8_bn64.cu.
 #include <mutex>
 
-#include "gemm_i8.cuh"
-#include "launch.h"
+#include "gemm_i8_launch.cuh"
 
 namespace dg {
 
@@ -39,41 +39,31 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
-size_t gemm_i8_smem_bytes(int rank) { return size_t(gemm::smem_bytes(rank)); }
+size_t gemm_i8_smem_bytes(int rank) { return size_t(GemmShape<256>::smem_bytes(rank)); }
 
-template <int R, int EPI, bool EXACT>
-static void launch_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
-  auto kern = gemm_i8_g64_kernel<R, EPI, EXACT>;
-  const int smem = gemm::smem_bytes(R);
-  static bool configured = false;  // per instantiation
-  if (!configured) {
-    DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
-  dim3 grid((args.M + gemm::BM - 1) / gemm::BM, args.N / gemm::BN);
-  kern<<<grid, gemm::NUM_THREADS, smem, s>>>(a, b, args);
-  DG_CUDA(cudaGetLastError());
+int gemm_i8_choose_bn(int M, int N, int epi, bool have_narrow_map) {
+  const int ctas256 = ((M + 127) / 128) * (N / 256);
+  if (epi == kEpiSwiGlu || !have_narrow_map || N % 64) return 256;
+  return ctas256 < 120 ? 64 : 256;
 }
 
-void launch_gemm_i8(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi, bool exact,
-                    cudaStream_t s) {
+void launch_gemm_i8(const CUtensorMap& a, const CUtensorMap& b256, const CUtensorMap* b64, const GemmArgs& args,
+                    int rank, int epi, bool exact, cudaStream_t s) {
   if (args.M <= 0) return;
-  if (args.N % gemm::BN || args.K % gemm::BK || args.K <= 0)
+  if (args.N % 256 || args.K % 128 || args.K <= 0)
     throw CudaError("gemm_i8: N must be a multiple of 256 and K a positive multiple of 128");
-  if (args.ldxs % gemm::BM || args.ldxs < ((args.M + gemm::BM - 1) / gemm::BM) * gemm::BM)
+  if (args.ldxs % 128 || args.ldxs < ((args.M + 127) / 128) * 128)
     throw CudaError("gemm_i8: activation-scale stride must cover whole 128-row tiles");
   if (rank != 0 && rank != 32) throw CudaError("gemm_i8: LoRA rank must be 0 or 32");
   if (rank && (args.ld_mid % 4 || !args.lora_mid || !args.lora_b || !args.chunk_pid))
     throw CudaError("gemm_i8: bad LoRA operands");
   if (epi == kEpiSwiGlu ? (args.ldo % 4) : (args.ldo % 4 || args.ldo < args.N))
     throw CudaError("gemm_i8: output stride must be a multiple of 4 covering the tile");
-#define DG_GEMM_CASE(R_, E_, X_) \
-  if (rank == R_ && epi == E_ && exact == X_) return launch_impl<R_, E_, X_>(a, b, args, s);
-  DG_GEMM_CASE(32, kEpiWrite, true) DG_GEMM_CASE(32, kEpiAdd, true) DG_GEMM_CASE(32, kEpiSwiGlu, true)
-  DG_GEMM_CASE(32, kEpiWrite, false) DG_GEMM_CASE(32, kEpiAdd, false) DG_GEMM_CASE(32, kEpiSwiGlu, false)
-  DG_GEMM_CASE(0, kEpiWrite, true) DG_GEMM_CASE(0, kEpiWrite, false)
-#undef DG_GEMM_CASE
-  throw CudaError("gemm_i8: unsupported rank/epilogue combination");
+  const int bn = gemm_i8_choose_bn(args.M, args.N, epi, b64 != nullptr);
+  if (bn == 64)
+    launch_gemm_i8_bn64(a, *b64, args, rank, epi, exact, s);
+  else
+    launch_gemm_i8_bn256(a, b256, args, rank, epi, exact, s);
 }
 
 }  // namespace dg

@@ -1,0 +1,27 @@
+// Per-tile-width launchers of the tcgen05 INT8 projection.
+#pragma once
+#include "gemm_i8.cuh"
+#include "launch.h"
+
+namespace dg {
+
+void launch_gemm_i8_bn256(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
+                          bool exact, cudaStream_t s);
+void launch_gemm_i8_bn64(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
+                         bool exact, cudaStream_t s);
+
+template <int BN, int R, int EPI, bool EXACT>
+void launch_gemm_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+  auto kern = gemm_i8_g64_kernel<BN, R, EPI, EXACT>;
+  const int smem = GemmShape<BN>::smem_bytes(R);
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  dim3 grid((args.M + 127) / 128, args.N / BN);
+  kern<<<grid, GemmShape<BN>::NUM_THREADS, smem, s>>>(a, b, args);
+  DG_CUDA(cudaGetLastError());
+}
+
+}  // namespace dg

@@ -122,38 +122,65 @@ __global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float
 // LoRA A: mid[m][r] = dot_scores(x[m], A[r]) in the reference's order
 // (src/tensor.rs:6-25): eight lanes over k % 8, each a sequential
 // multiply-then-add chain, the lanes summed from -0.0 in order, then the tail.
-// One thread per (row, output, lane): the eight lanes of an output are eight
-// consecutive threads, so each chain reads 32 contiguous bytes per step.
+// A thread runs lane `i` of a 4-row x 4-output tile (16 chains sharing 8 loads
+// per step); the eight lanes of a tile are eight consecutive threads.
 template <bool EXACT>
 __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                      const float* __restrict__ A, int R, float* __restrict__ mid,
                                                      int ldm) {
+  constexpr int TM = 4, TR = 4;
   const long gid = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane8 = int(gid & 7);
-  const long out = gid >> 3;
-  const int m = int(out / R), r = int(out % R);
-  const bool active = m < M;
-  const float* xr = x + size_t(active ? m : 0) * ldx;
-  const float* ar = A + size_t(r) * K;
+  const long tile = gid >> 3;
+  const int rtiles = (R + TR - 1) / TR;
+  const int m0 = int(tile / rtiles) * TM, r0 = int(tile % rtiles) * TR;
+  const float* xr[TM];
+  const float* ar[TR];
+#pragma unroll
+  for (int a = 0; a < TM; ++a) xr[a] = x + size_t(min(m0 + a, M - 1)) * ldx;
+#pragma unroll
+  for (int b = 0; b < TR; ++b) ar[b] = A + size_t(min(r0 + b, R - 1)) * K;
   const int kfull = (K / 8) * 8;
-  float acc = 0.0f;
-  if (active) {
-    int k = lane8;
-#pragma unroll 4
-    for (; k < kfull; k += 8) {
-      if (EXACT)
-        acc = __fadd_rn(acc, __fmul_rn(__ldg(xr + k), __ldg(ar + k)));
-      else
-        acc = __fmaf_rn(__ldg(xr + k), __ldg(ar + k), acc);
+  float acc[TM][TR];
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TR; ++b) acc[a][b] = 0.0f;
+  if (m0 < M) {
+#pragma unroll 2
+    for (int k = lane8; k < kfull; k += 8) {
+      float xv[TM], av[TR];
+#pragma unroll
+      for (int a = 0; a < TM; ++a) xv[a] = __ldg(xr[a] + k);
+#pragma unroll
+      for (int b = 0; b < TR; ++b) av[b] = __ldg(ar[b] + k);
+#pragma unroll
+      for (int a = 0; a < TM; ++a)
+#pragma unroll
+        for (int b = 0; b < TR; ++b) {
+          if (EXACT)
+            acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(xv[a], av[b]));
+          else
+            acc[a][b] = __fmaf_rn(xv[a], av[b], acc[a][b]);
+        }
     }
   }
-  // Gather the eight lanes into the group's first thread, summed in order.
-  float s = -0.0f;
+  // Each lane finalises two of the 16 outputs: the eight lane partials summed
+  // in lane order from -0.0, then the tail.
+  const int base = threadIdx.x & ~7;
 #pragma unroll
-  for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, (threadIdx.x & ~7) + l));
-  if (active && lane8 == 0) {
-    for (int k = kfull; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[k], ar[k]));
-    mid[size_t(m) * ldm + r] = s;
+  for (int o = 0; o < TM * TR; ++o) {
+    const int a = o / TR, b = o % TR;
+    float s = -0.0f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc[a][b], base + l));
+    if ((o >> 1) == lane8) {
+      const int m = m0 + a, r = r0 + b;
+      if (m < M && r < R) {
+        for (int k = kfull; k < K; ++k) s = __fadd_rn(s, __fmul_rn(xr[a][k], ar[b][k]));
+        mid[size_t(m) * ldm + r] = s;
+      }
+    }
   }
 }
 
@@ -263,7 +290,7 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
                    cudaStream_t s) {
   if (M <= 0 || R <= 0) return;
-  const long threads = long(M) * R * 8;
+  const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
   if (exact)
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
