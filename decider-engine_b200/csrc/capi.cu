@@ -348,32 +348,55 @@ void dg_linear_free(dg_linear* l) {
   delete l;
 }
 
+static dg::DeltaArgs delta_args(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                                int batch, int t, int heads, float* state, float* o) {
+  if (!q || !k || !v || !g || !beta || !state || !o) throw std::runtime_error("null argument");
+  if (batch <= 0 || t <= 0 || heads <= 0) throw std::runtime_error("bad gated delta rule shape");
+  dg::DeltaArgs a{};
+  const size_t row = size_t(heads) * 128;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.ld_qk = a.ld_v = int(row);
+  a.bs_qkv = size_t(t) * row;
+  a.decay = g;
+  a.beta = beta;
+  a.log_decay = 1;
+  a.ld_gb = heads;
+  a.bs_gb = size_t(t) * heads;
+  a.n = t;
+  a.key_heads = a.value_heads = heads;
+  a.dv = 128;
+  a.state = state;
+  a.bs_state = size_t(heads) * 128 * 128;
+  a.o = o;
+  a.ldo = int(row);
+  a.bs_o = size_t(t) * row;
+  return a;
+}
+
 int dg_gated_delta_rule_device(const float* q, const float* k, const float* v, const float* g, const float* beta,
                                int batch, int t, int heads, float* state, float* o, void* stream) {
   return guarded([&] {
-    if (!q || !k || !v || !g || !beta || !state || !o) throw std::runtime_error("null argument");
-    if (batch <= 0 || t <= 0 || heads <= 0) throw std::runtime_error("bad gated delta rule shape");
-    dg::DeltaArgs a{};
-    const size_t row = size_t(heads) * 128;
-    a.q = q;
-    a.k = k;
-    a.v = v;
-    a.ld_qk = a.ld_v = int(row);
-    a.bs_qkv = size_t(t) * row;
-    a.decay = g;
-    a.beta = beta;
-    a.log_decay = 1;
-    a.ld_gb = heads;
-    a.bs_gb = size_t(t) * heads;
-    a.n = t;
-    a.key_heads = a.value_heads = heads;
-    a.dv = 128;
-    a.state = state;
-    a.bs_state = size_t(heads) * 128 * 128;
-    a.o = o;
-    a.ldo = int(row);
-    a.bs_o = size_t(t) * row;
+    dg::DeltaArgs a = delta_args(q, k, v, g, beta, batch, t, heads, state, o);
     dg::launch_delta_rec128(a, batch, static_cast<cudaStream_t>(stream));
+    dg::note_launch();
+  });
+}
+
+size_t dg_gated_delta_chunk_workspace_bytes(int batch, int t, int heads) {
+  if (batch <= 0 || t <= 0 || heads <= 0) return 0;
+  return dg::delta_chunk_workspace_bytes(batch, heads, t);
+}
+
+int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const float* v, const float* g,
+                                       const float* beta, int batch, int t, int heads, float* state, float* o,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  return guarded([&] {
+    dg::DeltaArgs a = delta_args(q, k, v, g, beta, batch, t, heads, state, o);
+    if (!workspace) throw std::runtime_error("null workspace");
+    dg::launch_delta_chunked(a, batch, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+    dg::note_launch();
     dg::note_launch();
   });
 }

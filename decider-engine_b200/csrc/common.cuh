@@ -215,6 +215,34 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
          | ((m >> 4) << 24);  // M / 16
 }
 
+// ---------------------------------------------------------------- packed f32x2
+// Two FP32 lanes per instruction. The explicit .rn rounding keeps mul and add
+// separate (never contracted into a fused multiply-add), lane by lane IEEE.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "add.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 x, y, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\t"
+      "mul.rn.f32x2 z, x, y;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 x, y, w, z;\n\tmov.b64 x, {%2, %3};\n\tmov.b64 y, {%4, %5};\n\tmov.b64 w, {%6, %7};\n\t"
+      "fma.rn.f32x2 z, x, y, w;\n\tmov.b64 {%0, %1}, z;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
 // ---------------------------------------------------------------- math
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }

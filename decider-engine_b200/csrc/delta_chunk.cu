@@ -1,0 +1,280 @@
+// Chunked gated delta rule (the engine's fast mode; dk = dv = 128).
+//
+// The reference runs the recurrence token by token (Recurrence::head,
+// src/qwen.rs:813-875):  S <- g_t S ;  d_t = b_t (v_t - S^T k_t) ;
+// S <- S + k_t d_t^T ;  o_t = S^T q_t.  Over a chunk of C tokens starting
+// from state S0, with G_t = prod_{s<=t} g_s (log-space cumulative sums), the
+// same quantities are
+//   D = U - W S0,   U = T diag(b) V,   W = T diag(b G) K,
+//   T = (I + L)^-1, L[t][s] = b_t (G_t / G_s) k_t.k_s  (s < t),
+//   O = diag(G) Q S0 + (M o Q K^T) D,   M[t][s] = G_t / G_s (s <= t),
+//   S_C = G_C S0 + K^T diag(G_C / G) D,
+// so only the S0-dependent products are sequential across chunks.
+//
+// delta_chunk_prep_kernel (one CTA per sequence x head x chunk, all chunks in
+// parallel) builds T, U, W, the masked Q K^T and the decay vectors;
+// delta_chunk_scan_kernel (one CTA per sequence x head x 16 value columns)
+// carries the state slice through the chunks. FP32 throughout.
+#include "launch.h"
+
+namespace dg {
+
+namespace {
+
+constexpr int CK = 64, DK = 128, SC = 16;
+
+// Per-chunk products written by the prep kernel.
+struct ChunkOut {
+  float W[CK][DK];
+  float U[CK][DK];
+  float QK[CK][CK];
+  float gam[CK];    // G_t
+  float rem[CK];    // G_C / G_t
+  float gC;         // G_C
+  float pad[3];
+};
+
+__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, ChunkOut* __restrict__ outs,
+                                                               int chunks) {
+  extern __shared__ __align__(16) float sm[];
+  float* Ks = sm;                   // [CK][DK + 1]
+  float* Qs = Ks + CK * (DK + 1);   // [CK][DK + 1]
+  float* Vs = Qs + CK * (DK + 1);   // [CK][DK + 1]  (later reused)
+  float* L = Vs + CK * (DK + 1);    // [CK][CK + 1]
+  float* T = L + CK * (CK + 1);     // [CK][CK + 1]
+  float* lg = T + CK * (CK + 1);    // [CK] cumulative log decay
+  float* bt = lg + CK;              // [CK]
+  float* gm = bt + CK;              // [CK] G_t = exp(lg)
+  const int tid = threadIdx.x;
+  const int c = blockIdx.x % chunks, h = (blockIdx.x / chunks) % a.value_heads;
+  const size_t bi = blockIdx.x / (chunks * a.value_heads);
+  const int kh = h / (a.value_heads / a.key_heads);
+  const int t0 = c * CK, tn = min(CK, a.n - t0);
+  ChunkOut& o = outs[(bi * a.value_heads + h) * chunks + c];
+  const float* qb = a.q + bi * a.bs_qkv + kh * DK;
+  const float* kb = a.k + bi * a.bs_qkv + kh * DK;
+  const float* vb = a.v + bi * a.bs_qkv + h * a.dv;
+  for (int i = tid; i < CK * (DK / 4); i += 256) {
+    const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
+    float4 q4 = make_float4(0, 0, 0, 0), k4 = q4, v4 = q4;
+    if (t < tn) {
+      q4 = *reinterpret_cast<const float4*>(qb + size_t(t0 + t) * a.ld_qk + d);
+      k4 = *reinterpret_cast<const float4*>(kb + size_t(t0 + t) * a.ld_qk + d);
+      v4 = *reinterpret_cast<const float4*>(vb + size_t(t0 + t) * a.ld_v + d);
+    }
+    float* qd = Qs + t * (DK + 1) + d;
+    float* kd = Ks + t * (DK + 1) + d;
+    float* vd = Vs + t * (DK + 1) + d;
+    qd[0] = q4.x; qd[1] = q4.y; qd[2] = q4.z; qd[3] = q4.w;
+    kd[0] = k4.x; kd[1] = k4.y; kd[2] = k4.z; kd[3] = k4.w;
+    vd[0] = v4.x; vd[1] = v4.y; vd[2] = v4.z; vd[3] = v4.w;
+  }
+  if (tid < 32) {
+    // Cumulative log decay over the chunk (two tokens per lane, then a scan).
+    float g0 = 0.0f, g1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+    const int ta = 2 * tid, tb = 2 * tid + 1;
+    const float* gd = a.decay + bi * a.bs_gb + h;
+    const float* bd = a.beta + bi * a.bs_gb + h;
+    if (ta < tn) {
+      g0 = gd[size_t(t0 + ta) * a.ld_gb];
+      b0 = bd[size_t(t0 + ta) * a.ld_gb];
+    }
+    if (tb < tn) {
+      g1 = gd[size_t(t0 + tb) * a.ld_gb];
+      b1 = bd[size_t(t0 + tb) * a.ld_gb];
+    }
+    if (!a.log_decay) {
+      g0 = ta < tn ? logf(g0) : 0.0f;
+      g1 = tb < tn ? logf(g1) : 0.0f;
+    }
+    float pair = g0 + g1, incl = pair;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float v = __shfl_up_sync(0xffffffffu, incl, off);
+      if (tid >= off) incl += v;
+    }
+    const float excl = incl - pair;
+    lg[ta] = excl + g0;
+    lg[tb] = incl;
+    gm[ta] = expf(excl + g0);
+    gm[tb] = expf(incl);
+    bt[ta] = b0;
+    bt[tb] = b1;
+  }
+  __syncthreads();
+  // L (strictly lower) and the masked Q K^T (lower incl. diagonal).
+  for (int e = tid; e < CK * CK; e += 256) {
+    const int t = e / CK, s = e % CK;
+    float kk = 0.0f, qk = 0.0f;
+    if (s <= t && t < tn) {
+      const float* kt = Ks + t * (DK + 1);
+      const float* ks = Ks + s * (DK + 1);
+      const float* qt = Qs + t * (DK + 1);
+#pragma unroll 8
+      for (int d = 0; d < DK; ++d) {
+        kk = __fmaf_rn(kt[d], ks[d], kk);
+        qk = __fmaf_rn(qt[d], ks[d], qk);
+      }
+      const float ratio = expf(lg[t] - lg[s]);
+      qk *= ratio;
+      kk = s < t ? bt[t] * ratio * kk : 0.0f;
+    } else {
+      kk = 0.0f;
+      qk = 0.0f;
+    }
+    L[t * (CK + 1) + s] = kk;
+    o.QK[t][s] = qk;
+  }
+  __syncthreads();
+  // T = (I + L)^-1 by forward substitution, one row per step:
+  // T[t][s] = -sum_{u=s}^{t-1} L[t][u] T[u][s] (s < t), T[t][t] = 1.
+  for (int i = tid; i < CK * CK; i += 256) T[(i / CK) * (CK + 1) + i % CK] = (i / CK == i % CK) ? 1.0f : 0.0f;
+  __syncthreads();
+  for (int t = 1; t < CK; ++t) {
+    if (tid < t) {
+      const int s = tid;
+      float acc = 0.0f;
+      for (int u = s; u < t; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
+      T[t * (CK + 1) + s] = -acc;
+    }
+    __syncthreads();
+  }
+  // U = T diag(b) V and W = T diag(b G) K, row t over s <= t.
+  for (int e = tid; e < CK * DK; e += 256) {
+    const int t = e / DK, d = e % DK;
+    float u = 0.0f, w = 0.0f;
+    for (int s = 0; s <= t; ++s) {
+      const float tb = T[t * (CK + 1) + s] * bt[s];
+      u = __fmaf_rn(tb, Vs[s * (DK + 1) + d], u);
+      w = __fmaf_rn(tb * gm[s], Ks[s * (DK + 1) + d], w);
+    }
+    o.U[t][d] = u;
+    o.W[t][d] = w;
+  }
+  if (tid < CK) {
+    const float last = lg[max(tn - 1, 0)];
+    o.gam[tid] = tid < tn ? gm[tid] : 0.0f;
+    o.rem[tid] = tid < tn ? expf(last - lg[tid]) : 0.0f;
+    if (tid == 0) o.gC = expf(last);
+  }
+}
+
+// Sequential pass over the chunks for one sequence, head and 16 value
+// columns; the state slice S[128][16] lives in shared memory.
+__global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
+                                                               int chunks) {
+  extern __shared__ __align__(16) float sm[];
+  float* S = sm;                    // [DK][SC]
+  float* D = S + DK * SC;           // [CK][SC]
+  float* Ks = D + CK * SC;          // [CK][DK + 1]
+  float* Qs = Ks + CK * (DK + 1);   // [CK][DK + 1]
+  const int tid = threadIdx.x;
+  const int groups = a.dv / SC;
+  const int slice = blockIdx.x % groups, h = (blockIdx.x / groups) % a.value_heads;
+  const size_t bi = blockIdx.x / (groups * a.value_heads);
+  const int kh = h / (a.value_heads / a.key_heads), j0 = slice * SC;
+  const float* qb = a.q + bi * a.bs_qkv + kh * DK;
+  const float* kb = a.k + bi * a.bs_qkv + kh * DK;
+  float* Sg = a.state + bi * a.bs_state + size_t(h) * DK * a.dv;
+  float* ob = a.o + bi * a.bs_o + h * a.dv + j0;
+  for (int e = tid; e < DK * SC; e += 256) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
+  for (int c = 0; c < chunks; ++c) {
+    const ChunkOut& co = outs[(bi * a.value_heads + h) * chunks + c];
+    const int t0 = c * CK, tn = min(CK, a.n - t0);
+    for (int i = tid; i < CK * (DK / 4); i += 256) {
+      const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
+      float4 q4 = make_float4(0, 0, 0, 0), k4 = q4;
+      if (t < tn) {
+        q4 = *reinterpret_cast<const float4*>(qb + size_t(t0 + t) * a.ld_qk + d);
+        k4 = *reinterpret_cast<const float4*>(kb + size_t(t0 + t) * a.ld_qk + d);
+      }
+      float* qd = Qs + t * (DK + 1) + d;
+      float* kd = Ks + t * (DK + 1) + d;
+      qd[0] = q4.x; qd[1] = q4.y; qd[2] = q4.z; qd[3] = q4.w;
+      kd[0] = k4.x; kd[1] = k4.y; kd[2] = k4.z; kd[3] = k4.w;
+    }
+    __syncthreads();
+    // D = U - W S0 ; thread -> (t, 4 columns)
+    float qs[4];
+    {
+      const int t = tid / 4, jc = (tid % 4) * 4;
+      float ws[4] = {0, 0, 0, 0};
+      qs[0] = qs[1] = qs[2] = qs[3] = 0.0f;
+      for (int i = 0; i < DK; ++i) {
+        const float4 s4 = *reinterpret_cast<const float4*>(S + i * SC + jc);
+        const float w = co.W[t][i], q = Qs[t * (DK + 1) + i];
+        ws[0] = __fmaf_rn(w, s4.x, ws[0]); ws[1] = __fmaf_rn(w, s4.y, ws[1]);
+        ws[2] = __fmaf_rn(w, s4.z, ws[2]); ws[3] = __fmaf_rn(w, s4.w, ws[3]);
+        qs[0] = __fmaf_rn(q, s4.x, qs[0]); qs[1] = __fmaf_rn(q, s4.y, qs[1]);
+        qs[2] = __fmaf_rn(q, s4.z, qs[2]); qs[3] = __fmaf_rn(q, s4.w, qs[3]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) D[t * SC + jc + e] = t < tn ? co.U[t][j0 + jc + e] - ws[e] : 0.0f;
+    }
+    __syncthreads();
+    // O = diag(G) Q S0 + (M o Q K^T) D
+    {
+      const int t = tid / 4, jc = (tid % 4) * 4;
+      float acc[4];
+      const float gt = co.gam[t];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = gt * qs[e];
+      for (int s = 0; s <= t; ++s) {
+        const float m = co.QK[t][s];
+        const float4 d4 = *reinterpret_cast<const float4*>(D + s * SC + jc);
+        acc[0] = __fmaf_rn(m, d4.x, acc[0]); acc[1] = __fmaf_rn(m, d4.y, acc[1]);
+        acc[2] = __fmaf_rn(m, d4.z, acc[2]); acc[3] = __fmaf_rn(m, d4.w, acc[3]);
+      }
+      if (t < tn) *reinterpret_cast<float4*>(ob + size_t(t0 + t) * a.ldo + jc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    }
+    // S_C = G_C S0 + K^T diag(G_C / G) D ; thread -> (i, 8 columns)
+    __syncthreads();
+    {
+      const int i = tid / 2, jc = (tid % 2) * 8;
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = co.gC * S[i * SC + jc + e];
+      for (int t = 0; t < tn; ++t) {
+        const float kr = Ks[t * (DK + 1) + i] * co.rem[t];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(kr, D[t * SC + jc + e], acc[e]);
+      }
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < 8; ++e) S[i * SC + jc + e] = acc[e];
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < DK * SC; e += 256) Sg[size_t(e / SC) * a.dv + j0 + e % SC] = S[e];
+}
+
+}  // namespace
+
+size_t delta_chunk_workspace_bytes(int batch, int heads, int n) {
+  const int chunks = (n + CK - 1) / CK;
+  return size_t(batch) * heads * chunks * sizeof(ChunkOut);
+}
+
+void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  if (a.n <= 0 || batch <= 0) return;
+  if (a.dv != DK || a.value_heads % a.key_heads)
+    throw CudaError("delta_chunked: needs dk = dv = 128");
+  const int chunks = (a.n + CK - 1) / CK;
+  if (workspace_bytes < delta_chunk_workspace_bytes(batch, a.value_heads, a.n))
+    throw CudaError("delta_chunked: workspace too small");
+  ChunkOut* outs = static_cast<ChunkOut*>(workspace);
+  const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK) * sizeof(float);
+  const int scan_smem = (DK * SC + CK * SC + 2 * CK * (DK + 1)) * sizeof(float);
+  static bool configured = false;
+  if (!configured) {
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, scan_smem));
+    configured = true;
+  }
+  delta_chunk_prep_kernel<<<batch * a.value_heads * chunks, 256, prep_smem, s>>>(a, outs, chunks);
+  DG_CUDA(cudaGetLastError());
+  delta_chunk_scan_kernel<<<batch * a.value_heads * (a.dv / SC), 256, scan_smem, s>>>(a, outs, chunks);
+  DG_CUDA(cudaGetLastError());
+}
+
+}  // namespace dg

@@ -159,6 +159,7 @@ class Engine {
   DevBuf ids_, x_, n_, xq_, xs_, mid_, proj_, conv_, decay_, beta_, o_, ofin_, h_, qbuf_, att_;
   DevBuf hrows_, hnorm_, hq_, hk_, hlogits_, hrow_idx_;
   std::vector<DevBuf> kcache_, vcache_, state_;
+  DevBuf delta_ws_;  // chunked DeltaNet products (fast mode)
   DevBuf status_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
   DeviceStatus* status() const { return status_.as<DeviceStatus>(); }

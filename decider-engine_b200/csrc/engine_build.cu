@@ -238,6 +238,8 @@ void Engine::finalize() {
       state_[i] = DevBuf(size_t(c.value_heads) * c.dk * c.dv * 4);
     }
   }
+  if (c.dk == 128 && c.dv == 128)
+    delta_ws_ = DevBuf(delta_chunk_workspace_bytes(1, c.value_heads, M));
   constexpr int kMaxHeadRows = 512;
   hrow_idx_ = DevBuf(kMaxHeadRows * 4);
   hnorm_ = DevBuf(size_t(kMaxHeadRows) * H * 4);

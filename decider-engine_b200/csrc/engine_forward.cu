@@ -76,8 +76,32 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
     DG_CUDA(cudaMemcpyAsync(state_[i].ptr, past->state.ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
   else
     DG_CUDA(cudaMemsetAsync(state_[i].ptr, 0, sbytes, stream_));
-  launch_delta_recurrence(conv_.as<float>(), n, c.key_heads, c.dk, H, c.dv, decay_.as<float>(), beta_.as<float>(),
-                          state_[i].as<float>(), o_.as<float>(), stream_);
+  if (!exact && delta_ws_.ptr) {
+    // Fast mode: the chunked form (64-token chunks); its rounding depends on
+    // where chunks start, so prefix continuations match full passes to FP32
+    // rounding rather than bit for bit. Exact mode keeps the token recurrence.
+    DeltaArgs da{};
+    da.q = conv_.as<float>();
+    da.k = conv_.as<float>() + c.kd();
+    da.v = conv_.as<float>() + 2 * c.kd();
+    da.ld_qk = da.ld_v = W;
+    da.decay = decay_.as<float>();
+    da.beta = beta_.as<float>();
+    da.log_decay = 1;
+    da.ld_gb = H;
+    da.n = n;
+    da.key_heads = c.key_heads;
+    da.value_heads = H;
+    da.dv = c.dv;
+    da.state = state_[i].as<float>();
+    da.o = o_.as<float>();
+    da.ldo = H * c.dv;
+    launch_delta_chunked(da, 1, delta_ws_.ptr, delta_ws_.bytes, stream_);
+    note_launch();
+  } else {
+    launch_delta_recurrence(conv_.as<float>(), n, c.key_heads, c.dk, H, c.dv, decay_.as<float>(),
+                            beta_.as<float>(), state_[i].as<float>(), o_.as<float>(), stream_);
+  }
   const bool q = precision_ == kInt8Compute;
   launch_gated_norm_quant(o_.as<float>(), base + off[1], ldr, n, H, c.dv, L.norm.as<float>(), c.eps, ofin_.as<float>(),
                           xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);

@@ -208,13 +208,13 @@ __global__ void __launch_bounds__(384, 1)
             // Exact int32 -> float: bits of 1.5 * 2^23 + dot, minus 1.5 * 2^23.
             float2 fd = make_float2(__int_as_float(int32_t(d[j]) + 0x4B400000),
                                     __int_as_float(int32_t(d[j + 1]) + 0x4B400000));
-            fd = __fadd2_rn(fd, neg_magic);
-            const float2 sc = __fmul2_rn(xs2, e ? whi : wlo);
+            fd = add2_rn(fd, neg_magic);
+            const float2 sc = mul2_rn(xs2, e ? whi : wlo);
             float2& a2 = acc[(c * 16 + j) / 2];
             if (EXACT)
-              a2 = __fadd2_rn(a2, __fmul2_rn(fd, sc));
+              a2 = add2_rn(a2, mul2_rn(fd, sc));
             else
-              a2 = __ffma2_rn(fd, sc, a2);
+              a2 = fma2_rn(fd, sc, a2);
           }
         }
       }
@@ -274,14 +274,14 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int r = r4 * 4 + e;
-                  lanes[r & 7] = __fadd2_rn(lanes[r & 7], __fmul2_rn(make_float2(mid[r], mid[r]), wv[e]));
+                  lanes[r & 7] = add2_rn(lanes[r & 7], mul2_rn(make_float2(mid[r], mid[r]), wv[e]));
                 }
               }
               delta = make_float2(-0.0f, -0.0f);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) delta = __fadd2_rn(delta, lanes[i]);
-              delta = __fadd2_rn(delta, make_float2(0.0f, 0.0f));
-              const float2 scaled = __fmul2_rn(make_float2(p.lora_scale, p.lora_scale), delta);
+              for (int i = 0; i < 8; ++i) delta = add2_rn(delta, lanes[i]);
+              delta = add2_rn(delta, make_float2(0.0f, 0.0f));
+              const float2 scaled = mul2_rn(make_float2(p.lora_scale, p.lora_scale), delta);
               vals[j] = __fadd_rn(vals[j], scaled.x);
               vals[j + 1] = __fadd_rn(vals[j + 1], scaled.y);
             } else {
@@ -289,10 +289,10 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
               for (int r4 = 0; r4 < R / 4; ++r4) {
                 const float4 w0 = b0[r4], w1 = b1[r4];
-                delta = __ffma2_rn(make_float2(mid[r4 * 4], mid[r4 * 4]), make_float2(w0.x, w1.x), delta);
-                delta = __ffma2_rn(make_float2(mid[r4 * 4 + 1], mid[r4 * 4 + 1]), make_float2(w0.y, w1.y), delta);
-                delta = __ffma2_rn(make_float2(mid[r4 * 4 + 2], mid[r4 * 4 + 2]), make_float2(w0.z, w1.z), delta);
-                delta = __ffma2_rn(make_float2(mid[r4 * 4 + 3], mid[r4 * 4 + 3]), make_float2(w0.w, w1.w), delta);
+                delta = fma2_rn(make_float2(mid[r4 * 4], mid[r4 * 4]), make_float2(w0.x, w1.x), delta);
+                delta = fma2_rn(make_float2(mid[r4 * 4 + 1], mid[r4 * 4 + 1]), make_float2(w0.y, w1.y), delta);
+                delta = fma2_rn(make_float2(mid[r4 * 4 + 2], mid[r4 * 4 + 2]), make_float2(w0.z, w1.z), delta);
+                delta = fma2_rn(make_float2(mid[r4 * 4 + 3], mid[r4 * 4 + 3]), make_float2(w0.w, w1.w), delta);
               }
               vals[j] = __fmaf_rn(p.lora_scale, delta.x, vals[j]);
               vals[j + 1] = __fmaf_rn(p.lora_scale, delta.y, vals[j + 1]);

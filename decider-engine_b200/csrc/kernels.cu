@@ -184,6 +184,60 @@ __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x
   }
 }
 
+// LoRA A, fast mode (fused multiply-add, free summation order): one warp per
+// 4-row x 4-output tile, the 32 lanes striding K so loads stay coalesced and
+// plenty of chains are in flight; a butterfly reduction combines the lanes.
+__global__ void __launch_bounds__(256) lora_a_fast_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                          const float* __restrict__ A, int R, float* __restrict__ mid,
+                                                          int ldm) {
+  constexpr int TM = 4, TR = 4;
+  const long tile = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rtiles = (R + TR - 1) / TR;
+  const int m0 = int(tile / rtiles) * TM, r0 = int(tile % rtiles) * TR;
+  if (m0 >= M) return;  // whole warp leaves together
+  const float* xr[TM];
+  const float* ar[TR];
+#pragma unroll
+  for (int a = 0; a < TM; ++a) xr[a] = x + size_t(min(m0 + a, M - 1)) * ldx;
+#pragma unroll
+  for (int b = 0; b < TR; ++b) ar[b] = A + size_t(min(r0 + b, R - 1)) * K;
+  float acc[TM][TR];
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TR; ++b) acc[a][b] = 0.0f;
+#pragma unroll 4
+  for (int k = lane; k < K; k += 32) {
+    float xv[TM], av[TR];
+#pragma unroll
+    for (int a = 0; a < TM; ++a) xv[a] = __ldg(xr[a] + k);
+#pragma unroll
+    for (int b = 0; b < TR; ++b) av[b] = __ldg(ar[b] + k);
+#pragma unroll
+    for (int a = 0; a < TM; ++a)
+#pragma unroll
+      for (int b = 0; b < TR; ++b) acc[a][b] = __fmaf_rn(xv[a], av[b], acc[a][b]);
+  }
+#pragma unroll
+  for (int a = 0; a < TM; ++a)
+#pragma unroll
+    for (int b = 0; b < TR; ++b) {
+      float v = acc[a][b];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[a][b] = v;
+    }
+  if (lane < TM * TR) {
+    const int a = lane / TR, b = lane % TR, m = m0 + a, r = r0 + b;
+    float v = 0.0f;
+#pragma unroll
+    for (int o = 0; o < TM * TR; ++o)
+      if (o == lane) v = acc[o / TR][o % TR];
+    if (m < M && r < R) mid[size_t(m) * ldm + r] = v;
+  }
+}
+
 __device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale, int precision, int n, int k, int K) {
   const int G = (K + 63) / 64;
   const float sc = wscale[size_t(n) * G + k / 64];
@@ -292,10 +346,12 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
   if (M <= 0 || R <= 0) return;
   const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
-  if (exact)
+  if (exact) {
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
-  else
-    lora_a_kernel<false><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  } else {
+    const long warps = long((M + 3) / 4) * ((R + 3) / 4);
+    lora_a_fast_kernel<<<int((warps * 32 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  }
   DG_CUDA(cudaGetLastError());
 }
 

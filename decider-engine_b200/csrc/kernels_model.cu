@@ -50,7 +50,7 @@ __global__ void delta_prep_kernel(float* __restrict__ conv, int W, int key_heads
     for (int i = lane; i < dk; i += 32) x[i] = x[i] * norm;
   }
   for (int h = threadIdx.x; h < value_heads; h += blockDim.x) {
-    decay[size_t(t) * value_heads + h] = expf(rate[h] * softplus_f(a[size_t(t) * ldab + h] + dt[h]));
+    decay[size_t(t) * value_heads + h] = rate[h] * softplus_f(a[size_t(t) * ldab + h] + dt[h]);  // log of the decay
     beta[size_t(t) * value_heads + h] = sigmoid_f(b[size_t(t) * ldab + h]);
   }
 }
@@ -69,7 +69,7 @@ __global__ void delta_rec_generic_kernel(const float* __restrict__ conv, int n, 
     const float* q = conv + size_t(t) * W + kh * dk;
     const float* k = conv + size_t(t) * W + kd + kh * dk;
     const float v = conv[size_t(t) * W + 2 * kd + h * dv + j];
-    const float dec = decay[size_t(t) * value_heads + h], be = beta[size_t(t) * value_heads + h];
+    const float dec = expf(decay[size_t(t) * value_heads + h]), be = beta[size_t(t) * value_heads + h];
     float delta = 0.0f;
     for (int i = 0; i < dk; ++i) {
       const float s = S[size_t(i) * dv + j] * dec;
@@ -241,6 +241,7 @@ void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, in
     a.v = conv + 2 * key_heads * dk;
     a.ld_qk = a.ld_v = W;
     a.decay = decay;
+    a.log_decay = 1;
     a.beta = beta;
     a.ld_gb = value_heads;
     a.n = n;

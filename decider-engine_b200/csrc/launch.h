@@ -58,13 +58,13 @@ void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids,
 // tail of `tail_rows` raw rows that precede position `start`.
 void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W,
                       int kernel, const float* taps, float* out, cudaStream_t s);
-// Per token: q/k L2 norms (q also / sqrt(dk)), decay = exp(rate * softplus(a + dt)),
-// beta = sigmoid(b). Normalises conv[:, :2kd] in place.
+// Per token: q/k L2 norms (q also / sqrt(dk)), log decay g = rate * softplus(a + dt)
+// (the decay is exp(g)), beta = sigmoid(b). Normalises conv[:, :2kd] in place.
 void launch_delta_prep(float* conv, int W, int n, int key_heads, int dk, int value_heads, const float* a,
                        const float* b, int ldab, const float* decay_rate, const float* dt, float* decay,
                        float* beta, cudaStream_t s);
-// Gated delta rule over n tokens for every value head, state [H][dk][dv]
-// updated in place; o [n][H*dv] receives q^T S per token (before the norm).
+// Gated delta rule over n tokens for every value head (decay given as its log),
+// state [H][dk][dv] updated in place; o [n][H*dv] receives q^T S per token.
 void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, int value_heads, int dv,
                              const float* decay, const float* beta, float* state, float* o,
                              cudaStream_t s);
@@ -86,6 +86,10 @@ struct DeltaArgs {
   size_t bs_o;
 };
 void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s);
+// Chunked form (64-token chunks, dk = dv = 128) of the same rule; needs a
+// device workspace of delta_chunk_workspace_bytes(batch, heads, n).
+size_t delta_chunk_workspace_bytes(int batch, int heads, int n);
+void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s);
 void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
 // Split q|gate per head, centred RMSNorm of q and k, partial RoPE from the
 // precomputed table, append k/v to the cache at `start`.

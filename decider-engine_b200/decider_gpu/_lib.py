@@ -20,7 +20,7 @@ SYMBOLS = [
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_stream", "dg_linear_free",
-    "dg_gated_delta_rule_device",
+    "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
 ]
 
 
@@ -80,6 +80,9 @@ def load() -> C.CDLL:
     L.dg_linear_free.argtypes = [vp]
     L.dg_linear_free.restype = None
     L.dg_gated_delta_rule_device.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp]
+    L.dg_gated_delta_chunk_workspace_bytes.argtypes = [i32, i32, i32]
+    L.dg_gated_delta_chunk_workspace_bytes.restype = sz
+    L.dg_gated_delta_rule_chunked_device.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp]
     _lib = L
     return L
 

@@ -217,3 +217,14 @@ def gated_delta_rule(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads, stat
     dg_gated_delta_rule_device in include/decider_gpu.h."""
     check(load().dg_gated_delta_rule_device(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads, state_ptr,
                                             o_ptr, stream))
+
+
+def gated_delta_chunk_workspace_bytes(batch, t, heads) -> int:
+    return int(load().dg_gated_delta_chunk_workspace_bytes(batch, t, heads))
+
+
+def gated_delta_rule_chunked(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads, state_ptr, o_ptr, ws_ptr,
+                             ws_bytes, stream=0):
+    """Chunked form of `gated_delta_rule` with a caller-owned device workspace."""
+    check(load().dg_gated_delta_rule_chunked_device(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads,
+                                                    state_ptr, o_ptr, ws_ptr, ws_bytes, stream))

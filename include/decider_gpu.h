@@ -121,6 +121,14 @@ void dg_linear_free(dg_linear* l);
  * read as the initial state and left as the final one; o receives q^T S. */
 int dg_gated_delta_rule_device(const float* q, const float* k, const float* v, const float* g, const float* beta,
                                int batch, int t, int heads, float* state, float* o, void* stream);
+/* The same rule in its chunked form (64-token chunks: intra-chunk products in
+ * parallel, one sequential pass over chunks). `workspace` is a device buffer
+ * of at least dg_gated_delta_chunk_workspace_bytes(batch, t, heads) bytes,
+ * owned by the caller. */
+size_t dg_gated_delta_chunk_workspace_bytes(int batch, int t, int heads);
+int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const float* v, const float* g,
+                                       const float* beta, int batch, int t, int heads, float* state, float* o,
+                                       void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

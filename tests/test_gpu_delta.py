@@ -22,18 +22,26 @@ def _inputs(seed, b, t, h, d=128):
     return q, k, v, g, beta
 
 
+@pytest.mark.parametrize("chunked", [False, True])
 @pytest.mark.parametrize("b,t,h", [(1, 1, 1), (2, 70, 3), (3, 257, 2)])
-def test_gated_delta_rule_matches_oracle(oracle_mod, b, t, h):
+def test_gated_delta_rule_matches_oracle(oracle_mod, b, t, h, chunked):
     import torch
-    from decider_gpu import gated_delta_rule
+    from decider_gpu import gated_delta_chunk_workspace_bytes, gated_delta_rule, gated_delta_rule_chunked
     q, k, v, g, beta = _inputs(b * 1000 + t, b, t, h)
     rng = np.random.default_rng(1)
     s0 = (0.1 * rng.standard_normal((b, h, 128, 128))).astype(np.float32)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
     tq, tk, tv, tg, tb, ts = map(dev, (q, k, v, g, beta, s0))
     to = torch.zeros((b, t, h, 128), dtype=torch.float32, device="cuda")
-    gated_delta_rule(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), tg.data_ptr(), tb.data_ptr(), b, t, h,
-                     ts.data_ptr(), to.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    stream = torch.cuda.current_stream().cuda_stream
+    if chunked:
+        nbytes = gated_delta_chunk_workspace_bytes(b, t, h)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+        gated_delta_rule_chunked(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), tg.data_ptr(), tb.data_ptr(), b, t, h,
+                                 ts.data_ptr(), to.data_ptr(), ws.data_ptr(), nbytes, stream)
+    else:
+        gated_delta_rule(tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), tg.data_ptr(), tb.data_ptr(), b, t, h,
+                         ts.data_ptr(), to.data_ptr(), stream)
     torch.cuda.synchronize()
     o_gpu, s_gpu = to.cpu().numpy(), ts.cpu().numpy()
     for bi in range(b):
