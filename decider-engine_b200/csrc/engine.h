@@ -160,6 +160,7 @@ class Engine {
   DevBuf hrows_, hnorm_, hq_, hk_, hlogits_, hrow_idx_;
   std::vector<DevBuf> kcache_, vcache_, state_;
   DevBuf delta_ws_;  // chunked DeltaNet products (fast mode)
+  DevBuf lora_part_; // split-K LoRA-A partial sums (fast mode)
   DevBuf status_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
   DeviceStatus* status() const { return status_.as<DeviceStatus>(); }

@@ -240,6 +240,7 @@ void Engine::finalize() {
   }
   if (c.dk == 128 && c.dv == 128)
     delta_ws_ = DevBuf(delta_chunk_workspace_bytes(1, c.value_heads, M));
+  if (fast_) lora_part_ = DevBuf(lora_a_partial_floats(M) * 4);
   constexpr int kMaxHeadRows = 512;
   hrow_idx_ = DevBuf(kMaxHeadRows * 4);
   hnorm_ = DevBuf(size_t(kMaxHeadRows) * H * 4);

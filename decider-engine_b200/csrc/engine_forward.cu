@@ -133,7 +133,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   float* proj = proj_.as<float>();
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_);
+  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
   note_launch();
   note_launch();
   run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
@@ -167,18 +167,18 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     mixed_in = ofin_.as<float>();
     kin = c.vd();
   }
-  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_);
+  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
   note_launch();
   run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_);
+  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
   note_launch();
   note_launch();
   run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
   launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_);
+  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
   note_launch();
   note_launch();
   run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
@@ -310,12 +310,12 @@ void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* lo
   DG_CUDA(cudaMemcpyAsync(hrow_idx_.ptr, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, stream_));
   launch_head_norm(x_.as<float>(), H, hrow_idx_.as<int>(), n_pos + 1, head_norm_w_.as<float>(),
                    head_norm_b_.as<float>(), hnorm_.as<float>(), stream_);
-  launch_proj_generic(head_q_.g, hnorm_.as<float>(), H, nullptr, nullptr, 0, nullptr, 0, 1, hq_.as<float>(), P,
-                      kEpiWrite, stream_);
-  launch_proj_generic(head_k_.g, hnorm_.as<float>() + H, H, nullptr, nullptr, 0, nullptr, 0, n_pos, hk_.as<float>(), P,
-                      kEpiWrite, stream_);
-  launch_head_dot(hq_.as<float>(), hk_.as<float>(), n_pos, P, 1.0f / std::sqrt(float(P)), hlogits_.as<float>(),
-                  stream_);
+  // q = dot_scores(n, Wq[j]) (+ bq inside head_dot): the lane-ordered FP32
+  // dot of the LoRA-A kernel, with coalesced weight reads.
+  launch_lora_a(hnorm_.as<float>(), H, 1, H, head_q_.w_f32.as<float>(), P, hq_.as<float>(), P, true, stream_);
+  launch_lora_a(hnorm_.as<float>() + H, H, n_pos, H, head_k_.w_f32.as<float>(), P, hk_.as<float>(), P, true, stream_);
+  launch_head_dot(hq_.as<float>(), hk_.as<float>(), n_pos, P, 1.0f / std::sqrt(float(P)), head_q_.bias.as<float>(),
+                  head_k_.bias.as<float>(), hlogits_.as<float>(), stream_);
   for (int j = 0; j < 4; ++j) note_launch();
   DG_CUDA(cudaMemcpyAsync(logits_out, hlogits_.ptr, size_t(n_pos) * 4, cudaMemcpyDeviceToHost, stream_));
   DG_CUDA(cudaStreamSynchronize(stream_));

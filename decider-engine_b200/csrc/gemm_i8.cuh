@@ -208,13 +208,17 @@ __global__ void __launch_bounds__(384, 1)
             // Exact int32 -> float: bits of 1.5 * 2^23 + dot, minus 1.5 * 2^23.
             float2 fd = make_float2(__int_as_float(int32_t(d[j]) + 0x4B400000),
                                     __int_as_float(int32_t(d[j + 1]) + 0x4B400000));
-            fd = add2_rn(fd, neg_magic);
-            const float2 sc = mul2_rn(xs2, e ? whi : wlo);
             float2& a2 = acc[(c * 16 + j) / 2];
-            if (EXACT)
-              a2 = add2_rn(a2, mul2_rn(fd, sc));
-            else
-              a2 = fma2_rn(fd, sc, a2);
+            const float2 w2 = e ? whi : wlo;
+            if (EXACT) {
+              // Reference order with scalar IEEE operations (src/int8.rs:58):
+              // sum + float(dot) * (xs * ws), rounded after every step.
+              a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xsg, w2.x)));
+              a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xsg, w2.y)));
+            } else {
+              fd = add2_rn(fd, neg_magic);
+              a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
+            }
           }
         }
       }
@@ -274,16 +278,20 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int r = r4 * 4 + e;
-                  lanes[r & 7] = add2_rn(lanes[r & 7], mul2_rn(make_float2(mid[r], mid[r]), wv[e]));
+                  lanes[r & 7].x = __fadd_rn(lanes[r & 7].x, __fmul_rn(mid[r], wv[e].x));
+                  lanes[r & 7].y = __fadd_rn(lanes[r & 7].y, __fmul_rn(mid[r], wv[e].y));
                 }
               }
               delta = make_float2(-0.0f, -0.0f);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) delta = add2_rn(delta, lanes[i]);
-              delta = add2_rn(delta, make_float2(0.0f, 0.0f));
-              const float2 scaled = mul2_rn(make_float2(p.lora_scale, p.lora_scale), delta);
-              vals[j] = __fadd_rn(vals[j], scaled.x);
-              vals[j + 1] = __fadd_rn(vals[j + 1], scaled.y);
+              for (int i = 0; i < 8; ++i) {
+                delta.x = __fadd_rn(delta.x, lanes[i].x);
+                delta.y = __fadd_rn(delta.y, lanes[i].y);
+              }
+              delta.x = __fadd_rn(delta.x, 0.0f);
+              delta.y = __fadd_rn(delta.y, 0.0f);
+              vals[j] = __fadd_rn(vals[j], __fmul_rn(p.lora_scale, delta.x));
+              vals[j + 1] = __fadd_rn(vals[j + 1], __fmul_rn(p.lora_scale, delta.y));
             } else {
               delta = make_float2(0.0f, 0.0f);
 #pragma unroll

@@ -47,6 +47,78 @@ __device__ __forceinline__ void quantize_group_warp(const float* vals, int len, 
   if (l == 0) *scale_out = scale;
 }
 
+// Group-64 quantisation of the four values a lane holds; the 16 lanes of a
+// half-warp hold one 64-wide group (same formula as quantize_group_warp).
+__device__ __forceinline__ void quantize_vec4_halfwarp(float4 v, int8_t* q_out, float* scale_out, bool leader,
+                                                       bool* bad) {
+  float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  *bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+  const float scale = mx == 0.0f ? 1.0f : fmaxf(mx / 127.0f, FLT_MIN);
+  char4 q;
+  q.x = int8_t(fminf(fmaxf(roundf(v.x / scale), -127.0f), 127.0f));
+  q.y = int8_t(fminf(fmaxf(roundf(v.y / scale), -127.0f), 127.0f));
+  q.z = int8_t(fminf(fmaxf(roundf(v.z / scale), -127.0f), 127.0f));
+  q.w = int8_t(fminf(fmaxf(roundf(v.w / scale), -127.0f), 127.0f));
+  *reinterpret_cast<char4*>(q_out) = q;
+  if (leader) *scale_out = scale;
+}
+
+// Warp-per-row variant for K % 128 == 0: lane l holds float4 l + 32 i of the
+// row, so no shared memory or block barrier is needed. With gamma (NV float4
+// per lane kept in registers) the centred RMSNorm comes first.
+template <int NV>
+__global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                              const float* __restrict__ gamma, float eps,
+                                                              float* __restrict__ n_out, int ldn,
+                                                              int8_t* __restrict__ xq, float* __restrict__ xs,
+                                                              int ldxs, DeviceStatus* st) {
+  const int m = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (m >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + size_t(m) * ldx);
+  const int nv = K / 128;
+  bool bad = false;
+  if (NV > 0) {
+    float4 v[NV > 0 ? NV : 1];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      v[i] = xr[lane + 32 * i];
+      ss = __fmaf_rn(v[i].x, v[i].x, ss);
+      ss = __fmaf_rn(v[i].y, v[i].y, ss);
+      ss = __fmaf_rn(v[i].z, v[i].z, ss);
+      ss = __fmaf_rn(v[i].w, v[i].w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / float(K) + eps);
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float4 g = g4[lane + 32 * i];
+      v[i].x = v[i].x * (inv * (1.0f + g.x));
+      v[i].y = v[i].y * (inv * (1.0f + g.y));
+      v[i].z = v[i].z * (inv * (1.0f + g.z));
+      v[i].w = v[i].w * (inv * (1.0f + g.w));
+      if (n_out) reinterpret_cast<float4*>(n_out + size_t(m) * ldn)[lane + 32 * i] = v[i];
+      if (xq) {
+        const int col = 4 * (lane + 32 * i);
+        quantize_vec4_halfwarp(v[i], xq + size_t(m) * K + col, xs + size_t(col / 64) * ldxs + m, (lane & 15) == 0,
+                               &bad);
+      }
+    }
+  } else {
+    for (int i = 0; i < nv; ++i) {
+      const float4 v = xr[lane + 32 * i];
+      if (n_out) reinterpret_cast<float4*>(n_out + size_t(m) * ldn)[lane + 32 * i] = v;
+      const int col = 4 * (lane + 32 * i);
+      quantize_vec4_halfwarp(v, xq + size_t(m) * K + col, xs + size_t(col / 64) * ldxs + m, (lane & 15) == 0, &bad);
+    }
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0) report(st, kNonFinite, 1);
+}
+
 // One 256-thread CTA per row.
 __global__ void norm_quant_kernel(const float* __restrict__ x, int ldx, int K, const float* __restrict__ gamma,
                                   float eps, float* __restrict__ n_out, int ldn, int8_t* __restrict__ xq,
@@ -238,6 +310,71 @@ __global__ void __launch_bounds__(256) lora_a_fast_kernel(const float* __restric
   }
 }
 
+// LoRA A, fast mode, split over K so a skinny [M x R] output still fills the
+// GPU: CTA (64 rows x 64 outputs x one K slice) through shared-memory tiles,
+// 4 x 4 outputs per thread; partial sums go to partial[slice][m][r] and
+// lora_a_reduce_kernel adds the slices in a fixed order (deterministic).
+__global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                            const float* __restrict__ A, int R,
+                                                            float* __restrict__ partial, int kslice) {
+  __shared__ float xs_[64][33];
+  __shared__ float as_[64][33];
+  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
+  const int m_base = blockIdx.x * 64, r_base = blockIdx.y * 64;
+  const int k0 = blockIdx.z * kslice, k1 = min(K, k0 + kslice);
+  float acc[4][4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+  for (int kc = k0; kc < k1; kc += 32) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int i = tid + u * 256, row = i / 8, kk = (i % 8) * 4;
+      const int m = m_base + row, r = r_base + row, k = kc + kk;
+      float4 xv = make_float4(0, 0, 0, 0), av = xv;
+      if (m < M && k < k1) xv = __ldg(reinterpret_cast<const float4*>(x + size_t(m) * ldx + k));
+      if (r < R && k < k1) av = __ldg(reinterpret_cast<const float4*>(A + size_t(r) * K + k));
+      xs_[row][kk] = xv.x; xs_[row][kk + 1] = xv.y; xs_[row][kk + 2] = xv.z; xs_[row][kk + 3] = xv.w;
+      as_[row][kk] = av.x; as_[row][kk + 1] = av.y; as_[row][kk + 2] = av.z; as_[row][kk + 3] = av.w;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      float xv[4], av[4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) xv[a] = xs_[ty * 4 + a][kk];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) av[b] = as_[tx * 4 + b][kk];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(xv[a], av[b], acc[a][b]);
+    }
+    __syncthreads();
+  }
+  float* out = partial + size_t(blockIdx.z) * M * R;
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int m = m_base + ty * 4 + a;
+    if (m >= M) continue;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int r = r_base + tx * 4 + b;
+      if (r < R) out[size_t(m) * R + r] = acc[a][b];
+    }
+  }
+}
+
+__global__ void lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M, int R,
+                                     float* __restrict__ mid, int ldm) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M * R) return;
+  float s = 0.0f;
+  for (int z = 0; z < slices; ++z) s += partial[size_t(z) * M * R + i];
+  mid[size_t(i / R) * ldm + i % R] = s;
+}
+
 __device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale, int precision, int n, int k, int K) {
   const int G = (K + 63) / 64;
   const float sc = wscale[size_t(n) * G + k / 64];
@@ -328,7 +465,16 @@ void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma
                        int8_t* xq, float* xs, int ldxs, DeviceStatus* st, cudaStream_t s) {
   if (M <= 0) return;
   if (K > 12288) throw CudaError("norm_quant: row too wide");
-  norm_quant_kernel<<<M, 256, K * sizeof(float), s>>>(x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+  const bool aligned = K % 128 == 0 && ldx % 4 == 0 && (!n_out || ldn % 4 == 0) &&
+                       reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  const int blocks = (M + 7) / 8;
+  if (aligned && !gamma && xq) {
+    norm_quant_warp_kernel<0><<<blocks, 256, 0, s>>>(x, ldx, M, K, nullptr, eps, n_out, ldn, xq, xs, ldxs, st);
+  } else if (aligned && gamma && K == 2048) {
+    norm_quant_warp_kernel<16><<<blocks, 256, 0, s>>>(x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+  } else {
+    norm_quant_kernel<<<M, 256, K * sizeof(float), s>>>(x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+  }
   DG_CUDA(cudaGetLastError());
 }
 
@@ -342,12 +488,22 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 }
 
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
-                   cudaStream_t s) {
+                   cudaStream_t s, float* partial, size_t partial_floats) {
   if (M <= 0 || R <= 0) return;
   const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
   if (exact) {
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  } else if (partial && K % 128 == 0 && ldx % 4 == 0) {
+    const int tiles = ((M + 63) / 64) * ((R + 63) / 64);
+    const int slices = std::max(1, std::min(K / 128, (148 + tiles - 1) / tiles));
+    const int kslice = ((K + slices - 1) / slices + 31) / 32 * 32;
+    const int used = (K + kslice - 1) / kslice;
+    if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
+    lora_a_splitk_kernel<<<dim3((M + 63) / 64, (R + 63) / 64, used), 256, 0, s>>>(x, ldx, M, K, A, R, partial,
+                                                                                  kslice);
+    DG_CUDA(cudaGetLastError());
+    lora_a_reduce_kernel<<<(M * R + 255) / 256, 256, 0, s>>>(partial, used, M, R, mid, ldm);
   } else {
     const long warps = long((M + 3) / 4) * ((R + 3) / 4);
     lora_a_fast_kernel<<<int((warps * 32 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);

@@ -293,18 +293,22 @@ __global__ void head_norm_kernel(const float* __restrict__ hidden, int K, const 
     out[size_t(blockIdx.x) * K + k] = (x[k] - mean) * inv * w[k] + b[k];
 }
 
-// logits[i] = dot_scores(q, k_i) * scale (src/lib.rs:128).
+// logits[i] = dot_scores(q + bq, k_i + bk) * scale (src/lib.rs:120-128: the
+// head projections add their bias to the dot, then the query-key dot).
 __global__ void head_dot_kernel(const float* __restrict__ q, const float* __restrict__ k, int n_keys, int dim,
-                                float scale, float* __restrict__ logits) {
+                                float scale, const float* __restrict__ bq, const float* __restrict__ bk,
+                                float* __restrict__ logits) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n_keys) return;
   const float* kr = k + size_t(i) * dim;
+  auto qv = [&](int j) { return bq ? q[j] + bq[j] : q[j]; };
+  auto kv = [&](int j) { return bk ? kr[j] + bk[j] : kr[j]; };
   float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const int full = (dim / 8) * 8;
-  for (int j = 0; j < full; ++j) lanes[j & 7] = lanes[j & 7] + q[j] * kr[j];
+  for (int j = 0; j < full; ++j) lanes[j & 7] = lanes[j & 7] + qv(j) * kv(j);
   float s = -0.0f;
   for (int l = 0; l < 8; ++l) s = s + lanes[l];
-  for (int j = full; j < dim; ++j) s = s + q[j] * kr[j];
+  for (int j = full; j < dim; ++j) s = s + qv(j) * kv(j);
   logits[i] = s * scale;
 }
 
@@ -352,10 +356,10 @@ void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, c
   DG_CUDA(cudaGetLastError());
 }
 
-void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, float* logits,
-                     cudaStream_t s) {
+void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, const float* bq,
+                     const float* bk, float* logits, cudaStream_t s) {
   if (n_keys <= 0) return;
-  head_dot_kernel<<<(n_keys + 127) / 128, 128, 0, s>>>(q, k, n_keys, dim, scale, logits);
+  head_dot_kernel<<<(n_keys + 127) / 128, 128, 0, s>>>(q, k, n_keys, dim, scale, bq, bk, logits);
   DG_CUDA(cudaGetLastError());
 }
 

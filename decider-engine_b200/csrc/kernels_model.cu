@@ -15,17 +15,39 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 // convolve, src/qwen.rs:712-756: per channel, taps in order from a zero sum,
 // skipping taps before the sequence start, then SiLU.
+// One thread per channel and 16 consecutive tokens: the window of raw inputs
+// (16 + kernel - 1 rows) is loaded once and every tap reuses it.
+constexpr int CONV_T = 16, CONV_KMAX = 8;
 __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldr, const float* __restrict__ tail, int tail_rows,
-                                 int start, int W, int kernel, const float* __restrict__ taps, float* __restrict__ out) {
-  const int t = blockIdx.x, position = start + t;
-  for (int c = threadIdx.x; c < W; c += blockDim.x) {
+                                 int n, int start, int W, int kernel, const float* __restrict__ taps,
+                                 float* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, t0 = blockIdx.y * CONV_T;
+  if (c >= W) return;
+  float w[CONV_KMAX];
+  float win[CONV_T + CONV_KMAX - 1];
+#pragma unroll
+  for (int j = 0; j < CONV_KMAX; ++j) w[j] = j < kernel ? taps[size_t(j) * W + c] : 0.0f;
+  // win[i] holds the input at absolute position start + t0 - (kernel - 1) + i.
+#pragma unroll
+  for (int i = 0; i < CONV_T + CONV_KMAX - 1; ++i) {
+    const int source = start + t0 - (kernel - 1) + i;  // absolute position
+    float v = 0.0f;
+    if (i < CONV_T + kernel - 1 && source >= 0 && source < start + n) {
+      v = source >= start ? raw[size_t(source - start) * ldr + c] : tail[size_t(source + tail_rows - start) * W + c];
+    }
+    win[i] = v;
+  }
+#pragma unroll
+  for (int tt = 0; tt < CONV_T; ++tt) {
+    const int t = t0 + tt;
+    if (t >= n) break;
+    const int position = start + t;
     float sum = 0.0f;
-    for (int j = 0; j < kernel; ++j) {
-      if (position + j + 1 < kernel) continue;
-      const int source = position + j + 1 - kernel;
-      const float in = source >= start ? raw[size_t(source - start) * ldr + c]
-                                       : tail[size_t(source + tail_rows - start) * W + c];
-      sum = sum + in * taps[size_t(j) * W + c];
+#pragma unroll
+    for (int j = 0; j < CONV_KMAX; ++j) {
+      if (j >= kernel || position + j + 1 < kernel) continue;
+      // source = position + j + 1 - kernel  ->  window index tt + j
+      sum = sum + win[tt + j] * w[j];
     }
     out[size_t(t) * W + c] = silu_f(sum);
   }
@@ -218,7 +240,9 @@ __global__ void exp_kernel(const float* __restrict__ g, float* __restrict__ out,
 void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W, int kernel,
                       const float* taps, float* out, cudaStream_t s) {
   if (n <= 0) return;
-  conv_silu_kernel<<<n, 256, 0, s>>>(raw, ldr, tail, tail_rows, start, W, kernel, taps, out);
+  if (kernel < 1 || kernel > CONV_KMAX) throw CudaError("conv: kernel width must be 1..8");
+  dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T);
+  conv_silu_kernel<<<grid, 256, 0, s>>>(raw, ldr, tail, tail_rows, n, start, W, kernel, taps, out);
   DG_CUDA(cudaGetLastError());
 }
 

@@ -35,8 +35,11 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
                              const float* w, float eps, float* out, int8_t* xq, float* xs, int ldxs,
                              bool quantize, DeviceStatus* st, cudaStream_t s);
 // mid[m][r] = dot_scores(x[m], A[r]) for r < R (reference lane order when exact).
+// Fast mode with `partial` (lora_a_partial_floats(M) floats) splits K over
+// CTAs and reduces the slices in a fixed order.
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
-                   bool exact, cudaStream_t s);
+                   bool exact, cudaStream_t s, float* partial = nullptr, size_t partial_floats = 0);
+inline size_t lora_a_partial_floats(int max_rows) { return (size_t(148 * 64) + size_t(max_rows)) * 128; }
 // Generic SIMT projection for any shape and precision (reference order):
 // precision 0: w f32; 1: int8 weight-only; 2: int8-compute; 3: int4.
 struct GenericProj {
@@ -105,8 +108,8 @@ void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, De
 // Pointer-head LayerNorm (eps 1e-5, weight and bias) of selected rows.
 void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, const float* w, const float* b,
                       float* out, cudaStream_t s);
-// logits[i] = dot_scores(q, k_i) * scale.
-void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, float* logits,
-                     cudaStream_t s);
+// logits[i] = dot_scores(q + bq, k_i + bk) * scale (biases nullable).
+void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, const float* bq,
+                     const float* bk, float* logits, cudaStream_t s);
 
 }  // namespace dg
