@@ -102,54 +102,111 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
     bt[tb] = b1;
   }
   __syncthreads();
-  // L (strictly lower) and the masked Q K^T (lower incl. diagonal).
-  for (int e = tid; e < CK * CK; e += 256) {
-    const int t = e / CK, s = e % CK;
-    float kk = 0.0f, qk = 0.0f;
-    if (s <= t && t < tn) {
-      const float* kt = Ks + t * (DK + 1);
-      const float* ks = Ks + s * (DK + 1);
-      const float* qt = Qs + t * (DK + 1);
-#pragma unroll 8
+  // K K^T and Q K^T over the lower triangle, a 4 x 4 block of (t, s) per
+  // thread: L (strictly lower, scaled by b_t G_t/G_s) and the masked Q K^T.
+  {
+    const int bt4 = (tid / 16) * 4, bs4 = (tid % 16) * 4;
+    if (bs4 <= bt4 + 3) {
+      float kk[4][4], qk[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) kk[a][b] = qk[a][b] = 0.0f;
+#pragma unroll 4
       for (int d = 0; d < DK; ++d) {
-        kk = __fmaf_rn(kt[d], ks[d], kk);
-        qk = __fmaf_rn(qt[d], ks[d], qk);
+        float kt[4], qt[4], ks[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+          kt[a] = Ks[(bt4 + a) * (DK + 1) + d];
+          qt[a] = Qs[(bt4 + a) * (DK + 1) + d];
+          ks[a] = Ks[(bs4 + a) * (DK + 1) + d];
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            kk[a][b] = __fmaf_rn(kt[a], ks[b], kk[a][b]);
+            qk[a][b] = __fmaf_rn(qt[a], ks[b], qk[a][b]);
+          }
       }
-      const float ratio = expf(lg[t] - lg[s]);
-      qk *= ratio;
-      kk = s < t ? bt[t] * ratio * kk : 0.0f;
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int t = bt4 + a, s = bs4 + b;
+          float l = 0.0f, q = 0.0f;
+          if (s <= t && t < tn) {
+            const float ratio = expf(lg[t] - lg[s]);
+            q = qk[a][b] * ratio;
+            l = s < t ? bt[t] * ratio * kk[a][b] : 0.0f;
+          }
+          L[t * (CK + 1) + s] = l;
+          o.QK[t][s] = q;
+        }
     } else {
-      kk = 0.0f;
-      qk = 0.0f;
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          L[(bt4 + a) * (CK + 1) + bs4 + b] = 0.0f;
+          o.QK[bt4 + a][bs4 + b] = 0.0f;
+        }
     }
-    L[t * (CK + 1) + s] = kk;
-    o.QK[t][s] = qk;
   }
   __syncthreads();
-  // T = (I + L)^-1 by forward substitution, one row per step:
+  // T = (I + L)^-1 by forward substitution in one warp (rows in order, each
+  // lane owning columns lane and lane + 32):
   // T[t][s] = -sum_{u=s}^{t-1} L[t][u] T[u][s] (s < t), T[t][t] = 1.
-  for (int i = tid; i < CK * CK; i += 256) T[(i / CK) * (CK + 1) + i % CK] = (i / CK == i % CK) ? 1.0f : 0.0f;
-  __syncthreads();
-  for (int t = 1; t < CK; ++t) {
-    if (tid < t) {
-      const int s = tid;
-      float acc = 0.0f;
-      for (int u = s; u < t; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
-      T[t * (CK + 1) + s] = -acc;
+  if (tid < 32) {
+    for (int t = 0; t < CK; ++t) {
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int s = tid + 32 * h2;
+        float acc = 0.0f;
+        for (int u = s; u < t; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
+        T[t * (CK + 1) + s] = s < t ? -acc : (s == t ? 1.0f : 0.0f);
+      }
+      __syncwarp();
     }
-    __syncthreads();
   }
-  // U = T diag(b) V and W = T diag(b G) K, row t over s <= t.
-  for (int e = tid; e < CK * DK; e += 256) {
-    const int t = e / DK, d = e % DK;
-    float u = 0.0f, w = 0.0f;
-    for (int s = 0; s <= t; ++s) {
-      const float tb = T[t * (CK + 1) + s] * bt[s];
-      u = __fmaf_rn(tb, Vs[s * (DK + 1) + d], u);
-      w = __fmaf_rn(tb * gm[s], Ks[s * (DK + 1) + d], w);
+  __syncthreads();
+  // U = T diag(b) V and W = T diag(b G) K: a 4-row x 8-column block per thread.
+  {
+    const int t4 = (tid / 16) * 4, d8 = (tid % 16) * 8;
+    float u[4][8], w[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) u[a][e] = w[a][e] = 0.0f;
+    for (int s = 0; s <= t4 + 3; ++s) {
+      float tb[4], tg[4], vv[8], kv[8];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        tb[a] = T[(t4 + a) * (CK + 1) + s] * bt[s];  // zero above the diagonal
+        tg[a] = tb[a] * gm[s];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        vv[e] = Vs[s * (DK + 1) + d8 + e];
+        kv[e] = Ks[s * (DK + 1) + d8 + e];
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          u[a][e] = __fmaf_rn(tb[a], vv[e], u[a][e]);
+          w[a][e] = __fmaf_rn(tg[a], kv[e], w[a][e]);
+        }
     }
-    o.U[t][d] = u;
-    o.W[t][d] = w;
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      float4* uo = reinterpret_cast<float4*>(&o.U[t4 + a][d8]);
+      float4* wo = reinterpret_cast<float4*>(&o.W[t4 + a][d8]);
+      uo[0] = make_float4(u[a][0], u[a][1], u[a][2], u[a][3]);
+      uo[1] = make_float4(u[a][4], u[a][5], u[a][6], u[a][7]);
+      wo[0] = make_float4(w[a][0], w[a][1], w[a][2], w[a][3]);
+      wo[1] = make_float4(w[a][4], w[a][5], w[a][6], w[a][7]);
+    }
   }
   if (tid < CK) {
     const float last = lg[max(tn - 1, 0)];
@@ -160,14 +217,21 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
 }
 
 // Sequential pass over the chunks for one sequence, head and 16 value
-// columns; the state slice S[128][16] lives in shared memory.
+// columns; the state slice S[128][16] stays in shared memory and each chunk's
+// W, Q, K, masked Q K^T and U slice are staged there before use.
+constexpr int SCAN_LD = DK + 4;  // padded row stride, keeps float4 alignment
 __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
                                                                int chunks) {
   extern __shared__ __align__(16) float sm[];
-  float* S = sm;                    // [DK][SC]
-  float* D = S + DK * SC;           // [CK][SC]
-  float* Ks = D + CK * SC;          // [CK][DK + 1]
-  float* Qs = Ks + CK * (DK + 1);   // [CK][DK + 1]
+  float* S = sm;                      // [DK][SC]
+  float* D = S + DK * SC;             // [CK][SC]
+  float* Ws = D + CK * SC;            // [CK][SCAN_LD]
+  float* Qs = Ws + CK * SCAN_LD;      // [CK][SCAN_LD]
+  float* Ks = Qs + CK * SCAN_LD;      // [CK][SCAN_LD]
+  float* QKs = Ks + CK * SCAN_LD;     // [CK][CK + 4]
+  float* Us = QKs + CK * (CK + 4);    // [CK][SC]
+  float* rem = Us + CK * SC;          // [CK]
+  float* gam = rem + CK;              // [CK]
   const int tid = threadIdx.x;
   const int groups = a.dv / SC;
   const int slice = blockIdx.x % groups, h = (blockIdx.x / groups) % a.value_heads;
@@ -181,6 +245,7 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
   for (int c = 0; c < chunks; ++c) {
     const ChunkOut& co = outs[(bi * a.value_heads + h) * chunks + c];
     const int t0 = c * CK, tn = min(CK, a.n - t0);
+    // Stage the chunk: 4 x [64][128] + [64][64] floats, float4 at a time.
     for (int i = tid; i < CK * (DK / 4); i += 256) {
       const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
       float4 q4 = make_float4(0, 0, 0, 0), k4 = q4;
@@ -188,60 +253,77 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
         q4 = *reinterpret_cast<const float4*>(qb + size_t(t0 + t) * a.ld_qk + d);
         k4 = *reinterpret_cast<const float4*>(kb + size_t(t0 + t) * a.ld_qk + d);
       }
-      float* qd = Qs + t * (DK + 1) + d;
-      float* kd = Ks + t * (DK + 1) + d;
-      qd[0] = q4.x; qd[1] = q4.y; qd[2] = q4.z; qd[3] = q4.w;
-      kd[0] = k4.x; kd[1] = k4.y; kd[2] = k4.z; kd[3] = k4.w;
+      *reinterpret_cast<float4*>(Qs + t * SCAN_LD + d) = q4;
+      *reinterpret_cast<float4*>(Ks + t * SCAN_LD + d) = k4;
+      *reinterpret_cast<float4*>(Ws + t * SCAN_LD + d) = *reinterpret_cast<const float4*>(&co.W[t][d]);
     }
+    for (int i = tid; i < CK * (CK / 4); i += 256) {
+      const int t = i / (CK / 4), s4 = (i % (CK / 4)) * 4;
+      *reinterpret_cast<float4*>(QKs + t * (CK + 4) + s4) = *reinterpret_cast<const float4*>(&co.QK[t][s4]);
+    }
+    for (int i = tid; i < CK * (SC / 4); i += 256) {
+      const int t = i / (SC / 4), j4 = (i % (SC / 4)) * 4;
+      *reinterpret_cast<float4*>(Us + t * SC + j4) = *reinterpret_cast<const float4*>(&co.U[t][j0 + j4]);
+    }
+    if (tid < CK) {
+      rem[tid] = co.rem[tid];
+      gam[tid] = co.gam[tid];
+    }
+    const float gC = co.gC;
     __syncthreads();
-    // D = U - W S0 ; thread -> (t, 4 columns)
-    float qs[4];
+    // D = U - W S0 and Y = Q S0 ; thread -> (t, 4 columns)
+    const int t = tid / 4, jc = (tid % 4) * 4;
+    float qs[4] = {0, 0, 0, 0}, ws[4] = {0, 0, 0, 0};
+#pragma unroll 4
+    for (int i = 0; i < DK; ++i) {
+      const float4 s4 = *reinterpret_cast<const float4*>(S + i * SC + jc);
+      const float w = Ws[t * SCAN_LD + i], q = Qs[t * SCAN_LD + i];
+      ws[0] = __fmaf_rn(w, s4.x, ws[0]); ws[1] = __fmaf_rn(w, s4.y, ws[1]);
+      ws[2] = __fmaf_rn(w, s4.z, ws[2]); ws[3] = __fmaf_rn(w, s4.w, ws[3]);
+      qs[0] = __fmaf_rn(q, s4.x, qs[0]); qs[1] = __fmaf_rn(q, s4.y, qs[1]);
+      qs[2] = __fmaf_rn(q, s4.z, qs[2]); qs[3] = __fmaf_rn(q, s4.w, qs[3]);
+    }
     {
-      const int t = tid / 4, jc = (tid % 4) * 4;
-      float ws[4] = {0, 0, 0, 0};
-      qs[0] = qs[1] = qs[2] = qs[3] = 0.0f;
-      for (int i = 0; i < DK; ++i) {
-        const float4 s4 = *reinterpret_cast<const float4*>(S + i * SC + jc);
-        const float w = co.W[t][i], q = Qs[t * (DK + 1) + i];
-        ws[0] = __fmaf_rn(w, s4.x, ws[0]); ws[1] = __fmaf_rn(w, s4.y, ws[1]);
-        ws[2] = __fmaf_rn(w, s4.z, ws[2]); ws[3] = __fmaf_rn(w, s4.w, ws[3]);
-        qs[0] = __fmaf_rn(q, s4.x, qs[0]); qs[1] = __fmaf_rn(q, s4.y, qs[1]);
-        qs[2] = __fmaf_rn(q, s4.z, qs[2]); qs[3] = __fmaf_rn(q, s4.w, qs[3]);
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) D[t * SC + jc + e] = t < tn ? co.U[t][j0 + jc + e] - ws[e] : 0.0f;
+      const float4 u4 = *reinterpret_cast<const float4*>(Us + t * SC + jc);
+      const bool live = t < tn;
+      *reinterpret_cast<float4*>(D + t * SC + jc) =
+          make_float4(live ? u4.x - ws[0] : 0.0f, live ? u4.y - ws[1] : 0.0f, live ? u4.z - ws[2] : 0.0f,
+                      live ? u4.w - ws[3] : 0.0f);
     }
     __syncthreads();
     // O = diag(G) Q S0 + (M o Q K^T) D
     {
-      const int t = tid / 4, jc = (tid % 4) * 4;
       float acc[4];
-      const float gt = co.gam[t];
+      const float gt = gam[t];
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[e] = gt * qs[e];
       for (int s = 0; s <= t; ++s) {
-        const float m = co.QK[t][s];
+        const float m = QKs[t * (CK + 4) + s];
         const float4 d4 = *reinterpret_cast<const float4*>(D + s * SC + jc);
         acc[0] = __fmaf_rn(m, d4.x, acc[0]); acc[1] = __fmaf_rn(m, d4.y, acc[1]);
         acc[2] = __fmaf_rn(m, d4.z, acc[2]); acc[3] = __fmaf_rn(m, d4.w, acc[3]);
       }
-      if (t < tn) *reinterpret_cast<float4*>(ob + size_t(t0 + t) * a.ldo + jc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      if (t < tn)
+        *reinterpret_cast<float4*>(ob + size_t(t0 + t) * a.ldo + jc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     }
     // S_C = G_C S0 + K^T diag(G_C / G) D ; thread -> (i, 8 columns)
-    __syncthreads();
     {
-      const int i = tid / 2, jc = (tid % 2) * 8;
+      const int i = tid / 2, j8 = (tid % 2) * 8;
       float acc[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = co.gC * S[i * SC + jc + e];
-      for (int t = 0; t < tn; ++t) {
-        const float kr = Ks[t * (DK + 1) + i] * co.rem[t];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(kr, D[t * SC + jc + e], acc[e]);
+      for (int e = 0; e < 8; ++e) acc[e] = gC * S[i * SC + j8 + e];
+      for (int s = 0; s < tn; ++s) {
+        const float kr = Ks[s * SCAN_LD + i] * rem[s];
+        const float4 d0 = *reinterpret_cast<const float4*>(D + s * SC + j8);
+        const float4 d1 = *reinterpret_cast<const float4*>(D + s * SC + j8 + 4);
+        acc[0] = __fmaf_rn(kr, d0.x, acc[0]); acc[1] = __fmaf_rn(kr, d0.y, acc[1]);
+        acc[2] = __fmaf_rn(kr, d0.z, acc[2]); acc[3] = __fmaf_rn(kr, d0.w, acc[3]);
+        acc[4] = __fmaf_rn(kr, d1.x, acc[4]); acc[5] = __fmaf_rn(kr, d1.y, acc[5]);
+        acc[6] = __fmaf_rn(kr, d1.z, acc[6]); acc[7] = __fmaf_rn(kr, d1.w, acc[7]);
       }
-      __syncthreads();
+      __syncthreads();  // every thread has read the old S
 #pragma unroll
-      for (int e = 0; e < 8; ++e) S[i * SC + jc + e] = acc[e];
+      for (int e = 0; e < 8; ++e) S[i * SC + j8 + e] = acc[e];
     }
     __syncthreads();
   }
@@ -262,9 +344,11 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   const int chunks = (a.n + CK - 1) / CK;
   if (workspace_bytes < delta_chunk_workspace_bytes(batch, a.value_heads, a.n))
     throw CudaError("delta_chunked: workspace too small");
+  if (a.ld_qk % 4 || a.ld_v % 4) throw CudaError("delta_chunked: rows must be 16-byte aligned");
   ChunkOut* outs = static_cast<ChunkOut*>(workspace);
   const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK) * sizeof(float);
-  const int scan_smem = (DK * SC + CK * SC + 2 * CK * (DK + 1)) * sizeof(float);
+  const int scan_smem =
+      (DK * SC + CK * SC + 3 * CK * SCAN_LD + CK * (CK + 4) + CK * SC + 2 * CK) * sizeof(float);
   static bool configured = false;
   if (!configured) {
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));

@@ -20,8 +20,8 @@ static DevBuf upload(const std::vector<T>& v) {
 // Projections that read the same input, concatenated along the output for one
 // tcgen05 launch. Each part starts on a 32-column chunk (its LoRA block is
 // chosen per chunk); the total is padded to the 256-column tile with zero
-// weights. `interleave_mlp` places gate/up so every 128-column half-tile holds
-// 64 gate columns followed by the 64 matching up columns (SwiGLU epilogue).
+// weights. `interleave_mlp` places gate/up so every 64-column quarter-tile holds
+// 32 gate columns followed by the 32 matching up columns (SwiGLU epilogue).
 DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vector<int>& outs, int in,
                             bool interleave_mlp) {
   const int P = int(keys.size()), R = c_.rank, G = in / 64;
@@ -55,8 +55,10 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
     for (int j = 0; j < outs[p]; ++j) {
       int r;
       if (interleave_mlp) {
-        const int t = j / 128, w2 = j % 128;
-        r = w2 < 64 ? t * 256 + p * 64 + w2 : t * 256 + 128 + p * 64 + (w2 - 64);
+        // Each 64-column quarter of a 256-column tile (one promotion warp's
+        // slice) holds 32 gate columns then the 32 matching up columns.
+        const int t = j / 128, w2 = j % 128, s = w2 / 32;
+        r = t * 256 + s * 64 + p * 32 + (w2 % 32);
       } else {
         r = off[p] + j;
       }

@@ -7,14 +7,15 @@
 //                   + lora_scale * (dot_scores(mid[m, pid(n)], lora_b[n]) + 0.0) )
 //
 // One CTA owns a 128 x BN output tile (BN = 256, or 64 for narrow outputs so
-// more SMs share the work); 12 warps (3 warpgroups):
+// more SMs share the work); 20 warps (5 warpgroups):
 //   warp 0      TMA producer: int8 A/B tiles (128-byte swizzle) plus the two
 //               groups' activation and weight scales, multi-stage ring;
 //   warp 1      TMEM allocator and single-thread MMA issuer: per 64-wide K group,
 //               two tcgen05.mma kind::i8 (K=32) into a fresh int32 accumulator,
 //               double-buffered in TMEM (2 x BN columns);
 //   warps 2-3   no role (the block is sized in whole warpgroups);
-//   warps 4-11  promotion/epilogue: per group, tcgen05.ld the exact int32 dots and
+//   warps 4-19  promotion/epilogue, four per TMEM lane quarter, each owning a
+//               quarter of the tile's columns: per group, tcgen05.ld the exact int32 dots and
 //               scale them in FP32 in group order with packed f32x2 arithmetic
 //               (each lane op IEEE-rounded: reference order when EXACT, fused
 //               multiply-add otherwise). After the last group the FP32 sums move
@@ -51,9 +52,9 @@ struct GemmShape {
   static constexpr int STAGE_BYTES = (XS_OFF + 2 * BM * 4 + 1023) / 1024 * 1024;
   static constexpr int STAGES = BN == 256 ? 3 : 6;
   static constexpr int LORA_OFF = STAGES * STAGE_BYTES;
-  static constexpr int NUM_THREADS = 384;
-  static constexpr int EPI_WARP0 = 4, EPI_WARPS = 8;
-  static constexpr int HALF = BN / 2;                               // columns per epilogue warp
+  static constexpr int NUM_THREADS = 640;
+  static constexpr int EPI_WARP0 = 4, EPI_WARPS = 16;
+  static constexpr int HALF = BN / (EPI_WARPS / 4);                 // columns per epilogue warp
   static constexpr int ACC_LD = BN + 1;                             // padded smem row stride
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert(BM * ACC_LD * 4 <= STAGES * STAGE_BYTES, "FP32 sums must fit in the drained stage ring");
@@ -63,11 +64,11 @@ struct GemmShape {
 };
 
 __device__ __forceinline__ void epi_bar_sync() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");
+  asm volatile("bar.sync 1, 512;" ::: "memory");  // the 16 promotion warps
 }
 
 template <int BN, int R, int EPI, bool EXACT>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(640, 1)
     gemm_i8_g64_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        GemmArgs p) {
   using S = GemmShape<BN>;
@@ -166,9 +167,9 @@ __global__ void __launch_bounds__(384, 1)
       mbar_wait_bounded(mma_done, 0, p.status, 220, nullptr);
     }
   } else if (warp >= S::EPI_WARP0) {
-    // ---------------- promotion (warps 4..11)
+    // ---------------- promotion (warps 4..19)
     const int q = warp & 3;                          // TMEM lane quarter this warp may read
-    const int half = (warp - S::EPI_WARP0) >> 2;     // which half of the tile's columns
+    const int half = (warp - S::EPI_WARP0) >> 2;     // which quarter of the tile's columns
     const int row = q * 32 + lane;
     const int m = m0 + row;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
@@ -188,19 +189,19 @@ __global__ void __launch_bounds__(384, 1)
       const float2 xs2 = make_float2(xsg, xsg);
       const float* wsg = reinterpret_cast<const float*>(st + S::WS_OFF) + (g & 1) * BN + half * HALF;
 #pragma unroll
-      for (int c = 0; c < HALF / 16; ++c) {
-        uint32_t d[16];
-        tmem_ld_32x32b_x16(lane_addr + uint32_t(b * BN + half * HALF + c * 16), d);
+      for (int c = 0; c < HALF / 8; ++c) {
+        uint32_t d[8];
+        tmem_ld_32x32b_x8(lane_addr + uint32_t(b * BN + half * HALF + c * 8), d);
         tmem_wait_ld();
         if (p.dots != nullptr && m < p.M) {
-          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
+          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 8);
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4)
+          for (int j4 = 0; j4 < 2; ++j4)
             dd[j4] = make_int4(int(d[j4 * 4]), int(d[j4 * 4 + 1]), int(d[j4 * 4 + 2]), int(d[j4 * 4 + 3]));
         }
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 w4 = reinterpret_cast<const float4*>(wsg + c * 16)[j4];
+        for (int j4 = 0; j4 < 2; ++j4) {
+          const float4 w4 = reinterpret_cast<const float4*>(wsg + c * 8)[j4];
           const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -208,7 +209,7 @@ __global__ void __launch_bounds__(384, 1)
             // Exact int32 -> float: bits of 1.5 * 2^23 + dot, minus 1.5 * 2^23.
             float2 fd = make_float2(__int_as_float(int32_t(d[j]) + 0x4B400000),
                                     __int_as_float(int32_t(d[j + 1]) + 0x4B400000));
-            float2& a2 = acc[(c * 16 + j) / 2];
+            float2& a2 = acc[(c * 8 + j) / 2];
             const float2 w2 = e ? whi : wlo;
             if (EXACT) {
               // Reference order with scalar IEEE operations (src/int8.rs:58):
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     __syncwarp();
     if (ok && m < p.M) {
-      constexpr int CH = HALF < 32 ? HALF : 32;  // columns finished per pass
+      constexpr int CH = HALF < 16 ? HALF : 16;  // columns finished per pass
       float vals[CH];
 #pragma unroll 1
       for (int c = 0; c < HALF / CH; ++c) {

@@ -109,7 +109,10 @@ __global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __res
       }
     }
   } else {
-    for (int i = 0; i < nv; ++i) {
+    // Quantisation only: blockIdx.y selects a 512-column segment of the row.
+    const int i0 = blockIdx.y * 4, i1 = min(nv, i0 + 4);
+#pragma unroll 4
+    for (int i = i0; i < i1; ++i) {
       const float4 v = xr[lane + 32 * i];
       if (n_out) reinterpret_cast<float4*>(n_out + size_t(m) * ldn)[lane + 32 * i] = v;
       const int col = 4 * (lane + 32 * i);
@@ -469,7 +472,8 @@ void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma
                        reinterpret_cast<uintptr_t>(x) % 16 == 0;
   const int blocks = (M + 7) / 8;
   if (aligned && !gamma && xq) {
-    norm_quant_warp_kernel<0><<<blocks, 256, 0, s>>>(x, ldx, M, K, nullptr, eps, n_out, ldn, xq, xs, ldxs, st);
+    norm_quant_warp_kernel<0><<<dim3(blocks, (K / 128 + 3) / 4), 256, 0, s>>>(x, ldx, M, K, nullptr, eps, n_out, ldn,
+                                                                            xq, xs, ldxs, st);
   } else if (aligned && gamma && K == 2048) {
     norm_quant_warp_kernel<16><<<blocks, 256, 0, s>>>(x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
   } else {
