@@ -27,7 +27,7 @@ struct dg_linear {
   bool exact = true;
   cudaStream_t stream = nullptr;
   dg::DevBuf wq, ws_t, lora_a, lora_b, chunk_pid, status;
-  CUtensorMap map_b{}, map_b64{};
+  dg::WeightMaps maps{};
   int cap_m = 0, ldxs = 0;
   dg::DevBuf x, xq, xs, mid, y;
 };
@@ -129,7 +129,7 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
     dump = dots;
   }
   a.dots = dump;
-  launch_gemm_i8(map_a, l->map_b, &l->map_b64, a, l->rank, kEpiWrite, l->exact, l->stream);
+  launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
   note_launch();
   if (!direct)
     DG_CUDA(cudaMemcpy2DAsync(y_dev, size_t(l->n) * 4, l->y.ptr, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
@@ -282,7 +282,7 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
     };
     l->wq = up(wq.data(), wq.size());
     l->ws_t = up(ws.data(), ws.size() * 4);
-    std::vector<int> pid(N / 32, 0);
+    std::vector<int> pid(N / 16, 0);
     l->chunk_pid = up(pid.data(), pid.size() * 4);
     if (rank) {
       std::vector<float> lb(size_t(N) * rank, 0.0f);
@@ -291,8 +291,7 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
       l->lora_a = up(lora_a, size_t(rank) * k * 4);
     }
     l->status = DevBuf(sizeof(DeviceStatus));
-    make_tmap_i8_2d(&l->map_b, l->wq.ptr, uint64_t(k), uint64_t(N), 128, 256);
-    make_tmap_i8_2d(&l->map_b64, l->wq.ptr, uint64_t(k), uint64_t(N), 128, 64);
+    make_weight_maps(&l->maps, l->wq.ptr, k, N);
     DG_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
     *out = l.release();
   });

@@ -67,8 +67,8 @@ struct DevProj {
   int in = 0, out = 0, out_pad = 0;
   // tcgen05 path (int8-compute, aligned shapes)
   DevBuf wq, ws_t, lora_a, lora_b, chunk_pid;
-  CUtensorMap map_b{}, map_b64{};
-  int lora_rows = 0;            // rows of lora_a (= projections sharing the input x rank)
+  WeightMaps maps{};
+  int lora_rows = 0;           // rows of lora_a (= projections sharing the input x rank)
   std::vector<int> part_off;     // output column of each fused part
   // generic path
   GenericProj g{};

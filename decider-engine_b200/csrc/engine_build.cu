@@ -18,10 +18,10 @@ static DevBuf upload(const std::vector<T>& v) {
 }
 
 // Projections that read the same input, concatenated along the output for one
-// tcgen05 launch. Each part starts on a 32-column chunk (its LoRA block is
-// chosen per chunk); the total is padded to the 256-column tile with zero
-// weights. `interleave_mlp` places gate/up so every 64-column quarter-tile holds
-// 32 gate columns followed by the 32 matching up columns (SwiGLU epilogue).
+// tcgen05 launch. Each part starts on a 32-column boundary (the LoRA block is
+// chosen per 16-column chunk); the total is padded to the 256-column tile with
+// zero weights. `interleave_mlp` alternates 16 gate columns with the 16
+// matching up columns (SwiGLU epilogue).
 DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vector<int>& outs, int in,
                             bool interleave_mlp) {
   const int P = int(keys.size()), R = c_.rank, G = in / 64;
@@ -45,7 +45,7 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
   d.lora_rows = P * R;
   std::vector<uint8_t> wq(size_t(N) * in, 0);
   std::vector<float> ws(size_t(G) * N, 1.0f), lb(size_t(N) * R, 0.0f), la(size_t(P) * R * in);
-  std::vector<int> pid(N / 32, 0);
+  std::vector<int> pid(N / 16, 0);
   for (int p = 0; p < P; ++p) {
     HostTensor w = take(keys[p] + ".weight");
     if (!w.quantized || w.bits != 8) throw std::runtime_error("fused projection needs INT8 weights");
@@ -55,17 +55,16 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
     for (int j = 0; j < outs[p]; ++j) {
       int r;
       if (interleave_mlp) {
-        // Each 64-column quarter of a 256-column tile (one promotion warp's
-        // slice) holds 32 gate columns then the 32 matching up columns.
-        const int t = j / 128, w2 = j % 128, s = w2 / 32;
-        r = t * 256 + s * 64 + p * 32 + (w2 % 32);
+        // Every 32 fused columns hold 16 gate columns then the 16 matching up
+        // columns, so any tile of 128 or 256 columns splits into whole pairs.
+        r = (j / 16) * 32 + p * 16 + (j % 16);
       } else {
         r = off[p] + j;
       }
       std::memcpy(&wq[size_t(r) * in], &w.q[size_t(j) * in], in);
       for (int g = 0; g < G; ++g) ws[size_t(g) * N + r] = w.scales[size_t(j) * G + g];
       std::copy(B.f32.begin() + size_t(j) * R, B.f32.begin() + size_t(j + 1) * R, lb.begin() + size_t(r) * R);
-      pid[r / 32] = p;
+      pid[r / 16] = p;
     }
   }
   d.wq = upload(wq);
@@ -73,8 +72,7 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
   d.lora_a = upload(la);
   d.lora_b = upload(lb);
   d.chunk_pid = upload(pid);
-  make_tmap_i8_2d(&d.map_b, d.wq.ptr, uint64_t(in), uint64_t(N), 128, 256);
-  make_tmap_i8_2d(&d.map_b64, d.wq.ptr, uint64_t(in), uint64_t(N), 128, 64);
+  make_weight_maps(&d.maps, d.wq.ptr, in, N);
   return d;
 }
 

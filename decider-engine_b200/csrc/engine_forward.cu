@@ -41,7 +41,7 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.out = out;
   a.ldo = ldo;
   a.status = status();
-  launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.map_b, &p.map_b64, a, 32, epi, exact, stream_);
+  launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.maps, a, 32, epi, exact, stream_);
   note_launch();
 }
 

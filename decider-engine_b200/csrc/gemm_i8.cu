@@ -1,5 +1,5 @@
 // Tensor maps, tile-width choice and launch of the tcgen05 INT8 projection.
-// The kernel instantiations live in gemm_i8_bn256.cu and gemm_i8_bn64.cu.
+// The kernel instantiations live in gemm_i8_bn{256,128,64}.cu.
 #include <mutex>
 
 #include "gemm_i8_launch.cuh"
@@ -41,14 +41,31 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 
 size_t gemm_i8_smem_bytes(int rank) { return size_t(GemmShape<256>::smem_bytes(rank)); }
 
-int gemm_i8_choose_bn(int M, int N, int epi, bool have_narrow_map) {
-  const int ctas256 = ((M + 127) / 128) * (N / 256);
-  if (epi == kEpiSwiGlu || !have_narrow_map || N % 64) return 256;
-  return ctas256 < 120 ? 64 : 256;
+void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n) {
+  make_tmap_i8_2d(&maps->bn256, wq, uint64_t(k), uint64_t(n), 128, 256);
+  make_tmap_i8_2d(&maps->bn128, wq, uint64_t(k), uint64_t(n), 128, 128);
+  make_tmap_i8_2d(&maps->bn64, wq, uint64_t(k), uint64_t(n), 128, 64);
 }
 
-void launch_gemm_i8(const CUtensorMap& a, const CUtensorMap& b256, const CUtensorMap* b64, const GemmArgs& args,
-                    int rank, int epi, bool exact, cudaStream_t s) {
+// Cost model: a CTA's time grows with its tile width plus a fixed share
+// (pipeline fill, activation tiles, epilogue set-up) worth about 64 columns;
+// the grid takes ceil(ctas / 148) waves. SwiGLU needs at least 32 columns per
+// promotion warp (one gate/up chunk pair), so it never uses 64-wide tiles.
+int gemm_i8_choose_bn(int M, int N, int epi) {
+  const int mt = (M + 127) / 128;
+  int best = 256;
+  long best_cost = -1;
+  for (int bn : {256, 128, 64}) {
+    if (N % bn || (epi == kEpiSwiGlu && bn == 64)) continue;
+    const long ctas = long(mt) * (N / bn), waves = (ctas + 147) / 148;
+    const long cost = waves * (bn + 64);
+    if (best_cost < 0 || cost < best_cost) best = bn, best_cost = cost;
+  }
+  return best;
+}
+
+void launch_gemm_i8(const CUtensorMap& a, const WeightMaps& w, const GemmArgs& args, int rank, int epi,
+                    bool exact, cudaStream_t s) {
   if (args.M <= 0) return;
   if (args.N % 256 || args.K % 128 || args.K <= 0)
     throw CudaError("gemm_i8: N must be a multiple of 256 and K a positive multiple of 128");
@@ -59,11 +76,13 @@ void launch_gemm_i8(const CUtensorMap& a, const CUtensorMap& b256, const CUtenso
     throw CudaError("gemm_i8: bad LoRA operands");
   if (epi == kEpiSwiGlu ? (args.ldo % 4) : (args.ldo % 4 || args.ldo < args.N))
     throw CudaError("gemm_i8: output stride must be a multiple of 4 covering the tile");
-  const int bn = gemm_i8_choose_bn(args.M, args.N, epi, b64 != nullptr);
+  const int bn = gemm_i8_choose_bn(args.M, args.N, epi);
   if (bn == 64)
-    launch_gemm_i8_bn64(a, *b64, args, rank, epi, exact, s);
+    launch_gemm_i8_bn64(a, w.bn64, args, rank, epi, exact, s);
+  else if (bn == 128)
+    launch_gemm_i8_bn128(a, w.bn128, args, rank, epi, exact, s);
   else
-    launch_gemm_i8_bn256(a, b256, args, rank, epi, exact, s);
+    launch_gemm_i8_bn256(a, w.bn256, args, rank, epi, exact, s);
 }
 
 }  // namespace dg

@@ -50,7 +50,7 @@ struct GemmShape {
   static constexpr int WS_OFF = A_BYTES + B_BYTES;                  // [2][BN] floats
   static constexpr int XS_OFF = WS_OFF + 2 * BN * 4;                // [2][BM] floats
   static constexpr int STAGE_BYTES = (XS_OFF + 2 * BM * 4 + 1023) / 1024 * 1024;
-  static constexpr int STAGES = BN == 256 ? 3 : 6;
+  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 5 : 6);
   static constexpr int LORA_OFF = STAGES * STAGE_BYTES;
   static constexpr int NUM_THREADS = 640;
   static constexpr int EPI_WARP0 = 4, EPI_WARPS = 16;
@@ -67,7 +67,8 @@ __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 512;" ::: "memory");  // the 16 promotion warps
 }
 
-template <int BN, int R, int EPI, bool EXACT>
+// DUMP: also write the raw int32 group dots to p.dots (parity checks only).
+template <int BN, int R, int EPI, bool EXACT, bool DUMP>
 __global__ void __launch_bounds__(640, 1)
     gemm_i8_g64_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        GemmArgs p) {
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(640, 1)
         uint32_t d[8];
         tmem_ld_32x32b_x8(lane_addr + uint32_t(b * BN + half * HALF + c * 8), d);
         tmem_wait_ld();
-        if (p.dots != nullptr && m < p.M) {
+        if (DUMP && m < p.M) {
           int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 8);
 #pragma unroll
           for (int j4 = 0; j4 < 2; ++j4)
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(640, 1)
 #pragma unroll
         for (int j = 0; j < CH; ++j) vals[j] = accs[c * CH + j];
         if (R > 0) {
-          const int pid = p.chunk_pid[(n0 + col0) >> 5];
+          const int pid = p.chunk_pid[(n0 + col0) >> 4];
           float mid[R > 0 ? R : 1];
           const float4* mp = reinterpret_cast<const float4*>(p.lora_mid + size_t(m) * p.ld_mid + pid * R);
 #pragma unroll
@@ -309,23 +310,23 @@ __global__ void __launch_bounds__(640, 1)
           }
         }
         if (EPI == kEpiSwiGlu) {
-          // The first half of this warp's columns holds gate, the second half
-          // the matching up values: keep gate passes in shared memory and
-          // combine on the up passes.
-          constexpr int PASSES = HALF / CH;
-          if (c < PASSES / 2) {
+          // Fused columns come in pairs of 16-wide chunks: 16 gate columns,
+          // then the 16 matching up columns (outputs (n0 + col0) / 2 ...).
+          // Keep each gate pass in shared memory and combine on the up pass.
+          static_assert(CH == 16, "SwiGLU pairs 16-column chunks");
+          if ((c & 1) == 0) {
 #pragma unroll
             for (int j = 0; j < CH; ++j) accs[c * CH + j] = vals[j];
           } else {
-            const int gc = c - PASSES / 2;
-            float* o = p.out + size_t(m) * p.ldo + (n0 >> 1) + half * (HALF / 2) + gc * CH;
+            const float* gate = accs + (c - 1) * CH;
+            float* o = p.out + size_t(m) * p.ldo + ((n0 + col0 - CH) >> 1);
 #pragma unroll
             for (int j4 = 0; j4 < CH / 4; ++j4) {
               float4 v;
-              v.x = silu_f(accs[gc * CH + j4 * 4 + 0]) * vals[j4 * 4 + 0];
-              v.y = silu_f(accs[gc * CH + j4 * 4 + 1]) * vals[j4 * 4 + 1];
-              v.z = silu_f(accs[gc * CH + j4 * 4 + 2]) * vals[j4 * 4 + 2];
-              v.w = silu_f(accs[gc * CH + j4 * 4 + 3]) * vals[j4 * 4 + 3];
+              v.x = silu_f(gate[j4 * 4 + 0]) * vals[j4 * 4 + 0];
+              v.y = silu_f(gate[j4 * 4 + 1]) * vals[j4 * 4 + 1];
+              v.z = silu_f(gate[j4 * 4 + 2]) * vals[j4 * 4 + 2];
+              v.w = silu_f(gate[j4 * 4 + 3]) * vals[j4 * 4 + 3];
               reinterpret_cast<float4*>(o)[j4] = v;
             }
           }

@@ -7,12 +7,14 @@ namespace dg {
 
 void launch_gemm_i8_bn256(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
                           bool exact, cudaStream_t s);
+void launch_gemm_i8_bn128(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
+                          bool exact, cudaStream_t s);
 void launch_gemm_i8_bn64(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
                          bool exact, cudaStream_t s);
 
-template <int BN, int R, int EPI, bool EXACT>
-void launch_gemm_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
-  auto kern = gemm_i8_g64_kernel<BN, R, EPI, EXACT>;
+template <int BN, int R, int EPI, bool EXACT, bool DUMP>
+void launch_gemm_kernel(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+  auto kern = gemm_i8_g64_kernel<BN, R, EPI, EXACT, DUMP>;
   const int smem = GemmShape<BN>::smem_bytes(R);
   static bool configured = false;  // per instantiation
   if (!configured) {
@@ -22,6 +24,17 @@ void launch_gemm_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs
   dim3 grid((args.M + 127) / 128, args.N / BN);
   kern<<<grid, GemmShape<BN>::NUM_THREADS, smem, s>>>(a, b, args);
   DG_CUDA(cudaGetLastError());
+}
+
+// The group-dot dump exists only for reference-order WRITE projections.
+template <int BN, int R, int EPI, bool EXACT>
+void launch_gemm_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+  if constexpr (EPI == kEpiWrite && EXACT) {
+    if (args.dots) return launch_gemm_kernel<BN, R, EPI, EXACT, true>(a, b, args, s);
+  } else {
+    if (args.dots) throw CudaError("gemm_i8: group-dot dump needs the reference-order WRITE epilogue");
+  }
+  launch_gemm_kernel<BN, R, EPI, EXACT, false>(a, b, args, s);
 }
 
 }  // namespace dg

@@ -15,12 +15,17 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
                      uint32_t box_inner, uint32_t box_outer);
 
 // ---- INT8 tensor-core projection (tcgen05), gemm_i8.cu
+// Tensor maps of one int8 weight matrix [n][k] for each output-tile width.
+struct WeightMaps {
+  CUtensorMap bn256{}, bn128{}, bn64{};
+};
+void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n);
 // rank: 0 or 32. epi: kEpiWrite/kEpiAdd/kEpiSwiGlu. exact: reference FP32 order.
-// map_b: weights in 256-row boxes; map_b64 (nullable): 64-row boxes, used for
-// narrow outputs so more SMs share the work (gemm_i8_choose_bn).
-void launch_gemm_i8(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap* map_b64,
-                    const GemmArgs& args, int rank, int epi, bool exact, cudaStream_t stream);
-int gemm_i8_choose_bn(int M, int N, int epi, bool have_narrow_map);
+// The tile width is chosen per shape (gemm_i8_choose_bn) so the grid fills
+// the 148 SMs with the fewest waves.
+void launch_gemm_i8(const CUtensorMap& map_a, const WeightMaps& w, const GemmArgs& args, int rank, int epi,
+                    bool exact, cudaStream_t stream);
+int gemm_i8_choose_bn(int M, int N, int epi);
 size_t gemm_i8_smem_bytes(int rank);
 
 // ---- elementwise / normalisation / quantisation, kernels.cu
