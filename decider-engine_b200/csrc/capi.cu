@@ -401,3 +401,117 @@ int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const flo
 }
 
 }  // extern "C"
+
+// ---- Allocation-free projection call (no counterpart in the reference).
+// Some hosts cannot allocate device memory while serving a request: services
+// that reserve their whole device-memory budget at start-up (an allocation in
+// mid-request can fail under memory pressure), and latency-bound callers for
+// which cudaMalloc/cudaFree are too costly (cudaFree waits for the device).
+// dg_linear_forward_device_noalloc runs the same kernels as
+// dg_linear_forward_device, but its per-call scratch (quantised rows, their
+// group scales, the LoRA-A rows, a padded output and the status word) lives
+// in one fixed area of static device memory per device instead of buffers the
+// handle grows with cudaMalloc. Calls on one device share that area, so they
+// must not overlap in time (from several threads, or several handles).
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_base[kNoAllocMaxDevices] = {};
+
+// Address of this device's scratch area; resolved once per device, with that
+// device current, on the first call that needs it.
+unsigned char* noalloc_scratch(int device) {
+  if (device < 0 || device >= kNoAllocMaxDevices) throw std::runtime_error("dg_linear: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      throw std::runtime_error(std::string("dg_linear_forward_device_noalloc: cannot resolve its scratch area: ") +
+                               cudaGetErrorString(e));
+    g_noalloc_base[device] = p;
+  }
+  return static_cast<unsigned char*>(g_noalloc_base[device]);
+}
+
+size_t align256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+extern "C" {
+
+int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m, float* y_device) {
+  return guarded([&] {
+    using namespace dg;
+    if (!l || !x_device || !y_device) throw std::runtime_error("null argument");
+    if (m <= 0) throw std::runtime_error("dg_linear: need at least one row");
+    // Scratch layout: status | xs [k/64][ldxs] | xq [m][k] | mid [m][32] | y [m][n_pad]
+    const int ldxs = (m + 127) / 128 * 128;
+    const bool direct = l->n_pad == l->n;
+    const size_t st_off = 0;
+    const size_t xs_off = st_off + align256(sizeof(DeviceStatus));
+    const size_t xs_bytes = size_t(l->k / 64) * ldxs * 4;
+    const size_t xq_off = xs_off + align256(xs_bytes);
+    const size_t mid_off = xq_off + align256(size_t(m) * l->k);
+    const size_t y_off = mid_off + align256(l->rank ? size_t(m) * 32 * 4 : 0);
+    const size_t total = y_off + (direct ? 0 : size_t(m) * l->n_pad * 4);
+    if (total > kNoAllocScratchBytes)
+      throw std::runtime_error("dg_linear_forward_device_noalloc: " + std::to_string(m) + " rows of k=" +
+                               std::to_string(l->k) + " need " + std::to_string(total) +
+                               " bytes of scratch, more than its fixed " + std::to_string(kNoAllocScratchBytes) +
+                               "-byte area; split the rows over several calls");
+    DG_CUDA(cudaSetDevice(l->device));
+    unsigned char* base = noalloc_scratch(l->device);
+    DeviceStatus* st = reinterpret_cast<DeviceStatus*>(base + st_off);
+    float* xs = reinterpret_cast<float*>(base + xs_off);
+    int8_t* xq = reinterpret_cast<int8_t*>(base + xq_off);
+    float* mid = reinterpret_cast<float*>(base + mid_off);
+    float* ypad = reinterpret_cast<float*>(base + y_off);
+    // The status word must start at zero; the scale rows past m (read as part
+    // of the last 128-row tile) are cleared too so no stale value remains.
+    DG_CUDA(cudaMemsetAsync(st, 0, sizeof(DeviceStatus), l->stream));
+    DG_CUDA(cudaMemsetAsync(xs, 0, xs_bytes, l->stream));
+    launch_norm_quant(x_device, l->k, m, l->k, nullptr, 0.0f, nullptr, 0, xq, xs, ldxs, st, l->stream);
+    note_launch();
+    if (l->rank) {
+      launch_lora_a(x_device, l->k, m, l->k, l->lora_a.as<float>(), l->rank, mid, 32, l->exact, l->stream);
+      note_launch();
+    }
+    CUtensorMap map_a;
+    make_tmap_i8_2d(&map_a, xq, uint64_t(l->k), uint64_t(m), 128, 128);
+    GemmArgs a{};
+    a.M = m;
+    a.N = l->n_pad;
+    a.K = l->k;
+    a.xs = xs;
+    a.ldxs = ldxs;
+    a.ws = l->ws_t.as<float>();
+    a.lora_mid = mid;
+    a.ld_mid = 32;
+    a.lora_b = l->lora_b.as<float>();
+    a.chunk_pid = l->chunk_pid.as<int>();
+    a.lora_scale = l->scale;
+    a.out = direct ? y_device : ypad;
+    a.ldo = direct ? l->n : l->n_pad;
+    a.status = st;
+    a.dots = nullptr;
+    launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
+    note_launch();
+    if (!direct)
+      DG_CUDA(cudaMemcpy2DAsync(y_device, size_t(l->n) * 4, ypad, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
+                                cudaMemcpyDeviceToDevice, l->stream));
+    DeviceStatus h{};
+    DG_CUDA(cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, l->stream));
+    DG_CUDA(cudaStreamSynchronize(l->stream));
+    if (h.code == kNonFinite) throw std::runtime_error("non-finite projection input");
+    if (h.code)
+      throw std::runtime_error("device error code " + std::to_string(h.code) + " at " + std::to_string(h.where));
+  });
+}
+
+}  // extern "C"

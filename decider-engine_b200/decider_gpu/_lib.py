@@ -18,7 +18,8 @@ SYMBOLS = [
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
-    "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_last_quantized",
+    "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
+    "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_stream", "dg_linear_free",
     "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
 ]
@@ -75,6 +76,7 @@ def load() -> C.CDLL:
     L.dg_linear_create.argtypes = [f32p, i32, i32, f32p, f32p, i32, C.c_float, i32, C.POINTER(vp)]
     L.dg_linear_forward.argtypes = [vp, f32p, i32, f32p]
     L.dg_linear_forward_device.argtypes = [vp, vp, i32, vp, vp]
+    L.dg_linear_forward_device_noalloc.argtypes = [vp, vp, i32, vp]
     L.dg_linear_last_quantized.argtypes = [vp, i32, vp, vp]
     L.dg_linear_set_exact.argtypes = [vp, i32]
     L.dg_linear_free.argtypes = [vp]

@@ -200,6 +200,13 @@ class Linear:
     def forward_device(self, x_ptr: int, m: int, y_ptr: int, dots_ptr: int | None = None) -> None:
         check(load().dg_linear_forward_device(self.h, x_ptr, m, y_ptr, dots_ptr))
 
+    def forward_device_noalloc(self, x_ptr: int, m: int, y_ptr: int) -> None:
+        """`forward_device` without any device allocation: the per-call scratch
+        is a fixed 8 MiB static area per device (rows beyond it are rejected).
+        Calls on one device must not overlap in time; the first call on a
+        device should come before any stream capture begins."""
+        check(load().dg_linear_forward_device_noalloc(self.h, x_ptr, m, y_ptr))
+
     def last_quantized(self, m: int):
         xq = np.zeros((m, self.k), np.int8)
         xs = np.zeros((self.k // 64, m), np.float32)

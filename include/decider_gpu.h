@@ -106,6 +106,24 @@ int dg_linear_forward(dg_linear* l, const float* x, int m, float* y);
 /* Same on device buffers; group_dots_device (nullable) receives the exact
  * int32 group dots [k/64][m][n] the tensor cores produced. */
 int dg_linear_forward_device(dg_linear* l, const float* x_device, int m, float* y_device, int32_t* group_dots_device);
+/* Allocation-free form of dg_linear_forward_device (no counterpart in the
+ * reference, whose projection is CPU code). For hosts that must not allocate
+ * device memory while serving a request: those that reserve their whole
+ * device-memory budget at start-up, where an allocation in mid-request can
+ * fail under memory pressure, and latency-bound callers for which
+ * cudaMalloc/cudaFree cost too much (cudaFree waits for the device). Same
+ * kernels and results as dg_linear_forward_device without the group-dot dump;
+ * its scratch is one fixed 8 MiB area of static device memory per device, so
+ * it allocates nothing. Limits and rules:
+ *  - m rows must fit that area: about m*k + m*(k/16 + 128) bytes, plus
+ *    m*n_pad*4 when n % 256 != 0; larger calls fail with an error naming the
+ *    bytes needed (split the rows over several calls);
+ *  - the first call on each device resolves the area's address (with that
+ *    device current); make that first call before beginning any stream capture;
+ *  - calls on one device share the area, so they must not overlap in time,
+ *    from several threads or several handles alike: serialise them.
+ * Runs on, and synchronises, the handle's stream (dg_linear_stream). */
+int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m, float* y_device);
 /* Quantised activations of the last call: xq [m][k] int8 and scales [k/64][m] (host). */
 int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs);
 int dg_linear_set_exact(dg_linear* l, int exact);
