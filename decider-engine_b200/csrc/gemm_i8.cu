@@ -1,5 +1,6 @@
 // Tensor maps, tile-width choice and launch of the tcgen05 INT8 projection.
-// The kernel instantiations live in gemm_i8_bn{256,128,64}.cu.
+// The kernel instantiations live in gemm_i8_bn128.cu and gemm_i8_bn64.cu.
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_i8_launch.cuh"
@@ -39,23 +40,26 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
-size_t gemm_i8_smem_bytes(int rank) { return size_t(GemmShape<256>::smem_bytes(rank)); }
-
 void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n) {
-  make_tmap_i8_2d(&maps->bn256, wq, uint64_t(k), uint64_t(n), 128, 256);
   make_tmap_i8_2d(&maps->bn128, wq, uint64_t(k), uint64_t(n), 128, 128);
   make_tmap_i8_2d(&maps->bn64, wq, uint64_t(k), uint64_t(n), 128, 64);
 }
 
 // Cost model: a CTA's time grows with its tile width plus a fixed share
 // (pipeline fill, activation tiles, epilogue set-up) worth about 64 columns;
-// the grid takes ceil(ctas / 148) waves. SwiGLU needs at least 32 columns per
-// promotion warp (one gate/up chunk pair), so it never uses 64-wide tiles.
+// the grid takes ceil(ctas / 148) waves. SwiGLU pairs 16 gate with 16 up
+// columns per 32, which the epilogue finishes in 128-column tiles only.
+// DG_GEMM_TILE_N (64 or 128) forces the width where the shape allows it, for
+// tuning on new parts.
 int gemm_i8_choose_bn(int M, int N, int epi) {
+  if (const char* f = std::getenv("DG_GEMM_TILE_N")) {
+    const int bn = std::atoi(f);
+    if ((bn == 64 || bn == 128) && N % bn == 0 && !(epi == kEpiSwiGlu && bn == 64)) return bn;
+  }
   const int mt = (M + 127) / 128;
-  int best = 256;
+  int best = 128;
   long best_cost = -1;
-  for (int bn : {256, 128, 64}) {
+  for (int bn : {128, 64}) {
     if (N % bn || (epi == kEpiSwiGlu && bn == 64)) continue;
     const long ctas = long(mt) * (N / bn), waves = (ctas + 147) / 148;
     const long cost = waves * (bn + 64);
@@ -79,10 +83,8 @@ void launch_gemm_i8(const CUtensorMap& a, const WeightMaps& w, const GemmArgs& a
   const int bn = gemm_i8_choose_bn(args.M, args.N, epi);
   if (bn == 64)
     launch_gemm_i8_bn64(a, w.bn64, args, rank, epi, exact, s);
-  else if (bn == 128)
-    launch_gemm_i8_bn128(a, w.bn128, args, rank, epi, exact, s);
   else
-    launch_gemm_i8_bn256(a, w.bn256, args, rank, epi, exact, s);
+    launch_gemm_i8_bn128(a, w.bn128, args, rank, epi, exact, s);
 }
 
 }  // namespace dg

@@ -6,21 +6,22 @@
 //   out[m,n] = EPI( Σ_g float(dot_g(xq[m], wq[n])) * (xs[m,g] * ws[n,g])  + 0.0
 //                   + lora_scale * (dot_scores(mid[m, pid(n)], lora_b[n]) + 0.0) )
 //
-// One CTA owns a 128 x BN output tile (BN = 256, or 64 for narrow outputs so
-// more SMs share the work); 20 warps (5 warpgroups):
+// One CTA owns a 128 x BN output tile (BN = 128, or 64 for narrow outputs so
+// more SMs share the work); 18 warps:
 //   warp 0      TMA producer: int8 A/B tiles (128-byte swizzle) plus the two
-//               groups' activation and weight scales, multi-stage ring;
-//   warp 1      TMEM allocator and single-thread MMA issuer: per 64-wide K group,
-//               two tcgen05.mma kind::i8 (K=32) into a fresh int32 accumulator,
-//               double-buffered in TMEM (2 x BN columns);
-//   warps 2-3   no role (the block is sized in whole warpgroups);
-//   warps 4-19  promotion/epilogue, four per TMEM lane quarter, each owning a
-//               quarter of the tile's columns: per group, tcgen05.ld the exact int32 dots and
-//               scale them in FP32 in group order with packed f32x2 arithmetic
-//               (each lane op IEEE-rounded: reference order when EXACT, fused
-//               multiply-add otherwise). After the last group the FP32 sums move
-//               to shared memory (the drained stage ring) and each thread finishes
-//               its row: LoRA-B, the epilogue and the store.
+//               groups' activation and weight scales of each 128-wide K stage;
+//   warp 1      TMEM allocator and single-thread MMA issuer: per stage, two
+//               64-wide groups, each two tcgen05.mma kind::i8 (K=32) into its
+//               own int32 accumulator; 512 TMEM columns hold 512/BN group
+//               accumulators, so the MMAs run up to 256/BN stages ahead;
+//   warps 2-17  promotion and epilogue. Main loop: four warps per TMEM lane
+//               quarter (warp % 4), each owning a quarter of the tile's columns; per group
+//               they tcgen05.ld the accumulators and scale them in FP32 in group
+//               order (reference order when EXACT, fused multiply-add otherwise).
+//               Epilogue: the FP32 sums and this tile's LoRA-A rows go to shared
+//               memory (the drained stage ring); each thread then finishes a
+//               4-row x (BN/16)-column block: LoRA-B as a register-tiled
+//               rank-R product, the epilogue, and row-contiguous stores.
 // Every wait is bounded (mbar_wait_bounded); a stall records kWaitTimeout.
 #pragma once
 #include "common.cuh"
@@ -32,10 +33,11 @@ struct GemmArgs {
   const float* xs;          // activation scales [K/64][ldxs]
   int ldxs;                 // >= round_up(M, 128)
   const float* ws;          // weight scales [K/64][N]
-  const float* lora_mid;    // [M][ld_mid] LoRA-A outputs (nullable when R == 0)
+  const float* lora_mid;    // [M][ld_mid] LoRA-A outputs of all fused parts (nullable when R == 0)
   int ld_mid;
   const float* lora_b;      // [N][R]
-  const int* chunk_pid;     // [N/32] LoRA block index of each 32-column chunk
+  const int* chunk_pid;     // [N/16] LoRA part of each 16-column chunk (non-decreasing per tile
+                            // except SwiGLU's alternating gate/up chunks)
   float lora_scale;
   float* out;               // WRITE/ADD: [M][ldo] (N columns); SWIGLU: [M][ldo] (N/2 columns)
   int ldo;
@@ -45,56 +47,101 @@ struct GemmArgs {
 
 template <int BN_>
 struct GemmShape {
+  static_assert(BN_ == 64 || BN_ == 128, "tile width");
   static constexpr int BM = 128, BN = BN_, BK = 128;  // BK bytes = two 64-wide groups
   static constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
   static constexpr int WS_OFF = A_BYTES + B_BYTES;                  // [2][BN] floats
   static constexpr int XS_OFF = WS_OFF + 2 * BN * 4;                // [2][BM] floats
   static constexpr int STAGE_BYTES = (XS_OFF + 2 * BM * 4 + 1023) / 1024 * 1024;
-  static constexpr int STAGES = BN == 256 ? 3 : (BN == 128 ? 5 : 6);
-  static constexpr int LORA_OFF = STAGES * STAGE_BYTES;
-  static constexpr int NUM_THREADS = 640;
-  static constexpr int EPI_WARP0 = 4, EPI_WARPS = 16;
-  static constexpr int HALF = BN / (EPI_WARPS / 4);                 // columns per epilogue warp
-  static constexpr int ACC_LD = BN + 1;                             // padded smem row stride
-  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static_assert(BM * ACC_LD * 4 <= STAGES * STAGE_BYTES, "FP32 sums must fit in the drained stage ring");
-  __host__ __device__ static constexpr int lora_bytes(int R) { return BN * R * 4; }
-  __host__ __device__ static constexpr int bar_off(int R) { return LORA_OFF + lora_bytes(R); }
-  __host__ __device__ static constexpr int smem_bytes(int R) { return bar_off(R) + 128 + 1024; }
+  static constexpr int STAGES = BN == 128 ? 5 : 6;
+  static constexpr int RING = STAGES * STAGE_BYTES;
+  static constexpr int NUM_THREADS = 576;
+  static constexpr int EPI_WARP0 = 2, EPI_WARPS = 16, EPI_THREADS = EPI_WARPS * 32;
+  static constexpr int HALF = BN / 4;           // main loop: columns per promotion warp
+  static constexpr int NBUF = 512 / BN;         // group accumulators in TMEM
+  static constexpr int NPAIR = NBUF / 2;        // stages in flight between MMA and promotion
+  static constexpr uint32_t TMEM_COLS = 512;
+  // Epilogue layout inside the drained ring: FP32 sums [BM][ACC_LD], then the
+  // tile's LoRA-A rows [BM][MID_LD] (at most four fused parts of rank 32).
+  static constexpr int ACC_LD = BN + 4, MID_LD = 132, MID_MAX = 128;
+  static constexpr int MID_OFF = BM * ACC_LD * 4;
+  static_assert(MID_OFF + BM * MID_LD * 4 <= RING, "epilogue staging must fit in the ring");
+  // LoRA-B of the tile, transposed: [R][BT_LD].
+  static constexpr int BT_LD = BN + 4;
+  static constexpr int BT_OFF = RING;
+  static constexpr int CW = BN / 16, HW = CW / 2;  // epilogue: columns per thread, per half
+  static_assert((2 * STAGES + 2 * NPAIR + 1) * 8 + 8 <= 256, "barrier area");
+  __host__ __device__ static constexpr int bt_bytes(int R) { return R * BT_LD * 4; }
+  __host__ __device__ static constexpr int bar_off(int R) { return BT_OFF + bt_bytes(R); }
+  __host__ __device__ static constexpr int smem_bytes(int R) { return bar_off(R) + 256 + 1024; }
 };
 
 __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 512;" ::: "memory");  // the 16 promotion warps
 }
 
+// tcgen05.wait::ld that also orders every use of the loaded registers after it.
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Orders every later use of r after the preceding tcgen05.wait::ld.
+__device__ __forceinline__ void tmem_dep16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15])
+               :
+               : "memory");
+}
+
+// Loads HW consecutive floats (HW = 2 or 4) from shared memory.
+template <int HW>
+__device__ __forceinline__ void lds_vec(const float* p, float (&v)[HW]) {
+  if constexpr (HW == 4) {
+    const float4 t = *reinterpret_cast<const float4*>(p);
+    v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+  } else {
+    const float2 t = *reinterpret_cast<const float2*>(p);
+    v[0] = t.x; v[1] = t.y;
+  }
+}
+
 // DUMP: also write the raw int32 group dots to p.dots (parity checks only).
 template <int BN, int R, int EPI, bool EXACT, bool DUMP>
-__global__ void __launch_bounds__(640, 1)
+__global__ void __launch_bounds__(576, 1)
     gemm_i8_g64_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                        GemmArgs p) {
   using S = GemmShape<BN>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES, STAGE_BYTES = S::STAGE_BYTES, HALF = S::HALF;
+  constexpr int NPAIR = S::NPAIR;
+  static_assert(EPI != kEpiSwiGlu || BN == 128, "SwiGLU pairs need 128-column tiles");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::bar_off(R));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* mma_done = tempty + 2;
+  uint64_t* tempty = tfull + NPAIR;
+  uint64_t* mma_done = tempty + NPAIR;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* lora_smem = reinterpret_cast<float*>(smem + S::LORA_OFF);
+  float* bt_smem = reinterpret_cast<float*>(smem + S::BT_OFF);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-  const int G = p.K / 64, KS = p.K / BK;
+  const int KS = p.K / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + S::EPI_WARPS);
+      mbar_init(&empty[s], S::EPI_WARPS);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NPAIR; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], S::EPI_WARPS);
     }
@@ -109,10 +156,16 @@ __global__ void __launch_bounds__(640, 1)
     tmem_relinquish();
   }
   if (R > 0 && warp >= S::EPI_WARP0) {
-    // Stage this tile's LoRA-B rows [BN][R] (contiguous in global memory).
+    // This tile's LoRA-B rows [BN][R], transposed to [R][BT_LD].
     const float4* src = reinterpret_cast<const float4*>(p.lora_b + size_t(n0) * R);
-    float4* dst = reinterpret_cast<float4*>(lora_smem);
-    for (int i = threadIdx.x - S::EPI_WARP0 * 32; i < BN * R / 4; i += S::EPI_WARPS * 32) dst[i] = src[i];
+    for (int i = threadIdx.x - S::EPI_WARP0 * 32; i < BN * R / 4; i += S::EPI_THREADS) {
+      const float4 v = src[i];
+      const int n = i / (R / 4), r = (i % (R / 4)) * 4;
+      bt_smem[(r + 0) * S::BT_LD + n] = v.x;
+      bt_smem[(r + 1) * S::BT_LD + n] = v.y;
+      bt_smem[(r + 2) * S::BT_LD + n] = v.z;
+      bt_smem[(r + 3) * S::BT_LD + n] = v.w;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -147,21 +200,25 @@ __global__ void __launch_bounds__(640, 1)
     if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_i8(BM, BN);
-      bool ok = true;
-      for (int g = 0; g < G && ok; ++g) {
-        const int ks = g / 2, s = ks % STAGES, b = g & 1, use = g / 2;
-        if ((g & 1) == 0) ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag);
-        if (ok && use > 0) ok = mbar_wait_bounded(&tempty[b], (use - 1) & 1, p.status, 210 + b, abort_flag);
-        if (!ok) break;
+      for (int ks = 0; ks < KS; ++ks) {
+        const int s = ks % STAGES, pb = ks % NPAIR, pu = ks / NPAIR;
+        // Phase pu of tempty[pb]: the promotion warps have read the pair's
+        // previous stage and refilled its accumulators with the offset.
+        if (!mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag) ||
+            !mbar_wait_bounded(&tempty[pb], pu & 1, p.status, 210 + pb, abort_flag))
+          break;
         tc_fence_after();
-        const uint32_t a_addr = smem_addr(smem + s * STAGE_BYTES) + (g & 1) * 64;
-        const uint32_t b_addr = a_addr + S::A_BYTES;
-        const uint32_t d = tmem_base + uint32_t(b * BN);
 #pragma unroll
-        for (int kk = 0; kk < 2; ++kk)
-          mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, kk);
-        mma_commit(&tfull[b]);
-        if (g & 1) mma_commit(&empty[s]);
+        for (int j = 0; j < 2; ++j) {
+          const uint32_t a_addr = smem_addr(smem + s * STAGE_BYTES) + j * 64;
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+          const uint32_t d = tmem_base + uint32_t((2 * pb + j) * BN);
+          // Both MMAs accumulate onto the offset already in the accumulator.
+#pragma unroll
+          for (int kk = 0; kk < 2; ++kk)
+            mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, 1);
+        }
+        mma_commit(&tfull[pb]);
       }
       // All MMAs of this thread have completed once mma_done flips.
       mma_commit(mma_done);
@@ -173,174 +230,262 @@ __global__ void __launch_bounds__(640, 1)
     const int half = (warp - S::EPI_WARP0) >> 2;     // which quarter of the tile's columns
     const int row = q * 32 + lane;
     const int m = m0 + row;
-    const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16);
+    const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(half * HALF);
+    // Every accumulator word starts at the bits of 1.5 * 2^23 (0x4B400000), so
+    // after the group's MMAs it holds the bits of the float 1.5 * 2^23 + dot
+    // (|dot| <= 64 * 128 * 128 < 2^22): the exact int32 -> float conversion is
+    // one subtraction of 1.5 * 2^23.
+    constexpr uint32_t kOffsetBits = 0x4B400000u;
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
+#pragma unroll
+    for (int b = 0; b < S::NBUF; ++b)
+#pragma unroll
+      for (int c = 0; c < HALF / 16; ++c) tmem_fill_32x32b_x16(lane_addr + uint32_t(b * BN + c * 16), kOffsetBits);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+#pragma unroll
+      for (int b = 0; b < NPAIR; ++b) mbar_arrive(&tempty[b]);
+    }
     float2 acc[HALF / 2];
 #pragma unroll
     for (int j = 0; j < HALF / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
+    // A stage holds two groups of HALF/16 16-column chunks each; chunk c of
+    // both groups is loaded at once (one TMEM load latency per chunk).
+    constexpr int CPG = HALF / 16;
     bool ok = true;
-    for (int g = 0; g < G; ++g) {
-      const int ks = g / 2, s = ks % STAGES, b = g & 1, use = g / 2;
+    for (int ks = 0; ks < KS; ++ks) {
+      const int s = ks % STAGES, pb = ks % NPAIR, pu = ks / NPAIR;
       ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 300 + s, abort_flag) &&
-           mbar_wait_bounded(&tfull[b], use & 1, p.status, 310 + b, abort_flag);
+           mbar_wait_bounded(&tfull[pb], pu & 1, p.status, 310 + pb, abort_flag);
       if (!ok) break;
       tc_fence_after();
       const uint8_t* st = smem + s * STAGE_BYTES;
-      const float xsg = reinterpret_cast<const float*>(st + S::XS_OFF)[(g & 1) * BM + row];
-      const float2 xs2 = make_float2(xsg, xsg);
-      const float* wsg = reinterpret_cast<const float*>(st + S::WS_OFF) + (g & 1) * BN + half * HALF;
+      const float* xsp = reinterpret_cast<const float*>(st + S::XS_OFF);
+      const float xsg[2] = {xsp[row], xsp[BM + row]};
+      const float* wsp = reinterpret_cast<const float*>(st + S::WS_OFF) + half * HALF;
+      const bool refill = ks + NPAIR < KS;  // the pair's next stage needs the offset again
+      const uint32_t pair_addr = lane_addr + uint32_t(2 * pb * BN);
 #pragma unroll
-      for (int c = 0; c < HALF / 8; ++c) {
-        uint32_t d[8];
-        tmem_ld_32x32b_x8(lane_addr + uint32_t(b * BN + half * HALF + c * 8), d);
-        tmem_wait_ld();
+      for (int c = 0; c < CPG; ++c) {
+        uint32_t d[2][16];  // [group of the stage][column]
+        tmem_ld_32x32b_x16(pair_addr + uint32_t(c * 16), d[0]);
+        tmem_ld_32x32b_x16(pair_addr + uint32_t(BN + c * 16), d[1]);
+        tmem_wait_ld16(d[0]);
+        tmem_dep16(d[1]);
+#pragma unroll
+       for (int j = 0; j < 2; ++j) {
+        const uint32_t taddr = pair_addr + uint32_t(j * BN + c * 16);
+        uint32_t(&cur)[16] = d[j];
+        if (refill) tmem_fill_32x32b_x16(taddr, kOffsetBits);
         if (DUMP && m < p.M) {
-          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 8);
+          const int g = 2 * ks + j;
+          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
 #pragma unroll
-          for (int j4 = 0; j4 < 2; ++j4)
-            dd[j4] = make_int4(int(d[j4 * 4]), int(d[j4 * 4 + 1]), int(d[j4 * 4 + 2]), int(d[j4 * 4 + 3]));
+          for (int j4 = 0; j4 < 4; ++j4)
+            dd[j4] = make_int4(int(cur[j4 * 4] - kOffsetBits), int(cur[j4 * 4 + 1] - kOffsetBits),
+                               int(cur[j4 * 4 + 2] - kOffsetBits), int(cur[j4 * 4 + 3] - kOffsetBits));
         }
+        const float xs = xsg[j];
+        const float2 xs2 = make_float2(xs, xs);
 #pragma unroll
-        for (int j4 = 0; j4 < 2; ++j4) {
-          const float4 w4 = reinterpret_cast<const float4*>(wsg + c * 8)[j4];
+        for (int j4 = 0; j4 < 4; ++j4) {
+          const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
           const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int j = j4 * 4 + e * 2;
-            // Exact int32 -> float: bits of 1.5 * 2^23 + dot, minus 1.5 * 2^23.
-            float2 fd = make_float2(__int_as_float(int32_t(d[j]) + 0x4B400000),
-                                    __int_as_float(int32_t(d[j + 1]) + 0x4B400000));
-            float2& a2 = acc[(c * 8 + j) / 2];
+            const int k = j4 * 4 + e * 2;
+            float2 fd = make_float2(__uint_as_float(cur[k]), __uint_as_float(cur[k + 1]));
+            float2& a2 = acc[(c * 16 + k) / 2];
             const float2 w2 = e ? whi : wlo;
             if (EXACT) {
               // Reference order with scalar IEEE operations (src/int8.rs:58):
               // sum + float(dot) * (xs * ws), rounded after every step.
-              a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xsg, w2.x)));
-              a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xsg, w2.y)));
+              a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
+              a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
             } else {
               fd = add2_rn(fd, neg_magic);
               a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
             }
           }
         }
+       }
       }
+      if (refill) tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&tempty[b]);
-        if (g & 1) mbar_arrive(&empty[s]);
+        mbar_arrive(&tempty[pb]);
+        mbar_arrive(&empty[s]);
       }
     }
-    // ---------------- epilogue: sums to shared memory, then per-row finish.
-    // All stages are drained once every promotion warp has left the loop.
+    // ---------------- epilogue
+    epi_bar_sync();  // every promotion warp has left the loop: the ring is free
+    float* accs = reinterpret_cast<float*>(smem);
+    float* mids = reinterpret_cast<float*>(smem + S::MID_OFF);
+    {
+      float4* dst = reinterpret_cast<float4*>(accs + size_t(row) * S::ACC_LD + half * HALF);
+#pragma unroll
+      for (int j = 0; j < HALF / 4; ++j) {
+        // Bias-free projections add 0.0 as the reference does (src/tensor.rs:437).
+        dst[j] = make_float4(__fadd_rn(acc[2 * j].x, 0.0f), __fadd_rn(acc[2 * j].y, 0.0f),
+                             __fadd_rn(acc[2 * j + 1].x, 0.0f), __fadd_rn(acc[2 * j + 1].y, 0.0f));
+      }
+    }
+    const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
+    constexpr int MAXP = R > 0 ? S::MID_MAX / R : 1;  // LoRA parts one tile may span
+    int pmin = 0;
+    if constexpr (R > 0) {
+      // LoRA-A rows of the parts this tile's columns use, zero past row M.
+      int lo = 1 << 30, hi = 0;
+#pragma unroll
+      for (int c = 0; c < BN / 16; ++c) {
+        const int v = p.chunk_pid[(n0 >> 4) + c];
+        lo = min(lo, v);
+        hi = max(hi, v);
+      }
+      hi = min(hi, lo + MAXP - 1);
+      pmin = lo;
+      const int nc4 = (hi - lo + 1) * (R / 4);
+      for (int i = et; i < BM * nc4; i += S::EPI_THREADS) {
+        const int r = i / nc4, c4 = i % nc4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (m0 + r < p.M)
+          v = *reinterpret_cast<const float4*>(p.lora_mid + size_t(m0 + r) * p.ld_mid + lo * R + c4 * 4);
+        *reinterpret_cast<float4*>(mids + r * S::MID_LD + c4 * 4) = v;
+      }
+    }
     epi_bar_sync();
-    float* accs = reinterpret_cast<float*>(smem) + size_t(row) * S::ACC_LD + half * HALF;
-    if (ok) {
-      // Bias-free projections add 0.0 as the reference does (src/tensor.rs:437).
-#pragma unroll
-      for (int j = 0; j < HALF / 2; ++j) {
-        accs[2 * j] = __fadd_rn(acc[j].x, 0.0f);
-        accs[2 * j + 1] = __fadd_rn(acc[j].y, 0.0f);
+    if (!*abort_flag) {
+      // Each thread finishes rows r0..r0+3 of two HW-column halves: adjacent
+      // (WRITE/ADD) or a gate chunk and its up chunk 16 columns on (SWIGLU).
+      constexpr int HW = S::HW;
+      const int cg = et & 15, r0 = (et >> 4) * 4;
+      int col[2], ocol;
+      if constexpr (EPI == kEpiSwiGlu) {
+        col[0] = 32 * (cg >> 2) + 4 * (cg & 3);
+        col[1] = col[0] + 16;
+        ocol = (n0 >> 1) + 16 * (cg >> 2) + 4 * (cg & 3);
+      } else {
+        col[0] = cg * S::CW;
+        col[1] = col[0] + HW;
+        ocol = n0 + col[0];
       }
-    }
-    __syncwarp();
-    if (ok && m < p.M) {
-      constexpr int CH = HALF < 16 ? HALF : 16;  // columns finished per pass
-      float vals[CH];
+      // v: the FP32 sums, read half by half after that half's LoRA-B product.
+      float v[4][2][HW];
+      if constexpr (R == 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) lds_vec<HW>(accs + (r0 + i) * S::ACC_LD + col[h], v[i][h]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int part = min(max(p.chunk_pid[(n0 + col[h]) >> 4] - pmin, 0), MAXP - 1);
+          const float* mrow = mids + r0 * S::MID_LD + part * R;
+          const float* brow = bt_smem + col[h];
+          if constexpr (EXACT) {
+            // dot_scores order (src/tensor.rs:6-25): lane l sums ranks l, l+8,
+            // l+16, l+24 from 0.0; the lanes are added in order from -0.0.
+            float tot[4][HW];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int c = 0; c < HW; ++c) tot[i][c] = -0.0f;
 #pragma unroll 1
-      for (int c = 0; c < HALF / CH; ++c) {
-        const int col0 = half * HALF + c * CH;
+            for (int l = 0; l < 8; ++l) {
+              float lan[4][HW];
 #pragma unroll
-        for (int j = 0; j < CH; ++j) vals[j] = accs[c * CH + j];
-        if (R > 0) {
-          const int pid = p.chunk_pid[(n0 + col0) >> 4];
-          float mid[R > 0 ? R : 1];
-          const float4* mp = reinterpret_cast<const float4*>(p.lora_mid + size_t(m) * p.ld_mid + pid * R);
+              for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int r4 = 0; r4 < R / 4; ++r4) {
-            const float4 v = mp[r4];
-            mid[r4 * 4] = v.x; mid[r4 * 4 + 1] = v.y; mid[r4 * 4 + 2] = v.z; mid[r4 * 4 + 3] = v.w;
-          }
-#pragma unroll 2
-          for (int j = 0; j < CH; j += 2) {
-            // Two columns at a time: .x for column j, .y for column j + 1.
-            const float4* b0 = reinterpret_cast<const float4*>(lora_smem + (col0 + j) * R);
-            const float4* b1 = reinterpret_cast<const float4*>(lora_smem + (col0 + j + 1) * R);
-            float2 delta;
-            if (EXACT) {
-              // dot_scores order (src/tensor.rs:6-25): eight lanes, then their sum.
-              float2 lanes[8];
+                for (int c = 0; c < HW; ++c) lan[i][c] = 0.0f;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) lanes[i] = make_float2(0.0f, 0.0f);
+              for (int jj = 0; jj < R / 8; ++jj) {
+                const int r = l + 8 * jj;
+                float b[HW];
+                lds_vec<HW>(brow + r * S::BT_LD, b);
 #pragma unroll
-              for (int r4 = 0; r4 < R / 4; ++r4) {
-                const float4 w0 = b0[r4], w1 = b1[r4];
-                const float2 wv[4] = {make_float2(w0.x, w1.x), make_float2(w0.y, w1.y), make_float2(w0.z, w1.z),
-                                      make_float2(w0.w, w1.w)};
+                for (int i = 0; i < 4; ++i) {
+                  const float x = mrow[i * S::MID_LD + r];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int r = r4 * 4 + e;
-                  lanes[r & 7].x = __fadd_rn(lanes[r & 7].x, __fmul_rn(mid[r], wv[e].x));
-                  lanes[r & 7].y = __fadd_rn(lanes[r & 7].y, __fmul_rn(mid[r], wv[e].y));
+                  for (int c = 0; c < HW; ++c) lan[i][c] = __fadd_rn(lan[i][c], __fmul_rn(x, b[c]));
                 }
               }
-              delta = make_float2(-0.0f, -0.0f);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                delta.x = __fadd_rn(delta.x, lanes[i].x);
-                delta.y = __fadd_rn(delta.y, lanes[i].y);
-              }
-              delta.x = __fadd_rn(delta.x, 0.0f);
-              delta.y = __fadd_rn(delta.y, 0.0f);
-              vals[j] = __fadd_rn(vals[j], __fmul_rn(p.lora_scale, delta.x));
-              vals[j + 1] = __fadd_rn(vals[j + 1], __fmul_rn(p.lora_scale, delta.y));
-            } else {
-              delta = make_float2(0.0f, 0.0f);
+              for (int i = 0; i < 4; ++i)
 #pragma unroll
-              for (int r4 = 0; r4 < R / 4; ++r4) {
-                const float4 w0 = b0[r4], w1 = b1[r4];
-                delta = fma2_rn(make_float2(mid[r4 * 4], mid[r4 * 4]), make_float2(w0.x, w1.x), delta);
-                delta = fma2_rn(make_float2(mid[r4 * 4 + 1], mid[r4 * 4 + 1]), make_float2(w0.y, w1.y), delta);
-                delta = fma2_rn(make_float2(mid[r4 * 4 + 2], mid[r4 * 4 + 2]), make_float2(w0.z, w1.z), delta);
-                delta = fma2_rn(make_float2(mid[r4 * 4 + 3], mid[r4 * 4 + 3]), make_float2(w0.w, w1.w), delta);
+                for (int c = 0; c < HW; ++c) tot[i][c] = __fadd_rn(tot[i][c], lan[i][c]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              lds_vec<HW>(accs + (r0 + i) * S::ACC_LD + col[h], v[i][h]);
+#pragma unroll
+              for (int c = 0; c < HW; ++c)
+                v[i][h][c] = __fadd_rn(v[i][h][c], __fmul_rn(p.lora_scale, __fadd_rn(tot[i][c], 0.0f)));
+            }
+          } else {
+            float dl[4][HW];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+              for (int c = 0; c < HW; ++c) dl[i][c] = 0.0f;
+#pragma unroll 1
+            for (int r4 = 0; r4 < R / 4; ++r4) {
+              float b[4][HW];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) lds_vec<HW>(brow + (r4 * 4 + e) * S::BT_LD, b[e]);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 x = *reinterpret_cast<const float4*>(mrow + i * S::MID_LD + r4 * 4);
+#pragma unroll
+                for (int c = 0; c < HW; ++c) {
+                  dl[i][c] = __fmaf_rn(x.x, b[0][c], dl[i][c]);
+                  dl[i][c] = __fmaf_rn(x.y, b[1][c], dl[i][c]);
+                  dl[i][c] = __fmaf_rn(x.z, b[2][c], dl[i][c]);
+                  dl[i][c] = __fmaf_rn(x.w, b[3][c], dl[i][c]);
+                }
               }
-              vals[j] = __fmaf_rn(p.lora_scale, delta.x, vals[j]);
-              vals[j + 1] = __fmaf_rn(p.lora_scale, delta.y, vals[j + 1]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              lds_vec<HW>(accs + (r0 + i) * S::ACC_LD + col[h], v[i][h]);
+#pragma unroll
+              for (int c = 0; c < HW; ++c) v[i][h][c] = __fmaf_rn(p.lora_scale, dl[i][c], v[i][h][c]);
             }
           }
         }
-        if (EPI == kEpiSwiGlu) {
-          // Fused columns come in pairs of 16-wide chunks: 16 gate columns,
-          // then the 16 matching up columns (outputs (n0 + col0) / 2 ...).
-          // Keep each gate pass in shared memory and combine on the up pass.
-          static_assert(CH == 16, "SwiGLU pairs 16-column chunks");
-          if ((c & 1) == 0) {
+      }
 #pragma unroll
-            for (int j = 0; j < CH; ++j) accs[c * CH + j] = vals[j];
-          } else {
-            const float* gate = accs + (c - 1) * CH;
-            float* o = p.out + size_t(m) * p.ldo + ((n0 + col0 - CH) >> 1);
-#pragma unroll
-            for (int j4 = 0; j4 < CH / 4; ++j4) {
-              float4 v;
-              v.x = silu_f(gate[j4 * 4 + 0]) * vals[j4 * 4 + 0];
-              v.y = silu_f(gate[j4 * 4 + 1]) * vals[j4 * 4 + 1];
-              v.z = silu_f(gate[j4 * 4 + 2]) * vals[j4 * 4 + 2];
-              v.w = silu_f(gate[j4 * 4 + 3]) * vals[j4 * 4 + 3];
-              reinterpret_cast<float4*>(o)[j4] = v;
-            }
-          }
+      for (int i = 0; i < 4; ++i) {
+        const int mm = m0 + r0 + i;
+        if (mm >= p.M) continue;
+        float* o = p.out + size_t(mm) * p.ldo + ocol;
+        if constexpr (EPI == kEpiSwiGlu) {
+          *reinterpret_cast<float4*>(o) = make_float4(silu_f(v[i][0][0]) * v[i][1][0], silu_f(v[i][0][1]) * v[i][1][1],
+                                                      silu_f(v[i][0][2]) * v[i][1][2], silu_f(v[i][0][3]) * v[i][1][3]);
         } else {
-          float4* o = reinterpret_cast<float4*>(p.out + size_t(m) * p.ldo + n0 + col0);
 #pragma unroll
-          for (int j4 = 0; j4 < CH / 4; ++j4) {
-            float4 v = make_float4(vals[j4 * 4], vals[j4 * 4 + 1], vals[j4 * 4 + 2], vals[j4 * 4 + 3]);
-            if (EPI == kEpiAdd) {
-              const float4 old = o[j4];
-              v.x = __fadd_rn(old.x, v.x); v.y = __fadd_rn(old.y, v.y);
-              v.z = __fadd_rn(old.z, v.z); v.w = __fadd_rn(old.w, v.w);
+          for (int h = 0; h < 2; ++h) {
+            float w[HW];
+#pragma unroll
+            for (int c = 0; c < HW; ++c) w[c] = v[i][h][c];
+            if constexpr (EPI == kEpiAdd) {
+              float old[HW];
+              if constexpr (HW == 4) {
+                const float4 t = *reinterpret_cast<const float4*>(o + h * HW);
+                old[0] = t.x; old[1] = t.y; old[2] = t.z; old[3] = t.w;
+              } else {
+                const float2 t = *reinterpret_cast<const float2*>(o + h * HW);
+                old[0] = t.x; old[1] = t.y;
+              }
+#pragma unroll
+              for (int c = 0; c < HW; ++c) w[c] = __fadd_rn(old[c], w[c]);
             }
-            o[j4] = v;
+            if constexpr (HW == 4)
+              *reinterpret_cast<float4*>(o + h * HW) = make_float4(w[0], w[1], w[2], w[3]);
+            else
+              *reinterpret_cast<float2*>(o + h * HW) = make_float2(w[0], w[1]);
           }
         }
       }

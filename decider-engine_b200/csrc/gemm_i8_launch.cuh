@@ -5,8 +5,6 @@
 
 namespace dg {
 
-void launch_gemm_i8_bn256(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
-                          bool exact, cudaStream_t s);
 void launch_gemm_i8_bn128(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
                           bool exact, cudaStream_t s);
 void launch_gemm_i8_bn64(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,

@@ -17,7 +17,7 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 // ---- INT8 tensor-core projection (tcgen05), gemm_i8.cu
 // Tensor maps of one int8 weight matrix [n][k] for each output-tile width.
 struct WeightMaps {
-  CUtensorMap bn256{}, bn128{}, bn64{};
+  CUtensorMap bn128{}, bn64{};
 };
 void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n);
 // rank: 0 or 32. epi: kEpiWrite/kEpiAdd/kEpiSwiGlu. exact: reference FP32 order.
@@ -26,7 +26,6 @@ void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n);
 void launch_gemm_i8(const CUtensorMap& map_a, const WeightMaps& w, const GemmArgs& args, int rank, int epi,
                     bool exact, cudaStream_t stream);
 int gemm_i8_choose_bn(int M, int N, int epi);
-size_t gemm_i8_smem_bytes(int rank);
 
 // ---- elementwise / normalisation / quantisation, kernels.cu
 // Row-wise: optional centred RMSNorm (gamma != nullptr: x * (inv * (1 + g))),
