@@ -9,8 +9,9 @@ value  : prefill tokens/s with the ids already resident (device time of the
          forward kernels, CUDA events on the engine stream);
 e2e    : the same through the public C ABI call (dg_logits: host ids in,
          host logits out, copies inside the timed region);
-roofline: the dominant kernel, the tcgen05 INT8 projection, timed live on the
-         MLP gate|up shape (512 x 12288 x 2048, rank-32 LoRA, SwiGLU-sized N);
+roofline: the dominant kernel, the tcgen05 INT8 projection: every one of its
+         launches in the timed steps is bracketed by CUDA events on the engine
+         stream; achieved = sum of 2*M*N*K over the launches / their summed time;
 cpu_baseline: the oracle (C++ restatement of the reference CPU path) on one
          4-layer block of the same model over a token sample, extrapolated to
          24 layers.
@@ -38,6 +39,10 @@ import numpy as np  # noqa: E402
 
 METRIC = "prefill tok/s at 2B INT8 (1/2/4/8 B200)"
 TOKENS = 512
+# DRAM bytes (read + write) per gemm_i8_g64 launch from one ncu capture of the
+# bench's own launches; None until a capture of the current kernel is recorded
+# under profiles/.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = None
 
 
 def cfg2(layers=24):
@@ -115,7 +120,7 @@ def dist_setup():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=None)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=None)
         pg = dist
     return world, rank, local, pg
 
@@ -187,7 +192,7 @@ def run_ours(args, world, rank, local, dist):
     import torch
 
     import decider_gpu
-    from decider_gpu import GpuModel, Linear
+    from decider_gpu import GpuModel
     torch.cuda.set_device(local)
     L = decider_gpu.load()
     cfg = cfg2(24)
@@ -213,6 +218,9 @@ def run_ours(args, world, rank, local, dist):
     for _ in range(args.warmup):
         step()
     stream = torch.cuda.ExternalStream(L.dg_engine_stream(model.h), device=local)
+    # ---- roofline source: every tcgen05 projection launch of the timed steps,
+    # bracketed by CUDA events on the engine stream (the launching stream)
+    model.gemm_timing(True)
     # ---- e2e: through the public call, host buffers, copies inside the region
     barrier(dist, local)
     n0 = decider_gpu.launch_count()
@@ -234,29 +242,14 @@ def run_ours(args, world, rank, local, dist):
     dev_ms = max_over_ranks(dev_ms, dist, local)
     value = world * TOKENS / (dev_ms / 1000.0)
     e2e = world * TOKENS / (e2e_ms / 1000.0)
-    # ---- roofline: dominant kernel (tcgen05 INT8 projection) on the gate|up shape
-    M, N, K = TOKENS, 2 * cfg["intermediate_size"], cfg["hidden_size"]
-    g = np.random.default_rng(7)
-    lin = Linear((0.02 * g.standard_normal((N, K))).astype(np.float32),
-                 (0.02 * g.standard_normal((32, K))).astype(np.float32),
-                 (0.02 * g.standard_normal((N, 32))).astype(np.float32), 2.0, local)
-    lin.set_exact(args.exact)
-    xd = torch.randn((M, K), device=f"cuda:{local}")
-    yd = torch.empty((M, N), device=f"cuda:{local}")
-    for _ in range(3):
-        lin.forward_device(xd.data_ptr(), M, yd.data_ptr())
-    ls = torch.cuda.ExternalStream(L.dg_linear_stream(lin.h), device=local)
-    reps = 20
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record(ls)
-    for _ in range(reps):
-        lin.forward_device(xd.data_ptr(), M, yd.data_ptr())
-    a1.record(ls)
-    a1.synchronize()
-    lin_ms = a0.elapsed_time(a1) / reps  # quantize + LoRA-A + GEMM per call
+    # ---- roofline: the dominant kernel, gemm_i8_g64 (all projection launches)
+    g_ms, g_ops, g_n = model.gemm_time()
+    model.gemm_timing(False)
+    gemm_ms_per_launch = g_ms / max(g_n, 1)
+    gemm_share = g_ms / (dev_ms * args.steps) if dev_ms > 0 else None
     hbm, bf16, src = peaks()
     int8_peak = 2.0 * bf16
-    achieved = 2.0 * M * N * K / (lin_ms / 1000.0) / 1e12
+    achieved = g_ops / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
     if rank != 0:
         return
     cpu = None
@@ -277,9 +270,11 @@ def run_ours(args, world, rank, local, dist):
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": TOKENS * 4 + 16,
                 "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
-                     "frac": achieved / int8_peak, "traffic": None,
-                     "kernel": f"gemm_i8_g64 (incl. quantize + LoRA-A) {M}x{N}x{K}", "ms_per_launch": lin_ms,
-                     "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s)"},
+                     "frac": achieved / int8_peak, "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
+                     "kernel": "gemm_i8_g64_kernel, all projection launches of the timed steps "
+                               "(achieved = sum 2*M*N*K / sum event time)",
+                     "launches": int(g_n), "ms_per_launch": gemm_ms_per_launch, "share_of_step": gemm_share,
+                     "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }

@@ -207,6 +207,23 @@ float dg_engine_last_forward_ms(const dg_engine* e) { return e && e->e ? e->e->l
 
 int dg_engine_last_launches(const dg_engine* e) { return e && e->e ? e->e->last_launches : -1; }
 
+int dg_engine_gemm_timing(dg_engine* e, int enable) {
+  return guarded([&] {
+    check_engine(e);
+    e->e->set_gemm_timing(enable != 0);
+  });
+}
+
+int dg_engine_gemm_time(const dg_engine* e, double* ms, double* ops, uint64_t* launches) {
+  return guarded([&] {
+    check_engine(e);
+    if (!ms || !ops || !launches) throw std::runtime_error("null argument");
+    *ms = e->e->gemm_timing.ms;
+    *ops = e->e->gemm_timing.ops;
+    *launches = e->e->gemm_timing.launches;
+  });
+}
+
 int dg_forward_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, float* hidden_out) {
   return guarded([&] {
     check_engine(e);

@@ -164,6 +164,18 @@ class Engine {
   DevBuf status_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
   DeviceStatus* status() const { return status_.as<DeviceStatus>(); }
+  // Optional timing of every tcgen05 projection launch (event pairs on the
+  // engine stream), read back after each forward.
+  std::vector<cudaEvent_t> gemm_ev_;
+  std::vector<double> gemm_ops_pending_;
+  void collect_gemm_timing();
+
+ public:
+  struct GemmTiming {
+    double ms = 0.0, ops = 0.0;  // summed launch time and algorithmic ops (2*M*N*K)
+    uint64_t launches = 0;
+  } gemm_timing;
+  void set_gemm_timing(bool on);
 };
 
 }  // namespace dg

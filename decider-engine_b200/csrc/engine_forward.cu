@@ -41,8 +41,15 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.out = out;
   a.ldo = ldo;
   a.status = status();
+  const size_t k = gemm_ops_pending_.size();
+  const bool timed = 2 * k + 2 <= gemm_ev_.size();
+  if (timed) DG_CUDA(cudaEventRecord(gemm_ev_[2 * k], stream_));
   launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.maps, a, 32, epi, exact, stream_);
   note_launch();
+  if (timed) {
+    DG_CUDA(cudaEventRecord(gemm_ev_[2 * k + 1], stream_));
+    gemm_ops_pending_.push_back(2.0 * M * p.out * p.in);
+  }
 }
 
 void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi) {
@@ -275,6 +282,7 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
   }
   DG_CUDA(cudaMemcpyAsync(ids_.ptr, ids, size_t(n) * 4, cudaMemcpyHostToDevice, stream_));
   DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
+  gemm_ops_pending_.clear();
   DG_CUDA(cudaEventRecord(ev0_, stream_));
   launch_embed(embedding_.ptr, 0, c_.hidden, ids_.as<uint32_t>(), n, x_.as<float>(), stream_);
   note_launch();
@@ -293,6 +301,7 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
     DG_CUDA(cudaMemcpyAsync(hidden_out, x_.ptr, size_t(n) * c_.hidden * 4, cudaMemcpyDeviceToHost, stream_));
   check_status();
   DG_CUDA(cudaEventElapsedTime(&last_forward_ms, ev0_, ev1_));
+  collect_gemm_timing();
   last_launches = int(launch_count() - launches0);
   if (capture) *captured = std::move(cap);
 }

@@ -115,6 +115,33 @@ Engine::~Engine() {
   }
   if (ev0_) cudaEventDestroy(ev0_);
   if (ev1_) cudaEventDestroy(ev1_);
+  for (cudaEvent_t ev : gemm_ev_) cudaEventDestroy(ev);
+}
+
+// Timing covers up to 128 projection launches per forward (24 layers use 96).
+void Engine::set_gemm_timing(bool on) {
+  DG_CUDA(cudaSetDevice(device_));
+  DG_CUDA(cudaStreamSynchronize(stream_));
+  gemm_timing = GemmTiming{};
+  gemm_ops_pending_.clear();
+  if (on && gemm_ev_.empty()) {
+    gemm_ev_.resize(256, nullptr);
+    for (auto& ev : gemm_ev_) DG_CUDA(cudaEventCreate(&ev));
+  } else if (!on) {
+    for (cudaEvent_t ev : gemm_ev_) cudaEventDestroy(ev);
+    gemm_ev_.clear();
+  }
+}
+
+void Engine::collect_gemm_timing() {
+  for (size_t k = 0; k < gemm_ops_pending_.size(); ++k) {
+    float ms = 0.0f;
+    DG_CUDA(cudaEventElapsedTime(&ms, gemm_ev_[2 * k], gemm_ev_[2 * k + 1]));
+    gemm_timing.ms += ms;
+    gemm_timing.ops += gemm_ops_pending_[k];
+    gemm_timing.launches += 1;
+  }
+  gemm_ops_pending_.clear();
 }
 
 std::map<std::string, Engine::Expected> Engine::expected_names() const {

@@ -16,7 +16,7 @@ SYMBOLS = [
     "dg_last_error", "dg_launch_count",
     "dg_engine_create", "dg_engine_set_tensor", "dg_engine_fill_synthetic", "dg_engine_finalize",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
-    "dg_engine_last_forward_ms", "dg_engine_last_launches",
+    "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
@@ -64,6 +64,8 @@ def load() -> C.CDLL:
     L.dg_engine_last_forward_ms.argtypes = [vp]
     L.dg_engine_last_forward_ms.restype = C.c_float
     L.dg_engine_last_launches.argtypes = [vp]
+    L.dg_engine_gemm_timing.argtypes = [vp, i32]
+    L.dg_engine_gemm_time.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
     L.dg_linear_stream.argtypes = [vp]
     L.dg_linear_stream.restype = vp
     L.dg_forward_hidden.argtypes = [vp, vp, u32p, sz, f32p]

@@ -119,6 +119,16 @@ class GpuModel:
     def set_exact(self, exact: bool) -> None:
         check(load().dg_engine_set_exact(self.h, int(exact)))
 
+    def gemm_timing(self, enable: bool) -> None:
+        """Bracket every tcgen05 projection launch with CUDA events (resets the totals)."""
+        check(load().dg_engine_gemm_timing(self.h, int(enable)))
+
+    def gemm_time(self):
+        """(summed launch ms, summed 2*M*N*K ops, launches) since gemm_timing()."""
+        ms, ops, n = C.c_double(), C.c_double(), C.c_uint64()
+        check(load().dg_engine_gemm_time(self.h, C.byref(ms), C.byref(ops), C.byref(n)))
+        return ms.value, ops.value, n.value
+
     def __del__(self):
         if getattr(self, "h", None):
             load().dg_engine_free(self.h)

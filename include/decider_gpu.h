@@ -75,6 +75,13 @@ void* dg_engine_stream(const dg_engine* e);
  * the result download; and the number of kernels that forward launched. */
 float dg_engine_last_forward_ms(const dg_engine* e);
 int dg_engine_last_launches(const dg_engine* e);
+/* Measurement aid (no counterpart in the reference): with timing enabled,
+ * every tcgen05 projection launch of a forward is bracketed by CUDA events on
+ * the engine stream; dg_engine_gemm_time returns the summed launch time (ms),
+ * the summed algorithmic ops (2*M*N*K) and the launch count since the last
+ * dg_engine_gemm_timing call, which also resets them. */
+int dg_engine_gemm_timing(dg_engine* e, int enable);
+int dg_engine_gemm_time(const dg_engine* e, double* ms, double* ops, uint64_t* launches);
 
 /* ---- forward passes: Model::forward / prefill / forward_after
  * (src/qwen.rs:407-424). `past` may be NULL. hidden_out (nullable) receives
