@@ -195,7 +195,8 @@ def run_ours(args, world, rank, local, dist):
     from decider_gpu import GpuModel
     torch.cuda.set_device(local)
     L = decider_gpu.load()
-    cfg = cfg2(24)
+    cfg = cfg2(args.layers)
+    cfg["vocab_size"] = args.vocab
     t0 = time.time()
     model = GpuModel(cfg, "int8-compute", 32, 2.0, 256, local, TOKENS)
     model.fill_synthetic(seed=0, stddev=0.02)
@@ -263,8 +264,9 @@ def run_ours(args, world, rank, local, dist):
         "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)",
         "promotion": "reference-order" if args.exact else "fma", "data": "synthetic",
-        "config": {"workload": "cfg2: 2B decider forward (24 layers, LoRA r32) over a 512-token prompt + "
-                               "pointer head, int8-compute", "tokens_per_step": TOKENS, "parallelism": f"dp{world}",
+        "config": {"workload": f"cfg2: 2B decider forward ({args.layers} layers, vocab {args.vocab}, LoRA r32) "
+                               "over a 512-token prompt + pointer head, int8-compute",
+                   "tokens_per_step": TOKENS, "parallelism": f"dp{world}",
                    "l2": "not flushed: each step streams 1.4 GB of int8 weights, > 126 MB L2",
                    "setup_s": round(setup_s, 1)},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": TOKENS * 4 + 16,
@@ -293,7 +295,13 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--exact", action="store_true",
                     help="reference-order FP32 promotion instead of fused multiply-add")
+    ap.add_argument("--layers", type=int, default=24,
+                    help="fewer layers (multiple of 4) for small ncu captures; the bench line is 24")
+    ap.add_argument("--vocab", type=int, default=248320,
+                    help="smaller embedding table for small ncu captures; the bench line is 248320")
     args = ap.parse_args()
+    if args.layers % 4 or args.layers <= 0:
+        ap.error("--layers must be a positive multiple of 4")
     world, rank, local, dist = dist_setup()
     try:
         if args.impl == "reference":
