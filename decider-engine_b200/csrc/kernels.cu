@@ -313,69 +313,148 @@ __global__ void __launch_bounds__(256) lora_a_fast_kernel(const float* __restric
   }
 }
 
-// LoRA A, fast mode, split over K so a skinny [M x R] output still fills the
-// GPU: CTA (64 rows x 64 outputs x one K slice) through shared-memory tiles,
-// 4 x 4 outputs per thread; partial sums go to partial[slice][m][r] and
-// lora_a_reduce_kernel adds the slices in a fixed order (deterministic).
+// 16-byte global -> shared copy; src_bytes 0 fills the destination with zeros.
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_groups() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// LoRA A, fast mode: partial[slice] = x · Aᵀ over one K slice, split so the
+// skinny [M x R] output still fills the GPU; lora_a_reduce_kernel adds the
+// slices in a fixed order (deterministic). CTA = TM rows x RT outputs; 32-wide
+// K chunks go to shared memory K-contiguous (double-buffered cp.async). Each
+// thread owns 4 rows x OPT outputs, the outputs strided by NOG so the 16-byte
+// loads of one warp fall on distinct banks, and consumes four k per load: a
+// 16-byte load feeds 4 to 8 FMAs.
+template <int TM, int RT>
+struct LoraTile {
+  static constexpr int KC = 32, LD = KC + 4;  // floats per staged row (16-byte aligned)
+  static constexpr int NOG = 1024 / TM;       // output groups (threads per row group)
+  static constexpr int OPT = RT / NOG;        // outputs per thread
+  static constexpr int STAGE = (TM + RT) * LD;
+  static constexpr int SMEM = 2 * STAGE * 4;
+  static_assert(OPT >= 1 && RT % NOG == 0, "tile shape");
+};
+
+template <int TM, int RT>
 __global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                             const float* __restrict__ A, int R,
                                                             float* __restrict__ partial, int kslice) {
-  __shared__ float xs_[64][33];
-  __shared__ float as_[64][33];
-  const int tid = threadIdx.x, ty = tid / 16, tx = tid % 16;
-  const int m_base = blockIdx.x * 64, r_base = blockIdx.y * 64;
+  using T = LoraTile<TM, RT>;
+  constexpr int LD = T::LD, NOG = T::NOG, OPT = T::OPT, KC = T::KC;
+  extern __shared__ __align__(16) float lora_smem[];
+  const int tid = threadIdx.x, og = tid % NOG, rg = tid / NOG;
+  const int m_base = blockIdx.x * TM, r_base = blockIdx.y * RT;
   const int k0 = blockIdx.z * kslice, k1 = min(K, k0 + kslice);
-  float acc[4][4];
+  const int chunks = (k1 - k0) / KC;  // kslice and K are multiples of 32
+  auto stage_x = [&](int b) { return lora_smem + b * T::STAGE; };
+  auto stage_a = [&](int b) { return lora_smem + b * T::STAGE + TM * LD; };
+  auto load = [&](int c, int b) {
+    const int kc = k0 + c * KC;
+    for (int i = tid; i < (TM + RT) * (KC / 4); i += 256) {
+      const int row = i / (KC / 4), k4 = (i % (KC / 4)) * 4;
+      if (row < TM) {
+        const int m = m_base + row;
+        const float* src = m < M ? x + size_t(m) * ldx + kc + k4 : x;
+        cp_async16_zfill(stage_x(b) + row * LD + k4, src, m < M ? 16 : 0);
+      } else {
+        const int r = r_base + row - TM;
+        const float* src = r < R ? A + size_t(r) * K + kc + k4 : A;
+        cp_async16_zfill(stage_a(b) + (row - TM) * LD + k4, src, r < R ? 16 : 0);
+      }
+    }
+    cp_async_commit_group();
+  };
+  float acc[4][OPT];
 #pragma unroll
   for (int a = 0; a < 4; ++a)
 #pragma unroll
-    for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
-  for (int kc = k0; kc < k1; kc += 32) {
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int i = tid + u * 256, row = i / 8, kk = (i % 8) * 4;
-      const int m = m_base + row, r = r_base + row, k = kc + kk;
-      float4 xv = make_float4(0, 0, 0, 0), av = xv;
-      if (m < M && k < k1) xv = __ldg(reinterpret_cast<const float4*>(x + size_t(m) * ldx + k));
-      if (r < R && k < k1) av = __ldg(reinterpret_cast<const float4*>(A + size_t(r) * K + k));
-      xs_[row][kk] = xv.x; xs_[row][kk + 1] = xv.y; xs_[row][kk + 2] = xv.z; xs_[row][kk + 3] = xv.w;
-      as_[row][kk] = av.x; as_[row][kk + 1] = av.y; as_[row][kk + 2] = av.z; as_[row][kk + 3] = av.w;
+    for (int o = 0; o < OPT; ++o) acc[a][o] = 0.0f;
+  if (chunks > 0) load(0, 0);
+  for (int c = 0; c < chunks; ++c) {
+    if (c + 1 < chunks) {
+      load(c + 1, (c + 1) & 1);
+      cp_async_wait_groups<1>();
+    } else {
+      cp_async_wait_groups<0>();
     }
     __syncthreads();
-#pragma unroll 8
-    for (int kk = 0; kk < 32; ++kk) {
-      float xv[4], av[4];
+    const float* xs = stage_x(c & 1) + rg * 4 * LD;
+    const float* as = stage_a(c & 1) + og * LD;
 #pragma unroll
-      for (int a = 0; a < 4; ++a) xv[a] = xs_[ty * 4 + a][kk];
+    for (int k4 = 0; k4 < KC; k4 += 4) {
+      float4 xv[4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) av[b] = as_[tx * 4 + b][kk];
+      for (int a = 0; a < 4; ++a) xv[a] = *reinterpret_cast<const float4*>(xs + a * LD + k4);
 #pragma unroll
-      for (int a = 0; a < 4; ++a)
+      for (int o = 0; o < OPT; ++o) {
+        const float4 av = *reinterpret_cast<const float4*>(as + o * NOG * LD + k4);
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = __fmaf_rn(xv[a], av[b], acc[a][b]);
+        for (int a = 0; a < 4; ++a) {
+          acc[a][o] = __fmaf_rn(xv[a].x, av.x, acc[a][o]);
+          acc[a][o] = __fmaf_rn(xv[a].y, av.y, acc[a][o]);
+          acc[a][o] = __fmaf_rn(xv[a].z, av.z, acc[a][o]);
+          acc[a][o] = __fmaf_rn(xv[a].w, av.w, acc[a][o]);
+        }
+      }
     }
-    __syncthreads();
+    __syncthreads();  // the buffer is refilled two chunks on
   }
   float* out = partial + size_t(blockIdx.z) * M * R;
 #pragma unroll
   for (int a = 0; a < 4; ++a) {
-    const int m = m_base + ty * 4 + a;
+    const int m = m_base + rg * 4 + a;
     if (m >= M) continue;
 #pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int r = r_base + tx * 4 + b;
-      if (r < R) out[size_t(m) * R + r] = acc[a][b];
+    for (int o = 0; o < OPT; ++o) {
+      const int r = r_base + og + o * NOG;
+      if (r < R) out[size_t(m) * R + r] = acc[a][o];
     }
   }
 }
 
-__global__ void lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M, int R,
-                                     float* __restrict__ mid, int ldm) {
+// One output per thread; slice z goes to chain z % 4 and the chains are added
+// as (c0 + c1) + (c2 + c3): a fixed order, so the result is deterministic.
+__global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M,
+                                                            int R, float* __restrict__ mid, int ldm) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * R) return;
-  float s = 0.0f;
-  for (int z = 0; z < slices; ++z) s += partial[size_t(z) * M * R + i];
-  mid[size_t(i / R) * ldm + i % R] = s;
+  const size_t stride = size_t(M) * R;
+  float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int z = 0;
+  for (; z + 4 <= slices; z += 4) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[j] += __ldg(partial + size_t(z + j) * stride + i);
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+    if (z + j < slices) c[j] += __ldg(partial + size_t(z + j) * stride + i);
+  mid[size_t(i / R) * ldm + i % R] = (c[0] + c[1]) + (c[2] + c[3]);
+}
+
+template <int TM, int RT>
+void launch_lora_splitk(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
+                        float* partial, size_t partial_floats, cudaStream_t s) {
+  using T = LoraTile<TM, RT>;
+  static bool configured = false;  // per instantiation
+  if (!configured) {
+    DG_CUDA(cudaFuncSetAttribute(lora_a_splitk_kernel<TM, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 T::SMEM));
+    configured = true;
+  }
+  const int gx = (M + TM - 1) / TM, gy = (R + RT - 1) / RT;
+  const int slices = std::max(1, std::min(K / T::KC, (148 + gx * gy - 1) / (gx * gy)));
+  const int kslice = ((K + slices - 1) / slices + T::KC - 1) / T::KC * T::KC;
+  const int used = (K + kslice - 1) / kslice;
+  if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
+  lora_a_splitk_kernel<TM, RT><<<dim3(gx, gy, used), 256, T::SMEM, s>>>(x, ldx, M, K, A, R, partial, kslice);
+  DG_CUDA(cudaGetLastError());
+  lora_a_reduce_kernel<<<(M * R + 127) / 128, 128, 0, s>>>(partial, used, M, R, mid, ldm);
 }
 
 __device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale, int precision, int n, int k, int K) {
@@ -498,16 +577,14 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
   const int blocks = int((threads + 255) / 256);
   if (exact) {
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
-  } else if (partial && K % 128 == 0 && ldx % 4 == 0) {
-    const int tiles = ((M + 63) / 64) * ((R + 63) / 64);
-    const int slices = std::max(1, std::min(K / 128, (148 + tiles - 1) / tiles));
-    const int kslice = ((K + slices - 1) / slices + 31) / 32 * 32;
-    const int used = (K + kslice - 1) / kslice;
-    if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
-    lora_a_splitk_kernel<<<dim3((M + 63) / 64, (R + 63) / 64, used), 256, 0, s>>>(x, ldx, M, K, A, R, partial,
-                                                                                  kslice);
-    DG_CUDA(cudaGetLastError());
-    lora_a_reduce_kernel<<<(M * R + 255) / 256, 256, 0, s>>>(partial, used, M, R, mid, ldm);
+  } else if (partial && K % 32 == 0 && ldx % 4 == 0 && R % 4 == 0 && ldm % 4 == 0 &&
+             reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0) {
+    if (R <= 32)
+      launch_lora_splitk<128, 32>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
+    else if (R <= 64)
+      launch_lora_splitk<64, 64>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
+    else
+      launch_lora_splitk<64, 128>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
   } else {
     const long warps = long((M + 3) / 4) * ((R + 3) / 4);
     lora_a_fast_kernel<<<int((warps * 32 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
