@@ -34,6 +34,12 @@ struct ChunkOut {
   float pad[3];
 };
 
+// Per-chunk values of the sequential pass, read by the output pass.
+struct ChunkState {
+  float S[DK][DK];  // state at the chunk start (value columns j0.. of each slice)
+  float D[CK][DK];  // U - W S0
+};
+
 __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, ChunkOut* __restrict__ outs,
                                                                int chunks) {
   extern __shared__ __align__(16) float sm[];
@@ -45,6 +51,7 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
   float* lg = T + CK * (CK + 1);    // [CK] cumulative log decay
   float* bt = lg + CK;              // [CK]
   float* gm = bt + CK;              // [CK] G_t = exp(lg)
+  float* Xs = gm + CK;              // [CK / 16 - 1][16][16] block-row products
   const int tid = threadIdx.x;
   const int c = blockIdx.x % chunks, h = (blockIdx.x / chunks) % a.value_heads;
   const size_t bi = blockIdx.x / (chunks * a.value_heads);
@@ -153,23 +160,49 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
         }
     }
   }
+  // T = (I + L)^-1 (unit lower triangular), blocked by 16. The diagonal
+  // blocks by forward substitution, one warp each (lane = column, so every
+  // lane reads only the column it writes):
+  //   T[t][s] = -sum_{u=s}^{t-1} L[t][u] T[u][s] (s < t), T[t][t] = 1;
+  // then the block rows in order, all blocks of a row at once:
+  //   X_ij = sum_{k=j}^{i-1} L_ik T_kj,   T_ij = -T_ii X_ij   (j < i).
   __syncthreads();
-  // T = (I + L)^-1 by forward substitution in one warp (rows in order, each
-  // lane owning columns lane and lane + 32):
-  // T[t][s] = -sum_{u=s}^{t-1} L[t][u] T[u][s] (s < t), T[t][t] = 1.
-  if (tid < 32) {
-    for (int t = 0; t < CK; ++t) {
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const int s = tid + 32 * h2;
+  {
+    constexpr int NB = CK / 16;
+    const int warp = tid / 32, lane = tid % 32;
+    for (int i = tid; i < CK * CK; i += 256) {
+      const int t = i / CK, s = i % CK;
+      if (s / 16 != t / 16) T[t * (CK + 1) + s] = 0.0f;
+    }
+    if (warp < NB && lane < 16) {
+      const int b0 = warp * 16, s = b0 + lane;
+      for (int t = b0; t < b0 + 16; ++t) {
         float acc = 0.0f;
         for (int u = s; u < t; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
         T[t * (CK + 1) + s] = s < t ? -acc : (s == t ? 1.0f : 0.0f);
       }
-      __syncwarp();
+    }
+    __syncthreads();
+    float* X = Xs;  // [NB - 1][16][16]
+    for (int bi_ = 1; bi_ < NB; ++bi_) {
+      for (int e = tid; e < bi_ * 256; e += 256) {
+        const int j = e / 256, r = (e / 16) % 16, cc = e % 16;
+        const int t = bi_ * 16 + r, s = j * 16 + cc;
+        float acc = 0.0f;
+        for (int u = j * 16; u < bi_ * 16; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
+        X[e] = acc;
+      }
+      __syncthreads();
+      for (int e = tid; e < bi_ * 256; e += 256) {
+        const int j = e / 256, r = (e / 16) % 16, cc = e % 16;
+        const int t = bi_ * 16 + r;
+        float acc = 0.0f;
+        for (int u = 0; u <= r; ++u) acc = __fmaf_rn(T[t * (CK + 1) + bi_ * 16 + u], X[j * 256 + u * 16 + cc], acc);
+        T[t * (CK + 1) + j * 16 + cc] = -acc;
+      }
+      __syncthreads();
     }
   }
-  __syncthreads();
   // U = T diag(b) V and W = T diag(b G) K: a 4-row x 8-column block per thread.
   {
     const int t4 = (tid / 16) * 4, d8 = (tid % 16) * 8;
@@ -217,103 +250,104 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
 }
 
 // Sequential pass over the chunks for one sequence, head and 16 value
-// columns; the state slice S[128][16] stays in shared memory and each chunk's
-// W, Q, K, masked Q K^T and U slice are staged there before use.
-constexpr int SCAN_LD = DK + 4;  // padded row stride, keeps float4 alignment
+// columns: D = U - W S0 and S_C = G_C S0 + K^T diag(G_C / G) D. The state
+// slice S[128][16] stays in shared memory; chunk c + 1's W, K, U slice and
+// decay are copied in (cp.async) while chunk c is computed. Each chunk's
+// starting state and D go to `states` for the output pass.
+constexpr int SCAN_LD = DK + 4;  // padded row stride, keeps 16-byte alignment
+struct ScanStage {
+  float W[CK][SCAN_LD];
+  float K[CK][SCAN_LD];
+  float U[CK][SC];
+  float rem[CK];
+};
+
+__device__ __forceinline__ void cp16(void* smem, const void* gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+
 __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
-                                                               int chunks) {
+                                                               ChunkState* __restrict__ states, int chunks) {
   extern __shared__ __align__(16) float sm[];
-  float* S = sm;                      // [DK][SC]
-  float* D = S + DK * SC;             // [CK][SC]
-  float* Ws = D + CK * SC;            // [CK][SCAN_LD]
-  float* Qs = Ws + CK * SCAN_LD;      // [CK][SCAN_LD]
-  float* Ks = Qs + CK * SCAN_LD;      // [CK][SCAN_LD]
-  float* QKs = Ks + CK * SCAN_LD;     // [CK][CK + 4]
-  float* Us = QKs + CK * (CK + 4);    // [CK][SC]
-  float* rem = Us + CK * SC;          // [CK]
-  float* gam = rem + CK;              // [CK]
+  float* S = sm;                                            // [DK][SC]
+  float* D = S + DK * SC;                                   // [CK][SC]
+  ScanStage* stg = reinterpret_cast<ScanStage*>(D + CK * SC);  // [2]
   const int tid = threadIdx.x;
   const int groups = a.dv / SC;
   const int slice = blockIdx.x % groups, h = (blockIdx.x / groups) % a.value_heads;
   const size_t bi = blockIdx.x / (groups * a.value_heads);
   const int kh = h / (a.value_heads / a.key_heads), j0 = slice * SC;
-  const float* qb = a.q + bi * a.bs_qkv + kh * DK;
   const float* kb = a.k + bi * a.bs_qkv + kh * DK;
   float* Sg = a.state + bi * a.bs_state + size_t(h) * DK * a.dv;
-  float* ob = a.o + bi * a.bs_o + h * a.dv + j0;
-  for (int e = tid; e < DK * SC; e += 256) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
-  for (int c = 0; c < chunks; ++c) {
-    const ChunkOut& co = outs[(bi * a.value_heads + h) * chunks + c];
+  const size_t head = bi * a.value_heads + h;
+  auto stage = [&](int c, ScanStage& st) {
+    const ChunkOut& co = outs[head * chunks + c];
     const int t0 = c * CK, tn = min(CK, a.n - t0);
-    // Stage the chunk: 4 x [64][128] + [64][64] floats, float4 at a time.
     for (int i = tid; i < CK * (DK / 4); i += 256) {
       const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
-      float4 q4 = make_float4(0, 0, 0, 0), k4 = q4;
-      if (t < tn) {
-        q4 = *reinterpret_cast<const float4*>(qb + size_t(t0 + t) * a.ld_qk + d);
-        k4 = *reinterpret_cast<const float4*>(kb + size_t(t0 + t) * a.ld_qk + d);
-      }
-      *reinterpret_cast<float4*>(Qs + t * SCAN_LD + d) = q4;
-      *reinterpret_cast<float4*>(Ks + t * SCAN_LD + d) = k4;
-      *reinterpret_cast<float4*>(Ws + t * SCAN_LD + d) = *reinterpret_cast<const float4*>(&co.W[t][d]);
-    }
-    for (int i = tid; i < CK * (CK / 4); i += 256) {
-      const int t = i / (CK / 4), s4 = (i % (CK / 4)) * 4;
-      *reinterpret_cast<float4*>(QKs + t * (CK + 4) + s4) = *reinterpret_cast<const float4*>(&co.QK[t][s4]);
+      cp16(&st.W[t][d], &co.W[t][d], 16);
+      // K rows past the sequence are zero-filled (never read from memory).
+      cp16(&st.K[t][d], t < tn ? kb + size_t(t0 + t) * a.ld_qk + d : kb, t < tn ? 16 : 0);
     }
     for (int i = tid; i < CK * (SC / 4); i += 256) {
       const int t = i / (SC / 4), j4 = (i % (SC / 4)) * 4;
-      *reinterpret_cast<float4*>(Us + t * SC + j4) = *reinterpret_cast<const float4*>(&co.U[t][j0 + j4]);
+      cp16(&st.U[t][j4], &co.U[t][j0 + j4], 16);
     }
-    if (tid < CK) {
-      rem[tid] = co.rem[tid];
-      gam[tid] = co.gam[tid];
+    if (tid < CK / 4) cp16(&st.rem[tid * 4], &co.rem[tid * 4], 16);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int e = tid; e < DK * SC; e += 256) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
+  stage(0, stg[0]);
+  for (int c = 0; c < chunks; ++c) {
+    const ScanStage& st = stg[c & 1];
+    ChunkState& cs = states[head * chunks + c];
+    const int t0 = c * CK, tn = min(CK, a.n - t0);
+    if (c + 1 < chunks) {
+      stage(c + 1, stg[(c + 1) & 1]);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
-    const float gC = co.gC;
     __syncthreads();
-    // D = U - W S0 and Y = Q S0 ; thread -> (t, 4 columns)
-    const int t = tid / 4, jc = (tid % 4) * 4;
-    float qs[4] = {0, 0, 0, 0}, ws[4] = {0, 0, 0, 0};
+    // The state this chunk starts from, for the output pass.
+    for (int e = tid; e < DK * (SC / 4); e += 256) {
+      const int i = e / (SC / 4), j4 = (e % (SC / 4)) * 4;
+      *reinterpret_cast<float4*>(&cs.S[i][j0 + j4]) = *reinterpret_cast<const float4*>(S + i * SC + j4);
+    }
+    // D = U - W S0 ; thread -> (t, 4 columns)
+    {
+      const int t = tid / 4, jc = (tid % 4) * 4;
+      float ws[4] = {0, 0, 0, 0};
 #pragma unroll 4
-    for (int i = 0; i < DK; ++i) {
-      const float4 s4 = *reinterpret_cast<const float4*>(S + i * SC + jc);
-      const float w = Ws[t * SCAN_LD + i], q = Qs[t * SCAN_LD + i];
-      ws[0] = __fmaf_rn(w, s4.x, ws[0]); ws[1] = __fmaf_rn(w, s4.y, ws[1]);
-      ws[2] = __fmaf_rn(w, s4.z, ws[2]); ws[3] = __fmaf_rn(w, s4.w, ws[3]);
-      qs[0] = __fmaf_rn(q, s4.x, qs[0]); qs[1] = __fmaf_rn(q, s4.y, qs[1]);
-      qs[2] = __fmaf_rn(q, s4.z, qs[2]); qs[3] = __fmaf_rn(q, s4.w, qs[3]);
-    }
-    {
-      const float4 u4 = *reinterpret_cast<const float4*>(Us + t * SC + jc);
+      for (int i = 0; i < DK; i += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(&st.W[t][i]);
+        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int ii = 0; ii < 4; ++ii) {
+          const float4 s4 = *reinterpret_cast<const float4*>(S + (i + ii) * SC + jc);
+          ws[0] = __fmaf_rn(wv[ii], s4.x, ws[0]); ws[1] = __fmaf_rn(wv[ii], s4.y, ws[1]);
+          ws[2] = __fmaf_rn(wv[ii], s4.z, ws[2]); ws[3] = __fmaf_rn(wv[ii], s4.w, ws[3]);
+        }
+      }
+      const float4 u4 = *reinterpret_cast<const float4*>(&st.U[t][jc]);
       const bool live = t < tn;
-      *reinterpret_cast<float4*>(D + t * SC + jc) =
-          make_float4(live ? u4.x - ws[0] : 0.0f, live ? u4.y - ws[1] : 0.0f, live ? u4.z - ws[2] : 0.0f,
-                      live ? u4.w - ws[3] : 0.0f);
+      const float4 d4 = make_float4(live ? u4.x - ws[0] : 0.0f, live ? u4.y - ws[1] : 0.0f,
+                                    live ? u4.z - ws[2] : 0.0f, live ? u4.w - ws[3] : 0.0f);
+      *reinterpret_cast<float4*>(D + t * SC + jc) = d4;
+      *reinterpret_cast<float4*>(&cs.D[t][j0 + jc]) = d4;
     }
     __syncthreads();
-    // O = diag(G) Q S0 + (M o Q K^T) D
-    {
-      float acc[4];
-      const float gt = gam[t];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[e] = gt * qs[e];
-      for (int s = 0; s <= t; ++s) {
-        const float m = QKs[t * (CK + 4) + s];
-        const float4 d4 = *reinterpret_cast<const float4*>(D + s * SC + jc);
-        acc[0] = __fmaf_rn(m, d4.x, acc[0]); acc[1] = __fmaf_rn(m, d4.y, acc[1]);
-        acc[2] = __fmaf_rn(m, d4.z, acc[2]); acc[3] = __fmaf_rn(m, d4.w, acc[3]);
-      }
-      if (t < tn)
-        *reinterpret_cast<float4*>(ob + size_t(t0 + t) * a.ldo + jc) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-    }
     // S_C = G_C S0 + K^T diag(G_C / G) D ; thread -> (i, 8 columns)
     {
+      const float gC = outs[head * chunks + c].gC;
       const int i = tid / 2, j8 = (tid % 2) * 8;
       float acc[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = gC * S[i * SC + j8 + e];
-      for (int s = 0; s < tn; ++s) {
-        const float kr = Ks[s * SCAN_LD + i] * rem[s];
+#pragma unroll 4
+      for (int s = 0; s < CK; ++s) {
+        const float kr = st.K[s][i] * st.rem[s];
         const float4 d0 = *reinterpret_cast<const float4*>(D + s * SC + j8);
         const float4 d1 = *reinterpret_cast<const float4*>(D + s * SC + j8 + 4);
         acc[0] = __fmaf_rn(kr, d0.x, acc[0]); acc[1] = __fmaf_rn(kr, d0.y, acc[1]);
@@ -321,7 +355,7 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
         acc[4] = __fmaf_rn(kr, d1.x, acc[4]); acc[5] = __fmaf_rn(kr, d1.y, acc[5]);
         acc[6] = __fmaf_rn(kr, d1.z, acc[6]); acc[7] = __fmaf_rn(kr, d1.w, acc[7]);
       }
-      __syncthreads();  // every thread has read the old S
+      __syncthreads();  // every thread has read the old S (and this stage)
 #pragma unroll
       for (int e = 0; e < 8; ++e) S[i * SC + j8 + e] = acc[e];
     }
@@ -330,11 +364,101 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
   for (int e = tid; e < DK * SC; e += 256) Sg[size_t(e / SC) * a.dv + j0 + e % SC] = S[e];
 }
 
+// O = diag(G) Q S0 + (M o Q K^T) D for one chunk, head and 64 value columns,
+// all chunks in parallel once the scan has produced every S0 and D.
+// Thread -> 4 rows x 4 columns (columns strided by 16: conflict-free loads).
+constexpr int OUT_COLS = 64, OQ_LD = DK + 4, OS_LD = OUT_COLS + 4, OK_LD = CK + 4;
+__global__ void __launch_bounds__(256) delta_chunk_out_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
+                                                              const ChunkState* __restrict__ states, int chunks) {
+  extern __shared__ __align__(16) float sm[];
+  float* Qs = sm;                    // [CK][OQ_LD]
+  float* Ss = Qs + CK * OQ_LD;       // [DK][OS_LD]
+  float* QKs = Ss + DK * OS_LD;      // [CK][OK_LD]
+  float* Ds = QKs + CK * OK_LD;      // [CK][OS_LD]
+  const int tid = threadIdx.x;
+  const int halves = a.dv / OUT_COLS;
+  const int part = blockIdx.x % halves, c = (blockIdx.x / halves) % chunks;
+  const int h = (blockIdx.x / (halves * chunks)) % a.value_heads;
+  const size_t bi = blockIdx.x / (halves * chunks * a.value_heads);
+  const int kh = h / (a.value_heads / a.key_heads), j0 = part * OUT_COLS;
+  const int t0 = c * CK, tn = min(CK, a.n - t0);
+  const size_t head = bi * a.value_heads + h;
+  const ChunkOut& co = outs[head * chunks + c];
+  const ChunkState& cs = states[head * chunks + c];
+  const float* qb = a.q + bi * a.bs_qkv + kh * DK;
+  for (int i = tid; i < CK * (DK / 4); i += 256) {
+    const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
+    cp16(Qs + t * OQ_LD + d, t < tn ? qb + size_t(t0 + t) * a.ld_qk + d : qb, t < tn ? 16 : 0);
+  }
+  for (int i = tid; i < DK * (OUT_COLS / 4); i += 256) {
+    const int r = i / (OUT_COLS / 4), j4 = (i % (OUT_COLS / 4)) * 4;
+    cp16(Ss + r * OS_LD + j4, &cs.S[r][j0 + j4], 16);
+  }
+  for (int i = tid; i < CK * (CK / 4); i += 256) {
+    const int t = i / (CK / 4), s4 = (i % (CK / 4)) * 4;
+    cp16(QKs + t * OK_LD + s4, &co.QK[t][s4], 16);
+    cp16(Ds + t * OS_LD + s4, &cs.D[t][j0 + s4], 16);  // OUT_COLS == CK
+  }
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  const int rg = tid / 16, cg = tid % 16, r0 = rg * 4;
+  float acc[4][4], y[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = y[i][e] = 0.0f;
+#pragma unroll 2
+  for (int k = 0; k < DK; k += 4) {
+    float4 q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = *reinterpret_cast<const float4*>(Qs + (r0 + i) * OQ_LD + k);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      float sv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sv[e] = Ss[(k + kk) * OS_LD + cg + 16 * e];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float qv = kk == 0 ? q[i].x : kk == 1 ? q[i].y : kk == 2 ? q[i].z : q[i].w;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[i][e] = __fmaf_rn(qv, sv[e], y[i][e]);
+      }
+    }
+  }
+#pragma unroll 2
+  for (int s = 0; s < CK; s += 4) {
+    float4 m[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) m[i] = *reinterpret_cast<const float4*>(QKs + (r0 + i) * OK_LD + s);
+#pragma unroll
+    for (int ss = 0; ss < 4; ++ss) {
+      float dv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dv[e] = Ds[(s + ss) * OS_LD + cg + 16 * e];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float mv = ss == 0 ? m[i].x : ss == 1 ? m[i].y : ss == 2 ? m[i].z : m[i].w;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = __fmaf_rn(mv, dv[e], acc[i][e]);
+      }
+    }
+  }
+  float* ob = a.o + bi * a.bs_o + h * a.dv + j0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = r0 + i;
+    if (t >= tn) continue;
+    const float g = co.gam[t];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ob[size_t(t0 + t) * a.ldo + cg + 16 * e] = __fmaf_rn(g, y[i][e], acc[i][e]);
+  }
+}
+
 }  // namespace
 
 size_t delta_chunk_workspace_bytes(int batch, int heads, int n) {
   const int chunks = (n + CK - 1) / CK;
-  return size_t(batch) * heads * chunks * sizeof(ChunkOut);
+  return size_t(batch) * heads * chunks * (sizeof(ChunkOut) + sizeof(ChunkState));
 }
 
 void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s) {
@@ -344,21 +468,29 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   const int chunks = (a.n + CK - 1) / CK;
   if (workspace_bytes < delta_chunk_workspace_bytes(batch, a.value_heads, a.n))
     throw CudaError("delta_chunked: workspace too small");
-  if (a.ld_qk % 4 || a.ld_v % 4) throw CudaError("delta_chunked: rows must be 16-byte aligned");
+  if (a.ld_qk % 4 || a.ld_v % 4 || a.ldo % 4 || reinterpret_cast<uintptr_t>(workspace) % 16 ||
+      reinterpret_cast<uintptr_t>(a.q) % 16 || reinterpret_cast<uintptr_t>(a.k) % 16)
+    throw CudaError("delta_chunked: rows must be 16-byte aligned");
+  const size_t units = size_t(batch) * a.value_heads * chunks;
   ChunkOut* outs = static_cast<ChunkOut*>(workspace);
-  const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK) * sizeof(float);
-  const int scan_smem =
-      (DK * SC + CK * SC + 3 * CK * SCAN_LD + CK * (CK + 4) + CK * SC + 2 * CK) * sizeof(float);
+  ChunkState* states = reinterpret_cast<ChunkState*>(outs + units);
+  const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK + (CK / 16 - 1) * 256) * sizeof(float);
+  const int scan_smem = (DK * SC + CK * SC) * sizeof(float) + 2 * sizeof(ScanStage);
+  const int out_smem = (CK * OQ_LD + DK * OS_LD + CK * OK_LD + CK * OS_LD) * sizeof(float);
   static bool configured = false;
   if (!configured) {
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, scan_smem));
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, out_smem));
     configured = true;
   }
-  delta_chunk_prep_kernel<<<batch * a.value_heads * chunks, 256, prep_smem, s>>>(a, outs, chunks);
+  delta_chunk_prep_kernel<<<int(units), 256, prep_smem, s>>>(a, outs, chunks);
   DG_CUDA(cudaGetLastError());
-  delta_chunk_scan_kernel<<<batch * a.value_heads * (a.dv / SC), 256, scan_smem, s>>>(a, outs, chunks);
+  delta_chunk_scan_kernel<<<batch * a.value_heads * (a.dv / SC), 256, scan_smem, s>>>(a, outs, states, chunks);
+  DG_CUDA(cudaGetLastError());
+  delta_chunk_out_kernel<<<int(units) * (a.dv / OUT_COLS), 256, out_smem, s>>>(a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
 }
 
 }  // namespace dg
+

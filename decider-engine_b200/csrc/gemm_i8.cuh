@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(576, 1)
     tmem_alloc(tmem_holder, S::TMEM_COLS);
     tmem_relinquish();
   }
-  if (R > 0 && warp >= S::EPI_WARP0) {
+  if constexpr (R > 0) if (warp >= S::EPI_WARP0) {
     // This tile's LoRA-B rows [BN][R], transposed to [R][BT_LD].
     const float4* src = reinterpret_cast<const float4*>(p.lora_b + size_t(n0) * R);
     for (int i = threadIdx.x - S::EPI_WARP0 * 32; i < BN * R / 4; i += S::EPI_THREADS) {

@@ -127,8 +127,9 @@ def test_small_model_takes_the_tcgen05_path_and_matches_oracle(oracle_mod, small
     assert np.abs(lg - lo).max() < 1e-2 * max(1.0, np.abs(lo).max())
 
 
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
 @pytest.mark.parametrize("lt", ["linear_attention", "full_attention"])
-def test_small_model_single_layer_teacher_forced(oracle_mod, lt):
+def test_small_model_single_layer_teacher_forced(oracle_mod, lt, exact):
     """One DeltaNet layer and one attention layer as 1-layer models (identical
     inputs on both sides). Rows whose activations sit within FP32 rounding of
     an int8 rounding boundary flip one quantised value (a ~1e-3 row error, the
@@ -138,6 +139,7 @@ def test_small_model_single_layer_teacher_forced(oracle_mod, lt):
     c1 = small_config(layer_types=(lt,))
     t1 = random_tensors(c1, rank=32, pointer_dim=64, seed=11)
     m = _gpu_small(c1, t1)
+    m.set_exact(exact)  # FMA mode also runs the chunked DeltaNet
     ids = np.random.default_rng(4).integers(0, c1["vocab_size"], 257)
     exp, noise = _noise_sensitivity(oracle_mod, c1, t1, ids)
     got = m.forward(ids)
@@ -159,14 +161,26 @@ def test_small_model_prefix_continuation_is_bit_exact(small):
         assert np.array_equal(m.forward_after(p, ids[split:]), full[split:]), split
 
 
-def test_fma_promotion_mode_tracks_reference_order_mode(small):
-    """The engine's fused-multiply-add promotion (the benchmark mode) stays
-    within the int8-flip noise of the reference-order mode."""
+def test_fma_promotion_mode_tracks_reference_order_mode(oracle_mod, small):
+    """The engine's fused-multiply-add mode (the benchmark mode: FMA promotion,
+    split-K LoRA-A, chunked DeltaNet) stays within the int8-flip noise of the
+    reference-order mode, measured as the oracle's own row-wise movement under
+    1e-7 input noise over the same 4-layer stack."""
     cfg, tensors = small
     m = _gpu_small(cfg, tensors)
     ids = np.random.default_rng(8).integers(0, cfg["vocab_size"], 200)
     exact = m.forward(ids)
     m.set_exact(False)
     fast = m.forward(ids)
-    assert rel_err(fast, exact) < 5e-3
-    assert np.median(_row_errors(fast, exact)) < 1e-3
+    base, noise = _noise_sensitivity(oracle_mod, cfg, tensors, ids)
+    t2 = dict(tensors)
+    code, shp, arr = t2["embed_tokens.weight"]
+    rng = np.random.default_rng(9)
+    t2["embed_tokens.weight"] = (code, shp, (arr * (1 + 1e-7 * rng.standard_normal(arr.shape))).astype(np.float32))
+    moved = oracle_mod.OracleModel(cfg, t2, "int8-compute", 32, 2.0).forward(ids)
+    floor = np.median(_row_errors(moved, base))
+    med = np.median(_row_errors(fast, exact))
+    print(f"fma vs reference order: normwise {rel_err(fast, exact):.3e} (floor {noise:.3e}), "
+          f"median row {med:.3e} (floor {floor:.3e})")
+    assert rel_err(fast, exact) < max(5e-3, 4 * noise)
+    assert med < max(1e-3, 4 * floor)
