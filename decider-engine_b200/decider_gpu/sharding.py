@@ -1,0 +1,82 @@
+"""Request sharding across GPUs: one engine replica per rank, no collective on
+the data path.
+
+Requests are independent in the reference: `NativeEngine::evaluate` shares a
+prefix only among the questions of one request (src/lib.rs:477-559), and
+nothing crosses requests. A batch is therefore split by request. Each rank
+owns a replica and runs its share, and rank 0 gathers the answers in request
+order.
+
+The split is longest-processing-time first on the cost model
+`a * tokens + b * length**2`: computed tokens (the shared prefix once plus
+every question) plus the attention term of the longest window. Every rank
+computes the same plan from the same inputs, so no plan is exchanged.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Sequence
+
+
+@dataclass(frozen=True)
+class RequestShape:
+    """Token counts of one request: its shared prefix and each question's suffix."""
+    prefix: int
+    questions: tuple
+
+    @property
+    def tokens(self) -> int:
+        return self.prefix + sum(self.questions)
+
+    @property
+    def window(self) -> int:
+        return self.prefix + (max(self.questions) if self.questions else 0)
+
+
+def request_cost(shape: RequestShape, a: float = 1.0, b: float = 1.0 / 4096) -> float:
+    """Cost in token-equivalents; b = 1/4096 weighs one full 4096-token window's
+    attention like 4096 more tokens."""
+    return a * shape.tokens + b * shape.window * shape.window
+
+
+def shard_requests(costs: Sequence[float], world: int) -> list:
+    """Longest-processing-time assignment of request indices to `world` ranks.
+
+    Deterministic: ties are broken by request index, then by rank. Each rank's
+    list is in request order. The makespan is within 4/3 - 1/(3 world) of the
+    optimum (Graham's bound for LPT).
+    """
+    if world <= 0:
+        raise ValueError("world size must be positive")
+    order = sorted(range(len(costs)), key=lambda i: (-float(costs[i]), i))
+    loads = [0.0] * world
+    plan = [[] for _ in range(world)]
+    for i in order:
+        r = min(range(world), key=lambda k: (loads[k], k))
+        plan[r].append(i)
+        loads[r] += float(costs[i])
+    return [sorted(p) for p in plan]
+
+
+def run_sharded(requests: Sequence, shapes: Sequence[RequestShape], run: Callable, dist=None):
+    """Runs `run(request)` for this rank's share and gathers every answer on
+    rank 0 (None on the other ranks). `dist` is `torch.distributed` with an
+    initialised process group, or None for a single process.
+
+    The gather is the only collective: one object gather after all of a rank's
+    requests are done, never inside the device work.
+    """
+    world = dist.get_world_size() if dist is not None else 1
+    rank = dist.get_rank() if dist is not None else 0
+    plan = shard_requests([request_cost(s) for s in shapes], world)
+    mine = {i: run(requests[i]) for i in plan[rank]}
+    if dist is None:
+        return [mine[i] for i in range(len(requests))]
+    gathered = [None] * world if rank == 0 else None
+    dist.gather_object(mine, gathered, dst=0)
+    if rank != 0:
+        return None
+    merged = {}
+    for part in gathered:
+        merged.update(part)
+    return [merged[i] for i in range(len(requests))]
