@@ -74,17 +74,23 @@ __global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __res
                                                               float* __restrict__ n_out, int ldn,
                                                               int8_t* __restrict__ xq, float* __restrict__ xs,
                                                               int ldxs, DeviceStatus* st) {
-  const int m = blockIdx.x * 8 + threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
   if (m >= M) return;
   const float4* xr = reinterpret_cast<const float4*>(x + size_t(m) * ldx);
   const int nv = K / 128;
   bool bad = false;
   if (NV > 0) {
-    float4 v[NV > 0 ? NV : 1];
-    float ss = 0.0f;
+    // The row and gamma are loaded up front so every load is in flight at once.
+    float4 v[NV > 0 ? NV : 1], gv[NV > 0 ? NV : 1];
+    const float4* g4 = reinterpret_cast<const float4*>(gamma);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       v[i] = xr[lane + 32 * i];
+      gv[i] = __ldg(g4 + lane + 32 * i);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
       ss = __fmaf_rn(v[i].x, v[i].x, ss);
       ss = __fmaf_rn(v[i].y, v[i].y, ss);
       ss = __fmaf_rn(v[i].z, v[i].z, ss);
@@ -93,10 +99,9 @@ __global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __res
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     const float inv = 1.0f / sqrtf(ss / float(K) + eps);
-    const float4* g4 = reinterpret_cast<const float4*>(gamma);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const float4 g = g4[lane + 32 * i];
+      const float4 g = gv[i];
       v[i].x = v[i].x * (inv * (1.0f + g.x));
       v[i].y = v[i].y * (inv * (1.0f + g.y));
       v[i].z = v[i].z * (inv * (1.0f + g.z));
@@ -554,7 +559,8 @@ void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma
     norm_quant_warp_kernel<0><<<dim3(blocks, (K / 128 + 3) / 4), 256, 0, s>>>(x, ldx, M, K, nullptr, eps, n_out, ldn,
                                                                             xq, xs, ldxs, st);
   } else if (aligned && gamma && K == 2048) {
-    norm_quant_warp_kernel<16><<<blocks, 256, 0, s>>>(x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+    // Two rows (warps) per CTA: 256 CTAs at 512 tokens spread over every SM.
+    norm_quant_warp_kernel<16><<<(M + 1) / 2, 64, 0, s>>>(x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
   } else {
     norm_quant_kernel<<<M, 256, K * sizeof(float), s>>>(x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
   }

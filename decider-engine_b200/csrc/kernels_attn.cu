@@ -193,6 +193,175 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
   }
 }
 
+// Flash-style causal attention for head_dim 256, FP32, register-tiled. CTA: 32
+// query rows of one head; key blocks of 64 staged in shared memory by cp.async
+// (the next block's K is copied in during this block's softmax and P·V, its V
+// during the next Q·Kᵀ). Thread (rg, kg) = (tid / 16, tid % 16) owns rows
+// 2rg, 2rg + 1: scores against keys kg + 16 j (j < 4), outputs in columns
+// 4 kg + 64 j .. + 3. Online softmax per row across its 16 threads; output
+// multiplied by sigmoid(gate) (src/qwen.rs:581-583). The heaviest (last) row
+// blocks are scheduled first.
+constexpr int TQ = 32, TK = 64, TLD = AD + 4, PLD = TQ + 4;
+constexpr int ATT_SMEM = (TQ * TLD + TK * TLD + TK * AD + TK * PLD) * 4;
+
+__device__ __forceinline__ void att_cp16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void att_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void att_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __restrict__ q,
+                                                                 const float* __restrict__ kc,
+                                                                 const float* __restrict__ vc,
+                                                                 const float* __restrict__ gate_src, int ld_gate,
+                                                                 int n, int offset, int heads, int kv_heads,
+                                                                 float* __restrict__ out) {
+  extern __shared__ __align__(16) float sm[];
+  float* Qs = sm;               // [TQ][TLD]
+  float* Ks = Qs + TQ * TLD;    // [TK][TLD]
+  float* Vs = Ks + TK * TLD;    // [TK][AD]
+  float* PT = Vs + TK * AD;     // [TK][PLD]: probabilities, key-major
+  const int nrb = (n + TQ - 1) / TQ;
+  const int rb = nrb - 1 - int(blockIdx.x), h = blockIdx.y, kh = h / (heads / kv_heads);
+  const int t0 = rb * TQ, tid = threadIdx.x, rg = tid / 16, kg = tid % 16;
+  const int kw = kv_heads * AD, L = offset + n;
+  const int last_key = min(L - 1, offset + t0 + TQ - 1), nkb = last_key / TK + 1;
+  const float scale = 1.0f / sqrtf(float(AD));
+  auto load_rows = [&](float* dst, int ld, const float* src, int row0, int rows, int limit) {
+    for (int i = tid; i < rows * (AD / 4); i += 256) {
+      const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, s = row0 + r;
+      att_cp16(dst + r * ld + c, s < limit ? src + size_t(s) * kw + kh * AD + c : src, s < limit);
+    }
+  };
+  for (int i = tid; i < TQ * (AD / 4); i += 256) {
+    const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, t = t0 + r;
+    att_cp16(Qs + r * TLD + c, t < n ? q + (size_t(t) * heads + h) * AD + c : q, t < n);
+  }
+  load_rows(Ks, TLD, kc, 0, TK, L);
+  att_commit();
+  load_rows(Vs, AD, vc, 0, TK, L);
+  att_commit();
+  float o[2][16], mrow[2], lrow[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    mrow[i] = -INFINITY;
+    lrow[i] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o[i][e] = 0.0f;
+  }
+  for (int kb = 0; kb < nkb; ++kb) {
+    const int k0 = kb * TK;
+    att_wait<1>();  // this block's K (and Q) have landed
+    __syncthreads();
+    float sc[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+#pragma unroll 4
+    for (int c = 0; c < AD; c += 4) {
+      float4 qv[2], kv[4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (2 * rg + i) * TLD + c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (kg + 16 * j) * TLD + c);
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          sc[i][j] = __fmaf_rn(qv[i].x, kv[j].x, sc[i][j]);
+          sc[i][j] = __fmaf_rn(qv[i].y, kv[j].y, sc[i][j]);
+          sc[i][j] = __fmaf_rn(qv[i].z, kv[j].z, sc[i][j]);
+          sc[i][j] = __fmaf_rn(qv[i].w, kv[j].w, sc[i][j]);
+        }
+    }
+    __syncthreads();  // every thread is done with Ks
+    if (kb + 1 < nkb) {
+      load_rows(Ks, TLD, kc, k0 + TK, TK, L);
+      att_commit();
+      att_wait<1>();  // this block's V has landed
+    } else {
+      att_wait<0>();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = t0 + 2 * rg + i;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int key = k0 + kg + 16 * j;
+        float s = sc[i][j] * scale;
+        if (key > offset + t || key >= L) s = -INFINITY;
+        sc[i][j] = s;
+        mx = fmaxf(mx, s);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mnew = fmaxf(mrow[i], mx);
+      float psum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - mnew);
+        PT[(kg + 16 * j) * PLD + 2 * rg + i] = p;
+        psum += p;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+      const float corr = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mnew);
+      lrow[i] = lrow[i] * corr + psum;
+      mrow[i] = mnew;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) o[i][e] *= corr;
+    }
+    __syncthreads();  // PT and this block's V are visible
+    const int nk = min(TK, last_key + 1 - k0);
+#pragma unroll 4
+    for (int s = 0; s < nk; ++s) {
+      const float2 p = *reinterpret_cast<const float2*>(PT + s * PLD + 2 * rg);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(Vs + s * AD + 4 * kg + 64 * j);
+        o[0][4 * j + 0] = __fmaf_rn(p.x, v.x, o[0][4 * j + 0]);
+        o[0][4 * j + 1] = __fmaf_rn(p.x, v.y, o[0][4 * j + 1]);
+        o[0][4 * j + 2] = __fmaf_rn(p.x, v.z, o[0][4 * j + 2]);
+        o[0][4 * j + 3] = __fmaf_rn(p.x, v.w, o[0][4 * j + 3]);
+        o[1][4 * j + 0] = __fmaf_rn(p.y, v.x, o[1][4 * j + 0]);
+        o[1][4 * j + 1] = __fmaf_rn(p.y, v.y, o[1][4 * j + 1]);
+        o[1][4 * j + 2] = __fmaf_rn(p.y, v.z, o[1][4 * j + 2]);
+        o[1][4 * j + 3] = __fmaf_rn(p.y, v.w, o[1][4 * j + 3]);
+      }
+    }
+    __syncthreads();  // every thread is done with Vs and PT
+    if (kb + 1 < nkb) {
+      load_rows(Vs, AD, vc, k0 + TK, TK, L);
+      att_commit();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = t0 + 2 * rg + i;
+    if (t >= n) continue;
+    const float inv = 1.0f / lrow[i];
+    const float* g = gate_src + size_t(t) * ld_gate + size_t(h) * 2 * AD + AD;
+    float* dst = out + (size_t(t) * heads + h) * AD;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = 4 * kg + 64 * j;
+      float4 r;
+      r.x = (o[i][4 * j + 0] * inv) * sigmoid_f(g[c + 0]);
+      r.y = (o[i][4 * j + 1] * inv) * sigmoid_f(g[c + 1]);
+      r.z = (o[i][4 * j + 2] * inv) * sigmoid_f(g[c + 2]);
+      r.w = (o[i][4 * j + 3] * inv) * sigmoid_f(g[c + 3]);
+      *reinterpret_cast<float4*>(dst + c) = r;
+    }
+  }
+}
+
 // Generic causal attention (any head_dim): one thread per (token, head),
 // reference order (causal_attention, src/qwen.rs:610-629) with the scores
 // recomputed per pass instead of buffered.
@@ -326,7 +495,19 @@ void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_hea
 void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src, int ld_gate,
                       int n, int offset, int heads, int kv_heads, int d, float* out, cudaStream_t s) {
   if (n <= 0) return;
-  if (d == AD) {
+  const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(kcache) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(vcache) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (d == AD && aligned) {
+    static bool configured = false;
+    if (!configured) {
+      DG_CUDA(cudaFuncSetAttribute(attention256_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   ATT_SMEM));
+      configured = true;
+    }
+    dim3 grid((n + TQ - 1) / TQ, heads);
+    attention256_tiled_kernel<<<grid, 256, ATT_SMEM, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
+                                                          kv_heads, out);
+  } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
     static bool configured = false;
     if (!configured) {
