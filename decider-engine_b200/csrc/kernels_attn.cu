@@ -2,7 +2,11 @@
 // final norm, and the pointer head (src/qwen.rs:530-643, src/lib.rs:106-131).
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "launch.h"
+
+namespace cg = cooperative_groups;
 
 namespace dg {
 
@@ -193,16 +197,19 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
   }
 }
 
-// Flash-style causal attention for head_dim 256, FP32, register-tiled. CTA: 32
-// query rows of one head; key blocks of 64 staged in shared memory by cp.async
-// (the next block's K is copied in during this block's softmax and P·V, its V
-// during the next Q·Kᵀ). Thread (rg, kg) = (tid / 16, tid % 16) owns rows
-// 2rg, 2rg + 1: scores against keys kg + 16 j (j < 4), outputs in columns
-// 4 kg + 64 j .. + 3. Online softmax per row across its 16 threads; output
-// multiplied by sigmoid(gate) (src/qwen.rs:581-583). The heaviest (last) row
-// blocks are scheduled first.
-constexpr int TQ = 32, TK = 64, TLD = AD + 4, PLD = TQ + 4;
-constexpr int ATT_SMEM = (TQ * TLD + TK * TLD + TK * AD + TK * PLD) * 4;
+// Flash-style causal attention for head_dim 256, FP32, register-tiled, with
+// the key blocks of each 32-row query block dealt alternately to a cluster of
+// two CTAs.
+// Each CTA stages key blocks of 32 in shared memory with cp.async (the next
+// block's K is copied in during this block's softmax and P·V, its V during the
+// next Q·Kᵀ). Thread (rg, kg) = (tid / 16, tid % 16) owns rows 2rg, 2rg + 1:
+// scores against keys kg and kg + 16 of a block, outputs in columns
+// 4 kg + 64 j .. + 3. Online softmax per row across its 16 threads. CTA 1 of
+// the pair leaves its unnormalised (m, l, o) in shared memory; CTA 0 reads them
+// through distributed shared memory, merges, divides and multiplies by
+// sigmoid(gate) (src/qwen.rs:581-583). Heavy (late) query blocks go first.
+constexpr int TQ = 32, TK = 32, TLD = AD + 4, PLD = TQ + 4;
+constexpr int ATT_SMEM = (TQ * TLD + TK * TLD + TK * AD + TK * PLD + 2 * TQ) * 4;
 
 __device__ __forceinline__ void att_cp16(void* smem, const void* gmem, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem),
@@ -215,36 +222,43 @@ __device__ __forceinline__ void att_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __restrict__ q,
-                                                                 const float* __restrict__ kc,
-                                                                 const float* __restrict__ vc,
-                                                                 const float* __restrict__ gate_src, int ld_gate,
-                                                                 int n, int offset, int heads, int kv_heads,
-                                                                 float* __restrict__ out) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
+    attention256_split_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                              const float* __restrict__ gate_src, int ld_gate, int n, int offset, int heads,
+                              int kv_heads, float* __restrict__ out) {
   extern __shared__ __align__(16) float sm[];
   float* Qs = sm;               // [TQ][TLD]
-  float* Ks = Qs + TQ * TLD;    // [TK][TLD]
+  float* Ks = Qs + TQ * TLD;    // [TK][TLD]; at the end CTA 1's o [TQ][TLD]
   float* Vs = Ks + TK * TLD;    // [TK][AD]
   float* PT = Vs + TK * AD;     // [TK][PLD]: probabilities, key-major
+  float* ML = PT + TK * PLD;    // [2][TQ]: CTA 1's running max and sum
+  cg::cluster_group cluster = cg::this_cluster();
+  const int part = int(cluster.block_rank());
   const int nrb = (n + TQ - 1) / TQ;
-  const int rb = nrb - 1 - int(blockIdx.x), h = blockIdx.y, kh = h / (heads / kv_heads);
+  const int rb = nrb - 1 - int(blockIdx.x / 2), h = blockIdx.y, kh = h / (heads / kv_heads);
   const int t0 = rb * TQ, tid = threadIdx.x, rg = tid / 16, kg = tid % 16;
   const int kw = kv_heads * AD, L = offset + n;
   const int last_key = min(L - 1, offset + t0 + TQ - 1), nkb = last_key / TK + 1;
+  // CTA `part` takes key blocks part, part + 2, ...: every query row sees the
+  // same split and merge whatever block it sits in, so a prefix continuation
+  // reproduces the full forward bit for bit.
+  const int kb_begin = part, kb_end = nkb;
   const float scale = 1.0f / sqrtf(float(AD));
-  auto load_rows = [&](float* dst, int ld, const float* src, int row0, int rows, int limit) {
-    for (int i = tid; i < rows * (AD / 4); i += 256) {
+  auto load_rows = [&](float* dst, int ld, const float* src, int row0) {
+    for (int i = tid; i < TK * (AD / 4); i += 256) {
       const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, s = row0 + r;
-      att_cp16(dst + r * ld + c, s < limit ? src + size_t(s) * kw + kh * AD + c : src, s < limit);
+      att_cp16(dst + r * ld + c, s < L ? src + size_t(s) * kw + kh * AD + c : src, s < L);
     }
   };
   for (int i = tid; i < TQ * (AD / 4); i += 256) {
     const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, t = t0 + r;
     att_cp16(Qs + r * TLD + c, t < n ? q + (size_t(t) * heads + h) * AD + c : q, t < n);
   }
-  load_rows(Ks, TLD, kc, 0, TK, L);
-  att_commit();
-  load_rows(Vs, AD, vc, 0, TK, L);
+  if (kb_begin < kb_end) {
+    load_rows(Ks, TLD, kc, kb_begin * TK);
+    att_commit();
+    load_rows(Vs, AD, vc, kb_begin * TK);
+  }
   att_commit();
   float o[2][16], mrow[2], lrow[2];
 #pragma unroll
@@ -254,26 +268,24 @@ __global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __
 #pragma unroll
     for (int e = 0; e < 16; ++e) o[i][e] = 0.0f;
   }
-  for (int kb = 0; kb < nkb; ++kb) {
+  for (int kb = kb_begin; kb < kb_end; kb += 2) {
     const int k0 = kb * TK;
     att_wait<1>();  // this block's K (and Q) have landed
     __syncthreads();
-    float sc[2][4];
+    float sc[2][2];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) sc[i][j] = 0.0f;
+    for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = 0.0f;
 #pragma unroll 4
     for (int c = 0; c < AD; c += 4) {
-      float4 qv[2], kv[4];
+      float4 qv[2], kv[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) qv[i] = *reinterpret_cast<const float4*>(Qs + (2 * rg + i) * TLD + c);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (kg + 16 * j) * TLD + c);
+      for (int j = 0; j < 2; ++j) kv[j] = *reinterpret_cast<const float4*>(Ks + (kg + 16 * j) * TLD + c);
 #pragma unroll
       for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 2; ++j) {
           sc[i][j] = __fmaf_rn(qv[i].x, kv[j].x, sc[i][j]);
           sc[i][j] = __fmaf_rn(qv[i].y, kv[j].y, sc[i][j]);
           sc[i][j] = __fmaf_rn(qv[i].z, kv[j].z, sc[i][j]);
@@ -281,8 +293,8 @@ __global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __
         }
     }
     __syncthreads();  // every thread is done with Ks
-    if (kb + 1 < nkb) {
-      load_rows(Ks, TLD, kc, k0 + TK, TK, L);
+    if (kb + 2 < kb_end) {
+      load_rows(Ks, TLD, kc, k0 + 2 * TK);
       att_commit();
       att_wait<1>();  // this block's V has landed
     } else {
@@ -293,7 +305,7 @@ __global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __
       const int t = t0 + 2 * rg + i;
       float mx = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 2; ++j) {
         const int key = k0 + kg + 16 * j;
         float s = sc[i][j] * scale;
         if (key > offset + t || key >= L) s = -INFINITY;
@@ -305,7 +317,7 @@ __global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __
       const float mnew = fmaxf(mrow[i], mx);
       float psum = 0.0f;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 2; ++j) {
         const float p = sc[i][j] == -INFINITY ? 0.0f : expf(sc[i][j] - mnew);
         PT[(kg + 16 * j) * PLD + 2 * rg + i] = p;
         psum += p;
@@ -337,29 +349,57 @@ __global__ void __launch_bounds__(256) attention256_tiled_kernel(const float* __
       }
     }
     __syncthreads();  // every thread is done with Vs and PT
-    if (kb + 1 < nkb) {
-      load_rows(Vs, AD, vc, k0 + TK, TK, L);
+    if (kb + 2 < kb_end) {
+      load_rows(Vs, AD, vc, k0 + 2 * TK);
       att_commit();
     }
   }
+  att_wait<0>();
+  // Merge the two key halves: CTA 1 publishes, CTA 0 combines and stores.
+  if (part == 1) {
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int t = t0 + 2 * rg + i;
-    if (t >= n) continue;
-    const float inv = 1.0f / lrow[i];
-    const float* g = gate_src + size_t(t) * ld_gate + size_t(h) * 2 * AD + AD;
-    float* dst = out + (size_t(t) * heads + h) * AD;
+    for (int i = 0; i < 2; ++i) {
+      float* dst = Ks + (2 * rg + i) * TLD;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = 4 * kg + 64 * j;
-      float4 r;
-      r.x = (o[i][4 * j + 0] * inv) * sigmoid_f(g[c + 0]);
-      r.y = (o[i][4 * j + 1] * inv) * sigmoid_f(g[c + 1]);
-      r.z = (o[i][4 * j + 2] * inv) * sigmoid_f(g[c + 2]);
-      r.w = (o[i][4 * j + 3] * inv) * sigmoid_f(g[c + 3]);
-      *reinterpret_cast<float4*>(dst + c) = r;
+      for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4*>(dst + 4 * kg + 64 * j) =
+            make_float4(o[i][4 * j], o[i][4 * j + 1], o[i][4 * j + 2], o[i][4 * j + 3]);
+      if (kg == 0) {
+        ML[2 * rg + i] = mrow[i];
+        ML[TQ + 2 * rg + i] = lrow[i];
+      }
     }
   }
+  cluster.sync();
+  if (part == 0) {
+    const float* rKs = cluster.map_shared_rank(Ks, 1);
+    const float* rML = cluster.map_shared_rank(ML, 1);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int t = t0 + 2 * rg + i;
+      const float m1 = rML[2 * rg + i], l1 = rML[TQ + 2 * rg + i];
+      const float mm = fmaxf(mrow[i], m1);
+      const float a0 = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mm);
+      const float a1 = m1 == -INFINITY ? 0.0f : expf(m1 - mm);
+      const float inv = 1.0f / (lrow[i] * a0 + l1 * a1);
+      if (t >= n) continue;
+      const float* g = gate_src + size_t(t) * ld_gate + size_t(h) * 2 * AD + AD;
+      float* dst = out + (size_t(t) * heads + h) * AD;
+      const float* o1 = rKs + (2 * rg + i) * TLD;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = 4 * kg + 64 * j;
+        const float4 r1 = *reinterpret_cast<const float4*>(o1 + c);
+        float4 r;
+        r.x = ((o[i][4 * j + 0] * a0 + r1.x * a1) * inv) * sigmoid_f(g[c + 0]);
+        r.y = ((o[i][4 * j + 1] * a0 + r1.y * a1) * inv) * sigmoid_f(g[c + 1]);
+        r.z = ((o[i][4 * j + 2] * a0 + r1.z * a1) * inv) * sigmoid_f(g[c + 2]);
+        r.w = ((o[i][4 * j + 3] * a0 + r1.w * a1) * inv) * sigmoid_f(g[c + 3]);
+        *reinterpret_cast<float4*>(dst + c) = r;
+      }
+    }
+  }
+  cluster.sync();  // CTA 1's shared memory stays alive until CTA 0 has read it
 }
 
 // Generic causal attention (any head_dim): one thread per (token, head),
@@ -500,12 +540,12 @@ void launch_attention(const float* q, const float* kcache, const float* vcache, 
   if (d == AD && aligned) {
     static bool configured = false;
     if (!configured) {
-      DG_CUDA(cudaFuncSetAttribute(attention256_tiled_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      DG_CUDA(cudaFuncSetAttribute(attention256_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    ATT_SMEM));
       configured = true;
     }
-    dim3 grid((n + TQ - 1) / TQ, heads);
-    attention256_tiled_kernel<<<grid, 256, ATT_SMEM, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
+    dim3 grid(2 * ((n + TQ - 1) / TQ), heads);  // clusters of two along x
+    attention256_split_kernel<<<grid, 256, ATT_SMEM, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
                                                           kv_heads, out);
   } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
