@@ -190,6 +190,50 @@ int dg_engine_finalize(dg_engine* e) {
   });
 }
 
+int dg_read_checkpoint_config(const char* dir, dg_model_config* cfg, int32_t* layer_types, int max_layers) {
+  return guarded([&] {
+    if (!dir || !cfg || (max_layers > 0 && !layer_types)) throw std::runtime_error("null argument");
+    dg::Config c;
+    int pointer_dim = 0;
+    dg::read_checkpoint_config(dir, c, pointer_dim);
+    if (int(c.layer_types.size()) > max_layers) throw std::runtime_error("layer_types buffer too small");
+    std::copy(c.layer_types.begin(), c.layer_types.end(), layer_types);
+    cfg->hidden_size = c.hidden;
+    cfg->intermediate_size = c.intermediate;
+    cfg->num_hidden_layers = c.layers;
+    cfg->vocab_size = c.vocab;
+    cfg->num_attention_heads = c.heads;
+    cfg->num_key_value_heads = c.kv_heads;
+    cfg->head_dim = c.head_dim;
+    cfg->linear_conv_kernel_dim = c.conv_kernel;
+    cfg->linear_key_head_dim = c.dk;
+    cfg->linear_value_head_dim = c.dv;
+    cfg->linear_num_key_heads = c.key_heads;
+    cfg->linear_num_value_heads = c.value_heads;
+    cfg->rms_norm_eps = c.eps;
+    cfg->rope_theta = c.rope_theta;
+    cfg->partial_rotary_factor = c.partial_rotary;
+    cfg->layer_types = layer_types;
+    cfg->lora_rank = c.rank;
+    cfg->lora_scale = c.lora_scale;
+    cfg->pointer_dim = pointer_dim;
+  });
+}
+
+int dg_engine_load(const char* dir, int precision, int device, int max_tokens, dg_engine** out) {
+  return guarded([&] {
+    if (!dir || !out) throw std::runtime_error("null argument");
+    dg::Config c;
+    int pointer_dim = 0;
+    dg::read_checkpoint_config(dir, c, pointer_dim);
+    std::unique_ptr<dg_engine> e(new dg_engine());
+    e->e.reset(new dg::Engine(c, precision, device, max_tokens));
+    dg::load_checkpoint_tensors(*e->e, dir);
+    e->e->finalize();
+    *out = e.release();
+  });
+}
+
 int dg_engine_fast_path(const dg_engine* e) { return e && e->e && e->e->fast_path() ? 1 : 0; }
 
 int dg_engine_set_exact(dg_engine* e, int exact) {

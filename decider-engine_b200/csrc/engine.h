@@ -178,4 +178,10 @@ class Engine {
   void set_gemm_timing(bool on);
 };
 
+// Checkpoint directory in the reference's layout (loader.cu): the validated
+// model config (rank, LoRA scale, pointer dim included), and the tensors of the
+// three safetensors files streamed into an engine.
+void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim);
+void load_checkpoint_tensors(Engine& e, const std::string& dir);
+
 }  // namespace dg

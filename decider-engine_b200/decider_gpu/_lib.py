@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(PKG_ROOT, "libdecider_gpu.so")
 SYMBOLS = [
     "dg_last_error", "dg_launch_count",
     "dg_engine_create", "dg_engine_set_tensor", "dg_engine_fill_synthetic", "dg_engine_finalize",
+    "dg_engine_load", "dg_read_checkpoint_config",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
@@ -52,6 +53,8 @@ def load() -> C.CDLL:
     L.dg_last_error.restype = C.c_char_p
     L.dg_launch_count.restype = C.c_uint64
     L.dg_engine_create.argtypes = [C.POINTER(ModelConfig), i32, i32, i32, C.POINTER(vp)]
+    L.dg_engine_load.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp)]
+    L.dg_read_checkpoint_config.argtypes = [C.c_char_p, C.POINTER(ModelConfig), C.POINTER(C.c_int32), i32]
     L.dg_engine_set_tensor.argtypes = [vp, C.c_char_p, i32, vp, i32, vp]
     L.dg_engine_fill_synthetic.argtypes = [vp, C.c_uint64, C.c_float]
     L.dg_engine_finalize.argtypes = [vp]

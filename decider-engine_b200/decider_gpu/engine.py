@@ -65,6 +65,17 @@ def text_config_to_struct(cfg: dict, rank: int, scale: float, pointer_dim: int):
     return s, lt
 
 
+def read_checkpoint_config_native(d: str) -> dict:
+    """The library's own reading of a checkpoint's configs (dg_read_checkpoint_config,
+    no device needed), as a dict of the dg_model_config fields."""
+    s = ModelConfig()
+    lt = (C.c_int32 * 4096)()
+    check(load().dg_read_checkpoint_config(d.encode(), C.byref(s), lt, 4096))
+    out = {name: getattr(s, name) for name, _ in ModelConfig._fields_ if name != "layer_types"}
+    out["layer_types"] = [int(lt[i]) for i in range(s.num_hidden_layers)]
+    return out
+
+
 class GpuPrefix:
     """Device-resident, immutable prefix cache (Prefix, src/qwen.rs:509-526)."""
 
@@ -159,6 +170,21 @@ class GpuModel:
         check(load().dg_logits(self.h, None if prefix is None else prefix.h, p, len(ids), pos.ctypes.data,
                                len(pos), out.ctypes.data))
         return out
+
+    @classmethod
+    def load_native(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096):
+        """`from_dir` through the library's own checkpoint loader (dg_engine_load):
+        the C ABI reads the configs and the safetensors files itself."""
+        from .host import read_decider_config, read_text_config
+        m = cls.__new__(cls)
+        m.config = dict(read_text_config(d))
+        m.precision = precision
+        m.pointer_dim = read_decider_config(d)["pointer_dim"]
+        m.hidden = m.config["hidden_size"]
+        h = C.c_void_p()
+        check(load().dg_engine_load(d.encode(), PRECISIONS[precision], device, max_tokens, C.byref(h)))
+        m.h = h.value
+        return m
 
     @classmethod
     def from_dir(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096):

@@ -69,6 +69,19 @@ int dg_engine_fast_path(const dg_engine* e);
 /* 1: tcgen05 promotion in the reference's FP32 order (default); 0: fused multiply-add. */
 int dg_engine_set_exact(dg_engine* e, int exact);
 void dg_engine_free(dg_engine* e);
+/* Model::load + Head::load from a checkpoint directory in the reference's
+ * layout (src/lib.rs:287-367): validates strands_decider_config.json (or
+ * hobson_config.json, src/lib.rs:188-222), base/config.json's text_config
+ * (src/qwen.rs:133-188) and lora/adapter_config.json (src/lib.rs:300-358),
+ * then streams base/model.safetensors (without its "model.language_model."
+ * prefix), lora/adapter_model.safetensors and head.safetensors (prefixed
+ * "head.") into a new engine and finalizes it. Equivalent to
+ * dg_engine_create + dg_engine_set_tensor for every tensor + dg_engine_finalize. */
+int dg_engine_load(const char* dir, int precision, int device, int max_tokens, dg_engine** out);
+/* The validated model config of a checkpoint directory (no device needed):
+ * fills *cfg, with cfg->layer_types pointing at the caller's buffer of
+ * max_layers entries (0 DeltaNet, 1 attention). */
+int dg_read_checkpoint_config(const char* dir, dg_model_config* cfg, int32_t* layer_types, int max_layers);
 /* The engine's CUDA stream (cudaStream_t) for callers that time or order work. */
 void* dg_engine_stream(const dg_engine* e);
 /* Device time (ms) of the last forward's kernels, between the id upload and
