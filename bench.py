@@ -120,7 +120,9 @@ def dist_setup():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=None)
+        import torch
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device(f"cuda:{local}"))
         pg = dist
     return world, rank, local, pg
 
@@ -165,6 +167,14 @@ class CpuSample:
         return (time.perf_counter() - t0) * 6.0
 
 
+def workload_config(args, world):
+    """The `config` object both arms report."""
+    return {"workload": f"cfg2: 2B decider forward ({args.layers} layers, vocab {args.vocab}, LoRA r32) "
+                        "over a 512-token prompt + pointer head, int8-compute",
+            "tokens_per_step": TOKENS, "parallelism": f"dp{world}",
+            "l2": "not flushed: each step streams 1.4 GB of int8 weights, > 126 MB L2"}
+
+
 def run_reference(args, world, rank, local, dist):
     if rank != 0:
         return
@@ -179,10 +189,13 @@ def run_reference(args, world, rank, local, dist):
     value = tokens / sec
     sample = f"oracle port, one 4-layer block x {tokens} tokens per step, x6 for 24 layers"
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": 0,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000 * TOKENS / tokens,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8-compute",
-        "data": "synthetic", "config": {"workload": "cfg2 2B decider forward, 512-token prompt, int8-compute"},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)", "data": "synthetic",
+        "config": workload_config(args, world),
+        "note": "the reference's CPU algorithm (oracle restatement) on rank 0's host cores; the Rust crate "
+                "cannot be built here",
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cs.threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -264,11 +277,7 @@ def run_ours(args, world, rank, local, dist):
         "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)",
         "promotion": "reference-order" if args.exact else "fma", "data": "synthetic",
-        "config": {"workload": f"cfg2: 2B decider forward ({args.layers} layers, vocab {args.vocab}, LoRA r32) "
-                               "over a 512-token prompt + pointer head, int8-compute",
-                   "tokens_per_step": TOKENS, "parallelism": f"dp{world}",
-                   "l2": "not flushed: each step streams 1.4 GB of int8 weights, > 126 MB L2",
-                   "setup_s": round(setup_s, 1)},
+        "config": dict(workload_config(args, world), setup_s=round(setup_s, 1)),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": TOKENS * 4 + 16,
                 "d2h_bytes_per_step": 8, "ms_per_step": e2e_ms},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOP/s",
