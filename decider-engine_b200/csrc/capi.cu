@@ -352,7 +352,7 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
       l->lora_a = up(lora_a, size_t(rank) * k * 4);
     }
     l->status = DevBuf(sizeof(DeviceStatus));
-    make_weight_maps(&l->maps, l->wq.ptr, k, N);
+    make_weight_maps(&l->maps, l->wq.ptr, k, N, rank ? l->lora_b.as<float>() : nullptr, rank);
     DG_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
     *out = l.release();
   });

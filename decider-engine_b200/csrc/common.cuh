@@ -163,6 +163,20 @@ __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, FP32 operands read as TF32, FP32 accumulate.
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tensor core) before a barrier hands them over.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 // Arrive on `bar` once all previously issued tcgen05 MMAs of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
@@ -226,6 +240,15 @@ __host__ __device__ constexpr uint32_t idesc_i8(uint32_t m, uint32_t n) {
   return (2u << 4)            // D format S32
          | (1u << 7)          // A signed 8-bit
          | (1u << 10)         // B signed 8-bit
+         | ((n >> 3) << 17)   // N / 8
+         | ((m >> 4) << 24);  // M / 16
+}
+// Instruction descriptor for kind::tf32: TF32 A and B, F32 accumulator,
+// both operands K-major, M x N tile (M = 128: N % 16 == 0, 16 <= N <= 256).
+__host__ __device__ constexpr uint32_t idesc_tf32(uint32_t m, uint32_t n) {
+  return (1u << 4)            // D format F32
+         | (2u << 7)          // A TF32
+         | (2u << 10)         // B TF32
          | ((n >> 3) << 17)   // N / 8
          | ((m >> 4) << 24);  // M / 16
 }

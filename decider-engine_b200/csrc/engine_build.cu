@@ -72,7 +72,7 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
   d.lora_a = upload(la);
   d.lora_b = upload(lb);
   d.chunk_pid = upload(pid);
-  make_weight_maps(&d.maps, d.wq.ptr, in, N);
+  make_weight_maps(&d.maps, d.wq.ptr, in, N, d.lora_b.as<float>(), R);
   return d;
 }
 

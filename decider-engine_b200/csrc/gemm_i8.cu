@@ -40,9 +40,27 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
   if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
 }
 
-void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n) {
+// Row-major FP32 matrix [rows][ld] (ld >= cols), boxes of box_rows rows x 32
+// columns (128 bytes, the swizzle span), 128-byte swizzled.
+static void make_tmap_f32_rows(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld,
+                               uint32_t box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * 4) % 16 || cols < 32)
+    throw CudaError("TMA operand must be 16-byte aligned with a 16-byte multiple row stride");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {32, box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+                           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw CudaError("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+}
+
+void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n, const float* lora_b, int rank) {
   make_tmap_i8_2d(&maps->bn128, wq, uint64_t(k), uint64_t(n), 128, 128);
   make_tmap_i8_2d(&maps->bn64, wq, uint64_t(k), uint64_t(n), 128, 64);
+  maps->has_lb = lora_b != nullptr && rank == 32;
+  if (maps->has_lb) make_tmap_f32_rows(&maps->lb, lora_b, 32, uint64_t(n), 32, 16);
 }
 
 // Cost model: a CTA's time grows with its tile width plus a fixed share
@@ -81,10 +99,23 @@ void launch_gemm_i8(const CUtensorMap& a, const WeightMaps& w, const GemmArgs& a
   if (epi == kEpiSwiGlu ? (args.ldo % 4) : (args.ldo % 4 || args.ldo < args.N))
     throw CudaError("gemm_i8: output stride must be a multiple of 4 covering the tile");
   const int bn = gemm_i8_choose_bn(args.M, args.N, epi);
+  // The tensor-core LoRA path (fast mode, rank 32, 128-column tiles) reads the
+  // LoRA rows through tensor maps.
+  CUtensorMap none{}, mid{};
+  const CUtensorMap* lb = &none;
+  const CUtensorMap* mp = &none;
+  if (rank == 32 && !exact && bn == 128) {
+    if (!w.has_lb) throw CudaError("gemm_i8: the LoRA-B tensor map is missing");
+    if (args.ld_mid < 32) throw CudaError("gemm_i8: LoRA-A rows narrower than one part");
+    make_tmap_f32_rows(&mid, args.lora_mid, uint64_t(args.ld_mid), uint64_t(args.M), uint64_t(args.ld_mid), 128);
+    lb = &w.lb;
+    mp = &mid;
+  }
+  const GemmMaps m{&a, bn == 64 ? &w.bn64 : &w.bn128, lb, mp};
   if (bn == 64)
-    launch_gemm_i8_bn64(a, w.bn64, args, rank, epi, exact, s);
+    launch_gemm_i8_bn64(m, args, rank, epi, exact, s);
   else
-    launch_gemm_i8_bn128(a, w.bn128, args, rank, epi, exact, s);
+    launch_gemm_i8_bn128(m, args, rank, epi, exact, s);
 }
 
 }  // namespace dg

@@ -70,7 +70,7 @@ struct GemmShape {
   static constexpr int BT_LD = BN + 4;
   static constexpr int BT_OFF = RING;
   static constexpr int CW = BN / 16, HW = CW / 2;  // epilogue: columns per thread, per half
-  static_assert((2 * STAGES + 2 * NPAIR + 1) * 8 + 8 <= 256, "barrier area");
+  static_assert((2 * STAGES + 2 * NPAIR + 3) * 8 + 8 <= 256, "barrier area");
   __host__ __device__ static constexpr int bt_bytes(int R) { return R * BT_LD * 4; }
   __host__ __device__ static constexpr int bar_off(int R) { return BT_OFF + bt_bytes(R); }
   __host__ __device__ static constexpr int smem_bytes(int R) { return bar_off(R) + 256 + 1024; }
@@ -112,14 +112,64 @@ __device__ __forceinline__ void lds_vec(const float* p, float (&v)[HW]) {
   }
 }
 
+// LoRA-B on the tensor cores (fast mode, 128-column tiles): the tile's
+// 16-column chunks grouped by LoRA part, so each part is one MMA of N = 16 x
+// its chunk count. slot[c] is chunk c's position in that order; part p owns
+// slots [run[p], run[p + 1]).
+struct LoraPlan {
+  int nparts;
+  int pid[4];
+  int slot[8];
+  int run[5];
+};
+__device__ __forceinline__ LoraPlan lora_plan(const int* chunk_pid, int n0) {
+  LoraPlan pl;
+  int cp[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) cp[c] = chunk_pid[(n0 >> 4) + c];
+  pl.nparts = 0;
+  // Distinct parts in ascending order (at most four: the fused groups have <= 4).
+  int last = -1;
+  for (int k = 0; k < 4; ++k) {
+    int best = 1 << 30;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (cp[c] > last && cp[c] < best) best = cp[c];
+    if (best == (1 << 30)) break;
+    pl.pid[pl.nparts++] = best;
+    last = best;
+  }
+  int s = 0;
+  for (int k = 0; k < pl.nparts; ++k) {
+    pl.run[k] = s;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (cp[c] == pl.pid[k]) pl.slot[c] = s++;
+  }
+  pl.run[pl.nparts] = s;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    if (cp[c] > last) pl.slot[c] = 0;  // parts beyond four are not staged (not produced by the fused groups)
+  return pl;
+}
+
 // DUMP: also write the raw int32 group dots to p.dots (parity checks only).
+// map_lb / map_mid (LoRA-B rows [N][32] and LoRA-A rows [M][ld_mid], FP32,
+// 128-byte swizzle) are read only by the tensor-core LoRA path.
 template <int BN, int R, int EPI, bool EXACT, bool DUMP>
 __global__ void __launch_bounds__(576, 1)
     gemm_i8_g64_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_lb, const __grid_constant__ CUtensorMap map_mid,
                        GemmArgs p) {
   using S = GemmShape<BN>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES, STAGE_BYTES = S::STAGE_BYTES, HALF = S::HALF;
   constexpr int NPAIR = S::NPAIR;
+  // Tensor-core LoRA-B (3 x TF32): fast mode, rank 32, 128-column tiles. The
+  // LoRA operands come through the stage ring as stages KS (B rows) and
+  // KS + 1 + part (A rows), each FP32 tile followed by its low-order part.
+  constexpr bool TCL = R == 32 && !EXACT && !DUMP && BN == 128;
+  constexpr int LT = 128 * 128;  // bytes of one FP32 LoRA operand tile (128 rows x 32)
+  static_assert(!TCL || (2 * LT <= STAGE_BYTES && STAGES >= 5), "LoRA operands must fit the ring");
   static_assert(EPI != kEpiSwiGlu || BN == 128, "SwiGLU pairs need 128-column tiles");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -128,7 +178,9 @@ __global__ void __launch_bounds__(576, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + NPAIR;
   uint64_t* mma_done = tempty + NPAIR;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* lora_ready = mma_done + 1;  // lo parts written (promotion warps)
+  uint64_t* lora_done = lora_ready + 1;  // LoRA-B MMAs complete
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(lora_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* bt_smem = reinterpret_cast<float*>(smem + S::BT_OFF);
 
@@ -146,16 +198,22 @@ __global__ void __launch_bounds__(576, 1)
       mbar_init(&tempty[b], S::EPI_WARPS);
     }
     mbar_init(mma_done, 1);
+    mbar_init(lora_ready, S::EPI_WARPS);
+    mbar_init(lora_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tensormap(&map_a);
     prefetch_tensormap(&map_b);
+    if constexpr (TCL) {
+      prefetch_tensormap(&map_lb);
+      prefetch_tensormap(&map_mid);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, S::TMEM_COLS);
     tmem_relinquish();
   }
-  if constexpr (R > 0) if (warp >= S::EPI_WARP0) {
+  if constexpr (R > 0 && !TCL) if (warp >= S::EPI_WARP0) {
     // This tile's LoRA-B rows [BN][R], transposed to [R][BT_LD].
     const float4* src = reinterpret_cast<const float4*>(p.lora_b + size_t(n0) * R);
     for (int i = threadIdx.x - S::EPI_WARP0 * 32; i < BN * R / 4; i += S::EPI_THREADS) {
@@ -190,6 +248,26 @@ __global__ void __launch_bounds__(576, 1)
         }
         issued = ks + 1;
       }
+      if constexpr (TCL) {
+        // LoRA operand stages: KS = this tile's LoRA-B rows, chunk by chunk into
+        // their part-sorted slots; KS + 1 + k = the LoRA-A rows of part k.
+        if (issued == KS) {
+          const LoraPlan pl = lora_plan(p.chunk_pid, n0);
+          for (int j = 0; j <= pl.nparts; ++j) {
+            const int ls = KS + j, s = ls % STAGES, use = ls / STAGES;
+            if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 120 + s, abort_flag)) break;
+            uint8_t* st = smem + s * STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], LT);
+            if (j == 0) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) tma_load_2d(st + pl.slot[c] * 2048, &map_lb, &full[s], 0, n0 + 16 * c);
+            } else {
+              tma_load_2d(st, &map_mid, &full[s], pl.pid[j - 1] * 32, m0);
+            }
+            issued = ls + 1;
+          }
+        }
+      }
       if (*abort_flag) {
         // Let this CTA's copies in flight land before the CTA exits.
         for (int ks = (issued > STAGES ? issued - STAGES : 0); ks < issued; ++ks)
@@ -219,6 +297,34 @@ __global__ void __launch_bounds__(576, 1)
             mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, 1);
         }
         mma_commit(&tfull[pb]);
+      }
+      if constexpr (TCL) {
+        // delta = mid · Bᵀ in 3 x TF32 (hi·hi + hi·lo + lo·hi) into the group
+        // accumulator pair the main loop no longer needs.
+        const int pd = KS % NPAIR;
+        if (!*abort_flag && mbar_wait_bounded(&tempty[pd], (KS / NPAIR) & 1, p.status, 230, abort_flag) &&
+            mbar_wait_bounded(lora_ready, 0, p.status, 231, abort_flag)) {
+          tc_fence_after();
+          const LoraPlan pl = lora_plan(p.chunk_pid, n0);
+          const uint32_t d = tmem_base + uint32_t(2 * pd * BN);
+          const uint32_t b_hi = smem_addr(smem + (KS % STAGES) * STAGE_BYTES);
+          for (int k = 0; k < pl.nparts; ++k) {
+            const int s0 = pl.run[k], s1 = pl.run[k + 1];
+            if (s1 == s0) continue;
+            const uint32_t idesc = idesc_tf32(BM, uint32_t(16 * (s1 - s0)));
+            const uint32_t a_hi = smem_addr(smem + ((KS + 1 + k) % STAGES) * STAGE_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t ah = a_hi + kk * 32, al = ah + LT;
+              const uint32_t bh = b_hi + s0 * 2048 + kk * 32, bl = bh + LT;
+              const uint32_t dd = d + uint32_t(16 * s0);
+              mma_tf32(dd, smem_desc_sw128(ah), smem_desc_sw128(bh), idesc, kk > 0);
+              mma_tf32(dd, smem_desc_sw128(ah), smem_desc_sw128(bl), idesc, 1);
+              mma_tf32(dd, smem_desc_sw128(al), smem_desc_sw128(bh), idesc, 1);
+            }
+          }
+          mma_commit(lora_done);
+        }
       }
       // All MMAs of this thread have completed once mma_done flips.
       mma_commit(mma_done);
@@ -321,6 +427,53 @@ __global__ void __launch_bounds__(576, 1)
       }
     }
     // ---------------- epilogue
+    const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
+    if constexpr (TCL) {
+      // Split each LoRA operand tile into its TF32 part (low 13 mantissa bits
+      // cleared, in place) and the remainder (at +LT); the MMA issuer then runs
+      // hi·hi + hi·lo + lo·hi. Rows past M are zero (TMA fill).
+      const LoraPlan pl = lora_plan(p.chunk_pid, n0);
+      bool ready = ok;
+      for (int j = 0; j <= pl.nparts && ready; ++j) {
+        const int ls = KS + j, s = ls % STAGES;
+        ready = mbar_wait_bounded(&full[s], (ls / STAGES) & 1, p.status, 320 + s, abort_flag);
+        if (!ready) break;
+        float4* t = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
+        for (int i = et; i < LT / 16; i += S::EPI_THREADS) {
+          const float4 v = t[i];
+          float4 h;
+          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          t[i] = h;
+          t[i + LT / 16] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(lora_ready);
+      ok = ready && mbar_wait_bounded(lora_done, 0, p.status, 330, abort_flag);
+      if (ok) {
+        // This thread's 32 columns: two 16-column chunks, at their part-sorted
+        // slots of the delta accumulator.
+        tc_fence_after();
+        const uint32_t dcol = uint32_t(2 * (KS % NPAIR) * BN);
+        const int c0 = (half * HALF) >> 4;
+#pragma unroll
+        for (int cc = 0; cc < HALF / 16; ++cc) {
+          uint32_t dv[16];
+          tmem_ld_32x32b_x16(tmem_base + (uint32_t(q * 32) << 16) + dcol + uint32_t(16 * pl.slot[c0 + cc]), dv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float2& a2 = acc[cc * 8 + e];
+            a2.x = __fmaf_rn(p.lora_scale, __uint_as_float(dv[2 * e]), __fadd_rn(a2.x, 0.0f));
+            a2.y = __fmaf_rn(p.lora_scale, __uint_as_float(dv[2 * e + 1]), __fadd_rn(a2.y, 0.0f));
+          }
+        }
+      }
+    }
     epi_bar_sync();  // every promotion warp has left the loop: the ring is free
     float* accs = reinterpret_cast<float*>(smem);
     float* mids = reinterpret_cast<float*>(smem + S::MID_OFF);
@@ -328,15 +481,18 @@ __global__ void __launch_bounds__(576, 1)
       float4* dst = reinterpret_cast<float4*>(accs + size_t(row) * S::ACC_LD + half * HALF);
 #pragma unroll
       for (int j = 0; j < HALF / 4; ++j) {
-        // Bias-free projections add 0.0 as the reference does (src/tensor.rs:437).
-        dst[j] = make_float4(__fadd_rn(acc[2 * j].x, 0.0f), __fadd_rn(acc[2 * j].y, 0.0f),
-                             __fadd_rn(acc[2 * j + 1].x, 0.0f), __fadd_rn(acc[2 * j + 1].y, 0.0f));
+        // Bias-free projections add 0.0 as the reference does (src/tensor.rs:437);
+        // the tensor-core LoRA path has already added it (and the delta).
+        if constexpr (TCL)
+          dst[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+        else
+          dst[j] = make_float4(__fadd_rn(acc[2 * j].x, 0.0f), __fadd_rn(acc[2 * j].y, 0.0f),
+                               __fadd_rn(acc[2 * j + 1].x, 0.0f), __fadd_rn(acc[2 * j + 1].y, 0.0f));
       }
     }
-    const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
     constexpr int MAXP = R > 0 ? S::MID_MAX / R : 1;  // LoRA parts one tile may span
     int pmin = 0;
-    if constexpr (R > 0) {
+    if constexpr (R > 0 && !TCL) {
       // LoRA-A rows of the parts this tile's columns use, zero past row M.
       int lo = 1 << 30, hi = 0;
 #pragma unroll
@@ -374,7 +530,7 @@ __global__ void __launch_bounds__(576, 1)
       }
       // v: the FP32 sums, read half by half after that half's LoRA-B product.
       float v[4][2][HW];
-      if constexpr (R == 0) {
+      if constexpr (R == 0 || TCL) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
 #pragma unroll

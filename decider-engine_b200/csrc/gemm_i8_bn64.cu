@@ -3,10 +3,9 @@
 
 namespace dg {
 
-void launch_gemm_i8_bn64(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
-                          bool exact, cudaStream_t s) {
+void launch_gemm_i8_bn64(const GemmMaps& m, const GemmArgs& args, int rank, int epi, bool exact, cudaStream_t s) {
 #define DG_GEMM_CASE(R_, E_, X_) \
-  if (rank == R_ && epi == E_ && exact == X_) return launch_gemm_impl<64, R_, E_, X_>(a, b, args, s);
+  if (rank == R_ && epi == E_ && exact == X_) return launch_gemm_impl<64, R_, E_, X_>(m, args, s);
   DG_GEMM_CASE(32, kEpiWrite, true) DG_GEMM_CASE(32, kEpiAdd, true)
   DG_GEMM_CASE(32, kEpiWrite, false) DG_GEMM_CASE(32, kEpiAdd, false)
   DG_GEMM_CASE(0, kEpiWrite, true) DG_GEMM_CASE(0, kEpiWrite, false)

@@ -5,13 +5,20 @@
 
 namespace dg {
 
-void launch_gemm_i8_bn128(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
-                          bool exact, cudaStream_t s);
-void launch_gemm_i8_bn64(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int rank, int epi,
-                         bool exact, cudaStream_t s);
+// Tensor maps of one launch: activations, weights, and (tensor-core LoRA
+// path) LoRA-B rows and LoRA-A rows.
+struct GemmMaps {
+  const CUtensorMap* a;
+  const CUtensorMap* b;
+  const CUtensorMap* lb;
+  const CUtensorMap* mid;
+};
+
+void launch_gemm_i8_bn128(const GemmMaps& m, const GemmArgs& args, int rank, int epi, bool exact, cudaStream_t s);
+void launch_gemm_i8_bn64(const GemmMaps& m, const GemmArgs& args, int rank, int epi, bool exact, cudaStream_t s);
 
 template <int BN, int R, int EPI, bool EXACT, bool DUMP>
-void launch_gemm_kernel(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+void launch_gemm_kernel(const GemmMaps& m, const GemmArgs& args, cudaStream_t s) {
   auto kern = gemm_i8_g64_kernel<BN, R, EPI, EXACT, DUMP>;
   const int smem = GemmShape<BN>::smem_bytes(R);
   static bool configured = false;  // per instantiation
@@ -20,19 +27,19 @@ void launch_gemm_kernel(const CUtensorMap& a, const CUtensorMap& b, const GemmAr
     configured = true;
   }
   dim3 grid((args.M + 127) / 128, args.N / BN);
-  kern<<<grid, GemmShape<BN>::NUM_THREADS, smem, s>>>(a, b, args);
+  kern<<<grid, GemmShape<BN>::NUM_THREADS, smem, s>>>(*m.a, *m.b, *m.lb, *m.mid, args);
   DG_CUDA(cudaGetLastError());
 }
 
 // The group-dot dump exists only for reference-order WRITE projections.
 template <int BN, int R, int EPI, bool EXACT>
-void launch_gemm_impl(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, cudaStream_t s) {
+void launch_gemm_impl(const GemmMaps& m, const GemmArgs& args, cudaStream_t s) {
   if constexpr (EPI == kEpiWrite && EXACT) {
-    if (args.dots) return launch_gemm_kernel<BN, R, EPI, EXACT, true>(a, b, args, s);
+    if (args.dots) return launch_gemm_kernel<BN, R, EPI, EXACT, true>(m, args, s);
   } else {
     if (args.dots) throw CudaError("gemm_i8: group-dot dump needs the reference-order WRITE epilogue");
   }
-  launch_gemm_kernel<BN, R, EPI, EXACT, false>(a, b, args, s);
+  launch_gemm_kernel<BN, R, EPI, EXACT, false>(m, args, s);
 }
 
 }  // namespace dg

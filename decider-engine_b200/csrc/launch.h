@@ -16,10 +16,12 @@ void make_tmap_i8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 
 // ---- INT8 tensor-core projection (tcgen05), gemm_i8.cu
 // Tensor maps of one int8 weight matrix [n][k] for each output-tile width.
+// lb: the LoRA-B rows [n][32] (rank 32), read by the tensor-core LoRA path.
 struct WeightMaps {
-  CUtensorMap bn128{}, bn64{};
+  CUtensorMap bn128{}, bn64{}, lb{};
+  bool has_lb = false;
 };
-void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n);
+void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n, const float* lora_b = nullptr, int rank = 0);
 // rank: 0 or 32. epi: kEpiWrite/kEpiAdd/kEpiSwiGlu. exact: reference FP32 order.
 // The tile width is chosen per shape (gemm_i8_choose_bn) so the grid fills
 // the 148 SMs with the fewest waves.

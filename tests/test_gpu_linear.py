@@ -48,8 +48,13 @@ def test_projection_without_lora_matches_oracle(oracle_mod):
     assert np.array_equal(got, exp)
 
 
-def test_fma_mode_within_tolerance(oracle_mod):
+@pytest.mark.parametrize("tile_n", ["64", "128"])
+def test_fma_mode_within_tolerance(oracle_mod, monkeypatch, tile_n):
+    """FMA mode on both tile widths; 128-column tiles run LoRA-B on the tensor
+    cores (3 x TF32), whose error (about 2^-21 of |mid| |B|) stays far inside
+    the 1e-5 bar."""
     from decider_gpu import Linear
+    monkeypatch.setenv("DG_GEMM_TILE_N", tile_n)
     x, w, la, lb = _case(7, 256, 768, 2048)
     lin = Linear(w, la, lb, 2.0)
     lin.set_exact(False)
@@ -57,6 +62,20 @@ def test_fma_mode_within_tolerance(oracle_mod):
     exp = oracle_mod.linear(x, w, "int8-compute", lora_a=la, lora_b=lb, scale=2.0)
     rel = np.linalg.norm(got - exp) / np.linalg.norm(exp)
     assert rel < 1e-5, rel
+
+
+def test_tensor_core_lora_keeps_rows_past_m_out(oracle_mod, monkeypatch):
+    """A ragged row count (the last 128-row tile partly empty) through the
+    tensor-core LoRA path: LoRA-A rows past M come in as zeros."""
+    from decider_gpu import Linear
+    monkeypatch.setenv("DG_GEMM_TILE_N", "128")
+    x, w, la, lb = _case(9, 200, 512, 1024)
+    lin = Linear(w, la, lb, 2.0)
+    lin.set_exact(False)
+    got = lin(x)
+    exp = oracle_mod.linear(x, w, "int8-compute", lora_a=la, lora_b=lb, scale=2.0)
+    assert np.isfinite(got).all()
+    assert np.linalg.norm(got - exp) / np.linalg.norm(exp) < 1e-5
 
 
 def test_config1_group_accumulators_bit_exact(oracle_mod, torch_cuda):
