@@ -39,10 +39,10 @@ import numpy as np  # noqa: E402
 
 METRIC = "prefill tok/s at 2B INT8 (1/2/4/8 B200)"
 TOKENS = 512
-# DRAM bytes (read + write) per gemm_i8_g64 launch from one ncu capture of the
-# bench's own launches; None until a capture of the current kernel is recorded
-# under profiles/.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = None
+# DRAM bytes (read + write) per gemm_i8_g64 launch, averaged over the 32
+# projection launches of a 4-layer forward (the 24-layer model repeats the
+# same 4-layer pattern): one ncu capture, profiles/gemm_i8_g64_swiglu_512x12288x2048.md.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 20.62e6
 
 
 def cfg2(layers=24):
