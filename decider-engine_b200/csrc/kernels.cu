@@ -204,11 +204,12 @@ __global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float
 // multiply-then-add chain, the lanes summed from -0.0 in order, then the tail.
 // A thread runs lane `i` of a 4-row x 4-output tile (16 chains sharing 8 loads
 // per step); the eight lanes of a tile are eight consecutive threads.
-template <bool EXACT>
+// TM = 1 serves the few rows of the pointer head: more loads in flight per
+// thread instead of three padding rows.
+template <bool EXACT, int TM = 4, int TR = 4>
 __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                      const float* __restrict__ A, int R, float* __restrict__ mid,
                                                      int ldm) {
-  constexpr int TM = 4, TR = 4;
   const long gid = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane8 = int(gid & 7);
   const long tile = gid >> 3;
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x
 #pragma unroll
     for (int b = 0; b < TR; ++b) acc[a][b] = 0.0f;
   if (m0 < M) {
-#pragma unroll 2
+#pragma unroll(TM == 1 ? 4 : 2)
     for (int k = lane8; k < kfull; k += 8) {
       float xv[TM], av[TR];
 #pragma unroll
@@ -581,7 +582,12 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
   if (M <= 0 || R <= 0) return;
   const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
-  if (exact) {
+  if (exact && M <= 16) {
+    // One row x one output per group of eight lanes: the head's few rows
+    // still spread over R * M * 8 threads.
+    const long t1 = long(M) * R * 8;
+    lora_a_kernel<true, 1, 1><<<int((t1 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+  } else if (exact) {
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
   } else if (partial && K % 32 == 0 && ldx % 4 == 0 && R % 4 == 0 && ldm % 4 == 0 &&
              reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0) {

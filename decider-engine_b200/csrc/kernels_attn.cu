@@ -507,18 +507,25 @@ __global__ void head_norm_kernel(const float* __restrict__ hidden, int K, const 
 __global__ void head_dot_kernel(const float* __restrict__ q, const float* __restrict__ k, int n_keys, int dim,
                                 float scale, const float* __restrict__ bq, const float* __restrict__ bk,
                                 float* __restrict__ logits) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  // One warp per key; lane l < 8 runs the reference's lane l (indices l, l+8, ...).
+  const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
   if (i >= n_keys) return;
   const float* kr = k + size_t(i) * dim;
   auto qv = [&](int j) { return bq ? q[j] + bq[j] : q[j]; };
   auto kv = [&](int j) { return bk ? kr[j] + bk[j] : kr[j]; };
-  float lanes[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   const int full = (dim / 8) * 8;
-  for (int j = 0; j < full; ++j) lanes[j & 7] = lanes[j & 7] + qv(j) * kv(j);
+  float chain = 0.0f;
+  if (lane < 8) {
+#pragma unroll 8
+    for (int j = lane; j < full; j += 8) chain = chain + qv(j) * kv(j);
+  }
   float s = -0.0f;
-  for (int l = 0; l < 8; ++l) s = s + lanes[l];
-  for (int j = full; j < dim; ++j) s = s + qv(j) * kv(j);
-  logits[i] = s * scale;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) s = s + __shfl_sync(0xffffffffu, chain, l);
+  if (lane == 0) {
+    for (int j = full; j < dim; ++j) s = s + qv(j) * kv(j);
+    logits[i] = s * scale;
+  }
 }
 
 }  // namespace
@@ -580,7 +587,7 @@ void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, c
 void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, const float* bq,
                      const float* bk, float* logits, cudaStream_t s) {
   if (n_keys <= 0) return;
-  head_dot_kernel<<<(n_keys + 127) / 128, 128, 0, s>>>(q, k, n_keys, dim, scale, bq, bk, logits);
+  head_dot_kernel<<<(n_keys + 3) / 4, 128, 0, s>>>(q, k, n_keys, dim, scale, bq, bk, logits);
   DG_CUDA(cudaGetLastError());
 }
 
