@@ -10,18 +10,22 @@
 // more SMs share the work); 18 warps:
 //   warp 0      TMA producer: int8 A/B tiles (128-byte swizzle) plus the two
 //               groups' activation and weight scales of each 128-wide K stage;
+//               with tensor-core LoRA-B, also the LoRA operand tiles, which
+//               the whole warp splits into TF32 parts before the loop ends;
 //   warp 1      TMEM allocator and single-thread MMA issuer: per stage, two
 //               64-wide groups, each two tcgen05.mma kind::i8 (K=32) into its
-//               own int32 accumulator; 512 TMEM columns hold 512/BN group
-//               accumulators, so the MMAs run up to 256/BN stages ahead;
+//               own int32 accumulator (the first overwrites, the second adds);
+//               512 TMEM columns hold 512/BN group accumulators, so the MMAs
+//               run up to 512/BN - 1 groups ahead of the promotion;
 //   warps 2-17  promotion and epilogue. Main loop: four warps per TMEM lane
-//               quarter (warp % 4), each owning a quarter of the tile's columns; per group
-//               they tcgen05.ld the accumulators and scale them in FP32 in group
-//               order (reference order when EXACT, fused multiply-add otherwise).
-//               Epilogue: the FP32 sums and this tile's LoRA-A rows go to shared
-//               memory (the drained stage ring); each thread then finishes a
-//               4-row x (BN/16)-column block: LoRA-B as a register-tiled
-//               rank-R product, the epilogue, and row-contiguous stores.
+//               quarter (warp % 4), each owning a quarter of the tile's
+//               columns; per group they tcgen05.ld the accumulator, free it for
+//               the next MMA, and scale it in FP32 in group order (reference
+//               order when EXACT, fused multiply-add otherwise).
+//               Epilogue: the FP32 sums go to shared memory (the drained stage
+//               ring) and leave in row-contiguous copies; with CUDA-core LoRA-B
+//               each thread first finishes a 4-row x (BN/16)-column block as a
+//               register-tiled rank-R product over the tile's LoRA-A rows.
 // Every wait is bounded (mbar_wait_bounded); a stall records kWaitTimeout.
 #pragma once
 #include "common.cuh"
@@ -58,8 +62,7 @@ struct GemmShape {
   static constexpr int NUM_THREADS = 576;
   static constexpr int EPI_WARP0 = 2, EPI_WARPS = 16, EPI_THREADS = EPI_WARPS * 32;
   static constexpr int HALF = BN / 4;           // main loop: columns per promotion warp
-  static constexpr int NBUF = 512 / BN;         // group accumulators in TMEM
-  static constexpr int NPAIR = NBUF / 2;        // stages in flight between MMA and promotion
+  static constexpr int NBUF = 512 / BN;         // group accumulators in TMEM (MMAs run NBUF - 1 groups ahead)
   static constexpr uint32_t TMEM_COLS = 512;
   // Epilogue layout inside the drained ring: FP32 sums [BM][ACC_LD], then the
   // tile's LoRA-A rows [BM][MID_LD] (at most four fused parts of rank 32).
@@ -70,10 +73,11 @@ struct GemmShape {
   static constexpr int BT_LD = BN + 4;
   static constexpr int BT_OFF = RING;
   static constexpr int CW = BN / 16, HW = CW / 2;  // epilogue: columns per thread, per half
-  static_assert((2 * STAGES + 2 * NPAIR + 3) * 8 + 8 <= 256, "barrier area");
+  static_assert((2 * STAGES + 2 * NBUF + 3) * 8 + 8 <= 256, "barrier area");
   __host__ __device__ static constexpr int bt_bytes(int R) { return R * BT_LD * 4; }
   __host__ __device__ static constexpr int bar_off(int R) { return BT_OFF + bt_bytes(R); }
-  __host__ __device__ static constexpr int smem_bytes(int R) { return bar_off(R) + 256 + 1024; }
+  __host__ __device__ static constexpr int plan_off(int R) { return bar_off(R) + 256; }  // LoraPlan (128 bytes)
+  __host__ __device__ static constexpr int smem_bytes(int R) { return plan_off(R) + 128 + 1024; }
 };
 
 __device__ __forceinline__ void epi_bar_sync() {
@@ -122,6 +126,7 @@ struct LoraPlan {
   int slot[8];
   int run[5];
 };
+static_assert(sizeof(LoraPlan) <= 128, "plan area");
 __device__ __forceinline__ LoraPlan lora_plan(const int* chunk_pid, int n0) {
   LoraPlan pl;
   int cp[8];
@@ -163,10 +168,11 @@ __global__ void __launch_bounds__(576, 1)
                        GemmArgs p) {
   using S = GemmShape<BN>;
   constexpr int BM = S::BM, BK = S::BK, STAGES = S::STAGES, STAGE_BYTES = S::STAGE_BYTES, HALF = S::HALF;
-  constexpr int NPAIR = S::NPAIR;
+  constexpr int NBUF = S::NBUF;
   // Tensor-core LoRA-B (3 x TF32): fast mode, rank 32, 128-column tiles. The
   // LoRA operands come through the stage ring as stages KS (B rows) and
-  // KS + 1 + part (A rows), each FP32 tile followed by its low-order part.
+  // KS + 1 + part (A rows); the producer warp splits each FP32 tile into its
+  // TF32 part and the low-order remainder.
   constexpr bool TCL = R == 32 && !EXACT && !DUMP && BN == 128;
   constexpr int LT = 128 * 128;  // bytes of one FP32 LoRA operand tile (128 rows x 32)
   static_assert(!TCL || (2 * LT <= STAGE_BYTES && STAGES >= 5), "LoRA operands must fit the ring");
@@ -175,14 +181,15 @@ __global__ void __launch_bounds__(576, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::bar_off(R));
   uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + NPAIR;
-  uint64_t* mma_done = tempty + NPAIR;
-  uint64_t* lora_ready = mma_done + 1;  // lo parts written (promotion warps)
+  uint64_t* tfull = empty + STAGES;     // group accumulator b written by the MMAs
+  uint64_t* tempty = tfull + NBUF;      // group accumulator b read by every promotion warp
+  uint64_t* mma_done = tempty + NBUF;
+  uint64_t* lora_ready = mma_done + 1;  // LoRA operands split into TF32 parts (producer warp)
   uint64_t* lora_done = lora_ready + 1;  // LoRA-B MMAs complete
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(lora_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* bt_smem = reinterpret_cast<float*>(smem + S::BT_OFF);
+  LoraPlan* plan = reinterpret_cast<LoraPlan*>(smem + S::plan_off(R));
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
@@ -193,12 +200,12 @@ __global__ void __launch_bounds__(576, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], S::EPI_WARPS);
     }
-    for (int b = 0; b < NPAIR; ++b) {
+    for (int b = 0; b < NBUF; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], S::EPI_WARPS);
     }
     mbar_init(mma_done, 1);
-    mbar_init(lora_ready, S::EPI_WARPS);
+    mbar_init(lora_ready, 1);
     mbar_init(lora_done, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -207,6 +214,7 @@ __global__ void __launch_bounds__(576, 1)
     if constexpr (TCL) {
       prefetch_tensormap(&map_lb);
       prefetch_tensormap(&map_mid);
+      *plan = lora_plan(p.chunk_pid, n0);
     }
   }
   if (warp == 1) {
@@ -231,9 +239,9 @@ __global__ void __launch_bounds__(576, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   if (warp == 0) {
+    int issued = 0;
     if (lane == 0) {
       // ---------------- TMA producer
-      int issued = 0;
       for (int ks = 0; ks < KS; ++ks) {
         const int s = ks % STAGES, use = ks / STAGES;
         if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 100 + s, abort_flag)) break;
@@ -252,61 +260,93 @@ __global__ void __launch_bounds__(576, 1)
         // LoRA operand stages: KS = this tile's LoRA-B rows, chunk by chunk into
         // their part-sorted slots; KS + 1 + k = the LoRA-A rows of part k.
         if (issued == KS) {
-          const LoraPlan pl = lora_plan(p.chunk_pid, n0);
-          for (int j = 0; j <= pl.nparts; ++j) {
+          for (int j = 0; j <= plan->nparts; ++j) {
             const int ls = KS + j, s = ls % STAGES, use = ls / STAGES;
             if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 120 + s, abort_flag)) break;
             uint8_t* st = smem + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], LT);
             if (j == 0) {
 #pragma unroll
-              for (int c = 0; c < 8; ++c) tma_load_2d(st + pl.slot[c] * 2048, &map_lb, &full[s], 0, n0 + 16 * c);
+              for (int c = 0; c < 8; ++c) tma_load_2d(st + plan->slot[c] * 2048, &map_lb, &full[s], 0, n0 + 16 * c);
             } else {
-              tma_load_2d(st, &map_mid, &full[s], pl.pid[j - 1] * 32, m0);
+              tma_load_2d(st, &map_mid, &full[s], plan->pid[j - 1] * 32, m0);
             }
             issued = ls + 1;
           }
         }
       }
-      if (*abort_flag) {
-        // Let this CTA's copies in flight land before the CTA exits.
-        for (int ks = (issued > STAGES ? issued - STAGES : 0); ks < issued; ++ks)
-          mbar_wait_bounded(&full[ks % STAGES], (ks / STAGES) & 1, p.status, 190, nullptr, 100000000ull);
+    }
+    issued = __shfl_sync(0xffffffffu, issued, 0);
+    if constexpr (TCL) {
+      // The whole warp splits each LoRA operand tile into its TF32 part (low
+      // 13 mantissa bits cleared, in place) and the remainder (at +LT), while
+      // the promotion warps finish the main loop; the MMA issuer then runs
+      // hi·hi + hi·lo + lo·hi. Rows past M are zero (TMA fill).
+      bool ready = issued == KS + 1 + plan->nparts;
+      for (int j = 0; j <= plan->nparts && ready; ++j) {
+        const int ls = KS + j, s = ls % STAGES;
+        ready = mbar_wait_bounded(&full[s], (ls / STAGES) & 1, p.status, 140 + s, abort_flag);
+        if (!ready) break;
+        float4* t = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
+#pragma unroll 4
+        for (int i = lane; i < LT / 16; i += 32) {
+          const float4 v = t[i];
+          float4 h;
+          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
+          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
+          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
+          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
+          t[i] = h;
+          t[i + LT / 16] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && ready) mbar_arrive(lora_ready);
+    }
+    if (lane == 0 && *abort_flag) {
+      // Let this CTA's copies in flight land before the CTA exits.
+      for (int ks = (issued > STAGES ? issued - STAGES : 0); ks < issued; ++ks)
+        mbar_wait_bounded(&full[ks % STAGES], (ks / STAGES) & 1, p.status, 190, nullptr, 100000000ull);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t idesc = idesc_i8(BM, BN);
-      for (int ks = 0; ks < KS; ++ks) {
-        const int s = ks % STAGES, pb = ks % NPAIR, pu = ks / NPAIR;
-        // Phase pu of tempty[pb]: the promotion warps have read the pair's
-        // previous stage and refilled its accumulators with the offset.
-        if (!mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag) ||
-            !mbar_wait_bounded(&tempty[pb], pu & 1, p.status, 210 + pb, abort_flag))
-          break;
-        tc_fence_after();
+      bool run = true;
+      for (int ks = 0; ks < KS && run; ++ks) {
+        const int s = ks % STAGES;
+        if (!mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag)) break;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
+          // Group g goes to accumulator g % NBUF once every promotion warp
+          // has read that accumulator's previous group (phase g / NBUF).
+          const int g = 2 * ks + j, b = g % NBUF;
+          if (!mbar_wait_bounded(&tempty[b], (g / NBUF) & 1, p.status, 210 + b, abort_flag)) {
+            run = false;
+            break;
+          }
+          tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + s * STAGE_BYTES) + j * 64;
           const uint32_t b_addr = a_addr + S::A_BYTES;
-          const uint32_t d = tmem_base + uint32_t((2 * pb + j) * BN);
-          // Both MMAs accumulate onto the offset already in the accumulator.
+          const uint32_t d = tmem_base + uint32_t(b * BN);
+          // The group's first MMA overwrites the accumulator, the second adds.
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk)
-            mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, 1);
+            mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, kk);
+          mma_commit(&tfull[b]);
         }
-        mma_commit(&tfull[pb]);
       }
       if constexpr (TCL) {
         // delta = mid · Bᵀ in 3 x TF32 (hi·hi + hi·lo + lo·hi) into the group
-        // accumulator pair the main loop no longer needs.
-        const int pd = KS % NPAIR;
-        if (!*abort_flag && mbar_wait_bounded(&tempty[pd], (KS / NPAIR) & 1, p.status, 230, abort_flag) &&
+        // accumulator that the main loop's group 2 KS would have used.
+        const int gd = 2 * KS, bd = gd % NBUF;
+        if (run && !*abort_flag &&
+            mbar_wait_bounded(&tempty[bd], (gd / NBUF) & 1, p.status, 230, abort_flag) &&
             mbar_wait_bounded(lora_ready, 0, p.status, 231, abort_flag)) {
           tc_fence_after();
-          const LoraPlan pl = lora_plan(p.chunk_pid, n0);
-          const uint32_t d = tmem_base + uint32_t(2 * pd * BN);
+          const LoraPlan& pl = *plan;
+          const uint32_t d = tmem_base + uint32_t(bd * BN);
           const uint32_t b_hi = smem_addr(smem + (KS % STAGES) * STAGE_BYTES);
           for (int k = 0; k < pl.nparts; ++k) {
             const int s0 = pl.run[k], s1 = pl.run[k + 1];
@@ -331,134 +371,99 @@ __global__ void __launch_bounds__(576, 1)
       mbar_wait_bounded(mma_done, 0, p.status, 220, nullptr);
     }
   } else if (warp >= S::EPI_WARP0) {
-    // ---------------- promotion (warps 4..19)
+    // ---------------- promotion (warps 2..17)
     const int q = warp & 3;                          // TMEM lane quarter this warp may read
     const int half = (warp - S::EPI_WARP0) >> 2;     // which quarter of the tile's columns
     const int row = q * 32 + lane;
     const int m = m0 + row;
     const uint32_t lane_addr = tmem_base + (uint32_t(q * 32) << 16) + uint32_t(half * HALF);
-    // Every accumulator word starts at the bits of 1.5 * 2^23 (0x4B400000), so
-    // after the group's MMAs it holds the bits of the float 1.5 * 2^23 + dot
-    // (|dot| <= 64 * 128 * 128 < 2^22): the exact int32 -> float conversion is
-    // one subtraction of 1.5 * 2^23.
+    // Exact int32 -> float conversion: adding the bits of 1.5 * 2^23
+    // (0x4B400000) to the dot (|dot| <= 64 * 128 * 128 < 2^22) gives the bits of
+    // the float 1.5 * 2^23 + dot, so one subtraction of 1.5 * 2^23 is left.
     constexpr uint32_t kOffsetBits = 0x4B400000u;
     const float2 neg_magic = make_float2(-12582912.0f, -12582912.0f);
-#pragma unroll
-    for (int b = 0; b < S::NBUF; ++b)
-#pragma unroll
-      for (int c = 0; c < HALF / 16; ++c) tmem_fill_32x32b_x16(lane_addr + uint32_t(b * BN + c * 16), kOffsetBits);
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
     if (lane == 0) {
 #pragma unroll
-      for (int b = 0; b < NPAIR; ++b) mbar_arrive(&tempty[b]);
+      for (int b = 0; b < NBUF; ++b) mbar_arrive(&tempty[b]);  // every accumulator starts free
     }
     float2 acc[HALF / 2];
 #pragma unroll
     for (int j = 0; j < HALF / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
-    // A stage holds two groups of HALF/16 16-column chunks each; chunk c of
-    // both groups is loaded at once (one TMEM load latency per chunk).
+    // Per group: load this warp's HALF columns (HALF / 16 chunks of 16), hand
+    // the accumulator back to the MMA issuer, then scale in registers.
     constexpr int CPG = HALF / 16;
     bool ok = true;
-    for (int ks = 0; ks < KS; ++ks) {
-      const int s = ks % STAGES, pb = ks % NPAIR, pu = ks / NPAIR;
-      ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 300 + s, abort_flag) &&
-           mbar_wait_bounded(&tfull[pb], pu & 1, p.status, 310 + pb, abort_flag);
+    for (int ks = 0; ks < KS && ok; ++ks) {
+      const int s = ks % STAGES;
+      ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 300 + s, abort_flag);
       if (!ok) break;
-      tc_fence_after();
       const uint8_t* st = smem + s * STAGE_BYTES;
       const float* xsp = reinterpret_cast<const float*>(st + S::XS_OFF);
-      const float xsg[2] = {xsp[row], xsp[BM + row]};
       const float* wsp = reinterpret_cast<const float*>(st + S::WS_OFF) + half * HALF;
-      const bool refill = ks + NPAIR < KS;  // the pair's next stage needs the offset again
-      const uint32_t pair_addr = lane_addr + uint32_t(2 * pb * BN);
 #pragma unroll
-      for (int c = 0; c < CPG; ++c) {
-        uint32_t d[2][16];  // [group of the stage][column]
-        tmem_ld_32x32b_x16(pair_addr + uint32_t(c * 16), d[0]);
-        tmem_ld_32x32b_x16(pair_addr + uint32_t(BN + c * 16), d[1]);
-        tmem_wait_ld16(d[0]);
-        tmem_dep16(d[1]);
-#pragma unroll
-       for (int j = 0; j < 2; ++j) {
-        const uint32_t taddr = pair_addr + uint32_t(j * BN + c * 16);
-        uint32_t(&cur)[16] = d[j];
-        if (refill) tmem_fill_32x32b_x16(taddr, kOffsetBits);
-        if (DUMP && m < p.M) {
-          const int g = 2 * ks + j;
-          int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
-#pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4)
-            dd[j4] = make_int4(int(cur[j4 * 4] - kOffsetBits), int(cur[j4 * 4 + 1] - kOffsetBits),
-                               int(cur[j4 * 4 + 2] - kOffsetBits), int(cur[j4 * 4 + 3] - kOffsetBits));
+      for (int j = 0; j < 2; ++j) {
+        const int g = 2 * ks + j, b = g % NBUF;
+        const float xs = xsp[j * BM + row];
+        if (!mbar_wait_bounded(&tfull[b], (g / NBUF) & 1, p.status, 310 + b, abort_flag)) {
+          ok = false;
+          break;
         }
-        const float xs = xsg[j];
+        tc_fence_after();
+        uint32_t d[CPG][16];
+#pragma unroll
+        for (int c = 0; c < CPG; ++c) tmem_ld_32x32b_x16(lane_addr + uint32_t(b * BN + c * 16), d[c]);
+        tmem_wait_ld16(d[0]);
+#pragma unroll
+        for (int c = 1; c < CPG; ++c) tmem_dep16(d[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
         const float2 xs2 = make_float2(xs, xs);
 #pragma unroll
-        for (int j4 = 0; j4 < 4; ++j4) {
-          const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
-          const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
+        for (int c = 0; c < CPG; ++c) {
+          const uint32_t(&cur)[16] = d[c];
+          if (DUMP && m < p.M) {
+            int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int k = j4 * 4 + e * 2;
-            float2 fd = make_float2(__uint_as_float(cur[k]), __uint_as_float(cur[k + 1]));
-            float2& a2 = acc[(c * 16 + k) / 2];
-            const float2 w2 = e ? whi : wlo;
-            if (EXACT) {
-              // Reference order with scalar IEEE operations (src/int8.rs:58):
-              // sum + float(dot) * (xs * ws), rounded after every step.
-              a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
-              a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
-            } else {
-              fd = add2_rn(fd, neg_magic);
-              a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
+            for (int j4 = 0; j4 < 4; ++j4)
+              dd[j4] = make_int4(int(cur[j4 * 4]), int(cur[j4 * 4 + 1]), int(cur[j4 * 4 + 2]), int(cur[j4 * 4 + 3]));
+          }
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
+            const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int k = j4 * 4 + e * 2;
+              float2 fd = make_float2(__uint_as_float(cur[k] + kOffsetBits), __uint_as_float(cur[k + 1] + kOffsetBits));
+              float2& a2 = acc[(c * 16 + k) / 2];
+              const float2 w2 = e ? whi : wlo;
+              if (EXACT) {
+                // Reference order with scalar IEEE operations (src/int8.rs:58):
+                // sum + float(dot) * (xs * ws), rounded after every step.
+                a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
+                a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
+              } else {
+                fd = add2_rn(fd, neg_magic);
+                a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
+              }
             }
           }
         }
-       }
       }
-      if (refill) tmem_wait_st();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&tempty[pb]);
-        mbar_arrive(&empty[s]);
-      }
+      if (lane == 0) mbar_arrive(&empty[s]);  // scales and operands of the stage are consumed
     }
     // ---------------- epilogue
     const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
     if constexpr (TCL) {
-      // Split each LoRA operand tile into its TF32 part (low 13 mantissa bits
-      // cleared, in place) and the remainder (at +LT); the MMA issuer then runs
-      // hi·hi + hi·lo + lo·hi. Rows past M are zero (TMA fill).
-      const LoraPlan pl = lora_plan(p.chunk_pid, n0);
-      bool ready = ok;
-      for (int j = 0; j <= pl.nparts && ready; ++j) {
-        const int ls = KS + j, s = ls % STAGES;
-        ready = mbar_wait_bounded(&full[s], (ls / STAGES) & 1, p.status, 320 + s, abort_flag);
-        if (!ready) break;
-        float4* t = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
-        for (int i = et; i < LT / 16; i += S::EPI_THREADS) {
-          const float4 v = t[i];
-          float4 h;
-          h.x = __uint_as_float(__float_as_uint(v.x) & 0xFFFFE000u);
-          h.y = __uint_as_float(__float_as_uint(v.y) & 0xFFFFE000u);
-          h.z = __uint_as_float(__float_as_uint(v.z) & 0xFFFFE000u);
-          h.w = __uint_as_float(__float_as_uint(v.w) & 0xFFFFE000u);
-          t[i] = h;
-          t[i + LT / 16] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(lora_ready);
-      ok = ready && mbar_wait_bounded(lora_done, 0, p.status, 330, abort_flag);
+      const LoraPlan& pl = *plan;
+      ok = ok && mbar_wait_bounded(lora_done, 0, p.status, 330, abort_flag);
       if (ok) {
         // This thread's 32 columns: two 16-column chunks, at their part-sorted
         // slots of the delta accumulator.
         tc_fence_after();
-        const uint32_t dcol = uint32_t(2 * (KS % NPAIR) * BN);
+        const uint32_t dcol = uint32_t(((2 * KS) % NBUF) * BN);
         const int c0 = (half * HALF) >> 4;
 #pragma unroll
         for (int cc = 0; cc < HALF / 16; ++cc) {
@@ -513,9 +518,41 @@ __global__ void __launch_bounds__(576, 1)
       }
     }
     epi_bar_sync();
-    if (!*abort_flag) {
+    if (*abort_flag) {
+      // nothing is written after a failed wait
+    } else if constexpr (R == 0 || TCL) {
+      // The staged sums are final: row-contiguous copies, one float4 per
+      // thread and step (a warp covers 512 contiguous bytes of output).
+      if constexpr (EPI == kEpiSwiGlu) {
+        // Output column 16 k + t = silu(gate column 32 k + t) * (up column 32 k + 16 + t).
+        constexpr int O4 = BN / 8;
+        for (int i = et; i < BM * O4; i += S::EPI_THREADS) {
+          const int r = i / O4, o4 = i % O4, mm = m0 + r;
+          if (mm >= p.M) continue;
+          const float* src = accs + r * S::ACC_LD + 32 * (o4 >> 2) + 4 * (o4 & 3);
+          const float4 gt = *reinterpret_cast<const float4*>(src);
+          const float4 up = *reinterpret_cast<const float4*>(src + 16);
+          *reinterpret_cast<float4*>(p.out + size_t(mm) * p.ldo + (n0 >> 1) + 4 * o4) =
+              make_float4(silu_f(gt.x) * up.x, silu_f(gt.y) * up.y, silu_f(gt.z) * up.z, silu_f(gt.w) * up.w);
+        }
+      } else {
+        constexpr int C4 = BN / 4;
+        for (int i = et; i < BM * C4; i += S::EPI_THREADS) {
+          const int r = i / C4, c4 = i % C4, mm = m0 + r;
+          if (mm >= p.M) continue;
+          float4 v = *reinterpret_cast<const float4*>(accs + r * S::ACC_LD + 4 * c4);
+          float4* o = reinterpret_cast<float4*>(p.out + size_t(mm) * p.ldo + n0 + 4 * c4);
+          if constexpr (EPI == kEpiAdd) {
+            const float4 old = *o;
+            v = make_float4(__fadd_rn(old.x, v.x), __fadd_rn(old.y, v.y), __fadd_rn(old.z, v.z), __fadd_rn(old.w, v.w));
+          }
+          *o = v;
+        }
+      }
+    } else {
       // Each thread finishes rows r0..r0+3 of two HW-column halves: adjacent
-      // (WRITE/ADD) or a gate chunk and its up chunk 16 columns on (SWIGLU).
+      // (WRITE/ADD) or a gate chunk and its up chunk 16 columns on (SWIGLU),
+      // after the register-tiled LoRA-B product of those columns.
       constexpr int HW = S::HW;
       const int cg = et & 15, r0 = (et >> 4) * 4;
       int col[2], ocol;
@@ -530,12 +567,7 @@ __global__ void __launch_bounds__(576, 1)
       }
       // v: the FP32 sums, read half by half after that half's LoRA-B product.
       float v[4][2][HW];
-      if constexpr (R == 0 || TCL) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) lds_vec<HW>(accs + (r0 + i) * S::ACC_LD + col[h], v[i][h]);
-      } else {
+      {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int part = min(max(p.chunk_pid[(n0 + col[h]) >> 4] - pmin, 0), MAXP - 1);
