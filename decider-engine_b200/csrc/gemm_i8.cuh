@@ -84,26 +84,6 @@ __device__ __forceinline__ void epi_bar_sync() {
   asm volatile("bar.sync 1, 512;" ::: "memory");  // the 16 promotion warps
 }
 
-// tcgen05.wait::ld that also orders every use of the loaded registers after it.
-__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                 "+r"(r[15])
-               :
-               : "memory");
-}
-
-// Orders every later use of r after the preceding tcgen05.wait::ld.
-__device__ __forceinline__ void tmem_dep16(uint32_t (&r)[16]) {
-  asm volatile(""
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
-                 "+r"(r[15])
-               :
-               : "memory");
-}
-
 // Loads HW consecutive floats (HW = 2 or 4) from shared memory.
 template <int HW>
 __device__ __forceinline__ void lds_vec(const float* p, float (&v)[HW]) {
@@ -178,7 +158,11 @@ __global__ void __launch_bounds__(576, 1)
   static_assert(!TCL || (2 * LT <= STAGE_BYTES && STAGES >= 5), "LoRA operands must fit the ring");
   static_assert(EPI != kEpiSwiGlu || BN == 128, "SwiGLU pairs need 128-column tiles");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base (128-byte swizzled tiles). Pointer arithmetic on the
+  // __shared__ array, not an integer round trip, so that the compiler keeps
+  // every access through smem in the shared state space (ld.shared / st.shared):
+  // generic accesses would queue behind the global stores in the same path.
+  uint8_t* smem = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::bar_off(R));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;     // group accumulator b written by the MMAs
@@ -390,8 +374,11 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
     for (int j = 0; j < HALF / 2; ++j) acc[j] = make_float2(0.0f, 0.0f);
     // Per group: load this warp's HALF columns (HALF / 16 chunks of 16), hand
-    // the accumulator back to the MMA issuer, then scale in registers.
+    // the accumulator back to the MMA issuer, then scale in registers. With
+    // one chunk per group (64-column tiles) both groups of a stage share one
+    // TMEM load wait.
     constexpr int CPG = HALF / 16;
+    constexpr int GB = CPG == 1 ? 2 : 1;  // groups per TMEM load wait
     bool ok = true;
     for (int ks = 0; ks < KS && ok; ++ks) {
       const int s = ks % STAGES;
@@ -401,56 +388,71 @@ __global__ void __launch_bounds__(576, 1)
       const float* xsp = reinterpret_cast<const float*>(st + S::XS_OFF);
       const float* wsp = reinterpret_cast<const float*>(st + S::WS_OFF) + half * HALF;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int g = 2 * ks + j, b = g % NBUF;
-        const float xs = xsp[j * BM + row];
-        if (!mbar_wait_bounded(&tfull[b], (g / NBUF) & 1, p.status, 310 + b, abort_flag)) {
-          ok = false;
-          break;
+      for (int j0 = 0; j0 < 2; j0 += GB) {
+#pragma unroll
+        for (int jj = 0; jj < GB && ok; ++jj) {
+          const int g = 2 * ks + j0 + jj, b = g % NBUF;
+          ok = mbar_wait_bounded(&tfull[b], (g / NBUF) & 1, p.status, 310 + b, abort_flag);
         }
+        if (!ok) break;
         tc_fence_after();
-        uint32_t d[CPG][16];
-#pragma unroll
-        for (int c = 0; c < CPG; ++c) tmem_ld_32x32b_x16(lane_addr + uint32_t(b * BN + c * 16), d[c]);
-        tmem_wait_ld16(d[0]);
-#pragma unroll
-        for (int c = 1; c < CPG; ++c) tmem_dep16(d[c]);
+        // [group of the batch][chunk]: two 16-column loads per wait either way.
+        static_assert(GB * CPG == 2, "two loads per TMEM wait");
+        uint32_t d[2][16];
+        const uint32_t a0 = lane_addr + uint32_t(((2 * ks + j0) % NBUF) * BN);
+        tmem_ld16x2_sync(a0, GB == 2 ? lane_addr + uint32_t(((2 * ks + j0 + 1) % NBUF) * BN) : a0 + 16u, d[0], d[1]);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
-        const float2 xs2 = make_float2(xs, xs);
+        if (lane == 0) {
 #pragma unroll
-        for (int c = 0; c < CPG; ++c) {
-          const uint32_t(&cur)[16] = d[c];
-          if (DUMP && m < p.M) {
-            int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
+          for (int jj = 0; jj < GB; ++jj) mbar_arrive(&tempty[(2 * ks + j0 + jj) % NBUF]);
+        }
 #pragma unroll
-            for (int j4 = 0; j4 < 4; ++j4)
-              dd[j4] = make_int4(int(cur[j4 * 4]), int(cur[j4 * 4 + 1]), int(cur[j4 * 4 + 2]), int(cur[j4 * 4 + 3]));
-          }
+        for (int jj = 0; jj < GB; ++jj) {
+          const int j = j0 + jj, g = 2 * ks + j;
+          const float xs = xsp[j * BM + row];
+          const float2 xs2 = make_float2(xs, xs);
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
-            const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
-            const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
+          for (int c = 0; c < CPG; ++c) {
+            const uint32_t(&cur)[16] = d[jj * CPG + c];
+            if (DUMP && m < p.M) {
+              int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int k = j4 * 4 + e * 2;
-              float2 fd = make_float2(__uint_as_float(cur[k] + kOffsetBits), __uint_as_float(cur[k + 1] + kOffsetBits));
-              float2& a2 = acc[(c * 16 + k) / 2];
-              const float2 w2 = e ? whi : wlo;
-              if (EXACT) {
-                // Reference order with scalar IEEE operations (src/int8.rs:58):
-                // sum + float(dot) * (xs * ws), rounded after every step.
-                a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
-                a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
-              } else {
-                fd = add2_rn(fd, neg_magic);
-                a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
+              for (int j4 = 0; j4 < 4; ++j4)
+                dd[j4] = make_int4(int(cur[j4 * 4]), int(cur[j4 * 4 + 1]), int(cur[j4 * 4 + 2]), int(cur[j4 * 4 + 3]));
+            }
+#pragma unroll
+            for (int j4 = 0; j4 < 4; ++j4) {
+              const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
+              const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int k = j4 * 4 + e * 2;
+                float2 fd =
+                    make_float2(__uint_as_float(cur[k] + kOffsetBits), __uint_as_float(cur[k + 1] + kOffsetBits));
+                float2& a2 = acc[(c * 16 + k) / 2];
+                const float2 w2 = e ? whi : wlo;
+                if (EXACT) {
+                  // Reference order with scalar IEEE operations (src/int8.rs:58):
+                  // sum + float(dot) * (xs * ws), rounded after every step.
+                  a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
+                  a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
+                } else {
+                  fd = add2_rn(fd, neg_magic);
+                  a2 = fma2_rn(fd, mul2_rn(xs2, w2), a2);
+                }
               }
             }
           }
         }
       }
+      if (!ok) break;
+      // The stage's scales were read through the generic proxy and the next
+      // TMA into the stage writes through the async proxy: without the proxy
+      // fence the mbarrier release does not order the two, and a refill can
+      // land before reads still queued in the load path (seen when global
+      // stores sit ahead of them) have been performed.
+      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // scales and operands of the stage are consumed
     }
@@ -465,16 +467,17 @@ __global__ void __launch_bounds__(576, 1)
         tc_fence_after();
         const uint32_t dcol = uint32_t(((2 * KS) % NBUF) * BN);
         const int c0 = (half * HALF) >> 4;
+        static_assert(HALF == 32, "tensor-core LoRA-B: two 16-column chunks per thread");
+        const uint32_t dbase = tmem_base + (uint32_t(q * 32) << 16) + dcol;
+        uint32_t dv[2][16];
+        tmem_ld16x2_sync(dbase + uint32_t(16 * pl.slot[c0]), dbase + uint32_t(16 * pl.slot[c0 + 1]), dv[0], dv[1]);
 #pragma unroll
-        for (int cc = 0; cc < HALF / 16; ++cc) {
-          uint32_t dv[16];
-          tmem_ld_32x32b_x16(tmem_base + (uint32_t(q * 32) << 16) + dcol + uint32_t(16 * pl.slot[c0 + cc]), dv);
-          tmem_wait_ld();
+        for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             float2& a2 = acc[cc * 8 + e];
-            a2.x = __fmaf_rn(p.lora_scale, __uint_as_float(dv[2 * e]), __fadd_rn(a2.x, 0.0f));
-            a2.y = __fmaf_rn(p.lora_scale, __uint_as_float(dv[2 * e + 1]), __fadd_rn(a2.y, 0.0f));
+            a2.x = __fmaf_rn(p.lora_scale, __uint_as_float(dv[cc][2 * e]), __fadd_rn(a2.x, 0.0f));
+            a2.y = __fmaf_rn(p.lora_scale, __uint_as_float(dv[cc][2 * e + 1]), __fadd_rn(a2.y, 0.0f));
           }
         }
       }
