@@ -10,6 +10,7 @@ namespace dg {
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launch_count() { return g_launches.load(); }
 void note_launch() { g_launches.fetch_add(1); }
+void note_launches(uint64_t n) { g_launches.fetch_add(n); }
 }  // namespace dg
 
 struct dg_engine {
@@ -103,7 +104,6 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
   note_launch();
   if (l->rank) {
     launch_lora_a(x_dev, l->k, m, l->k, l->lora_a.as<float>(), l->rank, l->mid.as<float>(), 32, l->exact, l->stream);
-    note_launch();
   }
   CUtensorMap map_a;
   make_tmap_i8_2d(&map_a, l->xq.ptr, uint64_t(l->k), uint64_t(m), 128, 128);
@@ -541,7 +541,6 @@ int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m,
     note_launch();
     if (l->rank) {
       launch_lora_a(x_device, l->k, m, l->k, l->lora_a.as<float>(), l->rank, mid, 32, l->exact, l->stream);
-      note_launch();
     }
     CUtensorMap map_a;
     make_tmap_i8_2d(&map_a, xq, uint64_t(l->k), uint64_t(m), 128, 128);

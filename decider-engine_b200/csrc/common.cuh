@@ -57,6 +57,7 @@ struct CudaError : std::runtime_error {
 // Count of kernel launches issued by this library (host side), reported by
 // the C ABI so callers can see that device code ran.
 uint64_t launch_count();
+void note_launches(uint64_t n);
 void note_launch();
 
 // ---------------------------------------------------------------- PTX wrappers

@@ -142,6 +142,20 @@ class Engine {
   void mixer_tail(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap,
                   const float* raw, int ldr);
   void check_status();
+  void run_layers(int n, int start, const Prefix* past, Prefix* cap);
+  // The kernels of a forward without a prefix (no past, no capture) as one
+  // CUDA graph per token count and timing mode: the first such forward runs
+  // eagerly (first-use set-up stays outside any capture), the second is
+  // captured, later ones replay the graph.
+  struct FwdGraph {
+    int runs = 0;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t launches = 0;
+    std::vector<double> gemm_ops;
+  };
+  std::map<int, FwdGraph> graphs_;
+  bool graphs_on_ = true;
+  void drop_graphs();
 
   Config c_;
   int precision_, device_, max_tokens_;

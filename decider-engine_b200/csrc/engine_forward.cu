@@ -43,11 +43,18 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.status = status();
   const size_t k = gemm_ops_pending_.size();
   const bool timed = 2 * k + 2 <= gemm_ev_.size();
-  if (timed) DG_CUDA(cudaEventRecord(gemm_ev_[2 * k], stream_));
+  // While a graph is captured, external records become event nodes of it.
+  unsigned rec = cudaEventRecordDefault;
+  if (timed) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    DG_CUDA(cudaStreamIsCapturing(stream_, &cs));
+    if (cs == cudaStreamCaptureStatusActive) rec = cudaEventRecordExternal;
+    DG_CUDA(cudaEventRecordWithFlags(gemm_ev_[2 * k], stream_, rec));
+  }
   launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.maps, a, 32, epi, exact, stream_);
   note_launch();
   if (timed) {
-    DG_CUDA(cudaEventRecord(gemm_ev_[2 * k + 1], stream_));
+    DG_CUDA(cudaEventRecordWithFlags(gemm_ev_[2 * k + 1], stream_, rec));
     gemm_ops_pending_.push_back(2.0 * M * p.out * p.in);
   }
 }
@@ -55,7 +62,6 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
 void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi) {
   if (p.lora_rows) {
     launch_lora_a(x, ldx, M, p.in, p.lora_a.as<float>(), p.lora_rows, mid_.as<float>(), 128, true, stream_);
-    note_launch();
   }
   launch_proj_generic(p.g, x, ldx, xq_.as<int8_t>(), xs_.as<float>(), ldxs_, mid_.as<float>(), 128, M, out, ldo, epi,
                       stream_);
@@ -140,9 +146,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   float* proj = proj_.as<float>();
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
-  note_launch();
-  note_launch();
+  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
   run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
   const float* mixed_in;
   int kin;
@@ -174,20 +178,15 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     mixed_in = ofin_.as<float>();
     kin = c.vd();
   }
-  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
-  note_launch();
+  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
   run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
-  note_launch();
-  note_launch();
+  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
   run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
   launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4);
-  note_launch();
-  note_launch();
+  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
   run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
 }
 
@@ -260,6 +259,27 @@ void Engine::check_status() {
   if (st.code) throw DgError("device error code " + std::to_string(st.code));
 }
 
+void Engine::run_layers(int n, int start, const Prefix* past, Prefix* cap) {
+  launch_embed(embedding_.ptr, 0, c_.hidden, ids_.as<uint32_t>(), n, x_.as<float>(), stream_);
+  note_launch();
+  for (int i = 0; i < c_.layers; ++i) {
+    const Prefix::LayerState* lp = past ? &past->layers[i] : nullptr;
+    Prefix::LayerState* lc = cap ? &cap->layers[i] : nullptr;
+    if (fast_)
+      layer_fast(i, n, start, lp, lc);
+    else
+      layer_generic(i, n, start, lp, lc);
+  }
+  launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
+  note_launch();
+}
+
+void Engine::drop_graphs() {
+  for (auto& kv : graphs_)
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+  graphs_.clear();
+}
+
 void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool capture, float* hidden_out,
                      std::unique_ptr<Prefix>* captured) {
   if (!finalized_) throw DgError("engine is not finalized");
@@ -284,18 +304,36 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
   DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
   gemm_ops_pending_.clear();
   DG_CUDA(cudaEventRecord(ev0_, stream_));
-  launch_embed(embedding_.ptr, 0, c_.hidden, ids_.as<uint32_t>(), n, x_.as<float>(), stream_);
-  note_launch();
-  for (int i = 0; i < c_.layers; ++i) {
-    const Prefix::LayerState* lp = past ? &past->layers[i] : nullptr;
-    Prefix::LayerState* lc = cap ? &cap->layers[i] : nullptr;
-    if (fast_)
-      layer_fast(i, n, start, lp, lc);
-    else
-      layer_generic(i, n, start, lp, lc);
+  if (!graphs_on_ || past || capture) {
+    run_layers(n, start, past, cap.get());
+  } else {
+    FwdGraph& g = graphs_[4 * n + (gemm_ev_.empty() ? 0 : 2) + (exact ? 1 : 0)];
+    if (g.exec) {
+      DG_CUDA(cudaGraphLaunch(g.exec, stream_));
+      gemm_ops_pending_ = g.gemm_ops;
+      note_launches(g.launches);
+    } else if (g.runs++ == 0) {
+      run_layers(n, start, nullptr, nullptr);
+    } else {
+      const uint64_t l0 = launch_count();
+      cudaGraph_t graph = nullptr;
+      DG_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+      try {
+        run_layers(n, start, nullptr, nullptr);
+      } catch (...) {
+        cudaStreamEndCapture(stream_, &graph);
+        if (graph) cudaGraphDestroy(graph);
+        throw;
+      }
+      DG_CUDA(cudaStreamEndCapture(stream_, &graph));
+      const cudaError_t e = cudaGraphInstantiate(&g.exec, graph, 0);
+      cudaGraphDestroy(graph);
+      DG_CUDA(e);
+      g.launches = launch_count() - l0;
+      g.gemm_ops = gemm_ops_pending_;
+      DG_CUDA(cudaGraphLaunch(g.exec, stream_));
+    }
   }
-  launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
-  note_launch();
   DG_CUDA(cudaEventRecord(ev1_, stream_));
   if (hidden_out)
     DG_CUDA(cudaMemcpyAsync(hidden_out, x_.ptr, size_t(n) * c_.hidden * 4, cudaMemcpyDeviceToHost, stream_));
@@ -325,7 +363,7 @@ void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* lo
   launch_lora_a(hnorm_.as<float>() + H, H, n_pos, H, head_k_.w_f32.as<float>(), P, hk_.as<float>(), P, true, stream_);
   launch_head_dot(hq_.as<float>(), hk_.as<float>(), n_pos, P, 1.0f / std::sqrt(float(P)), head_q_.bias.as<float>(),
                   head_k_.bias.as<float>(), hlogits_.as<float>(), stream_);
-  for (int j = 0; j < 4; ++j) note_launch();
+  for (int j = 0; j < 2; ++j) note_launch();  // head norm and head dot (LoRA-A kernels count themselves)
   DG_CUDA(cudaMemcpyAsync(logits_out, hlogits_.ptr, size_t(n_pos) * 4, cudaMemcpyDeviceToHost, stream_));
   DG_CUDA(cudaStreamSynchronize(stream_));
 }

@@ -1,5 +1,6 @@
 // Engine construction: tensor staging, load-time weight quantisation (bit-exact
 // with Data::quantize, src/weights.rs:98-146), device layouts and workspaces.
+#include <cstdlib>
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -105,12 +106,15 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   DG_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
   DG_CUDA(cudaEventCreate(&ev0_));
   DG_CUDA(cudaEventCreate(&ev1_));
+  // DG_CUDA_GRAPHS=0 launches every forward kernel by kernel (A/B timing).
+  if (const char* g = std::getenv("DG_CUDA_GRAPHS")) graphs_on_ = std::atoi(g) != 0;
 }
 
 Engine::~Engine() {
   if (stream_) {
     cudaSetDevice(device_);
     cudaStreamSynchronize(stream_);
+    drop_graphs();
     cudaStreamDestroy(stream_);
   }
   if (ev0_) cudaEventDestroy(ev0_);
@@ -124,6 +128,7 @@ void Engine::set_gemm_timing(bool on) {
   DG_CUDA(cudaStreamSynchronize(stream_));
   gemm_timing = GemmTiming{};
   gemm_ops_pending_.clear();
+  drop_graphs();  // captured graphs record into the event pool
   if (on && gemm_ev_.empty()) {
     gemm_ev_.resize(256, nullptr);
     for (auto& ev : gemm_ev_) DG_CUDA(cudaEventCreate(&ev));

@@ -443,6 +443,15 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
   mid[size_t(i / R) * ldm + i % R] = (c[0] + c[1]) + (c[2] + c[3]);
 }
 
+}  // namespace
+
+void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s) {
+  lora_a_reduce_kernel<<<(M * R + 127) / 128, 128, 0, s>>>(partial, slices, M, R, mid, ldm);
+  DG_CUDA(cudaGetLastError());
+}
+
+namespace {
+
 template <int TM, int RT>
 void launch_lora_splitk(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
                         float* partial, size_t partial_floats, cudaStream_t s) {
@@ -460,7 +469,7 @@ void launch_lora_splitk(const float* x, int ldx, int M, int K, const float* A, i
   if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
   lora_a_splitk_kernel<TM, RT><<<dim3(gx, gy, used), 256, T::SMEM, s>>>(x, ldx, M, K, A, R, partial, kslice);
   DG_CUDA(cudaGetLastError());
-  lora_a_reduce_kernel<<<(M * R + 127) / 128, 128, 0, s>>>(partial, used, M, R, mid, ldm);
+  launch_lora_a_reduce(partial, used, M, R, mid, ldm, s);
 }
 
 __device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale, int precision, int n, int k, int K) {
@@ -578,7 +587,7 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 }
 
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
-                   cudaStream_t s, float* partial, size_t partial_floats) {
+                   cudaStream_t s, float* partial, size_t partial_floats, DeviceStatus* st) {
   if (M <= 0 || R <= 0) return;
   const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
@@ -587,8 +596,14 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
     // still spread over R * M * 8 threads.
     const long t1 = long(M) * R * 8;
     lora_a_kernel<true, 1, 1><<<int((t1 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    note_launch();
   } else if (exact) {
     lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    note_launch();
+  } else if (partial && lora_a_tc_supported(x, ldx, K, A, R, ldm)) {
+    launch_lora_a_tc(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, st, s);
+    note_launch();  // tensor-core pass and its reduction
+    note_launch();
   } else if (partial && K % 32 == 0 && ldx % 4 == 0 && R % 4 == 0 && ldm % 4 == 0 &&
              reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0) {
     if (R <= 32)
@@ -597,9 +612,12 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
       launch_lora_splitk<64, 64>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
     else
       launch_lora_splitk<64, 128>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
+    note_launch();  // split-K pass and its reduction
+    note_launch();
   } else {
     const long warps = long((M + 3) / 4) * ((R + 3) / 4);
     lora_a_fast_kernel<<<int((warps * 32 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    note_launch();
   }
   DG_CUDA(cudaGetLastError());
 }
