@@ -1,4 +1,5 @@
 // extern "C" boundary of libdecider_gpu (declared in include/decider_gpu.h).
+#include <cstdlib>
 #include <atomic>
 #include <cmath>
 #include <cstring>
@@ -10,6 +11,13 @@ namespace dg {
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launch_count() { return g_launches.load(); }
 void note_launch() { g_launches.fetch_add(1); }
+bool pdl_enabled() {  // opt-in: measured no faster than plain stream order inside the forward's graph
+  static const bool on = [] {
+    const char* v = std::getenv("DG_PDL");
+    return v && std::atoi(v) != 0;
+  }();
+  return on;
+}
 void note_launches(uint64_t n) { g_launches.fetch_add(n); }
 }  // namespace dg
 
@@ -255,6 +263,23 @@ int dg_engine_gemm_timing(dg_engine* e, int enable) {
   return guarded([&] {
     check_engine(e);
     e->e->set_gemm_timing(enable != 0);
+  });
+}
+
+int dg_engine_gemm_timing_layers(dg_engine* e, int first_layer, int layers) {
+  return guarded([&] {
+    check_engine(e);
+    if (first_layer < 0 || layers < 0) throw std::runtime_error("layer range must be non-negative");
+    e->e->set_gemm_timing(true, first_layer, layers);
+  });
+}
+
+int dg_engine_gemm_time_all(const dg_engine* e, double* ops_all, uint64_t* launches_all) {
+  return guarded([&] {
+    check_engine(e);
+    if (!ops_all || !launches_all) throw std::runtime_error("null argument");
+    *ops_all = e->e->gemm_timing.ops_all;
+    *launches_all = e->e->gemm_timing.launches_all;
   });
 }
 

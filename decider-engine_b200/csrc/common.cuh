@@ -10,6 +10,7 @@
 
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
 #error "decider GPU kernels target sm_100a only"
@@ -53,6 +54,31 @@ struct CudaError : std::runtime_error {
     if (_e != cudaSuccess)                                                              \
       throw ::dg::CudaError(std::string(#expr) + ": " + cudaGetErrorString(_e));        \
   } while (0)
+
+// Programmatic dependent launch. Every kernel is launched with programmatic
+// stream serialization (launch_pdl), so its CTAs may start while the previous
+// kernel in the stream is still finishing: each kernel calls griddep_wait()
+// before its first global access that can depend on earlier kernels (reads
+// of their outputs, or writes to buffers they may still read); set-up that
+// touches only shared memory, TMEM or read-only weights may come first.
+// griddep_launch() then lets the next kernel's CTAs be scheduled.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+bool pdl_enabled();  // DG_PDL=1 sets the attribute (default: plain stream order)
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DG_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
 
 // Count of kernel launches issued by this library (host side), reported by
 // the C ABI so callers can see that device code ran.

@@ -42,6 +42,8 @@ struct ChunkState {
 
 __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, ChunkOut* __restrict__ outs,
                                                                int chunks) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* Ks = sm;                   // [CK][DK + 1]
   float* Qs = Ks + CK * (DK + 1);   // [CK][DK + 1]
@@ -269,6 +271,8 @@ __device__ __forceinline__ void cp16(void* smem, const void* gmem, int src_bytes
 
 __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
                                                                ChunkState* __restrict__ states, int chunks) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* S = sm;                                            // [DK][SC]
   float* D = S + DK * SC;                                   // [CK][SC]
@@ -370,6 +374,8 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
 constexpr int OUT_COLS = 64, OQ_LD = DK + 4, OS_LD = OUT_COLS + 4, OK_LD = CK + 4;
 __global__ void __launch_bounds__(256) delta_chunk_out_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
                                                               const ChunkState* __restrict__ states, int chunks) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* Qs = sm;                    // [CK][OQ_LD]
   float* Ss = Qs + CK * OQ_LD;       // [DK][OS_LD]
@@ -484,11 +490,11 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, out_smem));
     configured = true;
   }
-  delta_chunk_prep_kernel<<<int(units), 256, prep_smem, s>>>(a, outs, chunks);
+  launch_pdl(delta_chunk_prep_kernel, dim3(int(units)), dim3(256), prep_smem, s, a, outs, chunks);
   DG_CUDA(cudaGetLastError());
-  delta_chunk_scan_kernel<<<batch * a.value_heads * (a.dv / SC), 256, scan_smem, s>>>(a, outs, states, chunks);
+  launch_pdl(delta_chunk_scan_kernel, dim3(batch * a.value_heads * (a.dv / SC)), dim3(256), scan_smem, s, a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
-  delta_chunk_out_kernel<<<int(units) * (a.dv / OUT_COLS), 256, out_smem, s>>>(a, outs, states, chunks);
+  launch_pdl(delta_chunk_out_kernel, dim3(int(units) * (a.dv / OUT_COLS)), dim3(256), out_smem, s, a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
 }
 

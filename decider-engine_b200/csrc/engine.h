@@ -152,6 +152,8 @@ class Engine {
     cudaGraphExec_t exec = nullptr;
     uint64_t launches = 0;
     std::vector<double> gemm_ops;
+    double ops_all = 0.0;
+    uint64_t proj = 0;
   };
   std::map<int, FwdGraph> graphs_;
   bool graphs_on_ = true;
@@ -182,14 +184,20 @@ class Engine {
   // engine stream), read back after each forward.
   std::vector<cudaEvent_t> gemm_ev_;
   std::vector<double> gemm_ops_pending_;
+  int gemm_lo_ = 0, gemm_hi_ = 1 << 30, cur_layer_ = -1;
+  double fwd_ops_all_ = 0.0;  // projection ops of the current forward
+  uint64_t fwd_proj_ = 0;     // projection launches of the current forward
   void collect_gemm_timing();
 
  public:
   struct GemmTiming {
-    double ms = 0.0, ops = 0.0;  // summed launch time and algorithmic ops (2*M*N*K)
+    double ms = 0.0, ops = 0.0;  // timed launches: summed time and algorithmic ops (2*M*N*K)
     uint64_t launches = 0;
+    double ops_all = 0.0;        // every projection launch of the timed forwards
+    uint64_t launches_all = 0;
   } gemm_timing;
-  void set_gemm_timing(bool on);
+  // Times the projections of layers [first_layer, first_layer + layers) only.
+  void set_gemm_timing(bool on, int first_layer = 0, int layers = 1 << 30);
 };
 
 // Checkpoint directory in the reference's layout (loader.cu): the validated

@@ -42,7 +42,9 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.ldo = ldo;
   a.status = status();
   const size_t k = gemm_ops_pending_.size();
-  const bool timed = 2 * k + 2 <= gemm_ev_.size();
+  fwd_ops_all_ += 2.0 * M * p.out * p.in;
+  ++fwd_proj_;
+  const bool timed = cur_layer_ >= gemm_lo_ && cur_layer_ < gemm_hi_ && 2 * k + 2 <= gemm_ev_.size();
   // While a graph is captured, external records become event nodes of it.
   unsigned rec = cudaEventRecordDefault;
   if (timed) {
@@ -265,11 +267,13 @@ void Engine::run_layers(int n, int start, const Prefix* past, Prefix* cap) {
   for (int i = 0; i < c_.layers; ++i) {
     const Prefix::LayerState* lp = past ? &past->layers[i] : nullptr;
     Prefix::LayerState* lc = cap ? &cap->layers[i] : nullptr;
+    cur_layer_ = i;
     if (fast_)
       layer_fast(i, n, start, lp, lc);
     else
       layer_generic(i, n, start, lp, lc);
   }
+  cur_layer_ = -1;
   launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
   note_launch();
 }
@@ -303,6 +307,8 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
   DG_CUDA(cudaMemcpyAsync(ids_.ptr, ids, size_t(n) * 4, cudaMemcpyHostToDevice, stream_));
   DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
   gemm_ops_pending_.clear();
+  fwd_ops_all_ = 0.0;
+  fwd_proj_ = 0;
   DG_CUDA(cudaEventRecord(ev0_, stream_));
   if (!graphs_on_ || past || capture) {
     run_layers(n, start, past, cap.get());
@@ -311,6 +317,8 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
     if (g.exec) {
       DG_CUDA(cudaGraphLaunch(g.exec, stream_));
       gemm_ops_pending_ = g.gemm_ops;
+      fwd_ops_all_ = g.ops_all;
+      fwd_proj_ = g.proj;
       note_launches(g.launches);
     } else if (g.runs++ == 0) {
       run_layers(n, start, nullptr, nullptr);
@@ -331,6 +339,8 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
       DG_CUDA(e);
       g.launches = launch_count() - l0;
       g.gemm_ops = gemm_ops_pending_;
+      g.ops_all = fwd_ops_all_;
+      g.proj = fwd_proj_;
       DG_CUDA(cudaGraphLaunch(g.exec, stream_));
     }
   }

@@ -123,11 +123,13 @@ Engine::~Engine() {
 }
 
 // Timing covers up to 128 projection launches per forward (24 layers use 96).
-void Engine::set_gemm_timing(bool on) {
+void Engine::set_gemm_timing(bool on, int first_layer, int layers) {
   DG_CUDA(cudaSetDevice(device_));
   DG_CUDA(cudaStreamSynchronize(stream_));
   gemm_timing = GemmTiming{};
   gemm_ops_pending_.clear();
+  gemm_lo_ = std::max(0, first_layer);
+  gemm_hi_ = layers >= (1 << 30) - gemm_lo_ ? (1 << 30) : gemm_lo_ + std::max(0, layers);
   drop_graphs();  // captured graphs record into the event pool
   if (on && gemm_ev_.empty()) {
     gemm_ev_.resize(256, nullptr);
@@ -139,6 +141,10 @@ void Engine::set_gemm_timing(bool on) {
 }
 
 void Engine::collect_gemm_timing() {
+  if (!gemm_ev_.empty()) {
+    gemm_timing.ops_all += fwd_ops_all_;
+    gemm_timing.launches_all += fwd_proj_;
+  }
   for (size_t k = 0; k < gemm_ops_pending_.size(); ++k) {
     float ms = 0.0f;
     DG_CUDA(cudaEventElapsedTime(&ms, gemm_ev_[2 * k], gemm_ev_[2 * k + 1]));

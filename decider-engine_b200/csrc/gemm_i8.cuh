@@ -221,6 +221,9 @@ __global__ void __launch_bounds__(576, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Set-up above touched only shared memory, TMEM and weights.
+  griddep_wait();
+  griddep_launch();
 
   if (warp == 0) {
     int issued = 0;

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __res
                                                               float* __restrict__ n_out, int ldn,
                                                               int8_t* __restrict__ xq, float* __restrict__ xs,
                                                               int ldxs, DeviceStatus* st) {
+  griddep_wait();
+  griddep_launch();
   const int m = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
   if (m >= M) return;
   const float4* xr = reinterpret_cast<const float4*>(x + size_t(m) * ldx);
@@ -131,6 +133,8 @@ __global__ void __launch_bounds__(256) norm_quant_warp_kernel(const float* __res
 __global__ void norm_quant_kernel(const float* __restrict__ x, int ldx, int K, const float* __restrict__ gamma,
                                   float eps, float* __restrict__ n_out, int ldn, int8_t* __restrict__ xq,
                                   float* __restrict__ xs, int ldxs, DeviceStatus* st) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float row[];
   __shared__ float red[8];
   const int m = blockIdx.x;
@@ -170,6 +174,8 @@ __global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float
                                         int dv, const float* __restrict__ w, float eps, float* __restrict__ out,
                                         int8_t* __restrict__ xq, float* __restrict__ xs, int ldxs, int quantize,
                                         DeviceStatus* st) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float row[];
   const int m = blockIdx.x, K = heads * dv;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -210,6 +216,8 @@ template <bool EXACT, int TM = 4, int TR = 4>
 __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                      const float* __restrict__ A, int R, float* __restrict__ mid,
                                                      int ldm) {
+  griddep_wait();
+  griddep_launch();
   const long gid = long(blockIdx.x) * blockDim.x + threadIdx.x;
   const int lane8 = int(gid & 7);
   const long tile = gid >> 3;
@@ -271,6 +279,8 @@ __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x
 __global__ void __launch_bounds__(256) lora_a_fast_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                           const float* __restrict__ A, int R, float* __restrict__ mid,
                                                           int ldm) {
+  griddep_wait();
+  griddep_launch();
   constexpr int TM = 4, TR = 4;
   const long tile = (long(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -351,6 +361,8 @@ template <int TM, int RT>
 __global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restrict__ x, int ldx, int M, int K,
                                                             const float* __restrict__ A, int R,
                                                             float* __restrict__ partial, int kslice) {
+  griddep_wait();
+  griddep_launch();
   using T = LoraTile<TM, RT>;
   constexpr int LD = T::LD, NOG = T::NOG, OPT = T::OPT, KC = T::KC;
   extern __shared__ __align__(16) float lora_smem[];
@@ -428,6 +440,8 @@ __global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restr
 // as (c0 + c1) + (c2 + c3): a fixed order, so the result is deterministic.
 __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M,
                                                             int R, float* __restrict__ mid, int ldm) {
+  griddep_wait();
+  griddep_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * R) return;
   const size_t stride = size_t(M) * R;
@@ -446,7 +460,7 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
 }  // namespace
 
 void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s) {
-  lora_a_reduce_kernel<<<(M * R + 127) / 128, 128, 0, s>>>(partial, slices, M, R, mid, ldm);
+  launch_pdl(lora_a_reduce_kernel, dim3((M * R + 127) / 128), dim3(128), 0, s, partial, slices, M, R, mid, ldm);
   DG_CUDA(cudaGetLastError());
 }
 
@@ -467,7 +481,7 @@ void launch_lora_splitk(const float* x, int ldx, int M, int K, const float* A, i
   const int kslice = ((K + slices - 1) / slices + T::KC - 1) / T::KC * T::KC;
   const int used = (K + kslice - 1) / kslice;
   if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
-  lora_a_splitk_kernel<TM, RT><<<dim3(gx, gy, used), 256, T::SMEM, s>>>(x, ldx, M, K, A, R, partial, kslice);
+  launch_pdl(lora_a_splitk_kernel<TM, RT>, dim3(dim3(gx, gy, used)), dim3(256), T::SMEM, s, x, ldx, M, K, A, R, partial, kslice);
   DG_CUDA(cudaGetLastError());
   launch_lora_a_reduce(partial, used, M, R, mid, ldm, s);
 }
@@ -489,6 +503,8 @@ __device__ __forceinline__ float dequant(const uint8_t* wq, const float* wscale,
 __global__ void proj_generic_kernel(GenericProj p, const float* __restrict__ x, int ldx, const int8_t* __restrict__ xq,
                                     const float* __restrict__ xs, int ldxs, const float* __restrict__ mid, int ldm,
                                     int M, float* __restrict__ out, int ldo, int epi) {
+  griddep_wait();
+  griddep_launch();
   const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
   if (n >= p.out || m >= M) return;
   const int K = p.in;
@@ -544,6 +560,8 @@ __global__ void proj_generic_kernel(GenericProj p, const float* __restrict__ x, 
 }
 
 __global__ void embed_kernel(const void* table, int dtype, int hidden, const uint32_t* ids, float* x) {
+  griddep_wait();
+  griddep_launch();
   const int t = blockIdx.x;
   const size_t row = size_t(ids[t]) * hidden;
   for (int k = threadIdx.x; k < hidden; k += blockDim.x) {
@@ -566,13 +584,13 @@ void launch_norm_quant(const float* x, int ldx, int M, int K, const float* gamma
                        reinterpret_cast<uintptr_t>(x) % 16 == 0;
   const int blocks = (M + 7) / 8;
   if (aligned && !gamma && xq) {
-    norm_quant_warp_kernel<0><<<dim3(blocks, (K / 128 + 3) / 4), 256, 0, s>>>(x, ldx, M, K, nullptr, eps, n_out, ldn,
+    launch_pdl(norm_quant_warp_kernel<0>, dim3(dim3(blocks, (K / 128 + 3) / 4)), dim3(256), 0, s, x, ldx, M, K, nullptr, eps, n_out, ldn,
                                                                             xq, xs, ldxs, st);
   } else if (aligned && gamma && K == 2048) {
     // Two rows (warps) per CTA: 256 CTAs at 512 tokens spread over every SM.
-    norm_quant_warp_kernel<16><<<(M + 1) / 2, 64, 0, s>>>(x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+    launch_pdl(norm_quant_warp_kernel<16>, dim3((M + 1) / 2), dim3(64), 0, s, x, ldx, M, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
   } else {
-    norm_quant_kernel<<<M, 256, K * sizeof(float), s>>>(x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
+    launch_pdl(norm_quant_kernel, dim3(M), dim3(256), K * sizeof(float), s, x, ldx, K, gamma, eps, n_out, ldn, xq, xs, ldxs, st);
   }
   DG_CUDA(cudaGetLastError());
 }
@@ -581,7 +599,7 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
                              float eps, float* out, int8_t* xq, float* xs, int ldxs, bool quantize, DeviceStatus* st,
                              cudaStream_t s) {
   if (M <= 0) return;
-  gated_norm_quant_kernel<<<M, 256, heads * dv * sizeof(float), s>>>(o, z, ldz, heads, dv, w, eps, out, xq, xs, ldxs,
+  launch_pdl(gated_norm_quant_kernel, dim3(M), dim3(256), heads * dv * sizeof(float), s, o, z, ldz, heads, dv, w, eps, out, xq, xs, ldxs,
                                                                       quantize ? 1 : 0, st);
   DG_CUDA(cudaGetLastError());
 }
@@ -595,10 +613,10 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
     // One row x one output per group of eight lanes: the head's few rows
     // still spread over R * M * 8 threads.
     const long t1 = long(M) * R * 8;
-    lora_a_kernel<true, 1, 1><<<int((t1 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    launch_pdl(lora_a_kernel<true, 1, 1>, dim3(int((t1 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
     note_launch();
   } else if (exact) {
-    lora_a_kernel<true><<<blocks, 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    launch_pdl(lora_a_kernel<true>, dim3(blocks), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
     note_launch();
   } else if (partial && lora_a_tc_supported(x, ldx, K, A, R, ldm)) {
     launch_lora_a_tc(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, st, s);
@@ -616,7 +634,7 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
     note_launch();
   } else {
     const long warps = long((M + 3) / 4) * ((R + 3) / 4);
-    lora_a_fast_kernel<<<int((warps * 32 + 255) / 256), 256, 0, s>>>(x, ldx, M, K, A, R, mid, ldm);
+    launch_pdl(lora_a_fast_kernel, dim3(int((warps * 32 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
     note_launch();
   }
   DG_CUDA(cudaGetLastError());
@@ -626,13 +644,13 @@ void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const in
                          const float* mid, int ldm, int M, float* out, int ldo, int epi, cudaStream_t s) {
   if (M <= 0) return;
   dim3 grid((p.out + 127) / 128, M);
-  proj_generic_kernel<<<grid, 128, 0, s>>>(p, x, ldx, xq, xs, ldxs, mid, ldm, M, out, ldo, epi);
+  launch_pdl(proj_generic_kernel, dim3(grid), dim3(128), 0, s, p, x, ldx, xq, xs, ldxs, mid, ldm, M, out, ldo, epi);
   DG_CUDA(cudaGetLastError());
 }
 
 void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids, int n, float* x, cudaStream_t s) {
   if (n <= 0) return;
-  embed_kernel<<<n, 256, 0, s>>>(table, dtype, hidden, ids, x);
+  launch_pdl(embed_kernel, dim3(n), dim3(256), 0, s, table, dtype, hidden, ids, x);
   DG_CUDA(cudaGetLastError());
 }
 

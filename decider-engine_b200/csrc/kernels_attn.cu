@@ -32,6 +32,8 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int ldq, int 
                                     const float* __restrict__ qn, const float* __restrict__ kn, float eps,
                                     const float* __restrict__ rope, int half, int start, float* __restrict__ q_out,
                                     float* __restrict__ kcache, float* __restrict__ vcache) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float buf[];  // [warps][d]
   const int t = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
   float* x = buf + warp * d;
@@ -91,6 +93,8 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
                                                            const float* __restrict__ gate_src, int ld_gate, int n,
                                                            int offset, int heads, int kv_heads,
                                                            float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float sm[];
   float* Qs = sm;                       // [ABQ][AD]
   float* Kt = Qs + ABQ * AD;            // [AD][ABK + 1]
@@ -226,6 +230,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
     attention256_split_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                               const float* __restrict__ gate_src, int ld_gate, int n, int offset, int heads,
                               int kv_heads, float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* Qs = sm;               // [TQ][TLD]
   float* Ks = Qs + TQ * TLD;    // [TK][TLD]; at the end CTA 1's o [TQ][TLD]
@@ -408,6 +414,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
 __global__ void attention_generic_kernel(const float* __restrict__ q, const float* __restrict__ kc,
                                          const float* __restrict__ vc, const float* __restrict__ gate_src, int ld_gate,
                                          int n, int offset, int heads, int kv_heads, int d, float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int id = blockIdx.x * blockDim.x + threadIdx.x;
   if (id >= n * heads) return;
   const int t = id / heads, h = id % heads, kh = h / (heads / kv_heads), kw = kv_heads * d;
@@ -443,6 +451,8 @@ __global__ void attention_generic_kernel(const float* __restrict__ q, const floa
 // check of src/qwen.rs:496-498. One 256-thread CTA per row.
 __global__ void final_norm_kernel(float* __restrict__ x, int K, const float* __restrict__ g, float eps,
                                   DeviceStatus* st) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[8];
   __shared__ int bad;
   float* r = x + size_t(blockIdx.x) * K;
@@ -472,6 +482,8 @@ __global__ void final_norm_kernel(float* __restrict__ x, int K, const float* __r
 // Head::normalize, src/lib.rs:106-115: mean, biased variance, eps 1e-5.
 __global__ void head_norm_kernel(const float* __restrict__ hidden, int K, const int* __restrict__ rows,
                                  const float* __restrict__ w, const float* __restrict__ b, float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[8];
   __shared__ float bc;
   const float* x = hidden + size_t(rows[blockIdx.x]) * K;
@@ -507,6 +519,8 @@ __global__ void head_norm_kernel(const float* __restrict__ hidden, int K, const 
 __global__ void head_dot_kernel(const float* __restrict__ q, const float* __restrict__ k, int n_keys, int dim,
                                 float scale, const float* __restrict__ bq, const float* __restrict__ bk,
                                 float* __restrict__ logits) {
+  griddep_wait();
+  griddep_launch();
   // One warp per key; lane l < 8 runs the reference's lane l (indices l, l+8, ...).
   const int i = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
   if (i >= n_keys) return;
@@ -534,7 +548,7 @@ void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_hea
                          const float* kn, float eps, const float* rope, int half, int start, float* q_out,
                          float* kcache, float* vcache, cudaStream_t s) {
   if (n <= 0) return;
-  qk_norm_rope_kernel<<<n, 256, 8 * d * sizeof(float), s>>>(qkv, ldq, heads, kv_heads, d, qn, kn, eps, rope, half,
+  launch_pdl(qk_norm_rope_kernel, dim3(n), dim3(256), 8 * d * sizeof(float), s, qkv, ldq, heads, kv_heads, d, qn, kn, eps, rope, half,
                                                             start, q_out, kcache, vcache);
   DG_CUDA(cudaGetLastError());
 }
@@ -552,7 +566,7 @@ void launch_attention(const float* q, const float* kcache, const float* vcache, 
       configured = true;
     }
     dim3 grid(2 * ((n + TQ - 1) / TQ), heads);  // clusters of two along x
-    attention256_split_kernel<<<grid, 256, ATT_SMEM, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
+    launch_pdl(attention256_split_kernel, dim3(grid), dim3(256), ATT_SMEM, s, q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
                                                           kv_heads, out);
   } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
@@ -562,10 +576,10 @@ void launch_attention(const float* q, const float* kcache, const float* vcache, 
       configured = true;
     }
     dim3 grid((n + ABQ - 1) / ABQ, heads);
-    attention256_kernel<<<grid, 128, smem, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out);
+    launch_pdl(attention256_kernel, dim3(grid), dim3(128), smem, s, q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out);
   } else {
     const int threads = n * heads;
-    attention_generic_kernel<<<(threads + 127) / 128, 128, 0, s>>>(q, kcache, vcache, gate_src, ld_gate, n, offset,
+    launch_pdl(attention_generic_kernel, dim3((threads + 127) / 128), dim3(128), 0, s, q, kcache, vcache, gate_src, ld_gate, n, offset,
                                                                    heads, kv_heads, d, out);
   }
   DG_CUDA(cudaGetLastError());
@@ -573,21 +587,21 @@ void launch_attention(const float* q, const float* kcache, const float* vcache, 
 
 void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, DeviceStatus* st, cudaStream_t s) {
   if (M <= 0) return;
-  final_norm_kernel<<<M, 256, 0, s>>>(x, K, gamma, eps, st);
+  launch_pdl(final_norm_kernel, dim3(M), dim3(256), 0, s, x, K, gamma, eps, st);
   DG_CUDA(cudaGetLastError());
 }
 
 void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, const float* w, const float* b,
                       float* out, cudaStream_t s) {
   if (n_rows <= 0) return;
-  head_norm_kernel<<<n_rows, 256, 0, s>>>(hidden, K, rows, w, b, out);
+  launch_pdl(head_norm_kernel, dim3(n_rows), dim3(256), 0, s, hidden, K, rows, w, b, out);
   DG_CUDA(cudaGetLastError());
 }
 
 void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, const float* bq,
                      const float* bk, float* logits, cudaStream_t s) {
   if (n_keys <= 0) return;
-  head_dot_kernel<<<(n_keys + 3) / 4, 128, 0, s>>>(q, k, n_keys, dim, scale, bq, bk, logits);
+  launch_pdl(head_dot_kernel, dim3((n_keys + 3) / 4), dim3(128), 0, s, q, k, n_keys, dim, scale, bq, bk, logits);
   DG_CUDA(cudaGetLastError());
 }
 

@@ -21,6 +21,8 @@ constexpr int CONV_T = 16, CONV_KMAX = 8;
 __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldr, const float* __restrict__ tail, int tail_rows,
                                  int n, int start, int W, int kernel, const float* __restrict__ taps,
                                  float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int c = blockIdx.x * blockDim.x + threadIdx.x, t0 = blockIdx.y * CONV_T;
   if (c >= W) return;
   float w[CONV_KMAX];
@@ -59,6 +61,8 @@ __global__ void delta_prep_kernel(float* __restrict__ conv, int W, int key_heads
                                   const float* __restrict__ a, const float* __restrict__ b, int ldab,
                                   const float* __restrict__ rate, const float* __restrict__ dt, float* __restrict__ decay,
                                   float* __restrict__ beta) {
+  griddep_wait();
+  griddep_launch();
   const int t = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nwarps = blockDim.x / 32;
   float* row = conv + size_t(t) * W;
   const float rdk = sqrtf(float(dk));
@@ -83,6 +87,8 @@ __global__ void delta_rec_generic_kernel(const float* __restrict__ conv, int n, 
                                          int value_heads, int dv, const float* __restrict__ decay,
                                          const float* __restrict__ beta, float* __restrict__ state,
                                          float* __restrict__ o) {
+  griddep_wait();
+  griddep_launch();
   const int id = blockIdx.x * blockDim.x + threadIdx.x;
   if (id >= value_heads * dv) return;
   const int h = id / dv, j = id % dv, kh = h / (value_heads / key_heads), kd = key_heads * dk;
@@ -132,6 +138,8 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 __global__ void __launch_bounds__(128) delta_rec128_kernel(DeltaArgs a) {
+  griddep_wait();
+  griddep_launch();
   constexpr int DK = 128;
   extern __shared__ __align__(16) uint8_t rec_smem[];
   RecStage* st = reinterpret_cast<RecStage*>(rec_smem);
@@ -231,6 +239,8 @@ __global__ void __launch_bounds__(128) delta_rec128_kernel(DeltaArgs a) {
 }
 
 __global__ void exp_kernel(const float* __restrict__ g, float* __restrict__ out, size_t n) {
+  griddep_wait();
+  griddep_launch();
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
     out[i] = expf(g[i]);
 }
@@ -242,7 +252,7 @@ void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int t
   if (n <= 0) return;
   if (kernel < 1 || kernel > CONV_KMAX) throw CudaError("conv: kernel width must be 1..8");
   dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T);
-  conv_silu_kernel<<<grid, 256, 0, s>>>(raw, ldr, tail, tail_rows, n, start, W, kernel, taps, out);
+  launch_pdl(conv_silu_kernel, dim3(grid), dim3(256), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps, out);
   DG_CUDA(cudaGetLastError());
 }
 
@@ -250,7 +260,7 @@ void launch_delta_prep(float* conv, int W, int n, int key_heads, int dk, int val
                        const float* b, int ldab, const float* decay_rate, const float* dt, float* decay, float* beta,
                        cudaStream_t s) {
   if (n <= 0) return;
-  delta_prep_kernel<<<n, 256, 0, s>>>(conv, W, key_heads, dk, value_heads, a, b, ldab, decay_rate, dt, decay, beta);
+  launch_pdl(delta_prep_kernel, dim3(n), dim3(256), 0, s, conv, W, key_heads, dk, value_heads, a, b, ldab, decay_rate, dt, decay, beta);
   DG_CUDA(cudaGetLastError());
 }
 
@@ -278,7 +288,7 @@ void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, in
     launch_delta_rec128(a, 1, s);
   } else {
     const int threads = value_heads * dv;
-    delta_rec_generic_kernel<<<(threads + 127) / 128, 128, 0, s>>>(conv, n, W, key_heads, dk, value_heads, dv, decay,
+    launch_pdl(delta_rec_generic_kernel, dim3((threads + 127) / 128), dim3(128), 0, s, conv, n, W, key_heads, dk, value_heads, dv, decay,
                                                                    beta, state, o);
     DG_CUDA(cudaGetLastError());
   }
@@ -294,13 +304,13 @@ void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s) {
     configured = true;
   }
   dim3 grid(a.value_heads * (a.dv / REC_COLS), batch);
-  delta_rec128_kernel<<<grid, 128, smem, s>>>(a);
+  launch_pdl(delta_rec128_kernel, dim3(grid), dim3(128), smem, s, a);
   DG_CUDA(cudaGetLastError());
 }
 
 void launch_exp(const float* g, float* out, size_t n, cudaStream_t s) {
   if (!n) return;
-  exp_kernel<<<592, 256, 0, s>>>(g, out, n);
+  launch_pdl(exp_kernel, dim3(592), dim3(256), 0, s, g, out, n);
   DG_CUDA(cudaGetLastError());
 }
 

@@ -73,6 +73,8 @@ __global__ void __launch_bounds__(kLaThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *holder;
+  griddep_wait();  // set-up above touched only shared memory and TMEM
+  griddep_launch();
   const uint32_t idesc = idesc_tf32(128, uint32_t(NP));
   const int items = (128 + NP) * 8;  // 16-byte pieces per chunk: x rows, then A rows
   bool ok = true;
@@ -177,7 +179,7 @@ void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int
   const int kslice = ((K + splits - 1) / splits + 31) / 32 * 32;
   const int used = (K + kslice - 1) / kslice;
   if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
-  lora_a_tc_kernel<<<dim3(mt, used), kLaThreads, lora_tc_smem_bytes(NP), s>>>(x, ldx, M, K, A, R, NP, partial, kslice,
+  launch_pdl(lora_a_tc_kernel, dim3(dim3(mt, used)), dim3(kLaThreads), lora_tc_smem_bytes(NP), s, x, ldx, M, K, A, R, NP, partial, kslice,
                                                                             st);
   DG_CUDA(cudaGetLastError());
   launch_lora_a_reduce(partial, used, M, R, mid, ldm, s);

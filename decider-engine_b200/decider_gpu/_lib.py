@@ -18,6 +18,7 @@ SYMBOLS = [
     "dg_engine_load", "dg_read_checkpoint_config",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
+    "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
@@ -68,6 +69,8 @@ def load() -> C.CDLL:
     L.dg_engine_last_forward_ms.restype = C.c_float
     L.dg_engine_last_launches.argtypes = [vp]
     L.dg_engine_gemm_timing.argtypes = [vp, i32]
+    L.dg_engine_gemm_timing_layers.argtypes = [vp, i32, i32]
+    L.dg_engine_gemm_time_all.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
     L.dg_engine_gemm_time.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
     L.dg_linear_stream.argtypes = [vp]
     L.dg_linear_stream.restype = vp

@@ -134,6 +134,16 @@ class GpuModel:
         """Bracket every tcgen05 projection launch with CUDA events (resets the totals)."""
         check(load().dg_engine_gemm_timing(self.h, int(enable)))
 
+    def gemm_timing_layers(self, first_layer: int, layers: int) -> None:
+        """Events around the projections of layers [first_layer, first_layer + layers) only."""
+        check(load().dg_engine_gemm_timing_layers(self.h, int(first_layer), int(layers)))
+
+    def gemm_time_all(self):
+        """(summed 2*M*N*K ops, launches) of every projection of the timed forwards."""
+        ops, n = C.c_double(), C.c_uint64()
+        check(load().dg_engine_gemm_time_all(self.h, C.byref(ops), C.byref(n)))
+        return ops.value, n.value
+
     def gemm_time(self):
         """(summed launch ms, summed 2*M*N*K ops, launches) since gemm_timing()."""
         ms, ops, n = C.c_double(), C.c_double(), C.c_uint64()

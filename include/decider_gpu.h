@@ -95,6 +95,12 @@ int dg_engine_last_launches(const dg_engine* e);
  * dg_engine_gemm_timing call, which also resets them. */
 int dg_engine_gemm_timing(dg_engine* e, int enable);
 int dg_engine_gemm_time(const dg_engine* e, double* ms, double* ops, uint64_t* launches);
+/* As dg_engine_gemm_timing(e, 1), but only the projections of layers
+ * [first_layer, first_layer + layers) get events (a sample that perturbs the
+ * forward less); dg_engine_gemm_time_all returns the algorithmic ops and launch
+ * count of every projection of the timed forwards, sampled or not. */
+int dg_engine_gemm_timing_layers(dg_engine* e, int first_layer, int layers);
+int dg_engine_gemm_time_all(const dg_engine* e, double* ops_all, uint64_t* launches_all);
 
 /* ---- forward passes: Model::forward / prefill / forward_after
  * (src/qwen.rs:407-424). `past` may be NULL. hidden_out (nullable) receives
