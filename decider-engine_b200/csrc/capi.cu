@@ -109,7 +109,6 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
   DeviceStatus* st = l->status.as<DeviceStatus>();
   launch_norm_quant(x_dev, l->k, m, l->k, nullptr, 0.0f, nullptr, 0, l->xq.as<int8_t>(), l->xs.as<float>(), l->ldxs, st,
                     l->stream);
-  note_launch();
   if (l->rank) {
     launch_lora_a(x_dev, l->k, m, l->k, l->lora_a.as<float>(), l->rank, l->mid.as<float>(), 32, l->exact, l->stream);
   }
@@ -138,7 +137,6 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
   }
   a.dots = dump;
   launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
-  note_launch();
   if (!direct)
     DG_CUDA(cudaMemcpy2DAsync(y_dev, size_t(l->n) * 4, l->y.ptr, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
                               cudaMemcpyDeviceToDevice, l->stream));
@@ -465,7 +463,6 @@ int dg_gated_delta_rule_device(const float* q, const float* k, const float* v, c
   return guarded([&] {
     dg::DeltaArgs a = delta_args(q, k, v, g, beta, batch, t, heads, state, o);
     dg::launch_delta_rec128(a, batch, static_cast<cudaStream_t>(stream));
-    dg::note_launch();
   });
 }
 
@@ -481,8 +478,6 @@ int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const flo
     dg::DeltaArgs a = delta_args(q, k, v, g, beta, batch, t, heads, state, o);
     if (!workspace) throw std::runtime_error("null workspace");
     dg::launch_delta_chunked(a, batch, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
-    dg::note_launch();
-    dg::note_launch();
   });
 }
 
@@ -563,7 +558,6 @@ int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m,
     DG_CUDA(cudaMemsetAsync(st, 0, sizeof(DeviceStatus), l->stream));
     DG_CUDA(cudaMemsetAsync(xs, 0, xs_bytes, l->stream));
     launch_norm_quant(x_device, l->k, m, l->k, nullptr, 0.0f, nullptr, 0, xq, xs, ldxs, st, l->stream);
-    note_launch();
     if (l->rank) {
       launch_lora_a(x_device, l->k, m, l->k, l->lora_a.as<float>(), l->rank, mid, 32, l->exact, l->stream);
     }
@@ -586,7 +580,6 @@ int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m,
     a.status = st;
     a.dots = nullptr;
     launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
-    note_launch();
     if (!direct)
       DG_CUDA(cudaMemcpy2DAsync(y_device, size_t(l->n) * 4, ypad, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
                                 cudaMemcpyDeviceToDevice, l->stream));

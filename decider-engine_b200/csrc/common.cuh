@@ -4,6 +4,8 @@
 // fused multiply-add explicitly (fmaf / __fmaf_rn), so the reference-order
 // paths reproduce the CPU engine's FP32 rounding.
 #pragma once
+#include <cfloat>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -55,6 +57,12 @@ struct CudaError : std::runtime_error {
       throw ::dg::CudaError(std::string(#expr) + ": " + cudaGetErrorString(_e));        \
   } while (0)
 
+// Count of kernel launches issued by this library (host side), reported by
+// the C ABI so callers can see that device code ran.
+uint64_t launch_count();
+void note_launches(uint64_t n);
+void note_launch();
+
 // Programmatic dependent launch. Every kernel is launched with programmatic
 // stream serialization (launch_pdl), so its CTAs may start while the previous
 // kernel in the stream is still finishing: each kernel calls griddep_wait()
@@ -78,13 +86,9 @@ void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   DG_CUDA(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  note_launch();  // every kernel of the library goes through here
 }
 
-// Count of kernel launches issued by this library (host side), reported by
-// the C ABI so callers can see that device code ran.
-uint64_t launch_count();
-void note_launches(uint64_t n);
-void note_launch();
 
 // ---------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -301,6 +305,24 @@ __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
       : "=f"(r.x), "=f"(r.y)
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
   return r;
+}
+
+// Group-64 quantisation of the four values a lane holds; the 16 lanes of a
+// half-warp hold one 64-wide group (same formula as quantize_group_warp).
+__device__ __forceinline__ void quantize_vec4_halfwarp(float4 v, int8_t* q_out, float* scale_out, bool leader,
+                                                       bool* bad) {
+  float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  *bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+  const float scale = mx == 0.0f ? 1.0f : fmaxf(mx / 127.0f, FLT_MIN);
+  char4 q;
+  q.x = int8_t(fminf(fmaxf(roundf(v.x / scale), -127.0f), 127.0f));
+  q.y = int8_t(fminf(fmaxf(roundf(v.y / scale), -127.0f), 127.0f));
+  q.z = int8_t(fminf(fmaxf(roundf(v.z / scale), -127.0f), 127.0f));
+  q.w = int8_t(fminf(fmaxf(roundf(v.w / scale), -127.0f), 127.0f));
+  *reinterpret_cast<char4*>(q_out) = q;
+  if (leader) *scale_out = scale;
 }
 
 // ---------------------------------------------------------------- math

@@ -54,7 +54,6 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
     DG_CUDA(cudaEventRecordWithFlags(gemm_ev_[2 * k], stream_, rec));
   }
   launch_gemm_i8(act_map(xq_.ptr, p.in, M), p.maps, a, 32, epi, exact, stream_);
-  note_launch();
   if (timed) {
     DG_CUDA(cudaEventRecordWithFlags(gemm_ev_[2 * k + 1], stream_, rec));
     gemm_ops_pending_.push_back(2.0 * M * p.out * p.in);
@@ -67,7 +66,6 @@ void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, 
   }
   launch_proj_generic(p.g, x, ldx, xq_.as<int8_t>(), xs_.as<float>(), ldxs_, mid_.as<float>(), 128, M, out, ldo, epi,
                       stream_);
-  note_launch();
 }
 
 // DeltaNet mixer after the input projections (src/qwen.rs:667-693): conv with
@@ -112,7 +110,6 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
     da.o = o_.as<float>();
     da.ldo = H * c.dv;
     launch_delta_chunked(da, 1, delta_ws_.ptr, delta_ws_.bytes, stream_);
-    note_launch();
   } else {
     launch_delta_recurrence(conv_.as<float>(), n, c.key_heads, c.dk, H, c.dv, decay_.as<float>(),
                             beta_.as<float>(), state_[i].as<float>(), o_.as<float>(), stream_);
@@ -120,7 +117,6 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
   const bool q = precision_ == kInt8Compute;
   launch_gated_norm_quant(o_.as<float>(), base + off[1], ldr, n, H, c.dv, L.norm.as<float>(), c.eps, ofin_.as<float>(),
                           xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);
-  for (int j = 0; j < 5; ++j) note_launch();
   if (cap) {
     cap->full = false;
     cap->state = DevBuf(sbytes);
@@ -165,7 +161,6 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
                      c.heads, c.kv_heads, d, att_.as<float>(), stream_);
     launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(),
                       xs_.as<float>(), ldxs_, status(), stream_);
-    for (int j = 0; j < 3; ++j) note_launch();
     if (cap) {
       cap->full = true;
       cap->k = DevBuf(size_t(start + n) * kw * 4);
@@ -202,7 +197,6 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
   float* proj = proj_.as<float>();
   int8_t* xq = q ? xq_.as<int8_t>() : nullptr;
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq, xs_.as<float>(), ldxs_, status(), stream_);
-  note_launch();
   const int* off = L.in_proj.part_off.data();
   int mlp = 0;
   if (L.full) {
@@ -217,12 +211,9 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
                         vcache_[i].as<float>(), stream_);
     launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
                      c.heads, c.kv_heads, d, att_.as<float>(), stream_);
-    note_launch();
-    note_launch();
     if (q) {
       launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq, xs_.as<float>(), ldxs_,
                         status(), stream_);
-      note_launch();
     }
     if (cap) {
       cap->full = true;
@@ -240,13 +231,11 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
     mlp = 5;
   }
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq, xs_.as<float>(), ldxs_, status(), stream_);
-  note_launch();
   run_proj_generic(L.parts[mlp], nb, H, n, h_.as<float>(), I, kEpiWrite);
   run_proj_generic(L.parts[mlp + 1], nb, H, n, h_.as<float>(), I, kEpiSwiGlu);
   if (q) {
     launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq, xs_.as<float>(), ldxs_, status(),
                       stream_);
-    note_launch();
   }
   run_proj_generic(L.parts[mlp + 2], h_.as<float>(), I, n, x, H, kEpiAdd);
 }
@@ -263,7 +252,6 @@ void Engine::check_status() {
 
 void Engine::run_layers(int n, int start, const Prefix* past, Prefix* cap) {
   launch_embed(embedding_.ptr, 0, c_.hidden, ids_.as<uint32_t>(), n, x_.as<float>(), stream_);
-  note_launch();
   for (int i = 0; i < c_.layers; ++i) {
     const Prefix::LayerState* lp = past ? &past->layers[i] : nullptr;
     Prefix::LayerState* lc = cap ? &cap->layers[i] : nullptr;
@@ -275,7 +263,6 @@ void Engine::run_layers(int n, int start, const Prefix* past, Prefix* cap) {
   }
   cur_layer_ = -1;
   launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
-  note_launch();
 }
 
 void Engine::drop_graphs() {
@@ -373,7 +360,6 @@ void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* lo
   launch_lora_a(hnorm_.as<float>() + H, H, n_pos, H, head_k_.w_f32.as<float>(), P, hk_.as<float>(), P, true, stream_);
   launch_head_dot(hq_.as<float>(), hk_.as<float>(), n_pos, P, 1.0f / std::sqrt(float(P)), head_q_.bias.as<float>(),
                   head_k_.bias.as<float>(), hlogits_.as<float>(), stream_);
-  for (int j = 0; j < 2; ++j) note_launch();  // head norm and head dot (LoRA-A kernels count themselves)
   DG_CUDA(cudaMemcpyAsync(logits_out, hlogits_.ptr, size_t(n_pos) * 4, cudaMemcpyDeviceToHost, stream_));
   DG_CUDA(cudaStreamSynchronize(stream_));
 }

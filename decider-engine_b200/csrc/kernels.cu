@@ -47,24 +47,6 @@ __device__ __forceinline__ void quantize_group_warp(const float* vals, int len, 
   if (l == 0) *scale_out = scale;
 }
 
-// Group-64 quantisation of the four values a lane holds; the 16 lanes of a
-// half-warp hold one 64-wide group (same formula as quantize_group_warp).
-__device__ __forceinline__ void quantize_vec4_halfwarp(float4 v, int8_t* q_out, float* scale_out, bool leader,
-                                                       bool* bad) {
-  float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  *bad |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
-  const float scale = mx == 0.0f ? 1.0f : fmaxf(mx / 127.0f, FLT_MIN);
-  char4 q;
-  q.x = int8_t(fminf(fmaxf(roundf(v.x / scale), -127.0f), 127.0f));
-  q.y = int8_t(fminf(fmaxf(roundf(v.y / scale), -127.0f), 127.0f));
-  q.z = int8_t(fminf(fmaxf(roundf(v.z / scale), -127.0f), 127.0f));
-  q.w = int8_t(fminf(fmaxf(roundf(v.w / scale), -127.0f), 127.0f));
-  *reinterpret_cast<char4*>(q_out) = q;
-  if (leader) *scale_out = scale;
-}
-
 // Warp-per-row variant for K % 128 == 0: lane l holds float4 l + 32 i of the
 // row, so no shared memory or block barrier is needed. With gamma (NV float4
 // per lane kept in registers) the centred RMSNorm comes first.
@@ -614,14 +596,10 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
     // still spread over R * M * 8 threads.
     const long t1 = long(M) * R * 8;
     launch_pdl(lora_a_kernel<true, 1, 1>, dim3(int((t1 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
-    note_launch();
   } else if (exact) {
     launch_pdl(lora_a_kernel<true>, dim3(blocks), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
-    note_launch();
   } else if (partial && lora_a_tc_supported(x, ldx, K, A, R, ldm)) {
     launch_lora_a_tc(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, st, s);
-    note_launch();  // tensor-core pass and its reduction
-    note_launch();
   } else if (partial && K % 32 == 0 && ldx % 4 == 0 && R % 4 == 0 && ldm % 4 == 0 &&
              reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0) {
     if (R <= 32)
@@ -630,12 +608,9 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
       launch_lora_splitk<64, 64>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
     else
       launch_lora_splitk<64, 128>(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, s);
-    note_launch();  // split-K pass and its reduction
-    note_launch();
   } else {
     const long warps = long((M + 3) / 4) * ((R + 3) / 4);
     launch_pdl(lora_a_fast_kernel, dim3(int((warps * 32 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
-    note_launch();
   }
   DG_CUDA(cudaGetLastError());
 }
