@@ -187,6 +187,59 @@ __global__ void gated_norm_quant_kernel(const float* __restrict__ o, const float
   }
 }
 
+// dv == 128: one warp per (row, head). Lane l holds elements l + 32 i
+// (i < 4) of the head, in the same order as gated_norm_quant_kernel, so the
+// sum of squares and every output are bit-identical; the head's two 64-wide
+// quantisation groups are elements {l, l + 32} and {l + 64, l + 96}, quantised
+// straight from registers (the scale depends only on the group maximum).
+__global__ void __launch_bounds__(256) gated_norm_quant_warp_kernel(const float* __restrict__ o,
+                                                                    const float* __restrict__ z, int ldz, int M,
+                                                                    int heads, const float* __restrict__ w, float eps,
+                                                                    float* __restrict__ out, int8_t* __restrict__ xq,
+                                                                    float* __restrict__ xs, int ldxs, int quantize,
+                                                                    DeviceStatus* st) {
+  griddep_wait();
+  griddep_launch();
+  constexpr int DV = 128;
+  const int gw = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (gw >= M * heads) return;
+  const int m = gw / heads, h = gw % heads, K = heads * DV;
+  const float* oh = o + size_t(m) * K + h * DV;
+  const float* zh = z + size_t(m) * ldz + h * DV;
+  float a[4], zv[4], wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    a[i] = oh[lane + 32 * i];
+    zv[i] = zh[lane + 32 * i];
+    wv[i] = __ldg(w + lane + 32 * i);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = __fmaf_rn(a[i], a[i], ss);
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / float(DV) + eps);
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = a[i] * (inv * wv[i]) * silu_f(zv[i]);
+    out[size_t(m) * K + h * DV + lane + 32 * i] = v[i];
+  }
+  if (!quantize) return;
+  bool bad = false;
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const float p0 = v[2 * g], p1 = v[2 * g + 1];
+    bad |= !isfinite(p0) || !isfinite(p1);
+    const float mx = warp_max(fmaxf(fabsf(p0), fabsf(p1)));
+    const float scale = mx == 0.0f ? 1.0f : fmaxf(mx / 127.0f, FLT_MIN);
+    int8_t* q = xq + size_t(m) * K + h * DV + 64 * g;
+    q[lane] = int8_t(fminf(fmaxf(roundf(p0 / scale), -127.0f), 127.0f));
+    q[lane + 32] = int8_t(fminf(fmaxf(roundf(p1 / scale), -127.0f), 127.0f));
+    if (lane == 0) xs[size_t((h * DV) / 64 + g) * ldxs + m] = scale;
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0) report(st, kNonFinite, 2);
+}
+
 // LoRA A: mid[m][r] = dot_scores(x[m], A[r]) in the reference's order
 // (src/tensor.rs:6-25): eight lanes over k % 8, each a sequential
 // multiply-then-add chain, the lanes summed from -0.0 in order, then the tail.
@@ -439,6 +492,7 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
   mid[size_t(i / R) * ldm + i % R] = (c[0] + c[1]) + (c[2] + c[3]);
 }
 
+
 }  // namespace
 
 void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s) {
@@ -581,8 +635,14 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
                              float eps, float* out, int8_t* xq, float* xs, int ldxs, bool quantize, DeviceStatus* st,
                              cudaStream_t s) {
   if (M <= 0) return;
-  launch_pdl(gated_norm_quant_kernel, dim3(M), dim3(256), heads * dv * sizeof(float), s, o, z, ldz, heads, dv, w, eps, out, xq, xs, ldxs,
-                                                                      quantize ? 1 : 0, st);
+  if (dv == 128) {
+    const long warps = long(M) * heads;
+    launch_pdl(gated_norm_quant_warp_kernel, dim3(int((warps + 7) / 8)), dim3(256), 0, s, o, z, ldz, M, heads, w, eps,
+               out, xq, xs, ldxs, quantize ? 1 : 0, st);
+  } else {
+    launch_pdl(gated_norm_quant_kernel, dim3(M), dim3(256), heads * dv * sizeof(float), s, o, z, ldz, heads, dv, w,
+               eps, out, xq, xs, ldxs, quantize ? 1 : 0, st);
+  }
   DG_CUDA(cudaGetLastError());
 }
 

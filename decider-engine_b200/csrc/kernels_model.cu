@@ -1,5 +1,6 @@
 // Mixer kernels of the Qwen3.5 torso: DeltaNet conv / recurrence, gated GQA
 // attention with partial RoPE, final norm and the pointer head.
+#include <cstdint>
 #include <cfloat>
 
 #include "launch.h"
@@ -247,12 +248,67 @@ __global__ void exp_kernel(const float* __restrict__ g, float* __restrict__ out,
 
 }  // namespace
 
+// Four adjacent channels per thread (float4 loads and stores; W, ldr % 4 == 0,
+// 16-byte aligned rows); per channel the same window and order as
+// conv_silu_kernel, so the outputs are bit-identical.
+__global__ void __launch_bounds__(128) conv_silu4_kernel(const float* __restrict__ raw, int ldr,
+                                                         const float* __restrict__ tail, int tail_rows, int n,
+                                                         int start, int W, int kernel,
+                                                         const float* __restrict__ taps, float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), t0 = blockIdx.y * CONV_T;
+  if (c >= W) return;
+  float4 w[CONV_KMAX];
+#pragma unroll
+  for (int j = 0; j < CONV_KMAX; ++j)
+    w[j] = j < kernel ? __ldg(reinterpret_cast<const float4*>(taps + size_t(j) * W + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 win[CONV_T + CONV_KMAX - 1];
+#pragma unroll
+  for (int i = 0; i < CONV_T + CONV_KMAX - 1; ++i) {
+    const int source = start + t0 - (kernel - 1) + i;  // absolute position
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < CONV_T + kernel - 1 && source >= 0 && source < start + n) {
+      const float* src = source >= start ? raw + size_t(source - start) * ldr + c
+                                         : tail + size_t(source + tail_rows - start) * W + c;
+      v = *reinterpret_cast<const float4*>(src);
+    }
+    win[i] = v;
+  }
+#pragma unroll
+  for (int tt = 0; tt < CONV_T; ++tt) {
+    const int t = t0 + tt;
+    if (t >= n) break;
+    const int position = start + t;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < CONV_KMAX; ++j) {
+      if (j >= kernel || position + j + 1 < kernel) continue;
+      sum.x = sum.x + win[tt + j].x * w[j].x;
+      sum.y = sum.y + win[tt + j].y * w[j].y;
+      sum.z = sum.z + win[tt + j].z * w[j].z;
+      sum.w = sum.w + win[tt + j].w * w[j].w;
+    }
+    *reinterpret_cast<float4*>(out + size_t(t) * W + c) =
+        make_float4(silu_f(sum.x), silu_f(sum.y), silu_f(sum.z), silu_f(sum.w));
+  }
+}
 void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W, int kernel,
                       const float* taps, float* out, cudaStream_t s) {
   if (n <= 0) return;
   if (kernel < 1 || kernel > CONV_KMAX) throw CudaError("conv: kernel width must be 1..8");
-  dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T);
-  launch_pdl(conv_silu_kernel, dim3(grid), dim3(256), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps, out);
+  const bool vec = W % 4 == 0 && ldr % 4 == 0 && reinterpret_cast<uintptr_t>(raw) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(taps) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                   (tail_rows == 0 || reinterpret_cast<uintptr_t>(tail) % 16 == 0);
+  if (vec) {
+    dim3 grid((W / 4 + 127) / 128, (n + CONV_T - 1) / CONV_T);
+    launch_pdl(conv_silu4_kernel, dim3(grid), dim3(128), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps,
+               out);
+  } else {
+    dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T);
+    launch_pdl(conv_silu_kernel, dim3(grid), dim3(256), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps,
+               out);
+  }
   DG_CUDA(cudaGetLastError());
 }
 
