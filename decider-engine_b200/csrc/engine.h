@@ -157,6 +157,10 @@ class Engine {
   };
   std::map<int, FwdGraph> graphs_;
   bool graphs_on_ = true;
+  // Projections wait for their LoRA-A kernels only before the epilogue
+  // (GemmArgs::late_dep), so their main loop overlaps LoRA-A; DG_LORA_OVERLAP=0
+  // serialises them again.
+  bool lora_overlap_ = true;
   void drop_graphs();
 
   Config c_;

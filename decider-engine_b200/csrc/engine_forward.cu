@@ -41,6 +41,8 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.out = out;
   a.ldo = ldo;
   a.status = status();
+  // Every fast projection directly follows its own LoRA-A launch.
+  a.late_dep = lora_overlap_ ? 1 : 0;
   const size_t k = gemm_ops_pending_.size();
   fwd_ops_all_ += 2.0 * M * p.out * p.in;
   ++fwd_proj_;
@@ -144,7 +146,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   float* proj = proj_.as<float>();
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
+  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
   const float* mixed_in;
   int kin;
@@ -175,15 +177,15 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     mixed_in = ofin_.as<float>();
     kin = c.vd();
   }
-  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
+  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
+  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
   launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
-  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status());
+  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
 }
 

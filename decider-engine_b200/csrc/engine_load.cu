@@ -108,6 +108,7 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   DG_CUDA(cudaEventCreate(&ev1_));
   // DG_CUDA_GRAPHS=0 launches every forward kernel by kernel (A/B timing).
   if (const char* g = std::getenv("DG_CUDA_GRAPHS")) graphs_on_ = std::atoi(g) != 0;
+  if (const char* o = std::getenv("DG_LORA_OVERLAP")) lora_overlap_ = std::atoi(o) != 0;
 }
 
 Engine::~Engine() {

@@ -47,6 +47,11 @@ struct GemmArgs {
   int ldo;
   DeviceStatus* status;
   int32_t* dots;            // optional debug dump of the exact group dots [K/64][M][N]
+  // Launched as a programmatic dependent of the LoRA-A kernels that produce
+  // lora_mid, whose own waits already ordered the activations: wait for the
+  // previous kernel only before reading lora_mid and writing out, so the main
+  // loop overlaps the LoRA-A pass.
+  int late_dep;
 };
 
 template <int BN_>
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(576, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   // Set-up above touched only shared memory, TMEM and weights.
-  griddep_wait();
+  if (!p.late_dep) griddep_wait();
   griddep_launch();
 
   if (warp == 0) {
@@ -247,6 +252,7 @@ __global__ void __launch_bounds__(576, 1)
         // LoRA operand stages: KS = this tile's LoRA-B rows, chunk by chunk into
         // their part-sorted slots; KS + 1 + k = the LoRA-A rows of part k.
         if (issued == KS) {
+          if (p.late_dep) griddep_wait();  // lora_mid comes from the previous kernel
           for (int j = 0; j <= plan->nparts; ++j) {
             const int ls = KS + j, s = ls % STAGES, use = ls / STAGES;
             if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 120 + s, abort_flag)) break;
@@ -460,6 +466,7 @@ __global__ void __launch_bounds__(576, 1)
       if (lane == 0) mbar_arrive(&empty[s]);  // scales and operands of the stage are consumed
     }
     // ---------------- epilogue
+    if (p.late_dep) griddep_wait();  // lora_mid and the output buffer
     const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
     if constexpr (TCL) {
       const LoraPlan& pl = *plan;

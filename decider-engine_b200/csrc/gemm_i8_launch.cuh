@@ -27,7 +27,8 @@ void launch_gemm_kernel(const GemmMaps& m, const GemmArgs& args, cudaStream_t s)
     configured = true;
   }
   dim3 grid((args.M + 127) / 128, args.N / BN);
-  launch_pdl(kern, dim3(grid), dim3(GemmShape<BN>::NUM_THREADS), smem, s, *m.a, *m.b, *m.lb, *m.mid, args);
+  launch_k(args.late_dep != 0 || pdl_enabled(), kern, dim3(grid), dim3(GemmShape<BN>::NUM_THREADS), smem, s, *m.a,
+           *m.b, *m.lb, *m.mid, args);
   DG_CUDA(cudaGetLastError());
 }
 

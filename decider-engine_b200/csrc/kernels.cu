@@ -475,8 +475,11 @@ __global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restr
 // as (c0 + c1) + (c2 + c3): a fixed order, so the result is deterministic.
 __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M,
                                                             int R, float* __restrict__ mid, int ldm) {
-  griddep_wait();
+  // Trigger first: a projection launched as this kernel's dependent may start
+  // its main loop while the LoRA-A pass still runs (it waits for this kernel
+  // before reading mid). This kernel itself waits before touching memory.
   griddep_launch();
+  griddep_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= M * R) return;
   const size_t stride = size_t(M) * R;
@@ -495,8 +498,10 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
 
 }  // namespace
 
-void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s) {
-  launch_pdl(lora_a_reduce_kernel, dim3((M * R + 127) / 128), dim3(128), 0, s, partial, slices, M, R, mid, ldm);
+void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s,
+                          bool pdl) {
+  launch_k(pdl || pdl_enabled(), lora_a_reduce_kernel, dim3((M * R + 127) / 128), dim3(128), 0, s, partial, slices, M,
+           R, mid, ldm);
   DG_CUDA(cudaGetLastError());
 }
 
@@ -647,7 +652,7 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 }
 
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm, bool exact,
-                   cudaStream_t s, float* partial, size_t partial_floats, DeviceStatus* st) {
+                   cudaStream_t s, float* partial, size_t partial_floats, DeviceStatus* st, bool overlap) {
   if (M <= 0 || R <= 0) return;
   const long threads = long((M + 3) / 4) * ((R + 3) / 4) * 8;
   const int blocks = int((threads + 255) / 256);
@@ -657,9 +662,10 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
     const long t1 = long(M) * R * 8;
     launch_pdl(lora_a_kernel<true, 1, 1>, dim3(int((t1 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
   } else if (exact) {
-    launch_pdl(lora_a_kernel<true>, dim3(blocks), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
+    launch_k(overlap || pdl_enabled(), lora_a_kernel<true>, dim3(blocks), dim3(256), 0, s, x, ldx, M, K, A, R, mid,
+             ldm);
   } else if (partial && lora_a_tc_supported(x, ldx, K, A, R, ldm)) {
-    launch_lora_a_tc(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, st, s);
+    launch_lora_a_tc(x, ldx, M, K, A, R, mid, ldm, partial, partial_floats, st, s, overlap);
   } else if (partial && K % 32 == 0 && ldx % 4 == 0 && R % 4 == 0 && ldm % 4 == 0 &&
              reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(A) % 16 == 0) {
     if (R <= 32)

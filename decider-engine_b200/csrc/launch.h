@@ -45,15 +45,19 @@ void launch_gated_norm_quant(const float* o, const float* z, int ldz, int M, int
 // CTAs and reduces the slices in a fixed order.
 void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
                    bool exact, cudaStream_t s, float* partial = nullptr, size_t partial_floats = 0,
-                   DeviceStatus* st = nullptr);
+                   DeviceStatus* st = nullptr, bool overlap = false);
+// overlap: the next launch is a projection with GemmArgs::late_dep set; the
+// LoRA-A kernels then run as its programmatic prerequisites on fewer SMs, so
+// that projection's main loop runs beside them.
 // Tensor-core LoRA A (lora_a_tc.cu): R <= 128, K % 32 == 0, 16-byte aligned
 // rows; the slices of each 128-row tile go to `partial`, then a fixed-order sum.
 bool lora_a_tc_supported(const float* x, int ldx, int K, const float* A, int R, int ldm);
 size_t lora_a_tc_partial_floats(int max_rows);
 void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
-                      float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s);
+                      float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s, bool overlap = false);
 // mid[m][r] = sum over z of partial[z][m][r], as four chains added pairwise.
-void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s);
+void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s,
+                          bool pdl = false);
 inline size_t lora_a_partial_floats(int max_rows) {
   const size_t simt = (size_t(148 * 64) + size_t(max_rows)) * 128;
   const size_t tc = lora_a_tc_partial_floats(max_rows);

@@ -166,7 +166,7 @@ bool lora_a_tc_supported(const float* x, int ldx, int K, const float* A, int R, 
 }
 
 void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
-                      float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s) {
+                      float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s, bool overlap) {
   static bool configured = false;
   if (!configured) {
     DG_CUDA(cudaFuncSetAttribute(lora_a_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -175,14 +175,18 @@ void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int
   }
   const int NP = (R + 15) / 16 * 16;
   const int mt = (M + 127) / 128;
+  // The grid fills the GPU. With `overlap` the kernels are launched as
+  // programmatic prerequisites of the next projection (measured: confining
+  // them to a third of the SMs instead delays that projection's first wave
+  // by more than it gains).
   const int splits = std::max(1, std::min(K / 32, (148 + mt - 1) / mt));
   const int kslice = ((K + splits - 1) / splits + 31) / 32 * 32;
   const int used = (K + kslice - 1) / kslice;
   if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
-  launch_pdl(lora_a_tc_kernel, dim3(dim3(mt, used)), dim3(kLaThreads), lora_tc_smem_bytes(NP), s, x, ldx, M, K, A, R, NP, partial, kslice,
-                                                                            st);
+  launch_k(overlap || pdl_enabled(), lora_a_tc_kernel, dim3(mt, used), dim3(kLaThreads), lora_tc_smem_bytes(NP), s, x,
+           ldx, M, K, A, R, NP, partial, kslice, st);
   DG_CUDA(cudaGetLastError());
-  launch_lora_a_reduce(partial, used, M, R, mid, ldm, s);
+  launch_lora_a_reduce(partial, used, M, R, mid, ldm, s, overlap);
 }
 
 }  // namespace dg
