@@ -22,6 +22,8 @@ namespace dg {
 namespace {
 
 constexpr int CK = 64, DK = 128, SC = 16;
+// Scan threads per CTA (measured in the 2B forward: 128 beats 64 and 256).
+constexpr int SCAN_NT = 128;
 
 // Per-chunk products written by the prep kernel.
 struct ChunkOut {
@@ -269,8 +271,18 @@ __device__ __forceinline__ void cp16(void* smem, const void* gmem, int src_bytes
                : "memory");
 }
 
-__global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
-                                                               ChunkState* __restrict__ states, int chunks) {
+// NT threads, register tiles: with NG = NT / 4 row groups, thread (g, q)
+// (g = tid / 4, q = tid % 4) owns in D = U - W S0 the rows g + NG r
+// (r < 64 / NG) and in the state update the rows 4g + (r % 4) + 64 (r / 4)
+// (r < 128 / NG), each at columns 4q .. 4q + 3. Every output keeps the single
+// FMA chain, in the same order, of a one-output-per-thread formulation, so
+// the results do not depend on the tiling; the tiles cut the shared-memory
+// operand traffic per FMA.
+template <int NT>
+__global__ void __launch_bounds__(NT) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
+                                                              ChunkState* __restrict__ states, int chunks) {
+  constexpr int SCAN_THREADS = NT, NG = NT / 4, RD = CK / NG, RS = DK / NG;
+  static_assert(RD >= 1 && RS % 4 == 0 && (RS == 4 || NG == 16), "tile shape");
   griddep_wait();
   griddep_launch();
   extern __shared__ __align__(16) float sm[];
@@ -288,21 +300,22 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
   auto stage = [&](int c, ScanStage& st) {
     const ChunkOut& co = outs[head * chunks + c];
     const int t0 = c * CK, tn = min(CK, a.n - t0);
-    for (int i = tid; i < CK * (DK / 4); i += 256) {
+    for (int i = tid; i < CK * (DK / 4); i += SCAN_THREADS) {
       const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
       cp16(&st.W[t][d], &co.W[t][d], 16);
       // K rows past the sequence are zero-filled (never read from memory).
       cp16(&st.K[t][d], t < tn ? kb + size_t(t0 + t) * a.ld_qk + d : kb, t < tn ? 16 : 0);
     }
-    for (int i = tid; i < CK * (SC / 4); i += 256) {
+    for (int i = tid; i < CK * (SC / 4); i += SCAN_THREADS) {
       const int t = i / (SC / 4), j4 = (i % (SC / 4)) * 4;
       cp16(&st.U[t][j4], &co.U[t][j0 + j4], 16);
     }
     if (tid < CK / 4) cp16(&st.rem[tid * 4], &co.rem[tid * 4], 16);
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  for (int e = tid; e < DK * SC; e += 256) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
+  for (int e = tid; e < DK * SC; e += SCAN_THREADS) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
   stage(0, stg[0]);
+  const int g = tid >> 2, jc = (tid & 3) * 4;
   for (int c = 0; c < chunks; ++c) {
     const ScanStage& st = stg[c & 1];
     ChunkState& cs = states[head * chunks + c];
@@ -315,57 +328,89 @@ __global__ void __launch_bounds__(256) delta_chunk_scan_kernel(DeltaArgs a, cons
     }
     __syncthreads();
     // The state this chunk starts from, for the output pass.
-    for (int e = tid; e < DK * (SC / 4); e += 256) {
+    for (int e = tid; e < DK * (SC / 4); e += SCAN_THREADS) {
       const int i = e / (SC / 4), j4 = (e % (SC / 4)) * 4;
       *reinterpret_cast<float4*>(&cs.S[i][j0 + j4]) = *reinterpret_cast<const float4*>(S + i * SC + j4);
     }
-    // D = U - W S0 ; thread -> (t, 4 columns)
+    // D = U - W S0: rows g + NG r, columns jc .. jc + 3.
     {
-      const int t = tid / 4, jc = (tid % 4) * 4;
-      float ws[4] = {0, 0, 0, 0};
-#pragma unroll 4
+      float ws[RD][4];
+#pragma unroll
+      for (int r = 0; r < RD; ++r)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ws[r][e] = 0.0f;
+#pragma unroll 2
       for (int i = 0; i < DK; i += 4) {
-        const float4 w4 = *reinterpret_cast<const float4*>(&st.W[t][i]);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+        float4 w4[RD];
+#pragma unroll
+        for (int r = 0; r < RD; ++r) w4[r] = *reinterpret_cast<const float4*>(&st.W[g + NG * r][i]);
 #pragma unroll
         for (int ii = 0; ii < 4; ++ii) {
           const float4 s4 = *reinterpret_cast<const float4*>(S + (i + ii) * SC + jc);
-          ws[0] = __fmaf_rn(wv[ii], s4.x, ws[0]); ws[1] = __fmaf_rn(wv[ii], s4.y, ws[1]);
-          ws[2] = __fmaf_rn(wv[ii], s4.z, ws[2]); ws[3] = __fmaf_rn(wv[ii], s4.w, ws[3]);
+#pragma unroll
+          for (int r = 0; r < RD; ++r) {
+            const float wv = ii == 0 ? w4[r].x : ii == 1 ? w4[r].y : ii == 2 ? w4[r].z : w4[r].w;
+            ws[r][0] = __fmaf_rn(wv, s4.x, ws[r][0]);
+            ws[r][1] = __fmaf_rn(wv, s4.y, ws[r][1]);
+            ws[r][2] = __fmaf_rn(wv, s4.z, ws[r][2]);
+            ws[r][3] = __fmaf_rn(wv, s4.w, ws[r][3]);
+          }
         }
       }
-      const float4 u4 = *reinterpret_cast<const float4*>(&st.U[t][jc]);
-      const bool live = t < tn;
-      const float4 d4 = make_float4(live ? u4.x - ws[0] : 0.0f, live ? u4.y - ws[1] : 0.0f,
-                                    live ? u4.z - ws[2] : 0.0f, live ? u4.w - ws[3] : 0.0f);
-      *reinterpret_cast<float4*>(D + t * SC + jc) = d4;
-      *reinterpret_cast<float4*>(&cs.D[t][j0 + jc]) = d4;
+#pragma unroll
+      for (int r = 0; r < RD; ++r) {
+        const int t = g + NG * r;
+        const float4 u4 = *reinterpret_cast<const float4*>(&st.U[t][jc]);
+        const bool live = t < tn;
+        const float4 d4 = make_float4(live ? u4.x - ws[r][0] : 0.0f, live ? u4.y - ws[r][1] : 0.0f,
+                                      live ? u4.z - ws[r][2] : 0.0f, live ? u4.w - ws[r][3] : 0.0f);
+        *reinterpret_cast<float4*>(D + t * SC + jc) = d4;
+        *reinterpret_cast<float4*>(&cs.D[t][j0 + jc]) = d4;
+      }
     }
     __syncthreads();
-    // S_C = G_C S0 + K^T diag(G_C / G) D ; thread -> (i, 8 columns)
+    // S_C = G_C S0 + K^T diag(G_C / G) D: rows 4g + (r % 4) + 64 (r / 4).
     {
       const float gC = outs[head * chunks + c].gC;
-      const int i = tid / 2, j8 = (tid % 2) * 8;
-      float acc[8];
+      float acc[RS][4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = gC * S[i * SC + j8 + e];
+      for (int r = 0; r < RS; ++r) {
+        const int i = 4 * g + (r % 4) + 64 * (r / 4);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[r][e] = gC * S[i * SC + jc + e];
+      }
 #pragma unroll 4
-      for (int s = 0; s < CK; ++s) {
-        const float kr = st.K[s][i] * st.rem[s];
-        const float4 d0 = *reinterpret_cast<const float4*>(D + s * SC + j8);
-        const float4 d1 = *reinterpret_cast<const float4*>(D + s * SC + j8 + 4);
-        acc[0] = __fmaf_rn(kr, d0.x, acc[0]); acc[1] = __fmaf_rn(kr, d0.y, acc[1]);
-        acc[2] = __fmaf_rn(kr, d0.z, acc[2]); acc[3] = __fmaf_rn(kr, d0.w, acc[3]);
-        acc[4] = __fmaf_rn(kr, d1.x, acc[4]); acc[5] = __fmaf_rn(kr, d1.y, acc[5]);
-        acc[6] = __fmaf_rn(kr, d1.z, acc[6]); acc[7] = __fmaf_rn(kr, d1.w, acc[7]);
+      for (int s2 = 0; s2 < CK; ++s2) {
+        const float rs = st.rem[s2];
+        float kv[RS];
+#pragma unroll
+        for (int r4 = 0; r4 < RS / 4; ++r4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(&st.K[s2][4 * g + 64 * r4]);
+          kv[4 * r4] = k4.x;
+          kv[4 * r4 + 1] = k4.y;
+          kv[4 * r4 + 2] = k4.z;
+          kv[4 * r4 + 3] = k4.w;
+        }
+        const float4 d4 = *reinterpret_cast<const float4*>(D + s2 * SC + jc);
+#pragma unroll
+        for (int r = 0; r < RS; ++r) {
+          const float kr = kv[r] * rs;
+          acc[r][0] = __fmaf_rn(kr, d4.x, acc[r][0]);
+          acc[r][1] = __fmaf_rn(kr, d4.y, acc[r][1]);
+          acc[r][2] = __fmaf_rn(kr, d4.z, acc[r][2]);
+          acc[r][3] = __fmaf_rn(kr, d4.w, acc[r][3]);
+        }
       }
       __syncthreads();  // every thread has read the old S (and this stage)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) S[i * SC + j8 + e] = acc[e];
+      for (int r = 0; r < RS; ++r) {
+        const int i = 4 * g + (r % 4) + 64 * (r / 4);
+        *reinterpret_cast<float4*>(S + i * SC + jc) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+      }
     }
     __syncthreads();
   }
-  for (int e = tid; e < DK * SC; e += 256) Sg[size_t(e / SC) * a.dv + j0 + e % SC] = S[e];
+  for (int e = tid; e < DK * SC; e += SCAN_THREADS) Sg[size_t(e / SC) * a.dv + j0 + e % SC] = S[e];
 }
 
 // O = diag(G) Q S0 + (M o Q K^T) D for one chunk, head and 64 value columns,
@@ -486,13 +531,15 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   static bool configured = false;
   if (!configured) {
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));
-    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, scan_smem));
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel<SCAN_NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 scan_smem));
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, out_smem));
     configured = true;
   }
   launch_pdl(delta_chunk_prep_kernel, dim3(int(units)), dim3(256), prep_smem, s, a, outs, chunks);
   DG_CUDA(cudaGetLastError());
-  launch_pdl(delta_chunk_scan_kernel, dim3(batch * a.value_heads * (a.dv / SC)), dim3(256), scan_smem, s, a, outs, states, chunks);
+  launch_pdl(delta_chunk_scan_kernel<SCAN_NT>, dim3(batch * a.value_heads * (a.dv / SC)), dim3(SCAN_NT), scan_smem,
+             s, a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
   launch_pdl(delta_chunk_out_kernel, dim3(int(units) * (a.dv / OUT_COLS)), dim3(256), out_smem, s, a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
