@@ -46,15 +46,8 @@ GEMM_TRAFFIC_BYTES_PER_LAUNCH = 20.62e6
 
 
 def cfg2(layers=24):
-    lt = (["linear_attention"] * 3 + ["full_attention"]) * (layers // 4)
-    return {
-        "hidden_size": 2048, "intermediate_size": 6144, "num_hidden_layers": layers, "vocab_size": 248320,
-        "layer_types": lt, "num_attention_heads": 8, "num_key_value_heads": 2, "head_dim": 256,
-        "rms_norm_eps": 1e-6, "linear_conv_kernel_dim": 4, "linear_key_head_dim": 128,
-        "linear_value_head_dim": 128, "linear_num_key_heads": 16, "linear_num_value_heads": 16,
-        "rope_parameters": {"rope_theta": 1e7, "partial_rotary_factor": 0.25, "rope_type": "default"},
-        "attention_bias": False, "attn_output_gate": True, "hidden_act": "silu",
-    }
+    from model_util import cfg2_config
+    return cfg2_config(layers)
 
 
 def peaks():
@@ -272,6 +265,18 @@ def run_ours(args, world, rank, local, dist):
     a_ops, a_n = model.gemm_time_all()
     a_ops, a_n = a_ops - a0_ops, a_n - a0_n
     model.gemm_timing(False)
+    # ---- p50 latency (BASELINE metric): wall time of single warm dg_logits
+    # calls (host ids in, host logits out), after the timed region.
+    for _ in range(3):
+        step()
+    lat = []
+    for _ in range(args.latency_calls):
+        t1 = time.perf_counter()
+        step()
+        lat.append((time.perf_counter() - t1) * 1000.0)
+    lat.sort()
+    p50 = max_over_ranks(lat[len(lat) // 2], dist, local) if lat else None
+    p99 = max_over_ranks(lat[min(len(lat) - 1, (99 * len(lat)) // 100)], dist, local) if lat else None
     gemm_ms_per_launch = g_ms / max(g_n, 1)
     # Projection time of a whole step, at the sampled launches' ops rate.
     gemm_step_ms = (g_ms / g_ops) * a_ops / args.steps if g_ops > 0 else 0.0
@@ -302,6 +307,9 @@ def run_ours(args, world, rank, local, dist):
                      "launches": int(g_n), "launches_per_step": int(a_n) // max(args.steps, 1),
                      "ms_per_launch": gemm_ms_per_launch, "share_of_step": gemm_share,
                      "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
+        "latency": {"p50_ms": p50, "p99_ms": p99, "calls": len(lat),
+                    "what": "wall time of one warm dg_logits call per request (512 ids in, 2 logits out), "
+                            "max over ranks"},
         "gpu_launches": int(launches),
         "clocks": clocks.summary(),
     }
@@ -315,6 +323,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--latency-calls", type=int, default=100, help="warm dg_logits calls timed for p50/p99")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")

@@ -16,6 +16,21 @@ def small_config(hidden=256, intermediate=512, layer_types=("linear_attention",)
     }
 
 
+def cfg2_config(layers=24, vocab=248320):
+    """the 2B decider shape (hidden 2048, 6 x [3 Gated
+    DeltaNet + 1 gated GQA attention] layers, 8 Q / 2 KV heads of 256, DeltaNet
+    16 x 128, SwiGLU 6144)."""
+    lt = (["linear_attention"] * 3 + ["full_attention"]) * (layers // 4)
+    return {
+        "hidden_size": 2048, "intermediate_size": 6144, "num_hidden_layers": layers, "vocab_size": vocab,
+        "layer_types": lt, "num_attention_heads": 8, "num_key_value_heads": 2, "head_dim": 256,
+        "rms_norm_eps": 1e-6, "linear_conv_kernel_dim": 4, "linear_key_head_dim": 128,
+        "linear_value_head_dim": 128, "linear_num_key_heads": 16, "linear_num_value_heads": 16,
+        "rope_parameters": {"rope_theta": 1e7, "partial_rotary_factor": 0.25, "rope_type": "default"},
+        "attention_bias": False, "attn_output_gate": True, "hidden_act": "silu",
+    }
+
+
 def expected_shapes(c, rank, pointer_dim):
     H, I = c["hidden_size"], c["intermediate_size"]
     qw, kw = c["num_attention_heads"] * c["head_dim"], c["num_key_value_heads"] * c["head_dim"]

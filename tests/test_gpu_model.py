@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 
 from conftest import TINY
-from model_util import random_tensors, rel_err, small_config
+from model_util import cfg2_config, random_tensors, rel_err, small_config
 
 pytestmark = pytest.mark.gpu
 
@@ -208,3 +208,30 @@ def test_scheduling_options_leave_results_bit_identical(small, monkeypatch, exac
         got = run(*opts)
         for o in got:
             assert np.array_equal(o, base[0]), opts
+
+
+def test_config4_shared_prefix_questions_continue_bit_exact():
+    """BASELINE config 4 at full size on the 2B shape (24 layers, synthetic
+    weights): one 3584-token prefix, then 8 questions of 64 tokens each
+    continuing from the cached K/V and DeltaNet state. In reference-order mode
+    each continuation's hidden rows equal, bit for bit, the last 64 rows of a
+    full forward over prefix + question (checked for two questions), and the
+    prefix is unchanged by its use: the first question repeated last gives the
+    same rows."""
+    from decider_gpu import GpuModel
+    cfg = cfg2_config()
+    m = GpuModel(cfg, "int8-compute", 32, 2.0, 256, 0, 4096)
+    m.fill_synthetic(seed=0, stddev=0.02)
+    m = m.finalize()
+    assert m.fast_path
+    m.set_exact(True)
+    rng = np.random.default_rng(4)
+    prefix_ids = rng.integers(0, cfg["vocab_size"], 3584)
+    questions = [rng.integers(0, cfg["vocab_size"], 64) for _ in range(8)]
+    prefix = m.prefill(prefix_ids)
+    rows = [m.forward_after(prefix, q) for q in questions]
+    assert all(np.isfinite(r).all() for r in rows)
+    for i in (0, 7):
+        full = m.forward(np.concatenate([prefix_ids, questions[i]]))
+        assert np.array_equal(rows[i], full[3584:]), i
+    assert np.array_equal(m.forward_after(prefix, questions[0]), rows[0])
