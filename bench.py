@@ -318,6 +318,436 @@ def run_ours(args, world, rank, local, dist):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ other configs
+# The default line is config 2. `--workload cfg1|cfg3|cfg4|cfg5` measures the
+# other BASELINE configs with the same contract (device-time value, e2e
+# through the public call with host buffers, roofline of the dominant kernel,
+# CPU baseline on rank 0 at N=1).
+
+CFG1 = (512, 6144, 2048)  # M tokens, N outputs, K inputs
+CFG3 = (64, 4096, 16, 128)  # sequences, tokens, heads, head dim
+# Algorithmic bytes of one config-3 call: q, k, v read, o written (4 x 512 B),
+# g and beta read (8 B) per token and head, the state read and written.
+CFG3_BYTES = 64 * 16 * 4096 * (4 * 128 * 4 + 8) + 2 * 64 * 16 * 128 * 128 * 4
+
+
+def _line(args, world, metric, value, unit, ms, config, dtype="int8-compute (i8 x i8 -> i32 groups, f32 promotion)",
+          **extra):
+    d = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+         "vs_baseline": None, "dtype": dtype, "promotion": "reference-order" if args.exact else "fma",
+         "data": "synthetic", "config": config}
+    d.update(extra)
+    return d
+
+
+def _cfg1_inputs():
+    M, N, K = CFG1
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    return x, w
+
+
+def _cfg1_config(world):
+    M, N, K = CFG1
+    return {"workload": f"cfg1: one group-64 INT8 linear, M={M} tokens x N={N} x K={K}, X ~ N(0,1), "
+                        "W ~ N(0,0.02^2), no LoRA", "parallelism": f"dp{world}",
+            "l2": "flushed before every call (256 MB write): X and W fit in the 126 MB L2"}
+
+
+def _cpu_cfg1(rows=512):
+    from oracle import oracle as O
+    O.build()
+    threads = os.cpu_count()
+    O.set_threads(threads)
+    x, w = _cfg1_inputs()
+    wq, ws = O.quantize_weights(w)
+    O.linear_int8_prequant(x[:4], wq, ws)
+    t0 = time.perf_counter()
+    O.linear_int8_prequant(x[:rows], wq, ws)
+    sec = time.perf_counter() - t0
+    M, N, K = CFG1
+    return (2.0 * rows * N * K / sec / 1e12, "TOP/s", threads,
+            f"oracle linear_int8 (scalar x86 path), {rows} of the {M} rows, weights quantised beforehand")
+
+
+def run_cfg1(args, world, rank, local, dist):
+    import torch
+
+    import decider_gpu
+    from decider_gpu import Linear
+    torch.cuda.set_device(local)
+    L = decider_gpu.load()
+    M, N, K = CFG1
+    x, w = _cfg1_inputs()
+    lin = Linear(w, device=local)
+    lin.set_exact(args.exact)
+    dev = f"cuda:{local}"
+    xd = torch.from_numpy(x).to(dev)
+    yd = torch.empty((M, N), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(lin.stream(), device=local)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(local)
+
+    def flush_l2():
+        with torch.cuda.stream(stream):
+            flush.zero_()
+
+    for _ in range(args.warmup):
+        flush_l2()
+        lin.forward_device(xd.data_ptr(), M, yd.data_ptr())
+    barrier(dist, local)
+    n0 = decider_gpu.launch_count()
+    tot, gem = [], []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            flush_l2()
+            lin.forward_device(xd.data_ptr(), M, yd.data_ptr())
+            t, g = lin.last_times()
+            tot.append(t)
+            gem.append(g)
+    launches = decider_gpu.launch_count() - n0
+    barrier(dist, local)
+    # e2e: dg_linear_forward with pinned host X in and Y out (copies inside).
+    hx = torch.from_numpy(x).pin_memory()
+    hy = torch.empty((M, N), dtype=torch.float32).pin_memory()
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        flush_l2()
+        torch.cuda.synchronize(local)
+        t0 = time.perf_counter()
+        decider_gpu._lib.check(L.dg_linear_forward(lin.h, hx.data_ptr(), M, hy.data_ptr()))
+        if i >= args.warmup:
+            e2e_ms.append((time.perf_counter() - t0) * 1000.0)
+    ops = 2.0 * M * N * K
+    dev_ms = max_over_ranks(sum(tot) / len(tot), dist, local)
+    gemm_ms = max_over_ranks(sum(gem) / len(gem), dist, local)
+    e2e = max_over_ranks(sum(e2e_ms) / len(e2e_ms), dist, local)
+    if rank != 0:
+        return
+    _, bf16, src = peaks()
+    peak = 2.0 * bf16
+    achieved = ops / (gemm_ms / 1000.0) / 1e12
+    line = _line(args, world, "INT8 GEMM TOP/s (cfg1: 512x6144x2048, group-64)",
+                 world * ops / (dev_ms / 1000.0) / 1e12, "TOP/s", dev_ms, _cfg1_config(world),
+                 e2e={"value": world * ops / (e2e / 1000.0) / 1e12, "unit": "TOP/s",
+                      "h2d_bytes_per_step": M * K * 4, "d2h_bytes_per_step": M * N * 4, "ms_per_step": e2e},
+                 roofline={"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                           "frac": achieved / peak, "traffic": None,
+                           "kernel": "gemm_i8_g64_kernel alone (events around its launch on the handle's stream); "
+                                     "value also counts the activation quantiser",
+                           "ms_per_launch": gemm_ms, "share_of_step": gemm_ms / dev_ms,
+                           "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
+                 gpu_launches=int(launches), clocks=clocks.summary())
+    if world == 1 and not args.no_cpu:
+        v, u, c, smp = _cpu_cfg1()
+        line["cpu_baseline"] = {"value": v, "unit": u, "cores": c, "kind": "port", "sample": smp}
+    print(json.dumps(line), flush=True)
+
+
+def _cfg3_config(world):
+    B, T, H, D = CFG3
+    return {"workload": f"cfg3: gated delta rule, {B} sequences x {T} tokens x {H} heads, dk = dv = {D}, "
+                        "chunk 64, zero initial state; q, k L2-normalised N(0,1), v ~ N(0,1), "
+                        "beta = sigmoid(N(0,1)), g = -softplus(N(0,1))",
+            "parallelism": f"dp{world}", "l2": "not flushed: 8.8 GB of inputs and outputs per step, > 126 MB L2"}
+
+
+def _cpu_cfg3():
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as O
+    O.build()
+    B, T, H, D = CFG3
+    threads = os.cpu_count()
+    rng = np.random.default_rng(0)
+    pairs = []
+    for _ in range(threads):
+        q = rng.standard_normal((T, D)).astype(np.float32)
+        k = rng.standard_normal((T, D)).astype(np.float32)
+        q = (q / np.linalg.norm(q, axis=1, keepdims=True) / np.sqrt(np.float32(D))).astype(np.float32)
+        k = (k / np.linalg.norm(k, axis=1, keepdims=True)).astype(np.float32)
+        v = rng.standard_normal((T, D)).astype(np.float32)
+        beta = (1.0 / (1.0 + np.exp(-rng.standard_normal(T)))).astype(np.float32)
+        g = (-np.log1p(np.exp(rng.standard_normal(T)))).astype(np.float32)
+        pairs.append((q, k, v, g, beta))
+    reps = 8
+    with ThreadPoolExecutor(threads) as ex:  # the oracle call releases the GIL
+        t0 = time.perf_counter()
+        list(ex.map(lambda a: O.gated_delta_rule(*a), pairs * reps))
+        sec = time.perf_counter() - t0
+    return (reps * threads * T / H / sec, "tok/s", threads,
+            f"oracle token recurrence, {reps * threads} (sequence, head) pairs x {T} tokens on {threads} threads; "
+            f"a token is one token of one sequence over all {H} heads")
+
+
+def run_cfg3(args, world, rank, local, dist):
+    import torch
+
+    import decider_gpu
+    from decider_gpu import gated_delta_chunk_workspace_bytes, gated_delta_rule_chunked
+    torch.cuda.set_device(local)
+    B, T, H, D = CFG3
+    dev = f"cuda:{local}"
+    gen = torch.Generator(device=dev).manual_seed(rank)
+    rn = lambda *shape: torch.randn(shape, generator=gen, device=dev, dtype=torch.float32)
+    q, k, v = rn(B, T, H, D), rn(B, T, H, D), rn(B, T, H, D)
+    q = (q / q.norm(dim=-1, keepdim=True) / np.sqrt(np.float32(D))).contiguous()
+    k = (k / k.norm(dim=-1, keepdim=True)).contiguous()
+    beta = torch.sigmoid(rn(B, T, H)).contiguous()
+    g = (-torch.nn.functional.softplus(rn(B, T, H))).contiguous()
+    state = torch.zeros((B, H, D, D), dtype=torch.float32, device=dev)
+    o = torch.empty((B, T, H, D), dtype=torch.float32, device=dev)
+    nbytes = gated_delta_chunk_workspace_bytes(B, T, H)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=local)
+    sptr = stream.cuda_stream
+
+    def run():
+        gated_delta_rule_chunked(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), B, T, H,
+                                 state.data_ptr(), o.data_ptr(), ws.data_ptr(), nbytes, sptr)
+
+    torch.cuda.synchronize(local)
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            state.zero_()
+        run()
+    barrier(dist, local)
+    n0 = decider_gpu.launch_count()
+    ms = []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            with torch.cuda.stream(stream):
+                state.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            e1.synchronize()
+            ms.append(e0.elapsed_time(e1))
+    launches = decider_gpu.launch_count() - n0
+    barrier(dist, local)
+    # e2e: pinned host inputs copied in and outputs copied out inside the region.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hg, hb = g.cpu().pin_memory(), beta.cpu().pin_memory()
+    hs = torch.zeros((B, H, D, D), dtype=torch.float32).pin_memory()
+    ho = torch.empty((B, T, H, D), dtype=torch.float32).pin_memory()
+    hs_out = torch.empty_like(hs).pin_memory()
+    e2e_ms = []
+    for i in range(1 + min(args.steps, 3)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for d_, h_ in ((q, hq), (k, hk), (v, hv), (g, hg), (beta, hb), (state, hs)):
+                d_.copy_(h_, non_blocking=True)
+            run()
+            ho.copy_(o, non_blocking=True)
+            hs_out.copy_(state, non_blocking=True)
+            e1.record(stream)
+        e1.synchronize()
+        if i:
+            e2e_ms.append(e0.elapsed_time(e1))
+    dev_ms = max_over_ranks(sum(ms) / len(ms), dist, local)
+    e2e = max_over_ranks(sum(e2e_ms) / len(e2e_ms), dist, local)
+    if rank != 0:
+        return
+    hbm, _, src = peaks()
+    achieved = CFG3_BYTES / (dev_ms / 1000.0) / 1e9
+    toks = B * T
+    in_bytes = sum(t.numel() * 4 for t in (hq, hk, hv, hg, hb, hs))
+    line = _line(args, world, "DeltaNet scan tok/s (cfg3: 64 x 4096 tokens x 16 heads)",
+                 world * toks / (dev_ms / 1000.0), "tok/s", dev_ms, _cfg3_config(world), dtype="f32",
+                 e2e={"value": world * toks / (e2e / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": in_bytes,
+                      "d2h_bytes_per_step": (ho.numel() + hs_out.numel()) * 4, "ms_per_step": e2e},
+                 roofline={"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                           "frac": achieved / hbm, "traffic": None,
+                           "kernel": "the chunked delta rule call (delta_chunk_prep, delta_chunk_scan, "
+                                     "delta_chunk_out), events around the call on its stream; achieved = "
+                                     f"{CFG3_BYTES / 1e9:.2f} GB algorithmic bytes per call / call time",
+                           "ms_per_launch": dev_ms, "peak_source": f"{src} HBM copy bandwidth"},
+                 gpu_launches=int(launches), clocks=clocks.summary(), promotion=None)
+    if world == 1 and not args.no_cpu:
+        v_, u, c, smp = _cpu_cfg3()
+        line["cpu_baseline"] = {"value": v_, "unit": u, "cores": c, "kind": "port", "sample": smp}
+    print(json.dumps(line), flush=True)
+
+
+def _cfg4_requests(vocab, seed):
+    """3584-token state prefix + 8 questions of 64 tokens, kinds mixed
+    (noul 2 options, choice 4, score 5), option positions in each question's
+    last 16 tokens."""
+    rng = np.random.default_rng(seed)
+    state = rng.integers(0, vocab, 3584)
+    qs = []
+    for i in range(8):
+        n_opt = (2, 4, 5)[i % 3]
+        qs.append((rng.integers(0, vocab, 64), [48 + 2 * j for j in range(n_opt)]))
+    return state, qs
+
+
+def _cfg5_sample(vocab, count, seed=0):
+    """The first `count` requests of config 5's seeded draw: bound length
+    L ~ U[128, 4096], 1-4 questions of 64 tokens; a request with one question
+    is one forward of L tokens, otherwise an (L - 64)-token state and its
+    questions."""
+    rng = np.random.default_rng(seed)
+    Ls = rng.integers(128, 4097, 8192)
+    qn = rng.integers(1, 5, 8192)
+    reqs, tokens = [], []
+    for i in range(count):
+        r = np.random.default_rng(seed * 100003 + i + 1)
+        L, q = int(Ls[i]), int(qn[i])
+        kinds = [(2, 4, 5)[(i + j) % 3] for j in range(q)]
+        if q == 1:
+            reqs.append({"questions": [(r.integers(0, vocab, L), [L - 16 + 2 * j for j in range(kinds[0])])]})
+            tokens.append(L)
+        else:
+            qs = [(r.integers(0, vocab, 64), [48 + 2 * j for j in range(k)]) for k in kinds]
+            reqs.append({"state": r.integers(0, vocab, L - 64), "questions": qs})
+            tokens.append(L - 64 + 64 * q)
+    return reqs, tokens, Ls[:count]
+
+
+def _model_for(args, local, max_tokens):
+    from decider_gpu import GpuModel
+    cfg = cfg2(args.layers)
+    cfg["vocab_size"] = args.vocab
+    t0 = time.time()
+    model = GpuModel(cfg, "int8-compute", 32, 2.0, 256, local, max_tokens)
+    model.fill_synthetic(seed=0, stddev=0.02)
+    model.finalize()
+    assert model.fast_path
+    model.set_exact(args.exact)
+    return model, time.time() - t0
+
+
+def run_batch(args, world, rank, local, dist, which):
+    """Configs 4 and 5 through dg_logits_batch: value from the device time
+    of every forward (request_ms), e2e from the wall time of the batch call
+    (host ids in, host logits out), roofline from the projection launches of
+    layers 0-3 in every forward."""
+    import torch
+
+    import decider_gpu
+    from decider_gpu.sharding import RequestShape, request_cost, shard_requests
+    torch.cuda.set_device(local)
+    model, setup_s = _model_for(args, local, 4096)
+    if which == "cfg4":
+        state, qs = _cfg4_requests(args.vocab, 1000 + rank)
+        mine = [{"state": state, "questions": qs}]
+        tokens_mine = 4096
+        tokens_all = world * 4096
+        config = {"workload": "cfg4: 2B decider, one 3584-token state prefix then 8 questions x 64 tokens "
+                              "(noul/choice(4)/score(5) mixed) continuing from its cached K/V and DeltaNet state; "
+                              "one request per rank",
+                  "tokens_per_step": 4096, "parallelism": f"dp{world}",
+                  "l2": "not flushed: every forward streams 1.4 GB of int8 weights, > 126 MB L2"}
+        scaling = "weak"
+    else:
+        reqs, toks, _ = _cfg5_sample(args.vocab, args.requests)
+        shapes = [RequestShape(len(r.get("state", ())), tuple(len(q[0]) for q in r["questions"])) for r in reqs]
+        plan = shard_requests([request_cost(s) for s in shapes], world)
+        mine = [reqs[i] for i in plan[rank]]
+        tokens_mine = sum(toks[i] for i in plan[rank])
+        tokens_all = sum(toks)
+        config = {"workload": f"cfg5: the first {args.requests} requests of the seeded 8192-request draw "
+                              "(L ~ U[128,4096], 1-4 questions of 64 tokens), LPT-sharded over the ranks",
+                  "tokens_per_step": tokens_all, "requests": args.requests, "parallelism": f"dp{world}",
+                  "l2": "not flushed: every forward streams 1.4 GB of int8 weights, > 126 MB L2"}
+        scaling = "strong"
+    model.gemm_timing_layers(0, min(4, args.layers))
+    for _ in range(args.warmup):
+        _, st, _, err = model.logits_batch(mine)
+        assert not st.any(), err
+    g0_ms, g0_ops, g0_n = model.gemm_time()
+    barrier(dist, local)
+    n0 = decider_gpu.launch_count()
+    dev, wall, per_req = [], [], []
+    with ClockSampler(local) as clocks:
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            _, st, ms, err = model.logits_batch(mine)
+            wall.append((time.perf_counter() - t0) * 1000.0)
+            assert not st.any(), err
+            dev.append(float(ms.sum()))
+            per_req += [float(x) for x in ms]
+    launches = decider_gpu.launch_count() - n0
+    barrier(dist, local)
+    g_ms, g_ops, g_n = model.gemm_time()
+    g_ms, g_ops, g_n = g_ms - g0_ms, g_ops - g0_ops, g_n - g0_n
+    model.gemm_timing(False)
+    dev_ms = max_over_ranks(sum(dev) / len(dev), dist, local)
+    e2e_ms = max_over_ranks(sum(wall) / len(wall), dist, local)
+    per_req.sort()
+    p50 = max_over_ranks(per_req[len(per_req) // 2], dist, local)
+    p99 = max_over_ranks(per_req[min(len(per_req) - 1, (99 * len(per_req)) // 100)], dist, local)
+    if rank != 0:
+        return
+    _, bf16, src = peaks()
+    peak = 2.0 * bf16
+    achieved = g_ops / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
+    n_ids = sum(len(r.get("state", [])) + sum(len(q[0]) for q in r["questions"]) for r in mine)
+    n_logits = sum(len(q[1]) for r in mine for q in r["questions"])
+    line = _line(args, world, f"prefill tok/s at 2B INT8 ({which})", tokens_all / (dev_ms / 1000.0), "tok/s",
+                 dev_ms, dict(config, setup_s=round(setup_s, 1)),
+                 e2e={"value": tokens_all / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": n_ids * 4,
+                      "d2h_bytes_per_step": n_logits * 4, "ms_per_step": e2e_ms},
+                 roofline={"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                           "frac": achieved / peak, "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
+                           "kernel": "gemm_i8_g64_kernel, the projection launches of layers 0-3 in every forward "
+                                     "of the timed steps (achieved = sum 2*M*N*K / sum event time)",
+                           "launches": int(g_n), "ms_per_launch": g_ms / max(g_n, 1),
+                           "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
+                 latency={"p50_ms": p50, "p99_ms": p99, "requests": len(per_req),
+                          "what": "device time of one request's forwards, max over ranks"},
+                 gpu_launches=int(launches), clocks=clocks.summary(), scaling=scaling)
+    line["config"]["tokens_rank0"] = tokens_mine
+    if world == 1 and not args.no_cpu:
+        cs = CpuSample()
+        sec = cs.time(args.cpu_tokens)
+        line["cpu_baseline"] = {"value": args.cpu_tokens / sec, "unit": "tok/s", "cores": cs.threads,
+                                "kind": "port",
+                                "sample": f"oracle port, one 4-layer block of the 2B model x {args.cpu_tokens} "
+                                          "tokens from an empty cache, x6 for 24 layers (short context: "
+                                          "favours the CPU)"}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_workload(args, world, rank, which):
+    """`--impl reference` for configs 1, 3, 4 and 5: the oracle's CPU path on
+    rank 0's host cores, one bounded sample per step."""
+    if rank != 0:
+        return
+    vals = []
+    for i in range(args.warmup + args.steps):
+        if which == "cfg1":
+            v, u, c, smp = _cpu_cfg1()
+            config = _cfg1_config(world)
+            metric = "INT8 GEMM TOP/s (cfg1: 512x6144x2048, group-64)"
+        elif which == "cfg3":
+            v, u, c, smp = _cpu_cfg3()
+            config = _cfg3_config(world)
+            metric = "DeltaNet scan tok/s (cfg3: 64 x 4096 tokens x 16 heads)"
+        else:
+            cs = CpuSample()
+            v, u, c = args.cpu_tokens / cs.time(args.cpu_tokens), "tok/s", cs.threads
+            smp = f"oracle port, one 4-layer block x {args.cpu_tokens} tokens, x6 for 24 layers"
+            config = {"workload": which}
+            metric = f"prefill tok/s at 2B INT8 ({which})"
+        if i >= args.warmup:
+            vals.append(v)
+    v = sum(vals) / len(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": v, "unit": u, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "data": "synthetic", "config": config,
+        "note": "the reference's CPU algorithm (oracle restatement) on rank 0's host cores",
+        "cpu_baseline": {"value": v, "unit": u, "cores": c, "kind": "port", "sample": smp},
+        "e2e": {"value": v, "unit": u, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -333,13 +763,25 @@ def main():
                     help="fewer layers (multiple of 4) for small ncu captures; the bench line is 24")
     ap.add_argument("--vocab", type=int, default=248320,
                     help="smaller embedding table for small ncu captures; the bench line is 248320")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"],
+                    help="BASELINE config to measure; the default line is cfg2")
+    ap.add_argument("--requests", type=int, default=48, help="cfg5: requests taken from the seeded draw")
     args = ap.parse_args()
     if args.layers % 4 or args.layers <= 0:
         ap.error("--layers must be a positive multiple of 4")
     world, rank, local, dist = dist_setup()
     try:
         if args.impl == "reference":
-            run_reference(args, world, rank, local, dist)
+            if args.workload == "cfg2":
+                run_reference(args, world, rank, local, dist)
+            else:
+                run_reference_workload(args, world, rank, args.workload)
+        elif args.workload == "cfg1":
+            run_cfg1(args, world, rank, local, dist)
+        elif args.workload == "cfg3":
+            run_cfg3(args, world, rank, local, dist)
+        elif args.workload in ("cfg4", "cfg5"):
+            run_batch(args, world, rank, local, dist, args.workload)
         else:
             run_ours(args, world, rank, local, dist)
     finally:

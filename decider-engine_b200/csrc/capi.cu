@@ -38,7 +38,11 @@ struct dg_linear {
   dg::DevBuf wq, ws_t, lora_a, lora_b, chunk_pid, status;
   dg::WeightMaps maps{};
   int cap_m = 0, ldxs = 0;
-  dg::DevBuf x, xq, xs, mid, y;
+  dg::DevBuf x, xq, xs, mid, y, yh;
+  // Device time of the last forward (events on `stream`): before the
+  // quantiser, before the projection kernel, after it.
+  cudaEvent_t ev[3] = {};
+  float last_total_ms = 0.0f, last_gemm_ms = 0.0f;
 };
 
 namespace {
@@ -97,6 +101,7 @@ void linear_reserve(dg_linear* l, int m) {
   DG_CUDA(cudaMemset(l->xs.ptr, 0, l->xs.bytes));
   l->mid = dg::DevBuf(size_t(cap) * 32 * 4);
   l->y = dg::DevBuf(size_t(cap) * l->n_pad * 4);
+  l->yh = dg::DevBuf(size_t(cap) * l->n * 4);
   l->cap_m = cap;
 }
 
@@ -107,6 +112,7 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
   linear_reserve(l, m);
   DG_CUDA(cudaMemsetAsync(l->status.ptr, 0, sizeof(DeviceStatus), l->stream));
   DeviceStatus* st = l->status.as<DeviceStatus>();
+  DG_CUDA(cudaEventRecord(l->ev[0], l->stream));
   launch_norm_quant(x_dev, l->k, m, l->k, nullptr, 0.0f, nullptr, 0, l->xq.as<int8_t>(), l->xs.as<float>(), l->ldxs, st,
                     l->stream);
   if (l->rank) {
@@ -136,13 +142,17 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
     dump = dots;
   }
   a.dots = dump;
+  DG_CUDA(cudaEventRecord(l->ev[1], l->stream));
   launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
+  DG_CUDA(cudaEventRecord(l->ev[2], l->stream));
   if (!direct)
     DG_CUDA(cudaMemcpy2DAsync(y_dev, size_t(l->n) * 4, l->y.ptr, size_t(l->n_pad) * 4, size_t(l->n) * 4, m,
                               cudaMemcpyDeviceToDevice, l->stream));
   DeviceStatus h{};
   DG_CUDA(cudaMemcpyAsync(&h, l->status.ptr, sizeof(h), cudaMemcpyDeviceToHost, l->stream));
   DG_CUDA(cudaStreamSynchronize(l->stream));
+  DG_CUDA(cudaEventElapsedTime(&l->last_total_ms, l->ev[0], l->ev[2]));
+  DG_CUDA(cudaEventElapsedTime(&l->last_gemm_ms, l->ev[1], l->ev[2]));
   if (h.code == kNonFinite) throw std::runtime_error("non-finite projection input");
   if (h.code) throw std::runtime_error("device error code " + std::to_string(h.code) + " at " + std::to_string(h.where));
 }
@@ -333,6 +343,60 @@ int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n
   });
 }
 
+int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
+                    float* request_ms) {
+  const int rc = guarded([&] {
+    check_engine(e);
+    if (n_requests && (!requests || !logits_out)) throw std::runtime_error("null argument");
+  });
+  if (rc) return rc;
+  std::string first_error;
+  size_t out = 0;
+  for (size_t r = 0; r < n_requests; ++r) {
+    const dg_request& q = requests[r];
+    size_t n_logits = 0;
+    for (size_t i = 0; q.questions && i < q.n_questions; ++i) n_logits += q.questions[i].n_opt;
+    float ms = 0.0f;
+    const int st = guarded([&] {
+      if (!q.questions || q.n_questions == 0) throw std::runtime_error("request has no questions");
+      if (q.past && q.past->owner != e) throw std::runtime_error("prefix belongs to another engine");
+      if (q.past && q.n_state) throw std::runtime_error("a request continues either a prefix or its own state ids");
+      if (q.n_state && !q.state_ids) throw std::runtime_error("null state ids");
+      for (size_t i = 0; i < q.n_questions; ++i) {
+        const dg_question& u = q.questions[i];
+        if (!u.ids || !u.opt_pos || u.n == 0 || u.n_opt == 0)
+          throw std::runtime_error("invalid encoding positions or window");
+        for (size_t j = 0; j < u.n_opt; ++j)
+          if (u.opt_pos[j] + 1 >= u.n) throw std::runtime_error("invalid encoding positions or window");
+      }
+      dg::Engine& g = *e->e;
+      std::lock_guard<std::mutex> lk(g.mu);
+      std::unique_ptr<dg::Prefix> state;
+      const dg::Prefix* past = q.past ? q.past->p.get() : nullptr;
+      if (q.n_state) {
+        g.forward(q.state_ids, int(std::min<size_t>(q.n_state, 1u << 30)), nullptr, true, nullptr, &state);
+        ms += g.last_forward_ms;
+        past = state.get();
+      }
+      size_t o = out;
+      for (size_t i = 0; i < q.n_questions; ++i) {
+        const dg_question& u = q.questions[i];
+        g.forward(u.ids, int(std::min<size_t>(u.n, 1u << 30)), past, false, nullptr, nullptr);
+        ms += g.last_forward_ms;
+        g.head_logits(int(u.n), u.opt_pos, int(u.n_opt), logits_out + o);
+        o += u.n_opt;
+      }
+    });
+    if (st && first_error.empty()) first_error = dg_last_error();
+    if (status_out) status_out[r] = st;
+    if (request_ms) request_ms[r] = ms;
+    out += n_logits;
+  }
+  if (first_error.empty()) return 0;
+  g_error = first_error;
+  return 1;
+}
+
 int dg_linear_create(const float* w, int n, int k, const float* lora_a, const float* lora_b, int rank, float lora_scale,
                      int device, dg_linear** out) {
   return guarded([&] {
@@ -377,6 +441,7 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
     l->status = DevBuf(sizeof(DeviceStatus));
     make_weight_maps(&l->maps, l->wq.ptr, k, N, rank ? l->lora_b.as<float>() : nullptr, rank);
     DG_CUDA(cudaStreamCreateWithFlags(&l->stream, cudaStreamNonBlocking));
+    for (auto& ev : l->ev) DG_CUDA(cudaEventCreate(&ev));
     *out = l.release();
   });
 }
@@ -387,9 +452,8 @@ int dg_linear_forward(dg_linear* l, const float* x, int m, float* y) {
     DG_CUDA(cudaSetDevice(l->device));
     linear_reserve(l, m);
     DG_CUDA(cudaMemcpyAsync(l->x.ptr, x, size_t(m) * l->k * 4, cudaMemcpyHostToDevice, l->stream));
-    dg::DevBuf out(size_t(m) * l->n * 4);
-    linear_run(l, l->x.as<float>(), m, out.as<float>(), nullptr);
-    DG_CUDA(cudaMemcpyAsync(y, out.ptr, size_t(m) * l->n * 4, cudaMemcpyDeviceToHost, l->stream));
+    linear_run(l, l->x.as<float>(), m, l->yh.as<float>(), nullptr);
+    DG_CUDA(cudaMemcpyAsync(y, l->yh.ptr, size_t(m) * l->n * 4, cudaMemcpyDeviceToHost, l->stream));
     DG_CUDA(cudaStreamSynchronize(l->stream));
   });
 }
@@ -414,6 +478,14 @@ int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs) {
 
 void* dg_linear_stream(const dg_linear* l) { return l ? static_cast<void*>(l->stream) : nullptr; }
 
+int dg_linear_last_times(const dg_linear* l, float* total_ms, float* gemm_ms) {
+  return guarded([&] {
+    if (!l) throw std::runtime_error("null argument");
+    if (total_ms) *total_ms = l->last_total_ms;
+    if (gemm_ms) *gemm_ms = l->last_gemm_ms;
+  });
+}
+
 int dg_linear_set_exact(dg_linear* l, int exact) {
   return guarded([&] {
     if (!l) throw std::runtime_error("null argument");
@@ -428,6 +500,8 @@ void dg_linear_free(dg_linear* l) {
     cudaStreamSynchronize(l->stream);
     cudaStreamDestroy(l->stream);
   }
+  for (auto& ev : l->ev)
+    if (ev) cudaEventDestroy(ev);
   delete l;
 }
 

@@ -20,9 +20,10 @@ SYMBOLS = [
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
     "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
+    "dg_logits_batch",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
-    "dg_linear_set_exact", "dg_linear_stream", "dg_linear_free",
+    "dg_linear_set_exact", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
     "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
 ]
 
@@ -74,6 +75,7 @@ def load() -> C.CDLL:
     L.dg_engine_gemm_time.argtypes = [vp, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_uint64)]
     L.dg_linear_stream.argtypes = [vp]
     L.dg_linear_stream.restype = vp
+    L.dg_linear_last_times.argtypes = [vp, C.POINTER(C.c_float), C.POINTER(C.c_float)]
     L.dg_forward_hidden.argtypes = [vp, vp, u32p, sz, f32p]
     L.dg_prefill.argtypes = [vp, u32p, sz, C.POINTER(vp)]
     L.dg_prefix_len.argtypes = [vp]
@@ -81,6 +83,7 @@ def load() -> C.CDLL:
     L.dg_prefix_free.argtypes = [vp]
     L.dg_prefix_free.restype = None
     L.dg_logits.argtypes = [vp, vp, u32p, sz, vp, sz, f32p]
+    L.dg_logits_batch.argtypes = [vp, vp, sz, f32p, vp, vp]
     L.dg_linear_create.argtypes = [f32p, i32, i32, f32p, f32p, i32, C.c_float, i32, C.POINTER(vp)]
     L.dg_linear_forward.argtypes = [vp, f32p, i32, f32p]
     L.dg_linear_forward_device.argtypes = [vp, vp, i32, vp, vp]

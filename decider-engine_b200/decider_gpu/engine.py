@@ -76,6 +76,15 @@ def read_checkpoint_config_native(d: str) -> dict:
     return out
 
 
+class _Question(C.Structure):
+    _fields_ = [("ids", C.c_void_p), ("n", C.c_size_t), ("opt_pos", C.c_void_p), ("n_opt", C.c_size_t)]
+
+
+class _Request(C.Structure):
+    _fields_ = [("past", C.c_void_p), ("state_ids", C.c_void_p), ("n_state", C.c_size_t),
+                ("questions", C.c_void_p), ("n_questions", C.c_size_t)]
+
+
 class GpuPrefix:
     """Device-resident, immutable prefix cache (Prefix, src/qwen.rs:509-526)."""
 
@@ -181,6 +190,51 @@ class GpuModel:
                                len(pos), out.ctypes.data))
         return out
 
+    # ---- batched requests (dg_logits_batch): the throughput form of
+    # NativeEngine::evaluate (src/lib.rs:477-559)
+    def logits_batch(self, requests):
+        """requests: dicts with `questions` [(ids, option_positions), ...] and
+        optionally `state` (ids prefilled once and shared by the questions) or
+        `past` (a GpuPrefix). Returns (logits per request: a list of arrays per
+        question, status per request (0 ok), device ms per request, first error
+        message or None)."""
+        keep = []
+        reqs = (_Request * max(1, len(requests)))()
+        sizes = []
+        for r, q in enumerate(requests):
+            qs = (_Question * len(q["questions"]))()
+            sz = []
+            for i, (ids, pos) in enumerate(q["questions"]):
+                ids, p = _u32(ids)
+                pos = np.ascontiguousarray(pos, np.uint64)
+                keep += [ids, pos]
+                qs[i].ids, qs[i].n, qs[i].opt_pos, qs[i].n_opt = p, len(ids), pos.ctypes.data, len(pos)
+                sz.append(len(pos))
+            keep.append(qs)
+            sizes.append(sz)
+            reqs[r].questions, reqs[r].n_questions = C.cast(qs, C.c_void_p), len(qs)
+            past = q.get("past")
+            reqs[r].past = None if past is None else past.h
+            state = q.get("state")
+            if state is not None and len(state):
+                st, sp = _u32(state)
+                keep.append(st)
+                reqs[r].state_ids, reqs[r].n_state = sp, len(st)
+        total = sum(sum(sz) for sz in sizes)
+        out = np.zeros(max(1, total), np.float32)
+        status = np.zeros(max(1, len(requests)), np.int32)
+        ms = np.zeros(max(1, len(requests)), np.float32)
+        rc = load().dg_logits_batch(self.h, C.cast(reqs, C.c_void_p), len(requests), out.ctypes.data, status.ctypes.data, ms.ctypes.data)
+        err = load().dg_last_error().decode() if rc else None
+        res, o = [], 0
+        for sz in sizes:
+            per = []
+            for k in sz:
+                per.append(out[o:o + k].copy())
+                o += k
+            res.append(per)
+        return res, status[:len(requests)].copy(), ms[:len(requests)].copy(), err
+
     @classmethod
     def load_native(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096):
         """`from_dir` through the library's own checkpoint loader (dg_engine_load):
@@ -252,6 +306,17 @@ class Linear:
         Calls on one device must not overlap in time; the first call on a
         device should come before any stream capture begins."""
         check(load().dg_linear_forward_device_noalloc(self.h, x_ptr, m, y_ptr))
+
+    def last_times(self):
+        """(total_ms, gemm_ms) of the last forward: device time from the
+        activation quantiser to the end of the projection, and of the
+        projection kernel alone (CUDA events on the handle's stream)."""
+        t, g = C.c_float(), C.c_float()
+        check(load().dg_linear_last_times(self.h, C.byref(t), C.byref(g)))
+        return t.value, g.value
+
+    def stream(self) -> int:
+        return int(load().dg_linear_stream(self.h) or 0)
 
     def last_quantized(self, m: int):
         xq = np.zeros((m, self.k), np.int8)

@@ -120,6 +120,41 @@ void dg_prefix_free(dg_prefix* p);
 int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, const size_t* opt_pos,
               size_t n_opt, float* logits_out);
 
+/* ---- batched requests: the throughput form of NativeEngine::evaluate
+ * (src/lib.rs:477-559), which prefills a request's state once
+ * (src/lib.rs:515-522, Model::prefill src/qwen.rs:413) and reads every
+ * question of the request after it (Model::forward_after src/qwen.rs:422 +
+ * Head::logits src/lib.rs:116-131). One request:
+ *   past        nullable: an existing prefix (dg_prefill) the questions continue;
+ *   state_ids   n_state tokens prefilled once and shared by the questions
+ *               (n_state 0: none; not combined with `past`);
+ *   questions   each a token sequence after the state with its option
+ *               positions (relative to the question's own ids).
+ * A request with neither past nor state and one question is one plain
+ * forward. logits_out receives the n_opt logits of every question of every
+ * request, concatenated in order. status_out (nullable, [n_requests]) gets
+ * 0 or 1 per request and request_ms (nullable) the device time of that
+ * request's forwards; a failed request's logits are unspecified and the
+ * batch continues with the next request. Returns 0 when every request succeeded, otherwise 1 with
+ * dg_last_error() holding the first failure's message. Requests run in order
+ * on the engine's device and stream; to spread a batch over several GPUs,
+ * give each device's engine its share (one host thread or process per GPU). */
+typedef struct dg_question {
+  const uint32_t* ids;
+  size_t n;
+  const size_t* opt_pos;
+  size_t n_opt;
+} dg_question;
+typedef struct dg_request {
+  const dg_prefix* past;
+  const uint32_t* state_ids;
+  size_t n_state;
+  const dg_question* questions;
+  size_t n_questions;
+} dg_request;
+int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
+                    float* request_ms);
+
 /* ---- isolated INT8 projection: the reference's
  * linear_int8 + Adapter::combine (src/tensor.rs:379-456,109-117) with
  * load-time weight quantisation (src/weights.rs:98-146). w: [n][k] FP32;
@@ -155,6 +190,12 @@ int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs);
 int dg_linear_set_exact(dg_linear* l, int exact);
 /* The CUDA stream the projection runs on (cudaStream_t). */
 void* dg_linear_stream(const dg_linear* l);
+/* Device time of the last dg_linear_forward / dg_linear_forward_device call,
+ * from CUDA events on the handle's stream, in milliseconds: total_ms from the
+ * activation quantiser to the end of the projection kernel, gemm_ms the
+ * projection kernel alone (either pointer nullable). A measurement aid with
+ * no counterpart in the reference. */
+int dg_linear_last_times(const dg_linear* l, float* total_ms, float* gemm_ms);
 void dg_linear_free(dg_linear* l);
 
 /* ---- isolated gated delta rule: Recurrence::head's

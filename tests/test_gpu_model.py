@@ -235,3 +235,42 @@ def test_config4_shared_prefix_questions_continue_bit_exact():
         full = m.forward(np.concatenate([prefix_ids, questions[i]]))
         assert np.array_equal(rows[i], full[3584:]), i
     assert np.array_equal(m.forward_after(prefix, questions[0]), rows[0])
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
+def test_logits_batch_equals_one_call_per_question(small, exact):
+    """dg_logits_batch (the throughput form of NativeEngine::evaluate,
+    src/lib.rs:477-559) gives every question the same logits, bit for bit, as
+    dg_prefill + one dg_logits call per question: a request with its own state
+    and three questions, a plain single forward, a request continuing a
+    caller-made prefix, and a failing request (option position outside its
+    question) that is reported in its status while the rest of the batch runs."""
+    cfg, tensors = small
+    m = _gpu_small(cfg, tensors)
+    m.set_exact(exact)
+    rng = np.random.default_rng(21)
+    ids = lambda n: rng.integers(0, cfg["vocab_size"], n)
+    state = ids(300)
+    qs = [(ids(40), [30, 31]), (ids(64), [50, 51, 52, 53]), (ids(17), [1, 5, 9, 12, 15])]
+    single = (ids(129), [120, 121])
+    past_ids = ids(77)
+    past = m.prefill(past_ids)
+    cont = (ids(33), [3, 30])
+    bad = (ids(10), [10])
+    got, status, ms, err = m.logits_batch([
+        {"state": state, "questions": qs},
+        {"questions": [single]},
+        {"past": past, "questions": [cont]},
+        {"questions": [bad]},
+        {"state": state[:50], "questions": [qs[0]]},
+    ])
+    assert list(status) == [0, 0, 0, 1, 0], status
+    assert err and "invalid encoding positions" in err
+    assert all(ms[i] > 0 for i in (0, 1, 2, 4)), ms
+    sp = m.prefill(state)
+    for i, (q, pos) in enumerate(qs):
+        assert np.array_equal(got[0][i], m.logits(q, pos, sp)), i
+    assert np.array_equal(got[1][0], m.logits(*single))
+    assert np.array_equal(got[2][0], m.logits(cont[0], cont[1], past))
+    assert np.array_equal(got[4][0], m.logits(qs[0][0], qs[0][1], m.prefill(state[:50])))
+    assert len(m.prefill(past_ids)) == len(past) == 77  # the caller's prefix is unchanged by its use
