@@ -343,6 +343,14 @@ int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n
   });
 }
 
+int dg_debug_layer(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out) {
+  return guarded([&] {
+    check_engine(e);
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->debug_layer(layer, x_in, int(std::min<size_t>(n, 1u << 30)), x_out);
+  });
+}
+
 int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
                     float* request_ms) {
   const int rc = guarded([&] {

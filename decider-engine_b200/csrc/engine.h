@@ -109,6 +109,9 @@ class Engine {
                std::unique_ptr<Prefix>* captured);
   // Head::logits on the last forward's hidden rows (device-resident).
   void head_logits(int rows, const size_t* positions, int n_pos, float* logits_out);
+  // One decoder layer, teacher-forced: residual rows x_in [n][hidden] (host)
+  // at positions 0..n-1 with no prefix -> the layer's output rows (host).
+  void debug_layer(int layer, const float* x_in, int n, float* x_out);
   const Config& config() const { return c_; }
   bool fast_path() const { return fast_; }
   int device() const { return device_; }

@@ -267,6 +267,35 @@ void Engine::run_layers(int n, int start, const Prefix* past, Prefix* cap) {
   launch_final_norm(x_.as<float>(), n, c_.hidden, final_norm_.as<float>(), c_.eps, status(), stream_);
 }
 
+void Engine::debug_layer(int layer, const float* x_in, int n, float* x_out) {
+  if (!finalized_) throw DgError("engine is not finalized");
+  if (layer < 0 || layer >= c_.layers) throw DgError("layer index out of range");
+  if (n <= 0 || n > 4096) throw DgError("token sequence must contain 1\xe2\x80\x93" "4096 tokens");
+  if (n > max_tokens_) throw DgError("token sequence exceeds the engine's max_tokens workspace");
+  if (!x_in || !x_out) throw DgError("null argument");
+  DG_CUDA(cudaSetDevice(device_));
+  const uint64_t launches0 = launch_count();
+  const size_t bytes = size_t(n) * c_.hidden * 4;
+  DG_CUDA(cudaMemcpyAsync(x_.ptr, x_in, bytes, cudaMemcpyHostToDevice, stream_));
+  DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
+  gemm_ops_pending_.clear();
+  fwd_ops_all_ = 0.0;
+  fwd_proj_ = 0;
+  DG_CUDA(cudaEventRecord(ev0_, stream_));
+  cur_layer_ = layer;
+  if (fast_)
+    layer_fast(layer, n, 0, nullptr, nullptr);
+  else
+    layer_generic(layer, n, 0, nullptr, nullptr);
+  cur_layer_ = -1;
+  DG_CUDA(cudaEventRecord(ev1_, stream_));
+  DG_CUDA(cudaMemcpyAsync(x_out, x_.ptr, bytes, cudaMemcpyDeviceToHost, stream_));
+  check_status();
+  DG_CUDA(cudaEventElapsedTime(&last_forward_ms, ev0_, ev1_));
+  collect_gemm_timing();
+  last_launches = int(launch_count() - launches0);
+}
+
 void Engine::drop_graphs() {
   for (auto& kv : graphs_)
     if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);

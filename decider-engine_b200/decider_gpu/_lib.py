@@ -20,7 +20,7 @@ SYMBOLS = [
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
     "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
-    "dg_logits_batch",
+    "dg_logits_batch", "dg_debug_layer",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
@@ -84,6 +84,7 @@ def load() -> C.CDLL:
     L.dg_prefix_free.restype = None
     L.dg_logits.argtypes = [vp, vp, u32p, sz, vp, sz, f32p]
     L.dg_logits_batch.argtypes = [vp, vp, sz, f32p, vp, vp]
+    L.dg_debug_layer.argtypes = [vp, i32, f32p, sz, f32p]
     L.dg_linear_create.argtypes = [f32p, i32, i32, f32p, f32p, i32, C.c_float, i32, C.POINTER(vp)]
     L.dg_linear_forward.argtypes = [vp, f32p, i32, f32p]
     L.dg_linear_forward_device.argtypes = [vp, vp, i32, vp, vp]

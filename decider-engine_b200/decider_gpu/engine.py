@@ -190,6 +190,14 @@ class GpuModel:
                                len(pos), out.ctypes.data))
         return out
 
+    def layer(self, index: int, x: np.ndarray) -> np.ndarray:
+        """One decoder layer teacher-forced on residual rows x [n][hidden]
+        (positions 0..n-1, no prefix): dg_debug_layer."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        check(load().dg_debug_layer(self.h, int(index), x.ctypes.data, x.shape[0], out.ctypes.data))
+        return out
+
     # ---- batched requests (dg_logits_batch): the throughput form of
     # NativeEngine::evaluate (src/lib.rs:477-559)
     def logits_batch(self, requests):

@@ -110,6 +110,13 @@ int dg_engine_gemm_time_all(const dg_engine* e, double* ops_all, uint64_t* launc
  * the layer types". */
 int dg_forward_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n, float* hidden_out);
 int dg_prefill(dg_engine* e, const uint32_t* ids, size_t n, dg_prefix** out);
+/* One decoder layer teacher-forced, for per-layer parity: the body of the
+ * layer loop of Model::run (src/qwen.rs:470-494: input norm, Full::forward or
+ * Delta::forward, residual_norm, SwiGLU MLP with the residual add) applied
+ * to the caller's residual rows x_in [n][hidden_size] at positions 0..n-1
+ * with no prefix; x_out receives the layer's output rows [n][hidden_size].
+ * Runs in the engine's current arithmetic mode. */
+int dg_debug_layer(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out);
 size_t dg_prefix_len(const dg_prefix* p);
 void dg_prefix_free(dg_prefix* p);
 

@@ -79,6 +79,8 @@ def lib():
         L.or_forward.argtypes = [_c.c_void_p, _u32p, _c.c_size_t, _c.c_void_p, _c.c_int,
                                  _c.c_void_p, _c.POINTER(_c.c_void_p)]
         L.or_head_logits.restype = _c.c_int
+        L.or_forward_trace.argtypes = [_c.c_void_p, _u32p, _c.c_size_t, _c.c_void_p]
+        L.or_layer.argtypes = [_c.c_void_p, _c.c_int, _f32p, _c.c_size_t, _f32p]
         L.or_head_logits.argtypes = [_c.c_void_p, _f32p, _c.c_size_t, _c.c_void_p, _c.c_size_t,
                                      _f32p]
         L.or_gated_delta_rule.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _c.c_size_t,
@@ -285,6 +287,24 @@ class OracleModel:
 
     def forward_after(self, prefix, ids):
         return self._run(ids, past=prefix)[0]
+
+    def layer_trace(self, ids):
+        """Residual rows through the layer loop of Model::run: [layers + 1][n][hidden],
+        the embedded input and then each layer's output (before the final norm)."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        c = self.config
+        out = np.zeros((c["num_hidden_layers"] + 1, len(ids), c["hidden_size"]), np.float32)
+        if lib().or_forward_trace(self.h, ids, len(ids), out.ctypes.data):
+            raise _err()
+        return out
+
+    def layer(self, index, x):
+        """One layer teacher-forced on residual rows x [n][hidden] (positions 0..n-1)."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        if lib().or_layer(self.h, int(index), x, x.shape[0], out):
+            raise _err()
+        return out
 
     def head_logits(self, hidden, positions):
         hidden = np.ascontiguousarray(hidden, np.float32)

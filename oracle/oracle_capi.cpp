@@ -287,6 +287,49 @@ int or_forward(void* h, const uint32_t* ids, size_t n, const void* past, int cap
   return 0;
 }
 
+// Model::run with every layer's residual rows recorded: trace_out receives
+// [layers + 1][n][hidden] (the embedded input, then each layer's output,
+// before the final norm).
+int or_forward_trace(void* h, const uint32_t* ids, size_t n, float* trace_out) {
+  auto* om = static_cast<OracleModel*>(h);
+  std::vector<float> x, trace;
+  std::string err;
+  int rc;
+  try {
+    rc = run(om->m, ids, n, nullptr, false, x, nullptr, err, &trace);
+  } catch (const std::exception& e) {
+    err = e.what();
+    rc = 1;
+  }
+  if (rc) {
+    g_error = err;
+    return 1;
+  }
+  std::copy(trace.begin(), trace.end(), trace_out);
+  return 0;
+}
+
+// One layer of the loop teacher-forced on the residual rows x [n][hidden]
+// (positions 0..n-1, no prefix); out receives the layer's output rows.
+int or_layer(void* h, int layer, const float* x, size_t n, float* out) {
+  auto* om = static_cast<OracleModel*>(h);
+  const Model& m = om->m;
+  if (layer < 0 || size_t(layer) >= m.layers.size() || n == 0 || n > 4096) {
+    g_error = "bad layer or row count";
+    return 1;
+  }
+  try {
+    std::vector<float> v(x, x + n * m.c.hidden);
+    LayerCache cache;
+    run_layer(m, size_t(layer), v, n, 0, rotary_angles(m, 0, n), nullptr, &cache);
+    std::copy(v.begin(), v.end(), out);
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+  return 0;
+}
+
 // Head::logits over `rows` hidden rows; the answer row is the last.
 int or_head_logits(void* h, const float* hidden, size_t rows, const size_t* positions, size_t n_pos,
                    float* out) {

@@ -263,9 +263,44 @@ static std::vector<float> delta_forward(const Layer& L, const Config& c, const f
   return L.out.apply(out.data(), n);
 }
 
+// Rotary angles of positions start..start+n-1 (src/qwen.rs:452-458).
+static std::vector<float> rotary_angles(const Model& m, size_t start, size_t n) {
+  size_t half = m.rotary_divisors.size();
+  std::vector<float> angles(n * half * 2);
+  for (size_t t = 0; t < n; ++t)
+    for (size_t i = 0; i < half; ++i) {
+      float a = float(start + t) / m.rotary_divisors[i];
+      angles[(t * half + i) * 2] = std::sin(a);
+      angles[(t * half + i) * 2 + 1] = std::cos(a);
+    }
+  return angles;
+}
+
+// One pass of the layer loop of Model::run (src/qwen.rs:470-494) on the
+// residual rows x [n, hidden]: input norm, Full/Delta forward, residual_norm,
+// SwiGLU MLP with the residual add.
+static void run_layer(const Model& m, size_t i, std::vector<float>& x, size_t n, size_t start,
+                      const std::vector<float>& angles, const LayerCache* lp, LayerCache* cache) {
+  const Config& c = m.c;
+  size_t h = c.hidden;
+  const Layer& L = m.layers[i];
+  std::vector<float> nrm = x;
+  rms(nrm.data(), nrm.size(), L.input_norm.data(), h, c.eps, true);
+  std::vector<float> mixed = L.full ? full_forward(L, c, nrm.data(), n, angles, lp, cache)
+                                    : delta_forward(L, c, nrm.data(), n, start, lp, cache);
+  residual_norm(x.data(), mixed.data(), nrm.data(), L.post_norm.data(), h, x.size(), c.eps);
+  std::shared_ptr<QuantizedInputs> shared;
+  bool done = false;
+  std::vector<float> gate(n * c.intermediate);
+  L.gate.apply_into(nrm.data(), n, gate.data(), Epilogue::Write, &shared, &done);
+  L.up.apply_into(nrm.data(), n, gate.data(), Epilogue::SwiGlu, &shared, &done);
+  L.down.apply_into(gate.data(), n, x.data(), Epilogue::Add, nullptr, nullptr);
+}
+
 // Model::run, src/qwen.rs:426-504. Returns 0, or an error message in `err`.
 static int run(const Model& m, const uint32_t* ids, size_t n, const Prefix* past, bool capture,
-               std::vector<float>& x, Prefix* captured, std::string& err) {
+               std::vector<float>& x, Prefix* captured, std::string& err,
+               std::vector<float>* layer_trace = nullptr) {
   const Config& c = m.c;
   size_t start = past ? past->len : 0;
   if (n == 0 || start + n > 4096) {
@@ -283,36 +318,19 @@ static int run(const Model& m, const uint32_t* ids, size_t n, const Prefix* past
     const float* row = m.embedding.row(size_t(ids[t]) * h, h, scratch);
     std::copy(row, row + h, x.begin() + t * h);
   }
-  size_t half = m.rotary_divisors.size();
-  std::vector<float> angles(n * half * 2);
-  for (size_t t = 0; t < n; ++t)
-    for (size_t i = 0; i < half; ++i) {
-      float a = float(start + t) / m.rotary_divisors[i];
-      angles[(t * half + i) * 2] = std::sin(a);
-      angles[(t * half + i) * 2 + 1] = std::cos(a);
-    }
-  std::vector<float> nrm(x.size());
+  std::vector<float> angles = rotary_angles(m, start, n);
+  if (layer_trace) layer_trace->assign(x.begin(), x.end());
   if (captured) captured->layers.clear();
   for (size_t i = 0; i < m.layers.size(); ++i) {
-    const Layer& L = m.layers[i];
-    nrm = x;
-    rms(nrm.data(), nrm.size(), L.input_norm.data(), h, c.eps, true);
     const LayerCache* lp = past ? &past->layers[i] : nullptr;
-    if (lp && lp->full != L.full) {
+    if (lp && lp->full != m.layers[i].full) {
       err = "prefix cache does not match the layer types";
       return 1;
     }
     LayerCache cache;
-    std::vector<float> mixed = L.full ? full_forward(L, c, nrm.data(), n, angles, lp, &cache)
-                                      : delta_forward(L, c, nrm.data(), n, start, lp, &cache);
+    run_layer(m, i, x, n, start, angles, lp, &cache);
+    if (layer_trace) layer_trace->insert(layer_trace->end(), x.begin(), x.end());
     if (capture) captured->layers.push_back(std::move(cache));
-    residual_norm(x.data(), mixed.data(), nrm.data(), L.post_norm.data(), h, x.size(), c.eps);
-    std::shared_ptr<QuantizedInputs> shared;
-    bool done = false;
-    std::vector<float> gate(n * c.intermediate);
-    L.gate.apply_into(nrm.data(), n, gate.data(), Epilogue::Write, &shared, &done);
-    L.up.apply_into(nrm.data(), n, gate.data(), Epilogue::SwiGlu, &shared, &done);
-    L.down.apply_into(gate.data(), n, x.data(), Epilogue::Add, nullptr, nullptr);
   }
   rms(x.data(), x.size(), m.norm.data(), h, c.eps, true);
   for (float v : x)

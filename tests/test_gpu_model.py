@@ -274,3 +274,41 @@ def test_logits_batch_equals_one_call_per_question(small, exact):
     assert np.array_equal(got[2][0], m.logits(cont[0], cont[1], past))
     assert np.array_equal(got[4][0], m.logits(qs[0][0], qs[0][1], m.prefill(state[:50])))
     assert len(m.prefill(past_ids)) == len(past) == 77  # the caller's prefix is unchanged by its use
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
+def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact):
+    """Per-layer parity at the 2B layer shapes (hidden 2048, DeltaNet 16 x 128,
+    attention 8 Q / 2 KV x 256, SwiGLU 6144, rank-32 LoRA) over the model's
+    repeating block of 3 DeltaNet + 1 attention layers: each layer gets the
+    oracle's residual input rows of that layer (teacher forcing through
+    dg_debug_layer) and its output is compared with the oracle's next rows.
+    Bar, as for the single-layer models: normwise within max(1e-3, 4 x the
+    oracle's own movement under 1e-7 input noise), median row within 1e-5, at
+    least 75 % of rows within 1e-5."""
+    from decider_gpu import GpuModel
+    c = cfg2_config(4, vocab=1024)
+    t = random_tensors(c, rank=32, pointer_dim=64, seed=3)
+    m = GpuModel(c, "int8-compute", 32, 2.0, 64, 0, 256)
+    m.set_tensors(t)
+    m = m.finalize()
+    assert m.fast_path
+    m.set_exact(exact)
+    o = oracle_mod.OracleModel(c, t, "int8-compute", 32, 2.0)
+    ids = np.random.default_rng(6).integers(0, c["vocab_size"], 160)
+    trace = o.layer_trace(ids)
+    rng = np.random.default_rng(12)
+    for i in range(4):
+        x = trace[i]
+        got = m.layer(i, x)
+        exp = trace[i + 1]
+        moved = o.layer(i, (x * (1 + 1e-7 * rng.standard_normal(x.shape))).astype(np.float32))
+        noise = rel_err(moved, exp)
+        err, rows = rel_err(got, exp), _row_errors(got, exp)
+        print(f"layer {i} ({c['layer_types'][i]}): normwise {err:.3e} (noise floor {noise:.3e}), "
+              f"median row {np.median(rows):.3e}, rows > 1e-5: {(rows > 1e-5).sum()} of {len(rows)}")
+        assert err < max(1e-3, 4 * noise), (i, err, noise)
+        assert np.median(rows) < 1e-5, (i, np.median(rows))
+        assert (rows <= 1e-5).mean() >= 0.75, (i, (rows > 1e-5).sum())
+    with pytest.raises(Exception, match="layer index out of range"):
+        m.layer(4, trace[0])

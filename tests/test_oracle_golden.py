@@ -150,3 +150,20 @@ def test_rejects_out_of_vocabulary_and_overlong_sequences(O, tiny):
         tiny.forward([100])
     with pytest.raises(O.OracleError, match="4096 tokens"):
         tiny.forward([])
+
+
+@pytest.mark.parametrize("precision", ["checkpoint", "int8-compute"])
+def test_layer_trace_and_single_layer_restate_the_forward(O, precision):
+    """The per-layer residual trace that the GPU per-layer parity test feeds
+    in (teacher forcing) is the forward itself: every layer re-run alone on
+    its traced input reproduces the next traced rows bit for bit
+    (src/qwen.rs:470-494), and the trace starts at the embedded ids."""
+    m = O.OracleModel.from_dir(TINY, precision)
+    ids = [(i * 11 + 3) % 32 for i in range(23)]
+    trace = m.layer_trace(ids)
+    assert trace.shape[0] == m.config["num_hidden_layers"] + 1
+    for i in range(trace.shape[0] - 1):
+        assert np.array_equal(m.layer(i, trace[i]), trace[i + 1]), i
+    # Rows with the same id enter the first layer identically.
+    assert np.array_equal(trace[0][0], trace[0][ids.index(ids[0], 1)]) if ids.count(ids[0]) > 1 else True
+    assert np.isfinite(trace).all()
