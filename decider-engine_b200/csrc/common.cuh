@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -56,6 +58,23 @@ struct CudaError : std::runtime_error {
     if (_e != cudaSuccess)                                                              \
       throw ::dg::CudaError(std::string(#expr) + ": " + cudaGetErrorString(_e));        \
   } while (0)
+
+// Runs `configure` once per device for one call site: kernel attributes such
+// as the dynamic shared-memory limit belong to the device's context, so each
+// device a process launches on needs its own call. `done` is the call site's
+// bit set of configured device ordinals (0-63).
+template <class F>
+inline void once_per_device(std::atomic<uint64_t>& done, F&& configure) {
+  int d = 0;
+  DG_CUDA(cudaGetDevice(&d));
+  const uint64_t bit = uint64_t(1) << (d & 63);
+  if (done.load(std::memory_order_acquire) & bit) return;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.load(std::memory_order_relaxed) & bit) return;
+  configure();
+  done.fetch_or(bit, std::memory_order_release);
+}
 
 // Count of kernel launches issued by this library (host side), reported by
 // the C ABI so callers can see that device code ran.

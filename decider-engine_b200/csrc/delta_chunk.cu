@@ -528,14 +528,13 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK + (CK / 16 - 1) * 256) * sizeof(float);
   const int scan_smem = (DK * SC + CK * SC) * sizeof(float) + 2 * sizeof(ScanStage);
   const int out_smem = (CK * OQ_LD + DK * OS_LD + CK * OK_LD + CK * OS_LD) * sizeof(float);
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [&] {
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel<SCAN_NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  scan_smem));
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, out_smem));
-    configured = true;
-  }
+  });
   launch_pdl(delta_chunk_prep_kernel, dim3(int(units)), dim3(256), prep_smem, s, a, outs, chunks);
   DG_CUDA(cudaGetLastError());
   launch_pdl(delta_chunk_scan_kernel<SCAN_NT>, dim3(batch * a.value_heads * (a.dv / SC)), dim3(SCAN_NT), scan_smem,

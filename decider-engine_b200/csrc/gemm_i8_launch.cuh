@@ -21,11 +21,8 @@ template <int BN, int R, int EPI, bool EXACT, bool DUMP>
 void launch_gemm_kernel(const GemmMaps& m, const GemmArgs& args, cudaStream_t s) {
   auto kern = gemm_i8_g64_kernel<BN, R, EPI, EXACT, DUMP>;
   const int smem = GemmShape<BN>::smem_bytes(R);
-  static bool configured = false;  // per instantiation
-  if (!configured) {
-    DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // per instantiation
+  once_per_device(configured, [&] { DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); });
   dim3 grid((args.M + 127) / 128, args.N / BN);
   launch_k(args.late_dep != 0 || pdl_enabled(), kern, dim3(grid), dim3(GemmShape<BN>::NUM_THREADS), smem, s, *m.a,
            *m.b, *m.lb, *m.mid, args);

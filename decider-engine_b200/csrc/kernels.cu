@@ -511,12 +511,11 @@ template <int TM, int RT>
 void launch_lora_splitk(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
                         float* partial, size_t partial_floats, cudaStream_t s) {
   using T = LoraTile<TM, RT>;
-  static bool configured = false;  // per instantiation
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};  // per instantiation
+  once_per_device(configured, [] {
     DG_CUDA(cudaFuncSetAttribute(lora_a_splitk_kernel<TM, RT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  T::SMEM));
-    configured = true;
-  }
+  });
   const int gx = (M + TM - 1) / TM, gy = (R + RT - 1) / RT;
   const int slices = std::max(1, std::min(K / T::KC, (148 + gx * gy - 1) / (gx * gy)));
   const int kslice = ((K + slices - 1) / slices + T::KC - 1) / T::KC * T::KC;

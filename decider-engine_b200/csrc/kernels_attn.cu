@@ -559,22 +559,20 @@ void launch_attention(const float* q, const float* kcache, const float* vcache, 
   const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(kcache) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(vcache) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
   if (d == AD && aligned) {
-    static bool configured = false;
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};
+    once_per_device(configured, [] {
       DG_CUDA(cudaFuncSetAttribute(attention256_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    ATT_SMEM));
-      configured = true;
-    }
+    });
     dim3 grid(2 * ((n + TQ - 1) / TQ), heads);  // clusters of two along x
     launch_pdl(attention256_split_kernel, dim3(grid), dim3(256), ATT_SMEM, s, q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
                                                           kv_heads, out);
   } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
-    static bool configured = false;
-    if (!configured) {
+    static std::atomic<uint64_t> configured{0};
+    once_per_device(configured, [&] {
       DG_CUDA(cudaFuncSetAttribute(attention256_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      configured = true;
-    }
+    });
     dim3 grid((n + ABQ - 1) / ABQ, heads);
     launch_pdl(attention256_kernel, dim3(grid), dim3(128), smem, s, q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out);
   } else {

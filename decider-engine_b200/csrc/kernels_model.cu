@@ -353,12 +353,11 @@ void launch_delta_recurrence(const float* conv, int n, int key_heads, int dk, in
 void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s) {
   if (a.n <= 0 || batch <= 0) return;
   if (a.dv % REC_COLS) throw CudaError("delta_rec128: value width must be a multiple of 16");
-  static bool configured = false;
+  static std::atomic<uint64_t> configured{0};
   const int smem = 2 * sizeof(RecStage);
-  if (!configured) {
+  once_per_device(configured, [&] {
     DG_CUDA(cudaFuncSetAttribute(delta_rec128_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    configured = true;
-  }
+  });
   dim3 grid(a.value_heads * (a.dv / REC_COLS), batch);
   launch_pdl(delta_rec128_kernel, dim3(grid), dim3(128), smem, s, a);
   DG_CUDA(cudaGetLastError());

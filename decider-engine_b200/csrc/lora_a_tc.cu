@@ -167,12 +167,11 @@ bool lora_a_tc_supported(const float* x, int ldx, int K, const float* A, int R, 
 
 void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int R, float* mid, int ldm,
                       float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s, bool overlap) {
-  static bool configured = false;
-  if (!configured) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
     DG_CUDA(cudaFuncSetAttribute(lora_a_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  lora_tc_smem_bytes(128)));
-    configured = true;
-  }
+  });
   const int NP = (R + 15) / 16 * 16;
   const int mt = (M + 127) / 128;
   // The grid fills the GPU. With `overlap` the kernels are launched as
