@@ -42,7 +42,13 @@ def test_plan_meets_the_lpt_bound():
 def test_cost_grows_with_the_window():
     short = RequestShape(prefix=64, questions=(64,))
     long = RequestShape(prefix=4032, questions=(64,))
-    assert request_cost(long) > request_cost(short) * 40
+    assert request_cost(long) > request_cost(short) * 10
+    # Each forward carries a fixed cost: four questions on a state cost more
+    # than one question over the same window.
+    many = RequestShape(prefix=1024, questions=(64, 64, 64, 64))
+    one = RequestShape(prefix=1024 + 192, questions=(64,))
+    assert many.forwards == 5 and one.forwards == 2
+    assert request_cost(many) > request_cost(one) + 3 * 250
 
 
 def _fake_engine(request):
