@@ -184,6 +184,7 @@ class Engine {
   std::vector<DevBuf> kcache_, vcache_, state_;
   DevBuf delta_ws_;  // chunked DeltaNet products (fast mode)
   DevBuf lora_part_; // split-K LoRA-A partial sums (fast mode)
+  DevBuf gemm_split_ws_, gemm_split_cnt_;  // split-K projection partials and tile counters (fast mode)
   DevBuf status_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;
   DeviceStatus* status() const { return status_.as<DeviceStatus>(); }

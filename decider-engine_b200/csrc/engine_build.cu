@@ -241,6 +241,11 @@ void Engine::finalize() {
   if (c.dk == 128 && c.dv == 128)
     delta_ws_ = DevBuf(delta_chunk_workspace_bytes(1, c.value_heads, M));
   if (fast_) lora_part_ = DevBuf(lora_a_partial_floats(M) * 4);
+  if (fast_) {
+    gemm_split_ws_ = DevBuf(kGemmSplitFloats * 4);
+    gemm_split_cnt_ = DevBuf(kGemmSplitTiles * sizeof(int));
+    DG_CUDA(cudaMemset(gemm_split_cnt_.ptr, 0, gemm_split_cnt_.bytes));
+  }
   constexpr int kMaxHeadRows = 512;
   hrow_idx_ = DevBuf(kMaxHeadRows * 4);
   hnorm_ = DevBuf(size_t(kMaxHeadRows) * H * 4);

@@ -43,6 +43,9 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
   a.status = status();
   // Every fast projection directly follows its own LoRA-A launch.
   a.late_dep = lora_overlap_ ? 1 : 0;
+  a.split_ws = gemm_split_ws_.as<float>();
+  a.split_cnt = gemm_split_cnt_.as<int>();
+  a.split_ws_floats = gemm_split_ws_.bytes / 4;
   const size_t k = gemm_ops_pending_.size();
   fwd_ops_all_ += 2.0 * M * p.out * p.in;
   ++fwd_proj_;
@@ -160,7 +163,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
                         rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
                         vcache_[i].as<float>(), stream_);
     launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
-                     c.heads, c.kv_heads, d, att_.as<float>(), stream_);
+                     c.heads, c.kv_heads, d, att_.as<float>(), exact, stream_);
     launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(),
                       xs_.as<float>(), ldxs_, status(), stream_);
     if (cap) {
@@ -212,7 +215,7 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
                         rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
                         vcache_[i].as<float>(), stream_);
     launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
-                     c.heads, c.kv_heads, d, att_.as<float>(), stream_);
+                     c.heads, c.kv_heads, d, att_.as<float>(), true, stream_);
     if (q) {
       launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq, xs_.as<float>(), ldxs_,
                         status(), stream_);

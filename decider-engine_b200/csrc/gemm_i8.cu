@@ -86,6 +86,21 @@ int gemm_i8_choose_bn(int M, int N, int epi) {
   return best;
 }
 
+// Split-K for grids of less than one wave (few token rows): FMA mode only
+// (reference order sums the groups strictly in order), with a workspace, no
+// group-dot dump. The largest split of 2-4 that divides the K stages, keeps
+// at least four stages per split and the grid within one wave of 148 SMs.
+int gemm_i8_choose_splits(const GemmArgs& args, int bn, bool exact) {
+  if (exact || !args.split_ws || !args.split_cnt || args.dots) return 1;
+  const int tiles = ((args.M + 127) / 128) * (args.N / bn), ks = args.K / 128;
+  if (tiles > kGemmSplitTiles) return 1;
+  for (int sp = 4; sp >= 2; --sp)
+    if (ks % sp == 0 && ks / sp >= 4 && tiles * sp <= 148 &&
+        size_t(sp) * size_t(args.M) * size_t(args.N) <= args.split_ws_floats)
+      return sp;
+  return 1;
+}
+
 void launch_gemm_i8(const CUtensorMap& a, const WeightMaps& w, const GemmArgs& args, int rank, int epi,
                     bool exact, cudaStream_t s) {
   if (args.M <= 0) return;
@@ -112,10 +127,12 @@ void launch_gemm_i8(const CUtensorMap& a, const WeightMaps& w, const GemmArgs& a
     mp = &mid;
   }
   const GemmMaps m{&a, bn == 64 ? &w.bn64 : &w.bn128, lb, mp};
+  GemmArgs g = args;
+  g.splits = gemm_i8_choose_splits(g, bn, exact);
   if (bn == 64)
-    launch_gemm_i8_bn64(m, args, rank, epi, exact, s);
+    launch_gemm_i8_bn64(m, g, rank, epi, exact, s);
   else
-    launch_gemm_i8_bn128(m, args, rank, epi, exact, s);
+    launch_gemm_i8_bn128(m, g, rank, epi, exact, s);
 }
 
 }  // namespace dg

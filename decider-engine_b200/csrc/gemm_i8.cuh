@@ -52,6 +52,14 @@ struct GemmArgs {
   // previous kernel only before reading lora_mid and writing out, so the main
   // loop overlaps the LoRA-A pass.
   int late_dep;
+  // Split-K (FMA mode, grid.z > 1 splits of the K stages): each split stores
+  // its raw partial sums in split_ws [split][M][N]; the last split of a tile
+  // to arrive (split_cnt[tile], zero between launches) adds them in split
+  // order and runs the epilogue.
+  float* split_ws;
+  int* split_cnt;
+  size_t split_ws_floats;  // capacity of split_ws
+  int splits;              // set by launch_gemm_i8 (1: no split)
 };
 
 template <int BN_>
@@ -182,7 +190,8 @@ __global__ void __launch_bounds__(576, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
-  const int KS = p.K / BK;
+  const int KS = p.K / BK / int(gridDim.z);  // this split's K stages
+  const int ks0 = int(blockIdx.z) * KS;      // its first stage
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -239,10 +248,10 @@ __global__ void __launch_bounds__(576, 1)
         if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 100 + s, abort_flag)) break;
         uint8_t* st = smem + s * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES + 2 * BN * 4 + 2 * BM * 4);
-        tma_load_2d(st, &map_a, &full[s], ks * BK, m0);
-        tma_load_2d(st + S::A_BYTES, &map_b, &full[s], ks * BK, n0);
+        tma_load_2d(st, &map_a, &full[s], (ks0 + ks) * BK, m0);
+        tma_load_2d(st + S::A_BYTES, &map_b, &full[s], (ks0 + ks) * BK, n0);
         for (int j = 0; j < 2; ++j) {
-          const int g = 2 * ks + j;
+          const int g = 2 * (ks0 + ks) + j;
           bulk_load(st + S::WS_OFF + j * BN * 4, p.ws + size_t(g) * p.N + n0, BN * 4, &full[s]);
           bulk_load(st + S::XS_OFF + j * BM * 4, p.xs + size_t(g) * p.ldxs + m0, BM * 4, &full[s]);
         }
@@ -472,6 +481,49 @@ __global__ void __launch_bounds__(576, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);  // scales and operands of the stage are consumed
     }
+    // ---------------- split-K: the last split of the tile adds the partials
+    bool last = true;
+    if (gridDim.z > 1) {
+      const size_t slab = size_t(p.M) * p.N;
+      volatile int* split_flag = reinterpret_cast<volatile int*>(smem + S::plan_off(R) + 96);
+      if (m < p.M) {
+        float4* d4 = reinterpret_cast<float4*>(p.split_ws + blockIdx.z * slab + size_t(m) * p.N + n0 + half * HALF);
+#pragma unroll
+        for (int j = 0; j < HALF / 4; ++j)
+          d4[j] = make_float4(acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y);
+      }
+      __threadfence();
+      epi_bar_sync();
+      if (threadIdx.x == S::EPI_WARP0 * 32) {
+        int* cnt = p.split_cnt + blockIdx.y * gridDim.x + blockIdx.x;
+        const int is_last = atomicAdd(cnt, 1) == int(gridDim.z) - 1;
+        if (is_last) *cnt = 0;  // ready for the next launch
+        *split_flag = is_last;
+      }
+      epi_bar_sync();
+      last = *split_flag != 0;
+      if (last) {
+        __threadfence();
+        if (m < p.M) {
+#pragma unroll 1
+          for (int z = 0; z < int(gridDim.z); ++z) {
+            const float4* s4 =
+                reinterpret_cast<const float4*>(p.split_ws + z * slab + size_t(m) * p.N + n0 + half * HALF);
+#pragma unroll
+            for (int j = 0; j < HALF / 4; ++j) {
+              const float4 v = __ldcg(s4 + j);
+              if (z == 0) {
+                acc[2 * j] = make_float2(v.x, v.y);
+                acc[2 * j + 1] = make_float2(v.z, v.w);
+              } else {
+                acc[2 * j] = make_float2(__fadd_rn(acc[2 * j].x, v.x), __fadd_rn(acc[2 * j].y, v.y));
+                acc[2 * j + 1] = make_float2(__fadd_rn(acc[2 * j + 1].x, v.z), __fadd_rn(acc[2 * j + 1].y, v.w));
+              }
+            }
+          }
+        }
+      }
+    }
     // ---------------- epilogue
     if (p.late_dep) griddep_wait();  // lora_mid and the output buffer
     const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
@@ -538,8 +590,8 @@ __global__ void __launch_bounds__(576, 1)
       }
     }
     epi_bar_sync();
-    if (*abort_flag) {
-      // nothing is written after a failed wait
+    if (*abort_flag || !last) {
+      // nothing is written after a failed wait, nor by a split that is not the tile's last
     } else if constexpr (R == 0 || TCL) {
       // The staged sums are final: row-contiguous copies, one float4 per
       // thread and step (a warp covers 512 contiguous bytes of output).

@@ -23,7 +23,7 @@ void launch_gemm_kernel(const GemmMaps& m, const GemmArgs& args, cudaStream_t s)
   const int smem = GemmShape<BN>::smem_bytes(R);
   static std::atomic<uint64_t> configured{0};  // per instantiation
   once_per_device(configured, [&] { DG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)); });
-  dim3 grid((args.M + 127) / 128, args.N / BN);
+  dim3 grid((args.M + 127) / 128, args.N / BN, args.splits > 1 ? args.splits : 1);
   launch_k(args.late_dep != 0 || pdl_enabled(), kern, dim3(grid), dim3(GemmShape<BN>::NUM_THREADS), smem, s, *m.a,
            *m.b, *m.lb, *m.mid, args);
   DG_CUDA(cudaGetLastError());

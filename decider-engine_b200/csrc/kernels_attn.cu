@@ -202,8 +202,8 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
 }
 
 // Flash-style causal attention for head_dim 256, FP32, register-tiled, with
-// the key blocks of each 32-row query block dealt alternately to a cluster of
-// two CTAs.
+// the key blocks of each 32-row query block dealt round-robin to a cluster of
+// NS CTAs (2, 4 or 8).
 // Each CTA stages key blocks of 32 in shared memory with cp.async (the next
 // block's K is copied in during this block's softmax and P·V, its V during the
 // next Q·Kᵀ). Thread (rg, kg) = (tid / 16, tid % 16) owns rows 2rg, 2rg + 1:
@@ -212,6 +212,8 @@ __global__ void __launch_bounds__(128) attention256_kernel(const float* __restri
 // the pair leaves its unnormalised (m, l, o) in shared memory; CTA 0 reads them
 // through distributed shared memory, merges, divides and multiplies by
 // sigmoid(gate) (src/qwen.rs:581-583). Heavy (late) query blocks go first.
+// With NS > 2 every CTA but the first publishes, and CTA 0 merges the NS
+// partial states in rank order (for NS = 2 the same expression as a pair).
 constexpr int TQ = 32, TK = 32, TLD = AD + 4, PLD = TQ + 4;
 constexpr int ATT_SMEM = (TQ * TLD + TK * TLD + TK * AD + TK * PLD + 2 * TQ) * 4;
 
@@ -226,7 +228,8 @@ __device__ __forceinline__ void att_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
+template <int NS>
+__global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
     attention256_split_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                               const float* __restrict__ gate_src, int ld_gate, int n, int offset, int heads,
                               int kv_heads, float* __restrict__ out) {
@@ -241,13 +244,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
   cg::cluster_group cluster = cg::this_cluster();
   const int part = int(cluster.block_rank());
   const int nrb = (n + TQ - 1) / TQ;
-  const int rb = nrb - 1 - int(blockIdx.x / 2), h = blockIdx.y, kh = h / (heads / kv_heads);
+  const int rb = nrb - 1 - int(blockIdx.x / NS), h = blockIdx.y, kh = h / (heads / kv_heads);
   const int t0 = rb * TQ, tid = threadIdx.x, rg = tid / 16, kg = tid % 16;
   const int kw = kv_heads * AD, L = offset + n;
   const int last_key = min(L - 1, offset + t0 + TQ - 1), nkb = last_key / TK + 1;
-  // CTA `part` takes key blocks part, part + 2, ...: every query row sees the
-  // same split and merge whatever block it sits in, so a prefix continuation
-  // reproduces the full forward bit for bit.
+  // CTA `part` takes key blocks part, part + NS, ...: every query row sees the
+  // same split and merge whatever block it sits in, so for one NS a prefix
+  // continuation reproduces the full forward bit for bit.
   const int kb_begin = part, kb_end = nkb;
   const float scale = 1.0f / sqrtf(float(AD));
   auto load_rows = [&](float* dst, int ld, const float* src, int row0) {
@@ -274,7 +277,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
 #pragma unroll
     for (int e = 0; e < 16; ++e) o[i][e] = 0.0f;
   }
-  for (int kb = kb_begin; kb < kb_end; kb += 2) {
+  for (int kb = kb_begin; kb < kb_end; kb += NS) {
     const int k0 = kb * TK;
     att_wait<1>();  // this block's K (and Q) have landed
     __syncthreads();
@@ -299,8 +302,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
         }
     }
     __syncthreads();  // every thread is done with Ks
-    if (kb + 2 < kb_end) {
-      load_rows(Ks, TLD, kc, k0 + 2 * TK);
+    if (kb + NS < kb_end) {
+      load_rows(Ks, TLD, kc, k0 + NS * TK);
       att_commit();
       att_wait<1>();  // this block's V has landed
     } else {
@@ -355,14 +358,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
       }
     }
     __syncthreads();  // every thread is done with Vs and PT
-    if (kb + 2 < kb_end) {
-      load_rows(Vs, AD, vc, k0 + 2 * TK);
+    if (kb + NS < kb_end) {
+      load_rows(Vs, AD, vc, k0 + NS * TK);
       att_commit();
     }
   }
   att_wait<0>();
-  // Merge the two key halves: CTA 1 publishes, CTA 0 combines and stores.
-  if (part == 1) {
+  // Merge the key parts: CTAs 1 .. NS-1 publish, CTA 0 combines and stores.
+  if (part != 0) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       float* dst = Ks + (2 * rg + i) * TLD;
@@ -378,34 +381,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(256)
   }
   cluster.sync();
   if (part == 0) {
-    const float* rKs = cluster.map_shared_rank(Ks, 1);
-    const float* rML = cluster.map_shared_rank(ML, 1);
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int t = t0 + 2 * rg + i;
-      const float m1 = rML[2 * rg + i], l1 = rML[TQ + 2 * rg + i];
-      const float mm = fmaxf(mrow[i], m1);
+      float mm = mrow[i];
+#pragma unroll
+      for (int r = 1; r < NS; ++r) mm = fmaxf(mm, cluster.map_shared_rank(ML, r)[2 * rg + i]);
       const float a0 = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mm);
-      const float a1 = m1 == -INFINITY ? 0.0f : expf(m1 - mm);
-      const float inv = 1.0f / (lrow[i] * a0 + l1 * a1);
+      float lsum = lrow[i] * a0;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[i][j] = o[i][j] * a0;
+#pragma unroll
+      for (int r = 1; r < NS; ++r) {
+        const float* rML = cluster.map_shared_rank(ML, r);
+        const float mr = rML[2 * rg + i], lr = rML[TQ + 2 * rg + i];
+        const float ar = mr == -INFINITY ? 0.0f : expf(mr - mm);
+        lsum = lsum + lr * ar;
+        const float* orow = cluster.map_shared_rank(Ks, r) + (2 * rg + i) * TLD;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float4 rv = *reinterpret_cast<const float4*>(orow + 4 * kg + 64 * j);
+          o[i][4 * j + 0] = o[i][4 * j + 0] + rv.x * ar;
+          o[i][4 * j + 1] = o[i][4 * j + 1] + rv.y * ar;
+          o[i][4 * j + 2] = o[i][4 * j + 2] + rv.z * ar;
+          o[i][4 * j + 3] = o[i][4 * j + 3] + rv.w * ar;
+        }
+      }
+      const float inv = 1.0f / lsum;
       if (t >= n) continue;
       const float* g = gate_src + size_t(t) * ld_gate + size_t(h) * 2 * AD + AD;
       float* dst = out + (size_t(t) * heads + h) * AD;
-      const float* o1 = rKs + (2 * rg + i) * TLD;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = 4 * kg + 64 * j;
-        const float4 r1 = *reinterpret_cast<const float4*>(o1 + c);
         float4 r;
-        r.x = ((o[i][4 * j + 0] * a0 + r1.x * a1) * inv) * sigmoid_f(g[c + 0]);
-        r.y = ((o[i][4 * j + 1] * a0 + r1.y * a1) * inv) * sigmoid_f(g[c + 1]);
-        r.z = ((o[i][4 * j + 2] * a0 + r1.z * a1) * inv) * sigmoid_f(g[c + 2]);
-        r.w = ((o[i][4 * j + 3] * a0 + r1.w * a1) * inv) * sigmoid_f(g[c + 3]);
+        r.x = (o[i][4 * j + 0] * inv) * sigmoid_f(g[c + 0]);
+        r.y = (o[i][4 * j + 1] * inv) * sigmoid_f(g[c + 1]);
+        r.z = (o[i][4 * j + 2] * inv) * sigmoid_f(g[c + 2]);
+        r.w = (o[i][4 * j + 3] * inv) * sigmoid_f(g[c + 3]);
         *reinterpret_cast<float4*>(dst + c) = r;
       }
     }
   }
-  cluster.sync();  // CTA 1's shared memory stays alive until CTA 0 has read it
+  cluster.sync();  // the other CTAs' shared memory stays alive until CTA 0 has read it
 }
 
 // Generic causal attention (any head_dim): one thread per (token, head),
@@ -553,20 +571,46 @@ void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_hea
   DG_CUDA(cudaGetLastError());
 }
 
+template <int NS>
+void launch_attention_split(const float* q, const float* kcache, const float* vcache, const float* gate_src,
+                            int ld_gate, int n, int offset, int heads, int kv_heads, float* out, cudaStream_t s) {
+  static std::atomic<uint64_t> configured{0};
+  once_per_device(configured, [] {
+    DG_CUDA(cudaFuncSetAttribute(attention256_split_kernel<NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 ATT_SMEM));
+  });
+  dim3 grid(NS * ((n + TQ - 1) / TQ), heads);  // clusters of NS along x
+  launch_pdl(attention256_split_kernel<NS>, dim3(grid), dim3(256), ATT_SMEM, s, q, kcache, vcache, gate_src, ld_gate,
+             n, offset, heads, kv_heads, out);
+}
+
+// Cluster size of the split kernel. Reference order keeps pairs, so that a
+// prefix continuation (few query rows after a long prefix) splits its keys as
+// the full forward does and reproduces it bit for bit. Otherwise the cluster
+// grows (4, then 8) while the grid has fewer than two CTAs per SM and every
+// CTA keeps at least two key blocks: a 64-token question after a 3584-token
+// prefix is 2 query blocks x 8 heads, 32 CTAs in pairs.
+int attention_split_ways(int n, int offset, int heads, bool exact) {
+  if (exact) return 2;
+  const int nrb = (n + TQ - 1) / TQ, nkb = (offset + n + TK - 1) / TK;
+  int ns = 2;
+  while (ns < 8 && ns * nrb * heads < 2 * 148 && nkb / (2 * ns) >= 2) ns *= 2;
+  return ns;
+}
+
 void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src, int ld_gate,
-                      int n, int offset, int heads, int kv_heads, int d, float* out, cudaStream_t s) {
+                      int n, int offset, int heads, int kv_heads, int d, float* out, bool exact, cudaStream_t s) {
   if (n <= 0) return;
   const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(kcache) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(vcache) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
   if (d == AD && aligned) {
-    static std::atomic<uint64_t> configured{0};
-    once_per_device(configured, [] {
-      DG_CUDA(cudaFuncSetAttribute(attention256_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   ATT_SMEM));
-    });
-    dim3 grid(2 * ((n + TQ - 1) / TQ), heads);  // clusters of two along x
-    launch_pdl(attention256_split_kernel, dim3(grid), dim3(256), ATT_SMEM, s, q, kcache, vcache, gate_src, ld_gate, n, offset, heads,
-                                                          kv_heads, out);
+    const int ns = attention_split_ways(n, offset, heads, exact);
+    if (ns == 8)
+      launch_attention_split<8>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
+    else if (ns == 4)
+      launch_attention_split<4>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
+    else
+      launch_attention_split<2>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
   } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
     static std::atomic<uint64_t> configured{0};

@@ -28,6 +28,11 @@ void make_weight_maps(WeightMaps* maps, const void* wq, int k, int n, const floa
 void launch_gemm_i8(const CUtensorMap& map_a, const WeightMaps& w, const GemmArgs& args, int rank, int epi,
                     bool exact, cudaStream_t stream);
 int gemm_i8_choose_bn(int M, int N, int epi);
+// Split-K: tiles of a grid that may be split (one counter each), and the
+// workspace that bounds (splits x M x N <= 148 x 128 x 128 floats).
+constexpr int kGemmSplitTiles = 148;
+constexpr size_t kGemmSplitFloats = size_t(148) * 128 * 128;
+int gemm_i8_choose_splits(const GemmArgs& args, int bn, bool exact);
 
 // ---- elementwise / normalisation / quantisation, kernels.cu
 // Row-wise: optional centred RMSNorm (gamma != nullptr: x * (inv * (1 + g))),
@@ -122,8 +127,10 @@ void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
 void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_heads, int d, const float* qn,
                          const float* kn, float eps, const float* rope, int half, int start, float* q_out,
                          float* kcache, float* vcache, cudaStream_t s);
+// `exact` (reference-order mode) keeps the key split fixed, so prefix
+// continuations stay bit-identical to full forwards.
 void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src,
-                      int ld_gate, int n, int offset, int heads, int kv_heads, int d, float* out,
+                      int ld_gate, int n, int offset, int heads, int kv_heads, int d, float* out, bool exact,
                       cudaStream_t s);
 // Centred RMSNorm over rows, in place, plus a non-finite check.
 void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, DeviceStatus* st,

@@ -133,9 +133,10 @@ def test_small_model_single_layer_teacher_forced(oracle_mod, lt, exact):
     """One DeltaNet layer and one attention layer as 1-layer models (identical
     inputs on both sides). Rows whose activations sit within FP32 rounding of
     an int8 rounding boundary flip one quantised value (a ~1e-3 row error, the
-    same jump the oracle itself makes under 1e-7 input noise); the bar is that
-    at least 75% of rows agree within 1e-5, the median row within 1e-5, and the
-    whole layer within 1e-3 normwise."""
+    same jump the oracle itself makes under 1e-7 input noise); the bar is the
+    median row within 1e-5 and the whole layer within max(1e-3, 4 x the noise
+    floor) normwise, and in reference order also at least 75% of rows within
+    1e-5 (FMA mode reorders FP32 work, which flips more rows: reported)."""
     c1 = small_config(layer_types=(lt,))
     t1 = random_tensors(c1, rank=32, pointer_dim=64, seed=11)
     m = _gpu_small(c1, t1)
@@ -148,7 +149,8 @@ def test_small_model_single_layer_teacher_forced(oracle_mod, lt, exact):
           f"rows > 1e-5: {(rows > 1e-5).sum()}")
     assert err < max(1e-3, 4 * noise), (lt, err, noise)
     assert np.median(rows) < 1e-5, (lt, np.median(rows))
-    assert (rows <= 1e-5).mean() >= 0.75, (lt, (rows > 1e-5).sum())
+    if exact:
+        assert (rows <= 1e-5).mean() >= 0.75, (lt, (rows > 1e-5).sum())
 
 
 def test_small_model_prefix_continuation_is_bit_exact(small):
@@ -276,8 +278,9 @@ def test_logits_batch_equals_one_call_per_question(small, exact):
     assert len(m.prefill(past_ids)) == len(past) == 77  # the caller's prefix is unchanged by its use
 
 
+@pytest.mark.parametrize("tokens", [160, 64])
 @pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
-def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact):
+def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact, tokens):
     """Per-layer parity at the 2B layer shapes (hidden 2048, DeltaNet 16 x 128,
     attention 8 Q / 2 KV x 256, SwiGLU 6144, rank-32 LoRA) over the model's
     repeating block of 3 DeltaNet + 1 attention layers: each layer gets the
@@ -288,7 +291,9 @@ def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact):
     reference order also at least 75 % of rows within 1e-5. FMA mode reorders
     the FP32 work (chunked delta rule, split-K tensor-core LoRA), a ~1e-6
     perturbation that flips an int8 code in more rows (each flip moves its
-    row by 1e-4 to 1e-3), so there the row count is reported, not gated."""
+    row by 1e-4 to 1e-3), so there the row count is reported, not gated.
+    In FMA mode the narrow projections (out_proj, o_proj, down_proj) split K
+    over 2 (160 tokens) or 4 (64 tokens) CTAs per tile."""
     from decider_gpu import GpuModel
     c = cfg2_config(4, vocab=1024)
     t = random_tensors(c, rank=32, pointer_dim=64, seed=3)
@@ -298,7 +303,7 @@ def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact):
     assert m.fast_path
     m.set_exact(exact)
     o = oracle_mod.OracleModel(c, t, "int8-compute", 32, 2.0)
-    ids = np.random.default_rng(6).integers(0, c["vocab_size"], 160)
+    ids = np.random.default_rng(6).integers(0, c["vocab_size"], tokens)
     trace = o.layer_trace(ids)
     rng = np.random.default_rng(12)
     for i in range(4):
@@ -316,3 +321,27 @@ def test_cfg2_shape_every_layer_teacher_forced(oracle_mod, exact):
             assert (rows <= 1e-5).mean() >= 0.75, (i, (rows > 1e-5).sum())
     with pytest.raises(Exception, match="layer index out of range"):
         m.layer(4, trace[0])
+
+
+@pytest.mark.parametrize("prefix_len", [200, 1000], ids=["4-way", "8-way"])
+def test_fma_mode_key_split_for_short_questions_matches_oracle(oracle_mod, prefix_len):
+    """In FMA mode a short question after a long prefix splits each query
+    block's keys over clusters of 4 or 8 CTAs (merged in rank order through
+    distributed shared memory) instead of pairs. One attention layer: the
+    continuation rows against the oracle's full forward, with the bar of the
+    single-layer test (normwise within max(1e-3, 4 x the oracle's own noise
+    floor), median row within 1e-5), and equal to the same continuation
+    repeated."""
+    c1 = small_config(layer_types=("full_attention",))
+    t1 = random_tensors(c1, rank=32, pointer_dim=64, seed=17)
+    m = _gpu_small(c1, t1)
+    m.set_exact(False)
+    ids = np.random.default_rng(23).integers(0, c1["vocab_size"], prefix_len + 64)
+    exp, noise = _noise_sensitivity(oracle_mod, c1, t1, ids)
+    prefix = m.prefill(ids[:prefix_len])
+    got = m.forward_after(prefix, ids[prefix_len:])
+    err, rows = rel_err(got, exp[prefix_len:]), _row_errors(got, exp[prefix_len:])
+    print(f"prefix {prefix_len}: normwise {err:.3e} (noise floor {noise:.3e}), median row {np.median(rows):.3e}")
+    assert err < max(1e-3, 4 * noise), (err, noise)
+    assert np.median(rows) < 1e-5, np.median(rows)
+    assert np.array_equal(m.forward_after(prefix, ids[prefix_len:]), got)
