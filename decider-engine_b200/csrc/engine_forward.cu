@@ -94,10 +94,12 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
     DG_CUDA(cudaMemcpyAsync(state_[i].ptr, past->state.ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
   else
     DG_CUDA(cudaMemsetAsync(state_[i].ptr, 0, sbytes, stream_));
-  if (!exact && delta_ws_.ptr) {
+  if (!exact && delta_ws_.ptr && n > kDeltaChunk) {
     // Fast mode: the chunked form (64-token chunks); its rounding depends on
     // where chunks start, so prefix continuations match full passes to FP32
-    // rounding rather than bit for bit. Exact mode keeps the token recurrence.
+    // rounding rather than bit for bit. Exact mode keeps the token recurrence,
+    // and so does a pass of one chunk or less (a question after a state),
+    // where the chunked form's prep runs one CTA per head.
     DeltaArgs da{};
     da.q = conv_.as<float>();
     da.k = conv_.as<float>() + c.kd();

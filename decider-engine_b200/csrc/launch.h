@@ -120,6 +120,7 @@ void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s);
 // Chunked form (64-token chunks, dk = dv = 128) of the same rule; needs a
 // device workspace of delta_chunk_workspace_bytes(batch, heads, n).
 size_t delta_chunk_workspace_bytes(int batch, int heads, int n);
+constexpr int kDeltaChunk = 64;  // tokens per chunk of the chunked form
 void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s);
 void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
 // Split q|gate per head, centred RMSNorm of q and k, partial RoPE from the
