@@ -471,8 +471,9 @@ __global__ void __launch_bounds__(256) lora_a_splitk_kernel(const float* __restr
   }
 }
 
-// One output per thread; slice z goes to chain z % 4 and the chains are added
-// as (c0 + c1) + (c2 + c3): a fixed order, so the result is deterministic.
+// Sums the split-K slices partial[z][M][R] into mid (row stride ldm): slice
+// z goes to chain z % 8 and the chains are added pairwise in a fixed order,
+// so the result is deterministic.
 __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restrict__ partial, int slices, int M,
                                                             int R, float* __restrict__ mid, int ldm) {
   // Trigger first: a projection launched as this kernel's dependent may start
@@ -480,19 +481,36 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
   // before reading mid). This kernel itself waits before touching memory.
   griddep_launch();
   griddep_wait();
+  // One thread per four outputs; eight slices in flight per round, added in
+  // a fixed order (deterministic).
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= M * R) return;
-  const size_t stride = size_t(M) * R;
-  float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  int z = 0;
-  for (; z + 4 <= slices; z += 4) {
+  const int n4 = M * R / 4;
+  if (i >= n4) return;
+  const float4* p4 = reinterpret_cast<const float4*>(partial);
+  float4 c[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) c[j] += __ldg(partial + size_t(z + j) * stride + i);
+  for (int j = 0; j < 8; ++j) c[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  auto add = [](float4& a, const float4 b) { a = make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); };
+  int z = 0;
+  for (; z + 8 <= slices; z += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __ldg(p4 + size_t(z + j) * n4 + i);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) add(c[j], v[j]);
   }
 #pragma unroll
-  for (int j = 0; j < 3; ++j)
-    if (z + j < slices) c[j] += __ldg(partial + size_t(z + j) * stride + i);
-  mid[size_t(i / R) * ldm + i % R] = (c[0] + c[1]) + (c[2] + c[3]);
+  for (int j = 0; j < 7; ++j)
+    if (z + j < slices) add(c[j], __ldg(p4 + size_t(z + j) * n4 + i));
+  add(c[0], c[1]);
+  add(c[2], c[3]);
+  add(c[4], c[5]);
+  add(c[6], c[7]);
+  add(c[0], c[2]);
+  add(c[4], c[6]);
+  add(c[0], c[4]);
+  const int e = 4 * i;
+  *reinterpret_cast<float4*>(mid + size_t(e / R) * ldm + e % R) = c[0];
 }
 
 
@@ -500,8 +518,10 @@ __global__ void __launch_bounds__(128) lora_a_reduce_kernel(const float* __restr
 
 void launch_lora_a_reduce(const float* partial, int slices, int M, int R, float* mid, int ldm, cudaStream_t s,
                           bool pdl) {
-  launch_k(pdl || pdl_enabled(), lora_a_reduce_kernel, dim3((M * R + 127) / 128), dim3(128), 0, s, partial, slices, M,
-           R, mid, ldm);
+  if (R % 4 || ldm % 4 || reinterpret_cast<uintptr_t>(mid) % 16 || reinterpret_cast<uintptr_t>(partial) % 16)
+    throw CudaError("lora_a_reduce: rank, row stride and buffers must be 16-byte aligned");
+  launch_k(pdl || pdl_enabled(), lora_a_reduce_kernel, dim3((M * R / 4 + 127) / 128), dim3(128), 0, s, partial, slices,
+           M, R, mid, ldm);
   DG_CUDA(cudaGetLastError());
 }
 
