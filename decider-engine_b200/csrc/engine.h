@@ -37,11 +37,21 @@ struct Config {
 struct DevBuf {
   void* ptr = nullptr;
   size_t bytes = 0;
+  bool pooled = false;  // from the device's stream-ordered pool (cudaMallocAsync)
+  int device = -1;      // the pool's device (pooled buffers)
   DevBuf() = default;
   explicit DevBuf(size_t n);
+  // Stream-ordered allocation from the device's default memory pool, for
+  // buffers made and dropped per request (prefix caches): no device-wide
+  // synchronisation on free, and the pool keeps released memory for reuse.
+  static DevBuf pooled_on(size_t n, cudaStream_t s);
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
-  DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes) { o.ptr = nullptr; o.bytes = 0; }
+  DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes), pooled(o.pooled), device(o.device) {
+    o.ptr = nullptr;
+    o.bytes = 0;
+    o.pooled = false;
+  }
   DevBuf& operator=(DevBuf&& o) noexcept;
   ~DevBuf();
   template <class T> T* as() const { return static_cast<T*>(ptr); }

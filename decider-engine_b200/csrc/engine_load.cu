@@ -16,19 +16,43 @@ namespace dg {
 DevBuf::DevBuf(size_t n) : bytes(n) {
   if (n) DG_CUDA(cudaMalloc(&ptr, n));
 }
+DevBuf DevBuf::pooled_on(size_t n, cudaStream_t s) {
+  DevBuf b;
+  b.bytes = n;
+  b.pooled = true;
+  DG_CUDA(cudaGetDevice(&b.device));
+  if (n) DG_CUDA(cudaMallocAsync(&b.ptr, n, s));
+  return b;
+}
+// A pooled buffer goes back on the legacy stream: every use of a prefix
+// buffer is a forward on the engine stream that the host has synchronised
+// before returning, so nothing is in flight when it is released.
+static void release(void* p, bool pooled, int device) {
+  if (!p) return;
+  if (!pooled) {
+    cudaFree(p);
+    return;
+  }
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != device) cudaSetDevice(device);
+  cudaFreeAsync(p, 0);  // the legacy stream of the pool's device
+  if (cur != device && cur >= 0) cudaSetDevice(cur);
+}
 DevBuf& DevBuf::operator=(DevBuf&& o) noexcept {
   if (this != &o) {
-    if (ptr) cudaFree(ptr);
+    release(ptr, pooled, device);
     ptr = o.ptr;
     bytes = o.bytes;
+    pooled = o.pooled;
+    device = o.device;
     o.ptr = nullptr;
     o.bytes = 0;
+    o.pooled = false;
   }
   return *this;
 }
-DevBuf::~DevBuf() {
-  if (ptr) cudaFree(ptr);
-}
+DevBuf::~DevBuf() { release(ptr, pooled, device); }
 
 static void host_parallel(size_t n, const std::function<void(size_t, size_t)>& f) {
   size_t t = std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), 32);
@@ -104,6 +128,15 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   DG_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
   if (major != 10) throw std::runtime_error("decider GPU kernels need an sm_100 (B200) device");
   DG_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+  {
+    // Prefix caches come from the device's default stream-ordered pool; keep
+    // up to 4 GiB of released blocks for the next requests instead of
+    // returning them to the driver at every synchronisation.
+    cudaMemPool_t pool = nullptr;
+    DG_CUDA(cudaDeviceGetDefaultMemPool(&pool, device_));
+    uint64_t keep = uint64_t(4) << 30;
+    DG_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  }
   DG_CUDA(cudaEventCreate(&ev0_));
   DG_CUDA(cudaEventCreate(&ev1_));
   // DG_CUDA_GRAPHS=0 launches every forward kernel by kernel (A/B timing).
