@@ -12,9 +12,9 @@ e2e    : the same through the public C ABI call (dg_logits: host ids in,
 roofline: the dominant kernel, the tcgen05 INT8 projection: every one of its
          launches in the timed steps is bracketed by CUDA events on the engine
          stream; achieved = sum of 2*M*N*K over the launches / their summed time;
-cpu_baseline: the oracle (C++ restatement of the reference CPU path) on one
-         4-layer block of the same model over a token sample, extrapolated to
-         24 layers.
+cpu_baseline: the oracle (C++ restatement of the reference CPU path, -O3)
+         running the whole 24-layer forward over a short prompt (--cpu-tokens)
+         on every host thread, the same step the reference arm times.
 
 Multi-GPU (torchrun): every rank owns a replica and its own request (weak
 scaling, no collective on the data path); time = max over ranks.
@@ -140,28 +140,39 @@ def barrier(dist, device):
     torch.cuda.synchronize(device)
 
 
-class CpuSample:
-    """The oracle on one 4-layer block (3 DeltaNet + 1 attention) of the 2B
-    model: `time(tokens)` returns seconds for the full 24-layer forward of
-    that many tokens (6 blocks)."""
+class CpuForward:
+    """The oracle (oracle/: the reference's CPU algorithm restated in C++,
+    built -O3 like the reference's release profile) on the full 2B model:
+    `time()` returns the seconds of one whole 24-layer int8-compute forward
+    over `tokens` ids plus the pointer-head readout of one noul question, with
+    every host thread. A 512-token step takes minutes on a CPU, so the CPU
+    timings run the same model over a shorter prompt. Only `tokens` embedding
+    rows are gathered, so a 4096-row table stands in for the 248320-row one."""
 
-    def __init__(self, threads=None):
+    def __init__(self, tokens, layers=24, threads=None):
         from model_util import random_tensors
         from oracle import oracle as O
         O.build()
         self.threads = threads or os.cpu_count()
         O.set_threads(self.threads)
-        c = cfg2(4)
-        c["vocab_size"] = 1024  # embedding rows are gathered, not computed
-        t = random_tensors(c, rank=32, pointer_dim=0, seed=0, std=0.02, norm_jitter=0.0)
+        c = cfg2(layers)
+        c["vocab_size"] = 4096
+        t = random_tensors(c, rank=32, pointer_dim=256, seed=0, std=0.02, norm_jitter=0.0, bias_std=0.0, f32=True)
         self.model = O.OracleModel(c, t, "int8-compute", 32, 2.0)
-        self.ids = np.random.default_rng(0).integers(0, 1024, 4096)
-        self.model.forward(self.ids[:8])
+        del t
+        self.tokens = tokens
+        self.ids = np.random.default_rng(0).integers(0, 4096, tokens)
+        self.pos = [tokens - 3, tokens - 2]
 
-    def time(self, tokens):
+    def time(self):
         t0 = time.perf_counter()
-        self.model.forward(self.ids[:tokens])
-        return (time.perf_counter() - t0) * 6.0
+        hidden = self.model.forward(self.ids)
+        self.model.head_logits(hidden, self.pos)
+        return time.perf_counter() - t0
+
+    def describe(self):
+        return (f"oracle port (-O3, {self.threads} threads): the whole 24-layer 2B int8-compute forward over "
+                f"{self.tokens} tokens + pointer head per step (measured, not extrapolated)")
 
 
 def workload_config(args, world):
@@ -173,29 +184,49 @@ def workload_config(args, world):
 
 
 def run_reference(args, world, rank, local, dist):
+    """The reference arm: the reference's CPU algorithm (the oracle port) on
+    rank 0's host cores, each step one whole 24-layer forward over the first
+    --cpu-tokens tokens (a bounded sample: the 512-token step takes minutes
+    on a CPU). ms_per_step is the measured step; config.tokens_per_step says
+    what ran."""
     if rank != 0:
         return
-    tokens = args.cpu_tokens
-    cs = CpuSample()
+    cf = CpuForward(args.cpu_tokens)
     times = []
     for i in range(args.warmup + args.steps):
-        s = cs.time(tokens)
+        s = cf.time()
         if i >= args.warmup:
             times.append(s)
     sec = sum(times) / len(times)
-    value = tokens / sec
-    sample = f"oracle port, one 4-layer block x {tokens} tokens per step, x6 for 24 layers"
+    value = cf.tokens / sec
+    config = dict(workload_config(args, world), tokens_per_step=cf.tokens,
+                  workload=f"cfg2 sample: 2B decider forward (24 layers, LoRA r32) over the first {cf.tokens} "
+                           "tokens of a prompt + pointer head, int8-compute")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000 * TOKENS / tokens,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1000,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8-compute (i8 x i8 -> i32 groups, f32 promotion)", "data": "synthetic",
-        "config": workload_config(args, world),
+        "config": config,
+        "extrapolated": {"ms_per_512_token_step": sec * 1000 * TOKENS / cf.tokens,
+                         "how": "linear in tokens from the measured step; drops attention's quadratic term, "
+                                "which favours the CPU"},
         "note": "the reference's CPU algorithm (oracle restatement) on rank 0's host cores; the Rust crate "
                 "cannot be built here",
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cs.threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cf.threads, "kind": "port",
+                         "sample": cf.describe()},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def _cpu_forward_baseline(args, note=""):
+    """cpu_baseline of the GPU arms: the reference arm's step (CpuForward), one
+    warm-up and two timed runs."""
+    cf = CpuForward(args.cpu_tokens)
+    cf.time()
+    sec = (cf.time() + cf.time()) / 2
+    return {"value": cf.tokens / sec, "unit": "tok/s", "cores": cf.threads, "kind": "port",
+            "sample": cf.describe() + note}
 
 
 def run_ours(args, world, rank, local, dist):
@@ -290,12 +321,10 @@ def run_ours(args, world, rank, local, dist):
     achieved = g_ops / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
     if rank != 0:
         return
+    i8_loop, i8_loop_ms = decider_gpu.measure_i8_peak(local)
     cpu = None
     if world == 1 and not args.no_cpu:
-        cs = CpuSample()
-        sec = cs.time(args.cpu_tokens)
-        cpu = {"value": args.cpu_tokens / sec, "unit": "tok/s", "cores": cs.threads, "kind": "port",
-               "sample": f"oracle port, one 4-layer block of the 2B model x {args.cpu_tokens} tokens, x6 for 24 layers"}
+        cpu = _cpu_forward_baseline(args)
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms, "higher_is_better": True, "scaling": "weak",
@@ -310,7 +339,11 @@ def run_ours(args, world, rank, local, dist):
                                "every timed step (achieved = sum 2*M*N*K / sum event time)",
                      "launches": int(g_n), "launches_per_step": int(a_n) // max(args.steps, 1),
                      "ms_per_launch": gemm_ms_per_launch, "share_of_step": gemm_share,
-                     "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
+                     "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16",
+                     "i8_loop_peak": i8_loop, "frac_of_i8_loop": achieved / i8_loop if i8_loop else None,
+                     "i8_loop": "dg_measure_i8_peak: one CTA per SM issuing back-to-back tcgen05.mma.kind::i8 "
+                                f"128x256x32 from shared memory ({i8_loop_ms:.1f} ms launch), measured after "
+                                "the timed region"},
         "latency": {"p50_ms": p50, "p99_ms": p99, "calls": len(lat),
                     "what": "wall time of one warm dg_logits call per request (512 ids in, 2 logits out), "
                             "max over ranks"},
@@ -708,13 +741,8 @@ def run_batch(args, world, rank, local, dist, which):
                  gpu_launches=int(launches), clocks=clocks.summary(), scaling=scaling)
     line["config"]["tokens_rank0"] = tokens_mine
     if world == 1 and not args.no_cpu:
-        cs = CpuSample()
-        sec = cs.time(args.cpu_tokens)
-        line["cpu_baseline"] = {"value": args.cpu_tokens / sec, "unit": "tok/s", "cores": cs.threads,
-                                "kind": "port",
-                                "sample": f"oracle port, one 4-layer block of the 2B model x {args.cpu_tokens} "
-                                          "tokens from an empty cache, x6 for 24 layers (short context: "
-                                          "favours the CPU)"}
+        line["cpu_baseline"] = _cpu_forward_baseline(args, note=" (from an empty cache: a short context, which "
+                                                                "favours the CPU)")
     print(json.dumps(line), flush=True)
 
 
@@ -724,6 +752,7 @@ def run_reference_workload(args, world, rank, which):
     if rank != 0:
         return
     vals = []
+    cf = None
     for i in range(args.warmup + args.steps):
         if which == "cfg1":
             v, u, c, smp = _cpu_cfg1()
@@ -734,9 +763,10 @@ def run_reference_workload(args, world, rank, which):
             config = _cfg3_config(world)
             metric = "DeltaNet scan tok/s (cfg3: 64 x 4096 tokens x 16 heads)"
         else:
-            cs = CpuSample()
-            v, u, c = args.cpu_tokens / cs.time(args.cpu_tokens), "tok/s", cs.threads
-            smp = f"oracle port, one 4-layer block x {args.cpu_tokens} tokens, x6 for 24 layers"
+            if cf is None:
+                cf = CpuForward(args.cpu_tokens)
+            v, u, c = cf.tokens / cf.time(), "tok/s", cf.threads
+            smp = cf.describe()
             config = {"workload": which}
             metric = f"prefill tok/s at 2B INT8 ({which})"
         if i >= args.warmup:
@@ -759,7 +789,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--latency-calls", type=int, default=100, help="warm dg_logits calls timed for p50/p99")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=256)
+    ap.add_argument("--cpu-tokens", type=int, default=32,
+                    help="tokens of the CPU forward per step (cpu_baseline and the reference arm)")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--exact", action="store_true",
                     help="reference-order FP32 promotion instead of fused multiply-add")

@@ -351,6 +351,21 @@ int dg_debug_layer(dg_engine* e, int layer, const float* x_in, size_t n, float* 
   });
 }
 
+int dg_measure_i8_peak(int device, int iters, double* tops_out, float* ms_out) {
+  return guarded([&] {
+    if (!tops_out) throw std::runtime_error("null argument");
+    *tops_out = dg::measure_i8_peak(device, iters, ms_out);
+  });
+}
+
+int dg_debug_layer_codes(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out, int8_t* codes_out) {
+  return guarded([&] {
+    check_engine(e);
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->debug_layer_codes(layer, x_in, int(std::min<size_t>(n, 1u << 30)), x_out, codes_out);
+  });
+}
+
 int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
                     float* request_ms) {
   const int rc = guarded([&] {

@@ -41,10 +41,10 @@ struct DevBuf {
   int device = -1;      // the pool's device (pooled buffers)
   DevBuf() = default;
   explicit DevBuf(size_t n);
-  // Stream-ordered allocation from the device's default memory pool, for
-  // buffers made and dropped per request (prefix caches): no device-wide
+  // Stream-ordered allocation from a memory pool (the engine's prefix pool),
+  // for buffers made and dropped per request (prefix caches): no device-wide
   // synchronisation on free, and the pool keeps released memory for reuse.
-  static DevBuf pooled_on(size_t n, cudaStream_t s);
+  static DevBuf pooled_on(size_t n, cudaStream_t s, cudaMemPool_t pool);
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
   DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes), pooled(o.pooled), device(o.device) {
@@ -122,6 +122,11 @@ class Engine {
   // One decoder layer, teacher-forced: residual rows x_in [n][hidden] (host)
   // at positions 0..n-1 with no prefix -> the layer's output rows (host).
   void debug_layer(int layer, const float* x_in, int n, float* x_out);
+  // debug_layer, also copying the int8 codes of the layer's four quantised
+  // projection inputs to codes (host, n * (hidden + mixer width + hidden +
+  // intermediate) bytes: input norm, mixer output, post norm, SwiGLU rows).
+  // int8-compute on the tcgen05 path only.
+  void debug_layer_codes(int layer, const float* x_in, int n, float* x_out, int8_t* codes);
   const Config& config() const { return c_; }
   bool fast_path() const { return fast_; }
   int device() const { return device_; }
@@ -155,6 +160,11 @@ class Engine {
   void mixer_tail(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap,
                   const float* raw, int ldr);
   void check_status();
+  // Debug copy of the quantised activations (xq_) after each quantisation of
+  // a debug_layer_codes call; a no-op otherwise.
+  int8_t* dbg_codes_ = nullptr;
+  size_t dbg_off_ = 0;
+  void dump_codes(int n, int K);
   void run_layers(int n, int start, const Prefix* past, Prefix* cap);
   // The kernels of a forward without a prefix (no past, no capture) as one
   // CUDA graph per token count and timing mode: the first such forward runs
@@ -180,6 +190,7 @@ class Engine {
   int precision_, device_, max_tokens_;
   bool fast_ = false, finalized_ = false;
   cudaStream_t stream_ = nullptr;
+  cudaMemPool_t prefix_pool_ = nullptr;  // prefix caches (pooled DevBufs)
   std::map<std::string, HostTensor> staged_;
   std::vector<Layer> layers_;
   DevBuf embedding_, final_norm_, rope_;

@@ -126,11 +126,11 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
                           xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);
   if (cap) {
     cap->full = false;
-    cap->state = DevBuf::pooled_on(sbytes, stream_);
+    cap->state = DevBuf::pooled_on(sbytes, stream_, prefix_pool_);
     DG_CUDA(cudaMemcpyAsync(cap->state.ptr, state_[i].ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
     const int keep = std::min(start + n, k - 1), from_tail = std::max(0, keep - n), from_raw = keep - from_tail;
     cap->tail_rows = keep;
-    cap->tail = DevBuf::pooled_on(size_t(std::max(keep, 1)) * W * 4, stream_);
+    cap->tail = DevBuf::pooled_on(size_t(std::max(keep, 1)) * W * 4, stream_, prefix_pool_);
     if (from_tail)
       DG_CUDA(cudaMemcpyAsync(cap->tail.ptr, tail + size_t(tail_rows - from_tail) * W, size_t(from_tail) * W * 4,
                               cudaMemcpyDeviceToDevice, stream_));
@@ -151,6 +151,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   float* proj = proj_.as<float>();
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
+  dump_codes(n, H);
   launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
   const float* mixed_in;
@@ -168,10 +169,11 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
                      c.heads, c.kv_heads, d, att_.as<float>(), exact, stream_);
     launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(),
                       xs_.as<float>(), ldxs_, status(), stream_);
+    dump_codes(n, c.qw());
     if (cap) {
       cap->full = true;
-      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
-      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
+      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
+      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
       DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
       DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
     }
@@ -179,6 +181,7 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     kin = c.qw();
   } else {
     mixer_tail(i, n, start, past, cap, proj, ld_proj_);
+    dump_codes(n, c.vd());
     mixed_in = ofin_.as<float>();
     kin = c.vd();
   }
@@ -186,10 +189,12 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
+  dump_codes(n, H);
   launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
   launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
+  dump_codes(n, I);
   launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
   run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
 }
@@ -224,8 +229,8 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
     }
     if (cap) {
       cap->full = true;
-      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
-      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
+      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
+      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
       DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
       DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
     }
@@ -299,6 +304,26 @@ void Engine::debug_layer(int layer, const float* x_in, int n, float* x_out) {
   DG_CUDA(cudaEventElapsedTime(&last_forward_ms, ev0_, ev1_));
   collect_gemm_timing();
   last_launches = int(launch_count() - launches0);
+}
+
+void Engine::dump_codes(int n, int K) {
+  if (!dbg_codes_) return;
+  DG_CUDA(cudaMemcpyAsync(dbg_codes_ + dbg_off_, xq_.ptr, size_t(n) * K, cudaMemcpyDeviceToHost, stream_));
+  dbg_off_ += size_t(n) * K;
+}
+
+void Engine::debug_layer_codes(int layer, const float* x_in, int n, float* x_out, int8_t* codes) {
+  if (!fast_) throw DgError("quantised codes are recorded on the int8-compute tcgen05 path only");
+  if (!codes) throw DgError("null argument");
+  dbg_codes_ = codes;
+  dbg_off_ = 0;
+  try {
+    debug_layer(layer, x_in, n, x_out);
+  } catch (...) {
+    dbg_codes_ = nullptr;
+    throw;
+  }
+  dbg_codes_ = nullptr;
 }
 
 void Engine::drop_graphs() {

@@ -16,12 +16,12 @@ namespace dg {
 DevBuf::DevBuf(size_t n) : bytes(n) {
   if (n) DG_CUDA(cudaMalloc(&ptr, n));
 }
-DevBuf DevBuf::pooled_on(size_t n, cudaStream_t s) {
+DevBuf DevBuf::pooled_on(size_t n, cudaStream_t s, cudaMemPool_t pool) {
   DevBuf b;
   b.bytes = n;
   b.pooled = true;
   DG_CUDA(cudaGetDevice(&b.device));
-  if (n) DG_CUDA(cudaMallocAsync(&b.ptr, n, s));
+  if (n) DG_CUDA(cudaMallocFromPoolAsync(&b.ptr, n, pool, s));
   return b;
 }
 // A pooled buffer goes back on the legacy stream: every use of a prefix
@@ -129,13 +129,19 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   if (major != 10) throw std::runtime_error("decider GPU kernels need an sm_100 (B200) device");
   DG_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
   {
-    // Prefix caches come from the device's default stream-ordered pool; keep
-    // up to 4 GiB of released blocks for the next requests instead of
-    // returning them to the driver at every synchronisation.
-    cudaMemPool_t pool = nullptr;
-    DG_CUDA(cudaDeviceGetDefaultMemPool(&pool, device_));
+    // Prefix caches come from this engine's own stream-ordered pool (not the
+    // device's default pool, whose settings other code in the process shares),
+    // which keeps up to 4 GiB of released blocks for the next requests instead
+    // of returning them to the driver at every synchronisation. The engine
+    // trims and destroys it when it is freed.
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = device_;
+    DG_CUDA(cudaMemPoolCreate(&prefix_pool_, &props));
     uint64_t keep = uint64_t(4) << 30;
-    DG_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+    DG_CUDA(cudaMemPoolSetAttribute(prefix_pool_, cudaMemPoolAttrReleaseThreshold, &keep));
   }
   DG_CUDA(cudaEventCreate(&ev0_));
   DG_CUDA(cudaEventCreate(&ev1_));
@@ -154,6 +160,14 @@ Engine::~Engine() {
   if (ev0_) cudaEventDestroy(ev0_);
   if (ev1_) cudaEventDestroy(ev1_);
   for (cudaEvent_t ev : gemm_ev_) cudaEventDestroy(ev);
+  if (prefix_pool_) {
+    // Released blocks go back to the driver now; prefixes that outlive the
+    // engine keep their memory, and the pool itself goes with the last of them.
+    cudaSetDevice(device_);
+    cudaDeviceSynchronize();
+    cudaMemPoolTrimTo(prefix_pool_, 0);
+    cudaMemPoolDestroy(prefix_pool_);
+  }
 }
 
 // Timing covers up to 128 projection launches per forward (24 layers use 96).

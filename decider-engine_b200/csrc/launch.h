@@ -34,6 +34,11 @@ constexpr int kGemmSplitTiles = 148;
 constexpr size_t kGemmSplitFloats = size_t(148) * 128 * 128;
 int gemm_i8_choose_splits(const GemmArgs& args, int bn, bool exact);
 
+// ---- dense tcgen05 kind::i8 throughput of `device` (tc_peak.cu): TOP/s of
+// `iters` x 4 MMAs of 128 x 256 x 32 per SM, one CTA per SM; ms_out gets the
+// timed launch's duration.
+double measure_i8_peak(int device, int iters, float* ms_out);
+
 // ---- elementwise / normalisation / quantisation, kernels.cu
 // Row-wise: optional centred RMSNorm (gamma != nullptr: x * (inv * (1 + g))),
 // optional FP32 output, optional group-64 quantisation into xq [M][K] and

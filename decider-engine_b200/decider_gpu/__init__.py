@@ -5,10 +5,10 @@ this package is the host-side mirror of the reference's model seam and API.
 """
 from ._lib import LIB_PATH, SYMBOLS, GpuError, launch_count, load
 from .engine import (GpuModel, GpuPrefix, Linear, gated_delta_chunk_workspace_bytes, gated_delta_rule,
-                     gated_delta_rule_chunked, read_safetensors)
+                     gated_delta_rule_chunked, measure_i8_peak, read_safetensors)
 from .host import (DecideError, Encoding, ErrorKind, InferenceLimits, NativeEngine, Precision, answer,
                    choice_confidence, score_confidence, softmax)
 
 __all__ = ["LIB_PATH", "SYMBOLS", "GpuError", "launch_count", "load", "GpuModel", "GpuPrefix", "Linear",
-           "gated_delta_rule", "gated_delta_rule_chunked", "gated_delta_chunk_workspace_bytes", "read_safetensors", "DecideError", "Encoding", "ErrorKind", "InferenceLimits",
+           "gated_delta_rule", "gated_delta_rule_chunked", "gated_delta_chunk_workspace_bytes", "measure_i8_peak", "read_safetensors", "DecideError", "Encoding", "ErrorKind", "InferenceLimits",
            "NativeEngine", "Precision", "answer", "choice_confidence", "score_confidence", "softmax"]

@@ -18,9 +18,9 @@ SYMBOLS = [
     "dg_engine_load", "dg_read_checkpoint_config",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
-    "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all",
+    "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all", "dg_measure_i8_peak",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
-    "dg_logits_batch", "dg_debug_layer",
+    "dg_logits_batch", "dg_debug_layer", "dg_debug_layer_codes",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
@@ -85,6 +85,8 @@ def load() -> C.CDLL:
     L.dg_logits.argtypes = [vp, vp, u32p, sz, vp, sz, f32p]
     L.dg_logits_batch.argtypes = [vp, vp, sz, f32p, vp, vp]
     L.dg_debug_layer.argtypes = [vp, i32, f32p, sz, f32p]
+    L.dg_measure_i8_peak.argtypes = [i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_float)]
+    L.dg_debug_layer_codes.argtypes = [vp, i32, f32p, sz, f32p, vp]
     L.dg_linear_create.argtypes = [f32p, i32, i32, f32p, f32p, i32, C.c_float, i32, C.POINTER(vp)]
     L.dg_linear_forward.argtypes = [vp, f32p, i32, f32p]
     L.dg_linear_forward_device.argtypes = [vp, vp, i32, vp, vp]

@@ -198,6 +198,27 @@ class GpuModel:
         check(load().dg_debug_layer(self.h, int(index), x.ctypes.data, x.shape[0], out.ctypes.data))
         return out
 
+    def layer_codes(self, index: int, x: np.ndarray):
+        """`layer`, also returning the int8 codes of the layer's four quantised
+        projection inputs: (out, [input norm, mixer output, post norm, SwiGLU
+        rows]) (dg_debug_layer_codes)."""
+        x = np.ascontiguousarray(x, np.float32)
+        c = self.config
+        n = x.shape[0]
+        full = c["layer_types"][index] == "full_attention"
+        mixw = (c["num_attention_heads"] * c["head_dim"] if full
+                else c["linear_num_value_heads"] * c["linear_value_head_dim"])
+        widths = (c["hidden_size"], mixw, c["hidden_size"], c["intermediate_size"])
+        out = np.zeros_like(x)
+        codes = np.zeros(n * sum(widths), np.int8)
+        check(load().dg_debug_layer_codes(self.h, int(index), x.ctypes.data, n, out.ctypes.data,
+                                          codes.ctypes.data))
+        blocks, off = [], 0
+        for w in widths:
+            blocks.append(codes[off:off + n * w].reshape(n, w))
+            off += n * w
+        return out, blocks
+
     # ---- batched requests (dg_logits_batch): the throughput form of
     # NativeEngine::evaluate (src/lib.rs:477-559)
     def logits_batch(self, requests):
@@ -354,3 +375,12 @@ def gated_delta_rule_chunked(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, hea
     """Chunked form of `gated_delta_rule` with a caller-owned device workspace."""
     check(load().dg_gated_delta_rule_chunked_device(q_ptr, k_ptr, v_ptr, g_ptr, beta_ptr, batch, t, heads,
                                                     state_ptr, o_ptr, ws_ptr, ws_bytes, stream))
+
+
+def measure_i8_peak(device: int = 0, iters: int = 1 << 16):
+    """(TOP/s, ms) of the dense tcgen05 kind::i8 probe on `device`
+    (dg_measure_i8_peak): one CTA per SM issuing back-to-back 128 x 256 x 32
+    MMAs. The INT8 tensor-core ceiling next to twice the measured bf16 rate."""
+    tops, ms = C.c_double(), C.c_float()
+    check(load().dg_measure_i8_peak(int(device), int(iters), C.byref(tops), C.byref(ms)))
+    return tops.value, ms.value

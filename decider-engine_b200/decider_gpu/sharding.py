@@ -74,19 +74,37 @@ def run_sharded(requests: Sequence, shapes: Sequence[RequestShape], run: Callabl
     initialised process group, or None for a single process.
 
     The gather is the only collective: one object gather after all of a rank's
-    requests are done, never inside the device work.
+    requests are done, never inside the device work. A request whose `run`
+    raises does not stop its rank: the exception travels with the answers, so
+    every rank still reaches the gather, and rank 0 re-raises the first
+    failure (in request order) once everything is gathered.
     """
     world = dist.get_world_size() if dist is not None else 1
     rank = dist.get_rank() if dist is not None else 0
     plan = shard_requests([request_cost(s) for s in shapes], world)
-    mine = {i: run(requests[i]) for i in plan[rank]}
+    mine = {}
+    for i in plan[rank]:
+        try:
+            mine[i] = (True, run(requests[i]))
+        except Exception as e:  # noqa: BLE001 - carried to rank 0 and re-raised there
+            mine[i] = (False, e)
     if dist is None:
-        return [mine[i] for i in range(len(requests))]
-    gathered = [None] * world if rank == 0 else None
-    dist.gather_object(mine, gathered, dst=0)
-    if rank != 0:
-        return None
-    merged = {}
-    for part in gathered:
-        merged.update(part)
-    return [merged[i] for i in range(len(requests))]
+        merged = mine
+    else:
+        gathered = [None] * world if rank == 0 else None
+        try:
+            dist.gather_object(mine, gathered, dst=0)
+        except Exception:
+            # An exception object that does not pickle: send its text instead.
+            mine = {i: v if v[0] else (False, RuntimeError(repr(v[1]))) for i, v in mine.items()}
+            dist.gather_object(mine, gathered, dst=0)
+        if rank != 0:
+            return None
+        merged = {}
+        for part in gathered:
+            merged.update(part)
+    for i in range(len(requests)):
+        ok, v = merged[i]
+        if not ok:
+            raise RuntimeError(f"request {i} failed: {v}") from v
+    return [merged[i][1] for i in range(len(requests))]

@@ -102,6 +102,13 @@ int dg_engine_gemm_time(const dg_engine* e, double* ms, double* ops, uint64_t* l
 int dg_engine_gemm_timing_layers(dg_engine* e, int first_layer, int layers);
 int dg_engine_gemm_time_all(const dg_engine* e, double* ops_all, uint64_t* launches_all);
 
+/* Measurement aid (no counterpart in the reference): the dense INT8
+ * tensor-core rate of `device` in TOP/s, from a timed launch of one CTA per SM
+ * issuing `iters` x 4 back-to-back tcgen05.mma.kind::i8 of 128 x 256 x 32
+ * (iters 1..4194304; ~2^16 runs for about 10 ms); ms_out (nullable) gets the
+ * launch's duration. */
+int dg_measure_i8_peak(int device, int iters, double* tops_out, float* ms_out);
+
 /* ---- forward passes: Model::forward / prefill / forward_after
  * (src/qwen.rs:407-424). `past` may be NULL. hidden_out (nullable) receives
  * [n][hidden_size] FP32. Errors mirror the reference's messages:
@@ -117,6 +124,16 @@ int dg_prefill(dg_engine* e, const uint32_t* ids, size_t n, dg_prefix** out);
  * with no prefix; x_out receives the layer's output rows [n][hidden_size].
  * Runs in the engine's current arithmetic mode. */
 int dg_debug_layer(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out);
+/* dg_debug_layer, also returning the int8 codes of the layer's four quantised
+ * projection inputs (QuantizedInputs::new, src/tensor.rs:315-353), for the
+ * per-layer parity protocol's check of which rows flipped a code: codes_out
+ * receives n x (hidden_size + mixer width + hidden_size + intermediate_size)
+ * bytes, the blocks [n][hidden] of the normalised input rows (q/k/v or
+ * qkv/z/a/b), [n][mixer width] of the mixer output (o_proj or out_proj input;
+ * heads x head_dim or DeltaNet value heads x value dim), [n][hidden] of the
+ * normalised post-mixer rows (gate/up) and [n][intermediate] of the SwiGLU
+ * rows (down_proj). int8-compute engines on the tcgen05 path only. */
+int dg_debug_layer_codes(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out, int8_t* codes_out);
 size_t dg_prefix_len(const dg_prefix* p);
 void dg_prefix_free(dg_prefix* p);
 
@@ -187,7 +204,9 @@ int dg_linear_forward_device(dg_linear* l, const float* x_device, int m, float* 
  *    m*n_pad*4 when n % 256 != 0; larger calls fail with an error naming the
  *    bytes needed (split the rows over several calls);
  *  - the first call on each device resolves the area's address (with that
- *    device current); make that first call before beginning any stream capture;
+ *    device current); make that first call before beginning any stream
+ *    capture; the address is kept for the process, so do not use this call
+ *    across a cudaDeviceReset of that device;
  *  - calls on one device share the area, so they must not overlap in time,
  *    from several threads or several handles alike: serialise them.
  * Runs on, and synchronises, the handle's stream (dg_linear_stream). */

@@ -83,6 +83,9 @@ def lib():
         L.or_layer.argtypes = [_c.c_void_p, _c.c_int, _f32p, _c.c_size_t, _f32p]
         L.or_head_logits.argtypes = [_c.c_void_p, _f32p, _c.c_size_t, _c.c_void_p, _c.c_size_t,
                                      _f32p]
+        L.or_layer_probe.restype = _c.c_int
+        L.or_layer_probe.argtypes = [_c.c_void_p, _c.c_int, _f32p, _c.c_size_t, _f32p, _f32p, _f32p,
+                                     _f32p, _f32p]
         L.or_gated_delta_rule.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _c.c_size_t,
                                           _c.c_size_t, _c.c_size_t, _f32p, _f32p]
         _lib = L
@@ -305,6 +308,22 @@ class OracleModel:
         if lib().or_layer(self.h, int(index), x, x.shape[0], out):
             raise _err()
         return out
+
+    def layer_probe(self, index, x):
+        """`layer`, also returning the FP32 inputs of the layer's four projection
+        groups: (out, [input norm, mixer output, post norm, SwiGLU rows])."""
+        x = np.ascontiguousarray(x, np.float32)
+        c = self.config
+        n = x.shape[0]
+        full = c["layer_types"][index] == "full_attention"
+        mixw = (c["num_attention_heads"] * c["head_dim"] if full
+                else c["linear_num_value_heads"] * c["linear_value_head_dim"])
+        out = np.zeros_like(x)
+        ins = [np.zeros((n, w), np.float32) for w in (c["hidden_size"], mixw, c["hidden_size"],
+                                                      c["intermediate_size"])]
+        if lib().or_layer_probe(self.h, int(index), x, n, out, *ins):
+            raise _err()
+        return out, ins
 
     def head_logits(self, hidden, positions):
         hidden = np.ascontiguousarray(hidden, np.float32)

@@ -330,6 +330,36 @@ int or_layer(void* h, int layer, const float* x, size_t n, float* out) {
   return 0;
 }
 
+// or_layer, also returning the FP32 inputs of the layer's four projection
+// groups (LayerProbe): in_norm [n][hidden], mix [n][mix_width] (attention
+// heads x head_dim, or DeltaNet value heads x dv), post [n][hidden], mlp
+// [n][intermediate]. Test infrastructure: the quantised codes of these rows
+// are compared with the device's.
+int or_layer_probe(void* h, int layer, const float* x, size_t n, float* out, float* in_norm, float* mix,
+                   float* post, float* mlp) {
+  auto* om = static_cast<OracleModel*>(h);
+  const Model& m = om->m;
+  if (layer < 0 || size_t(layer) >= m.layers.size() || n == 0 || n > 4096) {
+    g_error = "bad layer or row count";
+    return 1;
+  }
+  try {
+    std::vector<float> v(x, x + n * m.c.hidden);
+    LayerCache cache;
+    LayerProbe probe;
+    run_layer(m, size_t(layer), v, n, 0, rotary_angles(m, 0, n), nullptr, &cache, &probe);
+    std::copy(v.begin(), v.end(), out);
+    std::copy(probe.input.begin(), probe.input.end(), in_norm);
+    std::copy(probe.mix.begin(), probe.mix.end(), mix);
+    std::copy(probe.post.begin(), probe.post.end(), post);
+    std::copy(probe.mlp.begin(), probe.mlp.end(), mlp);
+  } catch (const std::exception& e) {
+    g_error = e.what();
+    return 1;
+  }
+  return 0;
+}
+
 // Head::logits over `rows` hidden rows; the answer row is the last.
 int or_head_logits(void* h, const float* hidden, size_t rows, const size_t* positions, size_t n_pos,
                    float* out) {

@@ -119,7 +119,7 @@ static std::vector<float> causal_attention(const float* q, const float* k, const
 // Full::forward, src/qwen.rs:530-585
 static std::vector<float> full_forward(const Layer& L, const Config& c, const float* x, size_t n,
                                        const std::vector<float>& angles, const LayerCache* past,
-                                       LayerCache* next) {
+                                       LayerCache* next, std::vector<float>* mix_probe = nullptr) {
   size_t d = c.head_dim, qw = c.heads * d, kw = c.kv_heads * d;
   std::shared_ptr<QuantizedInputs> shared;
   bool done = false;
@@ -157,6 +157,7 @@ static std::vector<float> full_forward(const Layer& L, const Config& c, const fl
   std::vector<float> out =
       causal_attention(q.data(), keys.data(), values.data(), n, c.heads, c.kv_heads, d, offset);
   for (size_t i = 0; i < out.size(); ++i) out[i] = out[i] * sigmoid(gate[i]);
+  if (mix_probe) *mix_probe = out;
   next->full = true;
   next->k = std::move(keys);
   next->v = std::move(values);
@@ -225,7 +226,8 @@ static void recurrence_head(const Layer& L, const Config& c, size_t head, const 
 
 // Delta::forward, src/qwen.rs:649-694 (+ Recurrence::run 775-809)
 static std::vector<float> delta_forward(const Layer& L, const Config& c, const float* x, size_t n,
-                                        size_t start, const LayerCache* past, LayerCache* next) {
+                                        size_t start, const LayerCache* past, LayerCache* next,
+                                        std::vector<float>* mix_probe = nullptr) {
   size_t dk = c.dk, dv = c.dv, kd = c.key_heads * dk, vd = c.value_heads * dv;
   size_t width = 2 * kd + vd, heads = c.value_heads;
   std::shared_ptr<QuantizedInputs> shared;
@@ -260,6 +262,7 @@ static std::vector<float> delta_forward(const Layer& L, const Config& c, const f
   next->tail.assign(tail.begin() + (tail_rows - from_tail) * width, tail.end());
   next->tail.insert(next->tail.end(), raw.begin() + (n - (keep - from_tail)) * width, raw.end());
   next->state = std::move(state);
+  if (mix_probe) *mix_probe = out;
   return L.out.apply(out.data(), n);
 }
 
@@ -276,24 +279,38 @@ static std::vector<float> rotary_angles(const Model& m, size_t start, size_t n) 
   return angles;
 }
 
+// FP32 inputs of a layer's four projection groups, recorded for parity
+// checks of the quantised activations (not part of the reference): the
+// normalised input rows (q/k/v or qkv/z/a/b), the mixer output (o_proj or
+// out_proj), the normalised post-mixer rows (gate/up) and the SwiGLU rows
+// (down_proj).
+struct LayerProbe {
+  std::vector<float> input, mix, post, mlp;
+};
+
 // One pass of the layer loop of Model::run (src/qwen.rs:470-494) on the
 // residual rows x [n, hidden]: input norm, Full/Delta forward, residual_norm,
 // SwiGLU MLP with the residual add.
 static void run_layer(const Model& m, size_t i, std::vector<float>& x, size_t n, size_t start,
-                      const std::vector<float>& angles, const LayerCache* lp, LayerCache* cache) {
+                      const std::vector<float>& angles, const LayerCache* lp, LayerCache* cache,
+                      LayerProbe* probe = nullptr) {
   const Config& c = m.c;
   size_t h = c.hidden;
   const Layer& L = m.layers[i];
   std::vector<float> nrm = x;
   rms(nrm.data(), nrm.size(), L.input_norm.data(), h, c.eps, true);
-  std::vector<float> mixed = L.full ? full_forward(L, c, nrm.data(), n, angles, lp, cache)
-                                    : delta_forward(L, c, nrm.data(), n, start, lp, cache);
+  if (probe) probe->input = nrm;
+  std::vector<float>* mp = probe ? &probe->mix : nullptr;
+  std::vector<float> mixed = L.full ? full_forward(L, c, nrm.data(), n, angles, lp, cache, mp)
+                                    : delta_forward(L, c, nrm.data(), n, start, lp, cache, mp);
   residual_norm(x.data(), mixed.data(), nrm.data(), L.post_norm.data(), h, x.size(), c.eps);
+  if (probe) probe->post = nrm;
   std::shared_ptr<QuantizedInputs> shared;
   bool done = false;
   std::vector<float> gate(n * c.intermediate);
   L.gate.apply_into(nrm.data(), n, gate.data(), Epilogue::Write, &shared, &done);
   L.up.apply_into(nrm.data(), n, gate.data(), Epilogue::SwiGlu, &shared, &done);
+  if (probe) probe->mlp = gate;
   L.down.apply_into(gate.data(), n, x.data(), Epilogue::Add, nullptr, nullptr);
 }
 

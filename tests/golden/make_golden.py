@@ -2,8 +2,8 @@
 
 Source: decider-engine tests/fixtures/tiny (a synthetic 2-layer checkpoint,
 seed 4242, with PyTorch/Transformers FP32 reference outputs generated upstream)
-and tests/request.json. The copies are byte-for-byte; run this script in a
-checkout that has the reference tree mounted:
+and tests/request.json. The copies are byte-for-byte; run this script with
+the reference checkout given as the argument or in DECIDER_REFERENCE:
 
     python tests/golden/make_golden.py /path/to/decider-engine
 """
@@ -35,4 +35,7 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DECIDER_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py <decider-engine checkout> (or set DECIDER_REFERENCE)")
+    main(ref)

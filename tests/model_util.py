@@ -78,22 +78,31 @@ def expected_shapes(c, rank, pointer_dim):
     return shapes
 
 
-def random_tensors(c, rank=32, pointer_dim=64, seed=0, std=0.02, norm_jitter=0.1):
-    """{name: (0 (F32), shape, array)}: N(0, std^2) weights, norms 1 + jitter."""
+def random_tensors(c, rank=32, pointer_dim=64, seed=0, std=0.02, norm_jitter=0.1, bias_std=0.1, f32=False):
+    """{name: (0 (F32), shape, array)}: N(0, std^2) weights, norms 1 + jitter,
+    biases N(0, bias_std^2). f32=True draws the normals directly in float32
+    (numpy's float32 ziggurat: a different, faster stream, for the 2B-sized
+    parity models)."""
     rng = np.random.default_rng(seed)
+    if f32:
+        normal = lambda shape: rng.standard_normal(shape, dtype=np.float32)
+    else:
+        normal = lambda shape: rng.standard_normal(shape)
     out = {}
     for name, shape in expected_shapes(c, rank, pointer_dim).items():
         if "norm" in name and name.endswith(".weight"):
-            arr = (1.0 + norm_jitter * rng.standard_normal(shape)).astype(np.float32)
+            arr = (1.0 + norm_jitter * normal(shape)).astype(np.float32)
         elif name.endswith(".bias"):
-            arr = (0.1 * rng.standard_normal(shape)).astype(np.float32)
+            arr = (bias_std * normal(shape)).astype(np.float32)
         elif name.endswith("embed_tokens.weight"):
-            arr = rng.standard_normal(shape).astype(np.float32)
+            arr = normal(shape).astype(np.float32)
         else:
             s = std
             if "lora_B" in name or "lora_A" in name:
                 s = 0.05
-            arr = (s * rng.standard_normal(shape)).astype(np.float32)
+            arr = normal(shape)
+            arr *= np.float32(s) if f32 else s
+            arr = arr.astype(np.float32, copy=False)
         out[name] = (0, list(shape), arr)
     return out
 
@@ -102,3 +111,61 @@ def rel_err(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ---------------------------------------------------------------- full-size parity inputs
+# The 2B decider of BASELINE config 2 (24 layers, vocab 248320, rank-32 LoRA
+# with alpha/r = 2, pointer head of 256), seeded weights N(0, 0.02^2) with
+# norms 1 and zero biases, shared by tests/golden/make_full_parity.py (which
+# runs the CPU oracle once and commits its outputs) and the GPU tests.
+FULL_SEED = 20261202
+FULL_POINTER_DIM = 256
+# temperature_by_kind of the reference's tiny fixture config (noul 0.8,
+# choice 0.7, score 1.2).
+TEMPERATURES = {"noul": 0.8, "choice": 0.7, "score": 1.2}
+KIND_OPTIONS = {"noul": 2, "choice": 4, "score": 5}
+
+
+def full_model_tensors():
+    c = cfg2_config(24)
+    t = random_tensors(c, rank=32, pointer_dim=FULL_POINTER_DIM, seed=FULL_SEED, std=0.02, norm_jitter=0.0,
+                       bias_std=0.0, f32=True)
+    return c, t
+
+
+def tensor_checksums(tensors, names=("layers.0.linear_attn.in_proj_qkv.weight", "layers.23.mlp.down_proj.weight",
+                                     "embed_tokens.weight", "head.q.weight")):
+    """float64 sums of a few tensors: the fixture records them so a test can
+    tell a different random stream from a parity failure."""
+    return {n: float(np.asarray(tensors[n][2], np.float64).sum()) for n in names}
+
+
+def cfg2_request(vocab=248320):
+    """512 ids uniform over the vocabulary (seed 0), one
+    noul question with options at [509, 510], answer at 511."""
+    ids = np.random.default_rng(0).integers(0, vocab, 512).astype(np.uint32)
+    return ids, [509, 510]
+
+
+def cfg4_request(vocab=248320, seed=4):
+    """a 3584-token state, then 8 questions of 64 tokens,
+    kinds noul / choice (4) / score (5) in turn, options in each question's
+    last 16 tokens."""
+    rng = np.random.default_rng(seed)
+    state = rng.integers(0, vocab, 3584).astype(np.uint32)
+    kinds = [("noul", "choice", "score")[i % 3] for i in range(8)]
+    qs = [(rng.integers(0, vocab, 64).astype(np.uint32), [48 + 2 * j for j in range(KIND_OPTIONS[k])], k)
+          for k in kinds]
+    return state, qs
+
+
+def probabilities(logits, kind):
+    """The reference's readout (src/lib.rs:525-548): logits / T_kind, then
+    softmax (max, exp, sequential sum, divide; src/tensor.rs:534-546)."""
+    v = (np.asarray(logits, np.float32) / np.float32(TEMPERATURES[kind])).astype(np.float32)
+    mx = np.float32(v.max())
+    e = np.exp((v - mx).astype(np.float32)).astype(np.float32)
+    total = np.float32(0.0)
+    for x in e:
+        total = np.float32(total + x)
+    return (e / total).astype(np.float32)

@@ -98,3 +98,55 @@ def test_two_gloo_ranks_gather_answers_in_request_order():
     assert results[1][1] is None
     serial = [_fake_engine({"id": i}) for i in range(n)]
     assert results[0][1] == serial
+
+
+def _failing_engine(request):
+    if request["id"] == 5:
+        raise ValueError("invalid encoding positions or window")
+    return _fake_engine(request)
+
+
+def _failing_worker(rank, world, port, n, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        try:
+            out = run_sharded([{"id": i} for i in range(n)], _shapes(n, 3), _failing_engine, dist)
+            q.put((rank, "ok", out))
+        except RuntimeError as e:
+            q.put((rank, "raised", str(e)))
+        # Both ranks still agree on the next collective: nobody was left behind.
+        t = torch_tensor(rank)
+        dist.all_reduce(t)
+        q.put((rank, "after", int(t.item())))
+    finally:
+        dist.destroy_process_group()
+
+
+def torch_tensor(v):
+    import torch
+    return torch.tensor([v])
+
+
+def test_a_failing_request_reaches_rank_0_without_stalling_the_gather():
+    """A request that raises on one rank does not keep that rank from the
+    gather: the failure travels with the answers, rank 0 re-raises it (naming
+    the request), the other rank returns None, and both ranks go on to the
+    next collective."""
+    world, n = 2, 23
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, n, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in range(2 * world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    by = {(r, kind): v for r, kind, v in got}
+    assert by[(0, "raised")].startswith("request 5 failed") and "invalid encoding" in by[(0, "raised")]
+    assert by[(1, "ok")] is None
+    assert by[(0, "after")] == by[(1, "after")] == 1

@@ -167,3 +167,29 @@ def test_layer_trace_and_single_layer_restate_the_forward(O, precision):
     # Rows with the same id enter the first layer identically.
     assert np.array_equal(trace[0][0], trace[0][ids.index(ids[0], 1)]) if ids.count(ids[0]) > 1 else True
     assert np.isfinite(trace).all()
+
+
+def test_layer_probe_records_the_projection_inputs(O):
+    """The per-layer flipped-code check reads the FP32 inputs of a layer's four
+    projection groups from the oracle: the probe's output equals the plain
+    layer's, and each recorded input is what its projection consumed (the
+    normalised input rows equal rms(x) with the layer's centred weight, and the
+    SwiGLU rows are finite and [n][intermediate])."""
+    from model_util import random_tensors, small_config
+    for lt in ("linear_attention", "full_attention"):
+        c = small_config(layer_types=(lt,))
+        t = random_tensors(c, rank=32, pointer_dim=0, seed=5)
+        m = O.OracleModel(c, t, "int8-compute", 32, 2.0)
+        x = np.random.default_rng(1).standard_normal((37, c["hidden_size"])).astype(np.float32)
+        out, ins = m.layer_probe(0, x)
+        assert np.array_equal(out, m.layer(0, x))
+        mixw = c["num_attention_heads"] * c["head_dim"] if lt == "full_attention" else \
+            c["linear_num_value_heads"] * c["linear_value_head_dim"]
+        assert [a.shape for a in ins] == [(37, c["hidden_size"]), (37, mixw), (37, c["hidden_size"]),
+                                          (37, c["intermediate_size"])]
+        w = t["layers.0.input_layernorm.weight"][2].astype(np.float64)
+        xd = x.astype(np.float64)
+        ref = xd / np.sqrt((xd * xd).mean(axis=1, keepdims=True) + 1e-6) * (1 + w)
+        assert np.abs(ins[0] - ref).max() < 1e-5 * np.abs(ref).max()
+        assert all(np.isfinite(a).all() and np.abs(a).max() > 0 for a in ins)
+        assert all(O.quantize_inputs(a) is not None for a in ins)

@@ -71,3 +71,23 @@ def test_noalloc_rejects_rows_beyond_its_area(torch_cuda):
     rows = np.ones((8, k), np.float32)
     ref, got = _both(torch_cuda, lin, rows, n)
     assert np.array_equal(got, ref)
+
+
+def test_noalloc_calls_take_no_device_memory(torch_cuda):
+    """The property the entry point exists for: once its first call on the
+    device has resolved the static area, further calls take no device memory
+    (the device's free bytes do not move over many calls of varying sizes)."""
+    from decider_gpu import Linear
+    n, k = 6144, 2048
+    x, w, la, lb = _case(7, 512, n, k)
+    lin = Linear(w, la, lb, 2.0)
+    xd = torch_cuda.from_numpy(x).cuda()
+    yd = torch_cuda.empty((512, n), dtype=torch_cuda.float32, device="cuda")
+    lin.forward_device_noalloc(xd.data_ptr(), 512, yd.data_ptr())  # first call: set-up
+    torch_cuda.cuda.synchronize()
+    free0, _ = torch_cuda.cuda.mem_get_info()
+    for rows in (512, 17, 300, 1, 512):
+        lin.forward_device_noalloc(xd.data_ptr(), rows, yd.data_ptr())
+    torch_cuda.cuda.synchronize()
+    free1, _ = torch_cuda.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
