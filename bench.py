@@ -1,23 +1,28 @@
-"""Prefill benchmark of the B200 decider engine (BASELINE config 2).
+"""Prefill benchmark of the B200 decider engine.
 
-One step = one full 2B int8-compute decide forward (24 layers: 6 x [3 Gated
-DeltaNet + 1 gated GQA], hidden 2048, LoRA rank 32, vocab 248320) over a
-512-token prompt plus the pointer-head readout of one noul question, weights
+Default line (the request-sharded throughput batch): one
+step = the first 256 requests of the seeded 8192-request draw (bound length
+L ~ U[128, 4096], 1-4 questions of 64 tokens; a request with several
+questions prefills its (L - 64)-token state once and runs its questions
+together after it), on the 2B int8-compute decider (24 layers: 6 x [3 Gated
+DeltaNet + 1 gated GQA], hidden 2048, LoRA rank 32, vocab 248320), weights
 random-initialised N(0, 0.02^2) with norms 1 (synthetic data, seed 0).
+Under torchrun the requests are sharded over the ranks by
+decider_gpu.sharding.shard_requests (longest processing time first): strong
+scaling, no collective on the data path, time = max over ranks.
+`--workload cfg2` measures config 2 (one 512-token prompt + one noul
+question per step); cfg1, cfg3 and cfg4 the other configs.
 
-value  : prefill tokens/s with the ids already resident (device time of the
-         forward kernels, CUDA events on the engine stream);
-e2e    : the same through the public C ABI call (dg_logits: host ids in,
-         host logits out, copies inside the timed region);
-roofline: the dominant kernel, the tcgen05 INT8 projection: every one of its
-         launches in the timed steps is bracketed by CUDA events on the engine
-         stream; achieved = sum of 2*M*N*K over the launches / their summed time;
+value  : prefill tokens/s from the device time of the forward kernels (CUDA
+         events on the engine stream), ids already resident;
+e2e    : the same through the public C ABI call (dg_logits_batch / dg_logits:
+         host ids in, host logits out, copies inside the timed region);
+roofline: the dominant kernel, the tcgen05 INT8 projection: its launches in
+         the timed steps are bracketed by CUDA events on the engine stream;
+         achieved = sum of 2*M*N*K over the launches / their summed time;
 cpu_baseline: the oracle (C++ restatement of the reference CPU path, -O3)
          running the whole 24-layer forward over a short prompt (--cpu-tokens)
          on every host thread, the same step the reference arm times.
-
-Multi-GPU (torchrun): every rank owns a replica and its own request (weak
-scaling, no collective on the data path); time = max over ranks.
 """
 from __future__ import annotations
 
@@ -356,7 +361,7 @@ def run_ours(args, world, rank, local, dist):
 
 
 # ------------------------------------------------------------------ other configs
-# The default line is config 2. `--workload cfg1|cfg3|cfg4|cfg5` measures the
+# The default line is config 5 (run_batch). `--workload cfg1|cfg2|cfg3|cfg4` measures the
 # other BASELINE configs with the same contract (device-time value, e2e
 # through the public call with host buffers, roofline of the dominant kernel,
 # CPU baseline on rank 0 at N=1).
@@ -693,6 +698,9 @@ def run_batch(args, world, rank, local, dist, which):
                   "tokens_per_step": tokens_all, "requests": args.requests, "parallelism": f"dp{world}",
                   "l2": "not flushed: every forward streams 1.4 GB of int8 weights, > 126 MB L2"}
         scaling = "strong"
+        # Every rank derives the same plan: the share of each rank, for the report.
+        shard = {"tokens_per_rank": [int(sum(toks[i] for i in p)) for p in plan],
+                 "requests_per_rank": [len(p) for p in plan]}
     model.gemm_timing_layers(0, min(4, args.layers))
     for _ in range(args.warmup):
         _, st, _, err = model.logits_batch(mine)
@@ -714,7 +722,14 @@ def run_batch(args, world, rank, local, dist, which):
     g_ms, g_ops, g_n = model.gemm_time()
     g_ms, g_ops, g_n = g_ms - g0_ms, g_ops - g0_ops, g_n - g0_n
     model.gemm_timing(False)
-    dev_ms = max_over_ranks(sum(dev) / len(dev), dist, local)
+    my_ms = sum(dev) / len(dev)
+    rank_ms = [my_ms]
+    if dist is not None:
+        t = torch.zeros(world, dtype=torch.float64, device=f"cuda:{local}")
+        t[rank] = my_ms
+        dist.all_reduce(t)
+        rank_ms = [float(x) for x in t.cpu()]
+    dev_ms = max_over_ranks(my_ms, dist, local)
     e2e_ms = max_over_ranks(sum(wall) / len(wall), dist, local)
     per_req.sort()
     p50 = max_over_ranks(per_req[len(per_req) // 2], dist, local)
@@ -724,9 +739,11 @@ def run_batch(args, world, rank, local, dist, which):
     _, bf16, src = peaks()
     peak = 2.0 * bf16
     achieved = g_ops / (g_ms / 1000.0) / 1e12 if g_ms > 0 else 0.0
+    i8_loop, i8_loop_ms = decider_gpu.measure_i8_peak(local)
     n_ids = sum(len(r.get("state", [])) + sum(len(q[0]) for q in r["questions"]) for r in mine)
     n_logits = sum(len(q[1]) for r in mine for q in r["questions"])
-    line = _line(args, world, f"prefill tok/s at 2B INT8 ({which})", tokens_all / (dev_ms / 1000.0), "tok/s",
+    metric = METRIC if which == "cfg5" and args.default_line else f"prefill tok/s at 2B INT8 ({which})"
+    line = _line(args, world, metric, tokens_all / (dev_ms / 1000.0), "tok/s",
                  dev_ms, dict(config, setup_s=round(setup_s, 1)),
                  e2e={"value": tokens_all / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": n_ids * 4,
                       "d2h_bytes_per_step": n_logits * 4, "ms_per_step": e2e_ms},
@@ -735,11 +752,23 @@ def run_batch(args, world, rank, local, dist, which):
                            "kernel": "gemm_i8_g64_kernel, the projection launches of layers 0-3 in every forward "
                                      "of the timed steps (achieved = sum 2*M*N*K / sum event time)",
                            "launches": int(g_n), "ms_per_launch": g_ms / max(g_n, 1),
-                           "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16"},
+                           "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16",
+                           "i8_loop_peak": i8_loop, "frac_of_i8_loop": achieved / i8_loop if i8_loop else None,
+                           "i8_loop": "dg_measure_i8_peak: one CTA per SM issuing back-to-back "
+                                      f"tcgen05.mma.kind::i8 128x256x32 ({i8_loop_ms:.1f} ms launch), after the "
+                                      "timed region"},
                  latency={"p50_ms": p50, "p99_ms": p99, "requests": len(per_req),
                           "what": "device time of one request's forwards, max over ranks"},
                  gpu_launches=int(launches), clocks=clocks.summary(), scaling=scaling)
     line["config"]["tokens_rank0"] = tokens_mine
+    if which == "cfg5":
+        tot = sum(shard["tokens_per_rank"])
+        line["sharding"] = dict(shard, device_ms_per_rank=rank_ms,
+                                worst_rank_token_share=max(shard["tokens_per_rank"]) / tot,
+                                ideal_share=1.0 / world,
+                                time_imbalance=max(rank_ms) / (sum(rank_ms) / len(rank_ms)),
+                                how="LPT over a token + window^2 + per-forward cost model "
+                                    "(decider_gpu.sharding.shard_requests); no collective on the data path")
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = _cpu_forward_baseline(args, note=" (from an empty cache: a short context, which "
                                                                 "favours the CPU)")
@@ -767,14 +796,20 @@ def run_reference_workload(args, world, rank, which):
                 cf = CpuForward(args.cpu_tokens)
             v, u, c = cf.tokens / cf.time(), "tok/s", cf.threads
             smp = cf.describe()
-            config = {"workload": which}
-            metric = f"prefill tok/s at 2B INT8 ({which})"
+            config = {"workload": f"{which} sample: 2B decider forward (24 layers, LoRA r32) over {cf.tokens} tokens "
+                                  "+ pointer head, int8-compute, from an empty cache",
+                      "tokens_per_step": cf.tokens, "parallelism": "rank 0 host cores"}
+            metric = METRIC if which == "cfg5" and args.default_line else f"prefill tok/s at 2B INT8 ({which})"
         if i >= args.warmup:
             vals.append(v)
     v = sum(vals) / len(vals)
+    extra = {}
+    if cf is not None:
+        # Mean step time of the timed CPU forwards (the value is tokens / that time, averaged).
+        extra["ms_per_step"] = 1000.0 * sum(cf.tokens / x for x in vals) / len(vals)
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": v, "unit": u, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "warmup": args.warmup, **extra, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "data": "synthetic", "config": config,
         "note": "the reference's CPU algorithm (oracle restatement) on rank 0's host cores",
         "cpu_baseline": {"value": v, "unit": u, "cores": c, "kind": "port", "sample": smp},
@@ -798,10 +833,14 @@ def main():
                     help="fewer layers (multiple of 4) for small ncu captures; the bench line is 24")
     ap.add_argument("--vocab", type=int, default=248320,
                     help="smaller embedding table for small ncu captures; the bench line is 248320")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"],
-                    help="BASELINE config to measure; the default line is cfg2")
-    ap.add_argument("--requests", type=int, default=48, help="cfg5: requests taken from the seeded draw")
+    ap.add_argument("--workload", default=None, choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5"],
+                    help="BASELINE config to measure; the default line is cfg5 (256 requests, LPT-sharded over the "
+                         "ranks)")
+    ap.add_argument("--requests", type=int, default=256, help="cfg5: requests taken from the seeded draw")
     args = ap.parse_args()
+    args.default_line = args.workload is None
+    if args.workload is None:
+        args.workload = "cfg5"
     if args.layers % 4 or args.layers <= 0:
         ap.error("--layers must be a positive multiple of 4")
     world, rank, local, dist = dist_setup()

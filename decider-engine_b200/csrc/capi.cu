@@ -236,18 +236,40 @@ int dg_read_checkpoint_config(const char* dir, dg_model_config* cfg, int32_t* la
   });
 }
 
-int dg_engine_load(const char* dir, int precision, int device, int max_tokens, dg_engine** out) {
+void dg_load_limits_default(dg_load_limits* out) {
+  if (!out) return;
+  const dg::LoadLimits d;
+  out->max_tensor_bytes = d.max_tensor_bytes;
+  out->max_weight_bytes = d.max_weight_bytes;
+  out->max_workspace_bytes = d.max_workspace_bytes;
+}
+
+int dg_engine_load_with_limits(const char* dir, int precision, const dg_load_limits* limits, int device,
+                               int max_tokens, dg_engine** out) {
   return guarded([&] {
     if (!dir || !out) throw std::runtime_error("null argument");
+    dg::LoadLimits lim;
+    if (limits) {
+      lim.max_tensor_bytes = limits->max_tensor_bytes;
+      lim.max_weight_bytes = limits->max_weight_bytes;
+      lim.max_workspace_bytes = limits->max_workspace_bytes;
+    }
     dg::Config c;
-    int pointer_dim = 0;
-    dg::read_checkpoint_config(dir, c, pointer_dim);
+    int pointer_dim = 0, max_length = 0;
+    dg::read_checkpoint_config(dir, c, pointer_dim, &max_length);
+    // Every budget is checked before the engine takes any device memory.
+    dg::validate_layout(c, max_length, c.rank, pointer_dim, lim);
+    dg::ensure_checkpoint_budget(dir, lim);
     std::unique_ptr<dg_engine> e(new dg_engine());
     e->e.reset(new dg::Engine(c, precision, device, max_tokens));
-    dg::load_checkpoint_tensors(*e->e, dir);
+    dg::load_checkpoint_tensors(*e->e, dir, lim);
     e->e->finalize();
     *out = e.release();
   });
+}
+
+int dg_engine_load(const char* dir, int precision, int device, int max_tokens, dg_engine** out) {
+  return dg_engine_load_with_limits(dir, precision, nullptr, device, max_tokens, out);
 }
 
 int dg_engine_fast_path(const dg_engine* e) { return e && e->e && e->e->fast_path() ? 1 : 0; }
@@ -366,6 +388,51 @@ int dg_debug_layer_codes(dg_engine* e, int layer, const float* x_in, size_t n, f
   });
 }
 
+size_t dg_attention_workspace_bytes(int heads, int kv_heads, int d, int n) {
+  if (!dg::attention_tc_supported(d, heads, kv_heads) || n <= 0) return 0;
+  return dg::attention_tc_workspace_floats(heads, kv_heads, d, n) * 4;
+}
+
+int dg_attention_device(const float* q, const float* kc, const float* vc, const float* gate, int ld_gate, int n,
+                        int offset, int heads, int kv_heads, int d, float* out, int tensor_cores, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return guarded([&] {
+    if (!q || !kc || !vc || !gate || !out) throw std::runtime_error("null argument");
+    if (n <= 0 || offset < 0 || offset + n > 4096 || heads <= 0 || kv_heads <= 0 || heads % kv_heads || d <= 0)
+      throw std::runtime_error("attention: bad shape");
+    auto s = static_cast<cudaStream_t>(stream);
+    static thread_local dg::DevBuf status;
+    if (!status.ptr) {
+      status = dg::DevBuf(sizeof(dg::DeviceStatus));
+    }
+    DG_CUDA(cudaMemsetAsync(status.ptr, 0, sizeof(dg::DeviceStatus), s));
+    if (tensor_cores) {
+      if (!workspace || workspace_bytes < dg_attention_workspace_bytes(heads, kv_heads, d, n))
+        throw std::runtime_error("attention: workspace too small");
+      dg::launch_attention_tc(q, kc, vc, gate, ld_gate, n, offset, heads, kv_heads, d, out,
+                              static_cast<float*>(workspace), workspace_bytes / 4, status.as<dg::DeviceStatus>(), s);
+    } else {
+      dg::launch_attention(q, kc, vc, gate, ld_gate, n, offset, heads, kv_heads, d, out, true, s);
+    }
+    dg::DeviceStatus h{};
+    DG_CUDA(cudaMemcpyAsync(&h, status.ptr, sizeof(h), cudaMemcpyDeviceToHost, s));
+    DG_CUDA(cudaStreamSynchronize(s));
+    if (h.code) throw std::runtime_error("attention: device error code " + std::to_string(h.code));
+  });
+}
+
+int dg_forward_segments_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t seg_len, size_t segs,
+                               float* hidden_out) {
+  return guarded([&] {
+    check_engine(e);
+    if (past && past->owner != e) throw std::runtime_error("prefix belongs to another engine");
+    if (!ids || seg_len == 0 || segs == 0 || seg_len * segs > (1u << 30))
+      throw std::runtime_error("token sequence must contain 1\xe2\x80\x93" "4096 tokens");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    e->e->forward_segments(ids, int(seg_len), int(segs), past ? past->p.get() : nullptr, hidden_out);
+  });
+}
+
 int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
                     float* request_ms) {
   const int rc = guarded([&] {
@@ -402,12 +469,35 @@ int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests,
         past = state.get();
       }
       size_t o = out;
-      for (size_t i = 0; i < q.n_questions; ++i) {
-        const dg_question& u = q.questions[i];
-        g.forward(u.ids, int(std::min<size_t>(u.n, 1u << 30)), past, false, nullptr, nullptr);
-        ms += g.last_forward_ms;
-        g.head_logits(int(u.n), u.opt_pos, int(u.n_opt), logits_out + o);
-        o += u.n_opt;
+      // Questions of one length continue the state together: one segmented
+      // forward per group of as many as the workspace holds, each question's
+      // rows the same as its own forward's (bit for bit in reference order).
+      const size_t nq = q.n_questions, len0 = q.questions[0].n;
+      bool together = nq >= 2 && g.batch_questions && g.segments_supported() && len0 <= size_t(g.max_tokens());
+      for (size_t i = 1; together && i < nq; ++i) together = q.questions[i].n == len0;
+      if (together) {
+        const size_t per = std::min(nq, std::max<size_t>(1, size_t(g.max_tokens()) / len0));
+        std::vector<uint32_t> ids;
+        for (size_t i0 = 0; i0 < nq; i0 += per) {
+          const size_t cnt = std::min(per, nq - i0);
+          ids.clear();
+          for (size_t i = i0; i < i0 + cnt; ++i) ids.insert(ids.end(), q.questions[i].ids, q.questions[i].ids + len0);
+          g.forward_segments(ids.data(), int(len0), int(cnt), past, nullptr);
+          ms += g.last_forward_ms;
+          for (size_t j = 0; j < cnt; ++j) {
+            const dg_question& u = q.questions[i0 + j];
+            g.head_logits(int(len0), u.opt_pos, int(u.n_opt), logits_out + o, int(j * len0));
+            o += u.n_opt;
+          }
+        }
+      } else {
+        for (size_t i = 0; i < nq; ++i) {
+          const dg_question& u = q.questions[i];
+          g.forward(u.ids, int(std::min<size_t>(u.n, 1u << 30)), past, false, nullptr, nullptr);
+          ms += g.last_forward_ms;
+          g.head_logits(int(u.n), u.opt_pos, int(u.n_opt), logits_out + o);
+          o += u.n_opt;
+        }
       }
     });
     if (st && first_error.empty()) first_error = dg_last_error();

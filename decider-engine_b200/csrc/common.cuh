@@ -271,13 +271,6 @@ __device__ __forceinline__ void tmem_fill_32x32b_x16(uint32_t taddr, uint32_t v)
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// 32 lanes x 8 columns set to v, without a compiler memory clobber (it
-// touches only TMEM; volatile asm statements keep their order among
-// themselves). The store reads its data from consecutive registers, so a
-// narrower shape needs fewer of them.
-__device__ __forceinline__ void tmem_fill_32x32b_x8(uint32_t taddr, uint32_t v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(v));
-}
 
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
 // layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes, 8-row

@@ -117,8 +117,23 @@ class Engine {
   // Model::run: hidden [n][hidden] to host (nullable); capture -> new prefix.
   void forward(const uint32_t* ids, int n, const Prefix* past, bool capture, float* hidden_out,
                std::unique_ptr<Prefix>* captured);
-  // Head::logits on the last forward's hidden rows (device-resident).
-  void head_logits(int rows, const size_t* positions, int n_pos, float* logits_out);
+  // Model::forward_after for `segs` sequences of seg_len tokens each (ids
+  // concatenated), every one continuing `past` (or starting at position 0
+  // when past is null): the questions of one request as ONE pass over
+  // segs * seg_len rows. Projections, norms and the MLP run once over all
+  // rows; RoPE positions, the attention (the prefix's keys plus each
+  // sequence's own), the conv (the prefix's tail) and the recurrence (a copy
+  // of the prefix state per sequence) keep the sequences apart. In reference
+  // order each sequence's rows equal those of forward(its ids, past) bit for
+  // bit. hidden_out (nullable) receives [segs * seg_len][hidden]; the rows
+  // stay on the device for head_logits with row_base = sequence * seg_len.
+  void forward_segments(const uint32_t* ids, int seg_len, int segs, const Prefix* past, float* hidden_out);
+  // Segmented forwards need the head_dim-256 attention and dk = dv = 128
+  // recurrence kernels (the 2B shape) on the tcgen05 path.
+  bool segments_supported() const;
+  // Head::logits on the last forward's hidden rows (device-resident):
+  // the answer is row row_base + rows - 1, the options rows row_base + positions.
+  void head_logits(int rows, const size_t* positions, int n_pos, float* logits_out, int row_base = 0);
   // One decoder layer, teacher-forced: residual rows x_in [n][hidden] (host)
   // at positions 0..n-1 with no prefix -> the layer's output rows (host).
   void debug_layer(int layer, const float* x_in, int n, float* x_out);
@@ -128,6 +143,10 @@ class Engine {
   // int8-compute on the tcgen05 path only.
   void debug_layer_codes(int layer, const float* x_in, int n, float* x_out, int8_t* codes);
   const Config& config() const { return c_; }
+  int max_tokens() const { return max_tokens_; }
+  // dg_logits_batch runs the equal-length questions of a request as one
+  // segmented forward (DG_BATCH_QUESTIONS=0: one forward per question).
+  bool batch_questions = true;
   bool fast_path() const { return fast_; }
   int device() const { return device_; }
   cudaStream_t stream() const { return stream_; }
@@ -204,6 +223,15 @@ class Engine {
   DevBuf hrows_, hnorm_, hq_, hk_, hlogits_, hrow_idx_;
   std::vector<DevBuf> kcache_, vcache_, state_;
   DevBuf delta_ws_;  // chunked DeltaNet products (fast mode)
+  // Segmented forwards (forward_segments): sequence length and count of the
+  // running pass (0 / 1 otherwise), the sequences' own K/V rows and one
+  // recurrent state per sequence.
+  int seg_len_ = 0, segs_ = 1;
+  DevBuf kseg_, vseg_, seg_state_;
+  // Fast-mode attention on the tensor cores (scores and Vᵀ workspace);
+  // DG_ATTN_TC=0 keeps the CUDA-core kernel.
+  DevBuf attn_ws_;
+  bool attn_tc_ = true;
   DevBuf lora_part_; // split-K LoRA-A partial sums (fast mode)
   DevBuf gemm_split_ws_, gemm_split_cnt_;  // split-K projection partials and tile counters (fast mode)
   DevBuf status_;
@@ -229,10 +257,23 @@ class Engine {
   void set_gemm_timing(bool on, int first_layer = 0, int layers = 1 << 30);
 };
 
+// LoadLimits (src/loading.rs:8-24): allocation budgets checked before any
+// payload is read or any memory taken. Defaults: 2 GiB per tensor, 12 GiB of
+// weights and conversion scratch, 2 GiB of forward workspace.
+struct LoadLimits {
+  uint64_t max_tensor_bytes = uint64_t(2) << 30;
+  uint64_t max_weight_bytes = uint64_t(12) << 30;
+  uint64_t max_workspace_bytes = uint64_t(2) << 30;
+};
+
 // Checkpoint directory in the reference's layout (loader.cu): the validated
-// model config (rank, LoRA scale, pointer dim included), and the tensors of the
-// three safetensors files streamed into an engine.
-void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim);
-void load_checkpoint_tensors(Engine& e, const std::string& dir);
+// model config (rank, LoRA scale, pointer dim included; max_length of the
+// decision window when max_length_out is given), the architecture's budget
+// check (Config::validate_layout), and the tensors of the safetensors files
+// charged to a budget and streamed into an engine.
+void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim, int* max_length_out = nullptr);
+void validate_layout(const Config& c, int tokens, int rank, int pointer, const LoadLimits& limits);
+void ensure_checkpoint_budget(const std::string& dir, const LoadLimits& limits);
+void load_checkpoint_tensors(Engine& e, const std::string& dir, const LoadLimits& limits = LoadLimits());
 
 }  // namespace dg

@@ -240,6 +240,13 @@ void Engine::finalize() {
   }
   if (c.dk == 128 && c.dv == 128)
     delta_ws_ = DevBuf(delta_chunk_workspace_bytes(1, c.value_heads, M));
+  if (fast_ && attention_tc_supported(c.head_dim, c.heads, c.kv_heads))
+    attn_ws_ = DevBuf(attention_tc_workspace_floats(c.heads, c.kv_heads, c.head_dim, M) * 4);
+  if (segments_supported()) {
+    // Segmented forwards: the sequences' own K/V rows (the shared prefix stays in the Prefix).
+    kseg_ = DevBuf(size_t(M) * c.kw() * 4);
+    vseg_ = DevBuf(size_t(M) * c.kw() * 4);
+  }
   if (fast_) lora_part_ = DevBuf(lora_a_partial_floats(M) * 4);
   if (fast_) {
     gemm_split_ws_ = DevBuf(kGemmSplitFloats * 4);

@@ -86,10 +86,53 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
   if (tail_rows != std::min(start, k - 1)) throw DgError("prefix cache does not match the layer types");
   const int* off = L.in_proj.part_off.data();
   float* base = proj_.as<float>();
+  const size_t sbytes = size_t(H) * c.dk * c.dv * 4;
+  if (seg_len_) {
+    // segs_ sequences of seg_len_ rows, each from the prefix's tail and state.
+    const int sl = seg_len_, ns = segs_;
+    launch_conv_silu(raw, ldr, sl, tail, tail_rows, start, W, k, L.conv.as<float>(), conv_.as<float>(), stream_, ns);
+    launch_delta_prep(conv_.as<float>(), W, n, c.key_heads, c.dk, H, base + off[2], base + off[3], ldr,
+                      L.decay_rate.as<float>(), L.dt.as<float>(), decay_.as<float>(), beta_.as<float>(), stream_);
+    if (past)
+      launch_broadcast_copy(seg_state_.ptr, past->state.ptr, sbytes, ns, stream_);
+    else
+      DG_CUDA(cudaMemsetAsync(seg_state_.ptr, 0, sbytes * ns, stream_));
+    DeltaArgs da{};
+    da.q = conv_.as<float>();
+    da.k = conv_.as<float>() + c.kd();
+    da.v = conv_.as<float>() + 2 * c.kd();
+    da.ld_qk = da.ld_v = W;
+    da.bs_qkv = size_t(sl) * W;
+    da.decay = decay_.as<float>();
+    da.beta = beta_.as<float>();
+    da.log_decay = 1;
+    da.ld_gb = H;
+    da.bs_gb = size_t(sl) * H;
+    da.n = sl;
+    da.key_heads = c.key_heads;
+    da.value_heads = H;
+    da.dv = c.dv;
+    da.state = seg_state_.as<float>();
+    da.bs_state = sbytes / 4;
+    da.o = o_.as<float>();
+    da.ldo = H * c.dv;
+    da.bs_o = size_t(sl) * H * c.dv;
+    // As for one sequence: the chunked form in fast mode for more than one
+    // chunk (when the workspace holds every sequence's chunks), else the
+    // token recurrence.
+    if (!exact && delta_ws_.ptr && sl > kDeltaChunk &&
+        delta_chunk_workspace_bytes(ns, H, sl) <= delta_ws_.bytes)
+      launch_delta_chunked(da, ns, delta_ws_.ptr, delta_ws_.bytes, stream_);
+    else
+      launch_delta_rec128(da, ns, stream_);
+    const bool q = precision_ == kInt8Compute;
+    launch_gated_norm_quant(o_.as<float>(), base + off[1], ldr, n, H, c.dv, L.norm.as<float>(), c.eps,
+                            ofin_.as<float>(), xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);
+    return;
+  }
   launch_conv_silu(raw, ldr, n, tail, tail_rows, start, W, k, L.conv.as<float>(), conv_.as<float>(), stream_);
   launch_delta_prep(conv_.as<float>(), W, n, c.key_heads, c.dk, H, base + off[2], base + off[3], ldr,
                     L.decay_rate.as<float>(), L.dt.as<float>(), decay_.as<float>(), beta_.as<float>(), stream_);
-  const size_t sbytes = size_t(H) * c.dk * c.dv * 4;
   if (past)
     DG_CUDA(cudaMemcpyAsync(state_[i].ptr, past->state.ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
   else
@@ -158,15 +201,30 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   int kin;
   if (L.full) {
     const int d = c.head_dim, kw = c.kw();
-    if (past) {
-      DG_CUDA(cudaMemcpyAsync(kcache_[i].ptr, past->k.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
-      DG_CUDA(cudaMemcpyAsync(vcache_[i].ptr, past->v.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+    if (seg_len_) {
+      // The prefix's keys are read in place; the sequences' own go to kseg_/vseg_.
+      launch_qk_norm_rope(proj, ld_proj_, n, c.heads, c.kv_heads, d, L.q_norm.as<float>(), L.k_norm.as<float>(),
+                          c.eps, rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kseg_.as<float>(),
+                          vseg_.as<float>(), stream_, seg_len_);
+      launch_attention(qbuf_.as<float>(), past ? past->k.as<float>() : kseg_.as<float>(),
+                       past ? past->v.as<float>() : vseg_.as<float>(), proj, ld_proj_, n, start, c.heads, c.kv_heads,
+                       d, att_.as<float>(), exact, stream_, seg_len_, kseg_.as<float>(), vseg_.as<float>());
+    } else {
+      if (past) {
+        DG_CUDA(cudaMemcpyAsync(kcache_[i].ptr, past->k.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+        DG_CUDA(cudaMemcpyAsync(vcache_[i].ptr, past->v.ptr, size_t(start) * kw * 4, cudaMemcpyDeviceToDevice, stream_));
+      }
+      launch_qk_norm_rope(proj, ld_proj_, n, c.heads, c.kv_heads, d, L.q_norm.as<float>(), L.k_norm.as<float>(),
+                          c.eps, rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
+                          vcache_[i].as<float>(), stream_);
+      if (!exact && attn_tc_ && attn_ws_.ptr)
+        launch_attention_tc(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n,
+                            start, c.heads, c.kv_heads, d, att_.as<float>(), attn_ws_.as<float>(), attn_ws_.bytes / 4,
+                            status(), stream_);
+      else
+        launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
+                         c.heads, c.kv_heads, d, att_.as<float>(), exact, stream_);
     }
-    launch_qk_norm_rope(proj, ld_proj_, n, c.heads, c.kv_heads, d, L.q_norm.as<float>(), L.k_norm.as<float>(), c.eps,
-                        rope_.as<float>(), rope_half_, start, qbuf_.as<float>(), kcache_[i].as<float>(),
-                        vcache_[i].as<float>(), stream_);
-    launch_attention(qbuf_.as<float>(), kcache_[i].as<float>(), vcache_[i].as<float>(), proj, ld_proj_, n, start,
-                     c.heads, c.kv_heads, d, att_.as<float>(), exact, stream_);
     launch_norm_quant(att_.as<float>(), c.qw(), n, c.qw(), nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(),
                       xs_.as<float>(), ldxs_, status(), stream_);
     dump_codes(n, c.qw());
@@ -402,14 +460,63 @@ void Engine::forward(const uint32_t* ids, int n, const Prefix* past, bool captur
   if (capture) *captured = std::move(cap);
 }
 
-void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* logits_out) {
+bool Engine::segments_supported() const {
+  return fast_ && c_.head_dim == 256 && c_.dk == 128 && c_.dv == 128 && (c_.kw() * 4) % 16 == 0;
+}
+
+void Engine::forward_segments(const uint32_t* ids, int seg_len, int segs, const Prefix* past, float* hidden_out) {
+  if (!finalized_) throw DgError("engine is not finalized");
+  if (!segments_supported()) throw DgError("segmented forwards need the 2B-shaped tcgen05 path");
+  if (segs == 1) return forward(ids, seg_len, past, false, hidden_out, nullptr);
+  const int start = past ? past->len : 0;
+  if (seg_len <= 0 || segs <= 0 || start + seg_len > 4096)
+    throw DgError("token sequence must contain 1\xe2\x80\x93" "4096 tokens");
+  const int n = seg_len * segs;
+  if (size_t(seg_len) * segs > size_t(max_tokens_)) throw DgError("token sequence exceeds the engine's max_tokens workspace");
+  for (int t = 0; t < n; ++t)
+    if (ids[t] >= uint32_t(c_.vocab)) throw DgError("token " + std::to_string(ids[t]) + " outside vocabulary");
+  if (past && int(past->layers.size()) != c_.layers) throw DgError("prefix cache does not match the layer types");
+  if (past)
+    for (int i = 0; i < c_.layers; ++i)
+      if (past->layers[i].full != layers_[i].full) throw DgError("prefix cache does not match the layer types");
+  DG_CUDA(cudaSetDevice(device_));
+  const size_t sbytes = size_t(c_.value_heads) * c_.dk * c_.dv * 4;
+  if (seg_state_.bytes < sbytes * segs) seg_state_ = DevBuf(sbytes * segs);
+  const uint64_t launches0 = launch_count();
+  DG_CUDA(cudaMemcpyAsync(ids_.ptr, ids, size_t(n) * 4, cudaMemcpyHostToDevice, stream_));
+  DG_CUDA(cudaMemsetAsync(status_.ptr, 0, sizeof(DeviceStatus), stream_));
+  gemm_ops_pending_.clear();
+  fwd_ops_all_ = 0.0;
+  fwd_proj_ = 0;
+  DG_CUDA(cudaEventRecord(ev0_, stream_));
+  seg_len_ = seg_len;
+  segs_ = segs;
+  try {
+    run_layers(n, start, past, nullptr);
+  } catch (...) {
+    seg_len_ = 0;
+    segs_ = 1;
+    throw;
+  }
+  seg_len_ = 0;
+  segs_ = 1;
+  DG_CUDA(cudaEventRecord(ev1_, stream_));
+  if (hidden_out)
+    DG_CUDA(cudaMemcpyAsync(hidden_out, x_.ptr, size_t(n) * c_.hidden * 4, cudaMemcpyDeviceToHost, stream_));
+  check_status();
+  DG_CUDA(cudaEventElapsedTime(&last_forward_ms, ev0_, ev1_));
+  collect_gemm_timing();
+  last_launches = int(launch_count() - launches0);
+}
+
+void Engine::head_logits(int rows, const size_t* positions, int n_pos, float* logits_out, int row_base) {
   if (c_.pointer_dim <= 0) throw DgError("engine has no pointer head");
   if (n_pos <= 0 || n_pos + 1 > 512) throw DgError("invalid encoding positions or window");
   std::vector<int> idx(n_pos + 1);
-  idx[0] = rows - 1;
+  idx[0] = row_base + rows - 1;
   for (int i = 0; i < n_pos; ++i) {
     if (positions[i] >= size_t(rows)) throw DgError("invalid encoding positions or window");
-    idx[i + 1] = int(positions[i]);
+    idx[i + 1] = row_base + int(positions[i]);
   }
   const int H = c_.hidden, P = c_.pointer_dim;
   DG_CUDA(cudaMemcpyAsync(hrow_idx_.ptr, idx.data(), idx.size() * 4, cudaMemcpyHostToDevice, stream_));

@@ -148,6 +148,8 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   // DG_CUDA_GRAPHS=0 launches every forward kernel by kernel (A/B timing).
   if (const char* g = std::getenv("DG_CUDA_GRAPHS")) graphs_on_ = std::atoi(g) != 0;
   if (const char* o = std::getenv("DG_LORA_OVERLAP")) lora_overlap_ = std::atoi(o) != 0;
+  if (const char* b = std::getenv("DG_BATCH_QUESTIONS")) batch_questions = std::atoi(b) != 0;
+  if (const char* a = std::getenv("DG_ATTN_TC")) attn_tc_ = std::atoi(a) != 0;
 }
 
 Engine::~Engine() {

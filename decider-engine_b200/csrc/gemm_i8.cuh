@@ -62,16 +62,6 @@ struct GemmArgs {
   int splits;              // set by launch_gemm_i8 (1: no split)
 };
 
-// Offset accumulators: every group accumulator holds the bits of 1.5 * 2^23
-// (0x4B400000) before its group's MMAs, which then all accumulate, so the
-// int32 result already reads as the float 1.5 * 2^23 + dot. The promotion
-// warps write the offset back (tcgen05.st) right after reading a group, in
-// place of an integer add per element.
-#ifndef DG_GEMM_OFFSET_ACC
-#define DG_GEMM_OFFSET_ACC 0
-#endif
-constexpr bool kOffsetAcc = DG_GEMM_OFFSET_ACC != 0;
-
 template <int BN_>
 struct GemmShape {
   static_assert(BN_ == 64 || BN_ == 128, "tile width");
@@ -345,8 +335,7 @@ __global__ void __launch_bounds__(576, 1)
           // The group's first MMA overwrites the accumulator, the second adds.
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk)
-            mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc,
-                   (kk || kOffsetAcc) ? 1u : 0u);
+            mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, kk);
           mma_commit(&tfull[b]);
         }
       }
@@ -394,16 +383,6 @@ __global__ void __launch_bounds__(576, 1)
     // (0x4B400000) to the dot (|dot| <= 64 * 128 * 128 < 2^22) gives the bits of
     // the float 1.5 * 2^23 + dot, so one subtraction of 1.5 * 2^23 is left.
     constexpr uint32_t kOffsetBits = 0x4B400000u;
-    if constexpr (kOffsetAcc) {
-      // This warp's columns of every accumulator start at the offset.
-#pragma unroll
-      for (int b = 0; b < NBUF; ++b)
-#pragma unroll
-        for (int c = 0; c < HALF / 16; ++c) tmem_fill_32x32b_x16(lane_addr + uint32_t(b * BN + 16 * c), kOffsetBits);
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-    }
     if (lane == 0) {
 #pragma unroll
       for (int b = 0; b < NBUF; ++b) mbar_arrive(&tempty[b]);  // every accumulator starts free
@@ -438,83 +417,57 @@ __global__ void __launch_bounds__(576, 1)
         static_assert(GB * CPG == 2, "two loads per TMEM wait");
         uint32_t d[2][16];
         const uint32_t a0 = lane_addr + uint32_t(((2 * ks + j0) % NBUF) * BN);
-        const uint32_t a1 = GB == 2 ? lane_addr + uint32_t(((2 * ks + j0 + 1) % NBUF) * BN) : a0 + 16u;
-        tmem_ld16x2_sync(a0, a1, d[0], d[1]);
-        if constexpr (!kOffsetAcc) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
+        tmem_ld16x2_sync(a0, GB == 2 ? lane_addr + uint32_t(((2 * ks + j0 + 1) % NBUF) * BN) : a0 + 16u, d[0], d[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
 #pragma unroll
-            for (int jj = 0; jj < GB; ++jj) mbar_arrive(&tempty[(2 * ks + j0 + jj) % NBUF]);
-          }
+          for (int jj = 0; jj < GB; ++jj) mbar_arrive(&tempty[(2 * ks + j0 + jj) % NBUF]);
         }
-        // The int32 accumulators read as floats once the offset bits are in:
-        // added here per element, or already there (offset accumulators).
-        {
-          constexpr uint32_t add_bits = kOffsetAcc ? 0u : kOffsetBits;
 #pragma unroll
-          for (int jj = 0; jj < GB; ++jj) {
-            const int j = j0 + jj, g = 2 * ks + j;
-            const float xs = xsp[j * BM + row];
-            // FMA mode folds the conversion into the row scale: with xs rounded
-            // to 22 significant bits, 1.5 * 2^23 * xs' = 3 * 2^22 * xs' is exact,
-            // so fma(1.5 * 2^23 + dot, xs', -1.5 * 2^23 * xs') = dot * xs'
-            // rounded once; the column scale then enters by one more fma. Two
-            // FP32 operations per element instead of three (xs' differs from xs
-            // by at most 2^-22 relative).
-            const float xsr = __uint_as_float((__float_as_uint(xs) + 2u) & ~3u);
-            const float2 xs2 = make_float2(xsr, xsr);
-            const float cxs = __fmul_rn(-12582912.0f, xsr);
-            const float2 cxs2 = make_float2(cxs, cxs);
+        for (int jj = 0; jj < GB; ++jj) {
+          const int j = j0 + jj, g = 2 * ks + j;
+          const float xs = xsp[j * BM + row];
+          // FMA mode folds the conversion into the row scale: with xs rounded
+          // to 22 significant bits, 1.5 * 2^23 * xs' = 3 * 2^22 * xs' is exact,
+          // so fma(1.5 * 2^23 + dot, xs', -1.5 * 2^23 * xs') = dot * xs'
+          // rounded once; the column scale then enters by one more fma. Two
+          // FP32 operations per element instead of three (xs' differs from xs
+          // by at most 2^-22 relative).
+          const float xsr = __uint_as_float((__float_as_uint(xs) + 2u) & ~3u);
+          const float2 xs2 = make_float2(xsr, xsr);
+          const float cxs = __fmul_rn(-12582912.0f, xsr);
+          const float2 cxs2 = make_float2(cxs, cxs);
 #pragma unroll
-            for (int c = 0; c < CPG; ++c) {
-              const uint32_t(&cur)[16] = d[jj * CPG + c];
-              if (DUMP && m < p.M) {
-                int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
+          for (int c = 0; c < CPG; ++c) {
+            const uint32_t(&cur)[16] = d[jj * CPG + c];
+            if (DUMP && m < p.M) {
+              int4* dd = reinterpret_cast<int4*>(p.dots + (size_t(g) * p.M + m) * p.N + n0 + half * HALF + c * 16);
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4)
-                  dd[j4] = make_int4(int(cur[j4 * 4] + add_bits - kOffsetBits), int(cur[j4 * 4 + 1] + add_bits - kOffsetBits),
-                                     int(cur[j4 * 4 + 2] + add_bits - kOffsetBits), int(cur[j4 * 4 + 3] + add_bits - kOffsetBits));
-              }
+              for (int j4 = 0; j4 < 4; ++j4)
+                dd[j4] = make_int4(int(cur[j4 * 4]), int(cur[j4 * 4 + 1]), int(cur[j4 * 4 + 2]), int(cur[j4 * 4 + 3]));
+            }
 #pragma unroll
-              for (int j4 = 0; j4 < 4; ++j4) {
-                const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
-                const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
+            for (int j4 = 0; j4 < 4; ++j4) {
+              const float4 w4 = reinterpret_cast<const float4*>(wsp + j * BN + c * 16)[j4];
+              const float2 wlo = make_float2(w4.x, w4.y), whi = make_float2(w4.z, w4.w);
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const int k = j4 * 4 + e * 2;
-                  float2 fd =
-                      make_float2(__uint_as_float(cur[k] + add_bits), __uint_as_float(cur[k + 1] + add_bits));
-                  float2& a2 = acc[(c * 16 + k) / 2];
-                  const float2 w2 = e ? whi : wlo;
-                  if (EXACT) {
-                    // Reference order with scalar IEEE operations (src/int8.rs:58):
-                    // sum + float(dot) * (xs * ws), rounded after every step.
-                    a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
-                    a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
-                  } else {
-                    a2 = fma2_rn(fma2_rn(fd, xs2, cxs2), w2, a2);
-                  }
+              for (int e = 0; e < 2; ++e) {
+                const int k = j4 * 4 + e * 2;
+                float2 fd =
+                    make_float2(__uint_as_float(cur[k] + kOffsetBits), __uint_as_float(cur[k + 1] + kOffsetBits));
+                float2& a2 = acc[(c * 16 + k) / 2];
+                const float2 w2 = e ? whi : wlo;
+                if (EXACT) {
+                  // Reference order with scalar IEEE operations (src/int8.rs:58):
+                  // sum + float(dot) * (xs * ws), rounded after every step.
+                  a2.x = __fadd_rn(a2.x, __fmul_rn(__fadd_rn(fd.x, -12582912.0f), __fmul_rn(xs, w2.x)));
+                  a2.y = __fadd_rn(a2.y, __fmul_rn(__fadd_rn(fd.y, -12582912.0f), __fmul_rn(xs, w2.y)));
+                } else {
+                  a2 = fma2_rn(fma2_rn(fd, xs2, cxs2), w2, a2);
                 }
               }
             }
-          }
-        }
-        if constexpr (kOffsetAcc) {
-          // Put the offset back for the accumulators' next groups once their
-          // values are consumed (the stores' data registers are then free),
-          // and hand them to the MMA issuer after the stores complete.
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tmem_fill_32x32b_x8(a0 + 8u * h, kOffsetBits);
-            tmem_fill_32x32b_x8(a1 + 8u * h, kOffsetBits);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-#pragma unroll
-            for (int jj = 0; jj < GB; ++jj) mbar_arrive(&tempty[(2 * ks + j0 + jj) % NBUF]);
           }
         }
       }

@@ -28,17 +28,21 @@ __device__ __forceinline__ float warp_max(float v) {
 // (i, i + half) from the table rope[pos][i] = (sin, cos), and append the
 // normalised, rotated k and the raw v at position start + t. One warp per
 // vector (heads q vectors + kv_heads k vectors + kv_heads v vectors per token).
+// Segmented forwards (seg_len > 0: rows are consecutive sequences of seg_len
+// tokens, each continuing the same `start` positions) put row t at position
+// start + t % seg_len and its k and v at row t of kcache / vcache, the
+// segment-local buffers the attention reads next to the shared prefix.
 __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int ldq, int heads, int kv_heads, int d,
                                     const float* __restrict__ qn, const float* __restrict__ kn, float eps,
                                     const float* __restrict__ rope, int half, int start, float* __restrict__ q_out,
-                                    float* __restrict__ kcache, float* __restrict__ vcache) {
+                                    float* __restrict__ kcache, float* __restrict__ vcache, int seg_len) {
   griddep_wait();
   griddep_launch();
   extern __shared__ float buf[];  // [warps][d]
   const int t = blockIdx.x, warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
   float* x = buf + warp * d;
   const float* row = qkv + size_t(t) * ldq;
-  const int pos = start + t, kw = kv_heads * d;
+  const int pos = start + (seg_len ? t % seg_len : t), kvrow = seg_len ? t : pos, kw = kv_heads * d;
   for (int v = warp; v < heads + 2 * kv_heads; v += nw) {
     const float* src;
     const float* g = nullptr;
@@ -51,11 +55,11 @@ __global__ void qk_norm_rope_kernel(const float* __restrict__ qkv, int ldq, int 
       const int kh = v - heads;
       src = row + size_t(heads) * 2 * d + kh * d;
       g = kn;
-      dst = kcache + size_t(pos) * kw + kh * d;
+      dst = kcache + size_t(kvrow) * kw + kh * d;
     } else {
       const int kh = v - heads - kv_heads;
       src = row + size_t(heads) * 2 * d + kw + kh * d;
-      dst = vcache + size_t(pos) * kw + kh * d;
+      dst = vcache + size_t(kvrow) * kw + kh * d;
     }
     float ss = 0.0f;
     for (int i = lane; i < d; i += 32) {
@@ -228,11 +232,20 @@ __device__ __forceinline__ void att_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+//
+// Segmented forwards (seg_len > 0): the rows are nseg consecutive sequences of
+// seg_len tokens, each continuing the same `offset` prefix positions. Keys
+// below `offset` come from kc / vc (the shared prefix), the rest from the
+// sequence's own rows of kc_own / vc_own; query block b of the grid is block
+// b / nseg (latest first) of sequence b % nseg. A sequence's key blocks are
+// the same absolute positions as in a forward of that sequence alone, so each
+// row's arithmetic is the same.
 template <int NS>
 __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
     attention256_split_kernel(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                               const float* __restrict__ gate_src, int ld_gate, int n, int offset, int heads,
-                              int kv_heads, float* __restrict__ out) {
+                              int kv_heads, float* __restrict__ out, int seg_len, int nseg,
+                              const float* __restrict__ kc_own, const float* __restrict__ vc_own) {
   griddep_wait();
   griddep_launch();
   extern __shared__ __align__(16) float sm[];
@@ -243,8 +256,10 @@ __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
   float* ML = PT + TK * PLD;    // [2][TQ]: CTA 1's running max and sum
   cg::cluster_group cluster = cg::this_cluster();
   const int part = int(cluster.block_rank());
-  const int nrb = (n + TQ - 1) / TQ;
-  const int rb = nrb - 1 - int(blockIdx.x / NS), h = blockIdx.y, kh = h / (heads / kv_heads);
+  if (seg_len) n = seg_len;  // rows of this block's sequence
+  const int nrb = (n + TQ - 1) / TQ, b = int(blockIdx.x / NS);
+  const int seg = seg_len ? b % nseg : 0, row0 = seg * n;  // the sequence's first row in q, gate and out
+  const int rb = nrb - 1 - (seg_len ? b / nseg : b), h = blockIdx.y, kh = h / (heads / kv_heads);
   const int t0 = rb * TQ, tid = threadIdx.x, rg = tid / 16, kg = tid % 16;
   const int kw = kv_heads * AD, L = offset + n;
   const int last_key = min(L - 1, offset + t0 + TQ - 1), nkb = last_key / TK + 1;
@@ -253,20 +268,23 @@ __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
   // continuation reproduces the full forward bit for bit.
   const int kb_begin = part, kb_end = nkb;
   const float scale = 1.0f / sqrtf(float(AD));
-  auto load_rows = [&](float* dst, int ld, const float* src, int row0) {
+  auto load_rows = [&](float* dst, int ld, const float* src, const float* own, int k0) {
     for (int i = tid; i < TK * (AD / 4); i += 256) {
-      const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, s = row0 + r;
-      att_cp16(dst + r * ld + c, s < L ? src + size_t(s) * kw + kh * AD + c : src, s < L);
+      const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, s = k0 + r;
+      const float* p = src;
+      if (s < L) p = (!seg_len || s < offset) ? src + size_t(s) * kw + kh * AD + c
+                                              : own + size_t(row0 + s - offset) * kw + kh * AD + c;
+      att_cp16(dst + r * ld + c, p, s < L);
     }
   };
   for (int i = tid; i < TQ * (AD / 4); i += 256) {
     const int r = i / (AD / 4), c = (i % (AD / 4)) * 4, t = t0 + r;
-    att_cp16(Qs + r * TLD + c, t < n ? q + (size_t(t) * heads + h) * AD + c : q, t < n);
+    att_cp16(Qs + r * TLD + c, t < n ? q + (size_t(row0 + t) * heads + h) * AD + c : q, t < n);
   }
   if (kb_begin < kb_end) {
-    load_rows(Ks, TLD, kc, kb_begin * TK);
+    load_rows(Ks, TLD, kc, kc_own, kb_begin * TK);
     att_commit();
-    load_rows(Vs, AD, vc, kb_begin * TK);
+    load_rows(Vs, AD, vc, vc_own, kb_begin * TK);
   }
   att_commit();
   float o[2][16], mrow[2], lrow[2];
@@ -303,7 +321,7 @@ __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
     }
     __syncthreads();  // every thread is done with Ks
     if (kb + NS < kb_end) {
-      load_rows(Ks, TLD, kc, k0 + NS * TK);
+      load_rows(Ks, TLD, kc, kc_own, k0 + NS * TK);
       att_commit();
       att_wait<1>();  // this block's V has landed
     } else {
@@ -359,7 +377,7 @@ __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
     }
     __syncthreads();  // every thread is done with Vs and PT
     if (kb + NS < kb_end) {
-      load_rows(Vs, AD, vc, k0 + NS * TK);
+      load_rows(Vs, AD, vc, vc_own, k0 + NS * TK);
       att_commit();
     }
   }
@@ -409,8 +427,8 @@ __global__ void __cluster_dims__(NS, 1, 1) __launch_bounds__(256)
       }
       const float inv = 1.0f / lsum;
       if (t >= n) continue;
-      const float* g = gate_src + size_t(t) * ld_gate + size_t(h) * 2 * AD + AD;
-      float* dst = out + (size_t(t) * heads + h) * AD;
+      const float* g = gate_src + size_t(row0 + t) * ld_gate + size_t(h) * 2 * AD + AD;
+      float* dst = out + (size_t(row0 + t) * heads + h) * AD;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = 4 * kg + 64 * j;
@@ -564,24 +582,27 @@ __global__ void head_dot_kernel(const float* __restrict__ q, const float* __rest
 
 void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_heads, int d, const float* qn,
                          const float* kn, float eps, const float* rope, int half, int start, float* q_out,
-                         float* kcache, float* vcache, cudaStream_t s) {
+                         float* kcache, float* vcache, cudaStream_t s, int seg_len) {
   if (n <= 0) return;
+  if (seg_len < 0 || (seg_len && n % seg_len)) throw CudaError("qk_norm_rope: rows must be whole segments");
   launch_pdl(qk_norm_rope_kernel, dim3(n), dim3(256), 8 * d * sizeof(float), s, qkv, ldq, heads, kv_heads, d, qn, kn, eps, rope, half,
-                                                            start, q_out, kcache, vcache);
+                                                            start, q_out, kcache, vcache, seg_len);
   DG_CUDA(cudaGetLastError());
 }
 
 template <int NS>
 void launch_attention_split(const float* q, const float* kcache, const float* vcache, const float* gate_src,
-                            int ld_gate, int n, int offset, int heads, int kv_heads, float* out, cudaStream_t s) {
+                            int ld_gate, int n, int offset, int heads, int kv_heads, float* out, cudaStream_t s,
+                            int seg_len, const float* kc_own, const float* vc_own) {
   static std::atomic<uint64_t> configured{0};
   once_per_device(configured, [] {
     DG_CUDA(cudaFuncSetAttribute(attention256_split_kernel<NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  ATT_SMEM));
   });
-  dim3 grid(NS * ((n + TQ - 1) / TQ), heads);  // clusters of NS along x
+  const int nl = seg_len ? seg_len : n, nseg = seg_len ? n / seg_len : 1;
+  dim3 grid(NS * nseg * ((nl + TQ - 1) / TQ), heads);  // clusters of NS along x
   launch_pdl(attention256_split_kernel<NS>, dim3(grid), dim3(256), ATT_SMEM, s, q, kcache, vcache, gate_src, ld_gate,
-             n, offset, heads, kv_heads, out);
+             n, offset, heads, kv_heads, out, seg_len, nseg, kc_own, vc_own);
 }
 
 // Cluster size of the split kernel. Reference order keeps pairs, so that a
@@ -590,27 +611,38 @@ void launch_attention_split(const float* q, const float* kcache, const float* vc
 // grows (4, then 8) while the grid has fewer than two CTAs per SM and every
 // CTA keeps at least two key blocks: a 64-token question after a 3584-token
 // prefix is 2 query blocks x 8 heads, 32 CTAs in pairs.
-int attention_split_ways(int n, int offset, int heads, bool exact) {
+int attention_split_ways(int n, int offset, int heads, bool exact, int nseg) {
   if (exact) return 2;
-  const int nrb = (n + TQ - 1) / TQ, nkb = (offset + n + TK - 1) / TK;
+  const int nrb = nseg * ((n + TQ - 1) / TQ), nkb = (offset + n + TK - 1) / TK;
   int ns = 2;
   while (ns < 8 && ns * nrb * heads < 2 * 148 && nkb / (2 * ns) >= 2) ns *= 2;
   return ns;
 }
 
 void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src, int ld_gate,
-                      int n, int offset, int heads, int kv_heads, int d, float* out, bool exact, cudaStream_t s) {
+                      int n, int offset, int heads, int kv_heads, int d, float* out, bool exact, cudaStream_t s,
+                      int seg_len, const float* kc_own, const float* vc_own) {
   if (n <= 0) return;
   const bool aligned = reinterpret_cast<uintptr_t>(q) % 16 == 0 && reinterpret_cast<uintptr_t>(kcache) % 16 == 0 &&
-                       reinterpret_cast<uintptr_t>(vcache) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
+                       reinterpret_cast<uintptr_t>(vcache) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(kc_own) % 16 == 0 && reinterpret_cast<uintptr_t>(vc_own) % 16 == 0;
+  if (seg_len) {
+    // Segmented forwards have only the head_dim-256 kernel.
+    if (seg_len < 0 || n % seg_len || d != AD || !aligned || !kc_own || !vc_own)
+      throw CudaError("attention: segmented rows need head_dim 256, aligned buffers and whole segments");
+  }
   if (d == AD && aligned) {
-    const int ns = attention_split_ways(n, offset, heads, exact);
+    const int nl = seg_len ? seg_len : n, nseg = seg_len ? n / seg_len : 1;
+    const int ns = attention_split_ways(nl, offset, heads, exact, nseg);
     if (ns == 8)
-      launch_attention_split<8>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
+      launch_attention_split<8>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s, seg_len, kc_own,
+                                vc_own);
     else if (ns == 4)
-      launch_attention_split<4>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
+      launch_attention_split<4>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s, seg_len, kc_own,
+                                vc_own);
     else
-      launch_attention_split<2>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s);
+      launch_attention_split<2>(q, kcache, vcache, gate_src, ld_gate, n, offset, heads, kv_heads, out, s, seg_len, kc_own,
+                                vc_own);
   } else if (d == AD) {
     const int smem = (ABQ * AD + AD * (ABK + 1) + ABK * AD) * sizeof(float);
     static std::atomic<uint64_t> configured{0};

@@ -3,6 +3,8 @@
 #include <cstdint>
 #include <cfloat>
 
+#include <algorithm>
+
 #include "launch.h"
 
 namespace dg {
@@ -26,6 +28,8 @@ __global__ void conv_silu_kernel(const float* __restrict__ raw, int ldr, const f
   griddep_launch();
   const int c = blockIdx.x * blockDim.x + threadIdx.x, t0 = blockIdx.y * CONV_T;
   if (c >= W) return;
+  raw += size_t(blockIdx.z) * n * ldr;  // segment z of equal-length sequences (same tail)
+  out += size_t(blockIdx.z) * n * W;
   float w[CONV_KMAX];
   float win[CONV_T + CONV_KMAX - 1];
 #pragma unroll
@@ -259,6 +263,8 @@ __global__ void __launch_bounds__(128) conv_silu4_kernel(const float* __restrict
   griddep_launch();
   const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x), t0 = blockIdx.y * CONV_T;
   if (c >= W) return;
+  raw += size_t(blockIdx.z) * n * ldr;  // segment z of equal-length sequences (same tail)
+  out += size_t(blockIdx.z) * n * W;
   float4 w[CONV_KMAX];
 #pragma unroll
   for (int j = 0; j < CONV_KMAX; ++j)
@@ -294,18 +300,18 @@ __global__ void __launch_bounds__(128) conv_silu4_kernel(const float* __restrict
   }
 }
 void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W, int kernel,
-                      const float* taps, float* out, cudaStream_t s) {
-  if (n <= 0) return;
+                      const float* taps, float* out, cudaStream_t s, int segs) {
+  if (n <= 0 || segs <= 0) return;
   if (kernel < 1 || kernel > CONV_KMAX) throw CudaError("conv: kernel width must be 1..8");
   const bool vec = W % 4 == 0 && ldr % 4 == 0 && reinterpret_cast<uintptr_t>(raw) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(taps) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
                    (tail_rows == 0 || reinterpret_cast<uintptr_t>(tail) % 16 == 0);
   if (vec) {
-    dim3 grid((W / 4 + 127) / 128, (n + CONV_T - 1) / CONV_T);
+    dim3 grid((W / 4 + 127) / 128, (n + CONV_T - 1) / CONV_T, segs);
     launch_pdl(conv_silu4_kernel, dim3(grid), dim3(128), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps,
                out);
   } else {
-    dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T);
+    dim3 grid((W + 255) / 256, (n + CONV_T - 1) / CONV_T, segs);
     launch_pdl(conv_silu_kernel, dim3(grid), dim3(256), 0, s, raw, ldr, tail, tail_rows, n, start, W, kernel, taps,
                out);
   }
@@ -360,6 +366,26 @@ void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s) {
   });
   dim3 grid(a.value_heads * (a.dv / REC_COLS), batch);
   launch_pdl(delta_rec128_kernel, dim3(grid), dim3(128), smem, s, a);
+  DG_CUDA(cudaGetLastError());
+}
+
+__global__ void broadcast_copy_kernel(float4* __restrict__ dst, const float4* __restrict__ src, size_t n4, int copies) {
+  griddep_wait();
+  griddep_launch();
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n4; i += size_t(gridDim.x) * blockDim.x) {
+    const float4 v = src[i];
+    for (int c = 0; c < copies; ++c) dst[size_t(c) * n4 + i] = v;
+  }
+}
+
+void launch_broadcast_copy(void* dst, const void* src, size_t bytes, int copies, cudaStream_t s) {
+  if (!bytes || copies <= 0) return;
+  if (bytes % 16 || reinterpret_cast<uintptr_t>(dst) % 16 || reinterpret_cast<uintptr_t>(src) % 16)
+    throw CudaError("broadcast_copy: 16-byte aligned whole float4 rows only");
+  const size_t n4 = bytes / 16;
+  const int blocks = int(std::min<size_t>((n4 + 255) / 256, 592));
+  launch_pdl(broadcast_copy_kernel, dim3(blocks), dim3(256), 0, s, reinterpret_cast<float4*>(dst),
+             reinterpret_cast<const float4*>(src), n4, copies);
   DG_CUDA(cudaGetLastError());
 }
 

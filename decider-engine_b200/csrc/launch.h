@@ -93,7 +93,10 @@ void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids,
 // Causal depthwise conv (tap-major weights [k][W]) + SiLU, continuing from a
 // tail of `tail_rows` raw rows that precede position `start`.
 void launch_conv_silu(const float* raw, int ldr, int n, const float* tail, int tail_rows, int start, int W,
-                      int kernel, const float* taps, float* out, cudaStream_t s);
+                      int kernel, const float* taps, float* out, cudaStream_t s, int segs = 1);
+// dst[i] = src for i < copies (bytes % 16 == 0, 16-byte aligned): one prefix
+// state per sequence of a segmented forward.
+void launch_broadcast_copy(void* dst, const void* src, size_t bytes, int copies, cudaStream_t s);
 // Per token: q/k L2 norms (q also / sqrt(dk)), log decay g = rate * softplus(a + dt)
 // (the decay is exp(g)), beta = sigmoid(b). Normalises conv[:, :2kd] in place.
 void launch_delta_prep(float* conv, int W, int n, int key_heads, int dk, int value_heads, const float* a,
@@ -129,15 +132,63 @@ constexpr int kDeltaChunk = 64;  // tokens per chunk of the chunked form
 void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s);
 void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
 // Split q|gate per head, centred RMSNorm of q and k, partial RoPE from the
-// precomputed table, append k/v to the cache at `start`.
+// precomputed table, append k/v to the cache at `start`. seg_len > 0: the n
+// rows are n / seg_len sequences of seg_len tokens each at positions start..,
+// and row t's k/v go to row t of kcache / vcache.
 void launch_qk_norm_rope(const float* qkv, int ldq, int n, int heads, int kv_heads, int d, const float* qn,
                          const float* kn, float eps, const float* rope, int half, int start, float* q_out,
-                         float* kcache, float* vcache, cudaStream_t s);
+                         float* kcache, float* vcache, cudaStream_t s, int seg_len = 0);
 // `exact` (reference-order mode) keeps the key split fixed, so prefix
-// continuations stay bit-identical to full forwards.
+// continuations stay bit-identical to full forwards. seg_len > 0 (head_dim
+// 256): n / seg_len sequences of seg_len rows continuing the same `offset`
+// prefix keys in kcache / vcache, their own keys in kc_own / vc_own (row t of
+// the n rows).
 void launch_attention(const float* q, const float* kcache, const float* vcache, const float* gate_src,
                       int ld_gate, int n, int offset, int heads, int kv_heads, int d, float* out, bool exact,
-                      cudaStream_t s);
+                      cudaStream_t s, int seg_len = 0, const float* kc_own = nullptr, const float* vc_own = nullptr);
+// ---- causal attention on the tensor cores, fast mode (attn_tc.cu)
+// C[m][n] = alpha * sum_k A[m][k] * B[n][k] (then + C when accumulate, then
+// * sigmoid(gate[m][n])), FP32 operands as 3 x TF32 on tcgen05. Batch z =
+// outer * inner_count + inner offsets A by outer * a_outer + inner * a_inner,
+// B by outer * b_outer + (inner / b_inner_div) * b_inner, C and the gate
+// alike. diag >= 0: row m sees columns n <= diag + m only; tiles wholly past
+// that are skipped (k_causal = 0), or the K range is cut there (k_causal = 1:
+// the K index is the key). K % 32 == 0; operands 16-byte aligned.
+struct TcGemmArgs {
+  const float* A = nullptr;
+  int lda = 0;
+  long a_outer = 0, a_inner = 0;
+  const float* B = nullptr;
+  int ldb = 0;
+  long b_outer = 0, b_inner = 0;
+  int b_inner_div = 1;
+  float* C = nullptr;
+  int ldc = 0;
+  long c_outer = 0, c_inner = 0;
+  const float* gate = nullptr;
+  int ldg = 0;
+  long g_outer = 0, g_inner = 0;
+  int M = 0, N = 0, K = 0;
+  float alpha = 1.0f;
+  int inner_count = 1;
+  int diag = -1;
+  int k_causal = 0;
+  int accumulate = 0;
+  DeviceStatus* status = nullptr;
+};
+void launch_tc_gemm(const TcGemmArgs& g, int batches, cudaStream_t s);
+// Query rows per pass of launch_attention_tc (bounds its score workspace).
+constexpr int kAttnTcChunk = 1024;
+size_t attention_tc_workspace_floats(int heads, int kv_heads, int d, int max_rows);
+bool attention_tc_supported(int d, int heads, int kv_heads);
+// Gated causal attention of n query rows at positions offset.. against the
+// offset + n keys of kcache / vcache ([keys][kv_heads * d]); q [n][heads][d];
+// the gate is column h * 2d + d + c of gate_src's rows; out [n][heads][d].
+// ws: attention_tc_workspace_floats floats (scores and Vᵀ).
+void launch_attention_tc(const float* q, const float* kc, const float* vc, const float* gate_src, int ld_gate, int n,
+                         int offset, int heads, int kv_heads, int d, float* out, float* ws, size_t ws_floats,
+                         DeviceStatus* st, cudaStream_t s);
+
 // Centred RMSNorm over rows, in place, plus a non-finite check.
 void launch_final_norm(float* x, int M, int K, const float* gamma, float eps, DeviceStatus* st,
                        cudaStream_t s);

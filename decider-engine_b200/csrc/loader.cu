@@ -12,6 +12,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <memory>
 #include <cmath>
 #include <cstring>
 #include <fstream>
@@ -351,11 +352,105 @@ struct Safetensors {
   Safetensors& operator=(const Safetensors&) = delete;
 };
 
+// ---- allocation budgets at the checkpoint boundary (src/loading.rs:27-80).
+// Checked size arithmetic: an overflow is an error, never a wrapped size.
+size_t checked_product(const std::string& name, std::initializer_list<size_t> dims) {
+  size_t n = 1;
+  for (size_t d : dims)
+    if (__builtin_mul_overflow(n, d, &n)) throw std::runtime_error(name + ": dimension product overflow");
+  return n;
+}
+size_t checked_sum(const std::string& name, std::initializer_list<size_t> values) {
+  size_t n = 0;
+  for (size_t v : values)
+    if (__builtin_add_overflow(n, v, &n)) throw std::runtime_error(name + ": dimension sum overflow");
+  return n;
+}
+void within(const std::string& name, size_t bytes, uint64_t limit) {
+  if (bytes > limit || bytes > size_t(INT64_MAX))
+    throw std::runtime_error(name + ": allocation of " + std::to_string(bytes) + " bytes exceeds budget " +
+                             std::to_string(limit));
+}
+
+// WeightBudget (src/loading.rs:52-80): every tensor is charged as FP32 plus
+// its possible group-64 scales, against the per-tensor budget and, with the
+// tensor counted twice (the original plus its conversion scratch), against
+// the aggregate budget shared by every file of the checkpoint.
+struct WeightBudget {
+  LoadLimits limits;
+  size_t used = 0;
+  explicit WeightBudget(const LoadLimits& l) : limits(l) {}
+  void charge(const std::string& name, const std::vector<size_t>& shape) {
+    size_t elements = 1;
+    for (size_t d : shape)
+      if (__builtin_mul_overflow(elements, d, &elements)) throw std::runtime_error(name + ": dimension product overflow");
+    size_t bytes = checked_product(name, {elements, 4});
+    if (shape.size() == 2)
+      bytes = checked_sum(name, {bytes, checked_product(name, {shape[0], (shape[1] + 63) / 64, 4})});
+    within(name, bytes, limits.max_tensor_bytes);
+    used = checked_sum("checkpoint weights", {used, bytes});
+    within("checkpoint weights and conversion scratch", checked_sum(name, {used, bytes}), limits.max_weight_bytes);
+  }
+};
+
 }  // namespace
+
+// Config::validate_layout (src/qwen.rs:37-135): the architecture's weights
+// (FP32 estimates, LoRA included) charged against a fresh budget and the
+// forward workspace bound, all before any payload is read or any device
+// memory is taken.
+void validate_layout(const Config& c, int tokens, int rank, int pointer, const LoadLimits& limits) {
+  const size_t h = size_t(c.hidden);
+  const size_t qw = checked_product("query width", {size_t(c.heads), size_t(c.head_dim)});
+  const size_t kw = checked_product("key/value width", {size_t(c.kv_heads), size_t(c.head_dim)});
+  const size_t kd = checked_product("delta key width", {size_t(c.key_heads), size_t(c.dk)});
+  const size_t vd = checked_product("delta value width", {size_t(c.value_heads), size_t(c.dv)});
+  const size_t qkv = checked_sum("delta QKV width", {checked_product("delta keys", {2, kd}), vd});
+  const size_t recurrent =
+      checked_product("recurrent state", {size_t(c.value_heads), size_t(c.dk), size_t(c.dv)});
+  WeightBudget w(limits);
+  w.charge("embedding", {size_t(c.vocab), h});
+  w.charge("final norm", {h});
+  w.charge("pointer head", {2, size_t(pointer), h});
+  w.charge("pointer norms/biases", {2, checked_sum("pointer norms", {h, size_t(pointer)})});
+  size_t max_width = std::max({h, size_t(c.intermediate), size_t(rank), size_t(pointer)});
+  for (int kind : c.layer_types) {
+    std::vector<std::pair<size_t, size_t>> projections = {
+        {h, size_t(c.intermediate)}, {h, size_t(c.intermediate)}, {size_t(c.intermediate), h}};
+    w.charge("layer norms", {2, h});
+    if (kind == 1) {
+      projections.push_back({h, checked_product("gated query width", {2, qw})});
+      projections.push_back({h, kw});
+      projections.push_back({h, kw});
+      projections.push_back({qw, h});
+      w.charge("attention norms", {2, size_t(c.head_dim)});
+    } else {
+      projections.push_back({h, qkv});
+      projections.push_back({h, vd});
+      projections.push_back({h, size_t(c.value_heads)});
+      projections.push_back({h, size_t(c.value_heads)});
+      projections.push_back({vd, h});
+      w.charge("convolution", {qkv, size_t(c.conv_kernel)});
+      w.charge("delta constants",
+               {checked_sum("delta constants",
+                            {checked_product("delta heads", {2, size_t(c.value_heads)}), size_t(c.dv)})});
+    }
+    for (const auto& io : projections) {
+      w.charge("projection", {io.second, io.first});
+      w.charge("LoRA A", {size_t(rank), io.first});
+      w.charge("LoRA B", {io.second, size_t(rank)});
+      max_width = std::max({max_width, io.first, io.second});
+    }
+  }
+  const size_t activations = checked_product("activation workspace", {size_t(tokens), max_width, 16});
+  const size_t angles = checked_product("rotary workspace", {size_t(tokens), size_t(c.rotary_dim()), 2});
+  const size_t elements = checked_sum("forward workspace", {activations, angles, recurrent});
+  within("forward workspace", checked_product("forward workspace", {elements, 4}), limits.max_workspace_bytes);
+}
 
 // read_config (src/lib.rs:188-222), Config::validate's config checks
 // (src/qwen.rs:133-188) and the adapter checks (src/lib.rs:300-358).
-void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim) {
+void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim, int* max_length_out) {
   std::string dpath = dir + "/strands_decider_config.json";
   if (!exists(dpath)) dpath = dir + "/hobson_config.json";
   const json::Value d = read_json(dpath);
@@ -365,6 +460,7 @@ void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim)
     throw std::runtime_error(
         "native engine requires Qwen3.5-2B-Base, pointer head, LoRA, and default BOS behavior");
   const int max_length = integer(d, "max_length", dpath);
+  if (max_length_out) *max_length_out = max_length;
   pointer_dim = integer(d, "pointer_dim", dpath);
   const double temp = d.get("temperature") ? num(d, "temperature", dpath) : 0.0;
   const double smooth = d.get("ordinal_smoothing") ? num(d, "ordinal_smoothing", dpath) : 0.0;
@@ -423,25 +519,86 @@ void read_checkpoint_config(const std::string& dir, Config& c, int& pointer_dim)
   c.pointer_dim = pointer_dim;
 }
 
+// The base checkpoint's files: model.safetensors, or the distinct files of
+// model.safetensors.index.json's weight_map in name order (Weights::base,
+// src/weights.rs:218-259).
+static std::vector<std::string> base_files(const std::string& dir) {
+  const std::string single = dir + "/base/model.safetensors";
+  if (exists(single)) return {single};
+  const std::string ipath = dir + "/base/model.safetensors.index.json";
+  const json::Value idx = read_json(ipath);
+  const json::Value* map = idx.get("weight_map");
+  if (!map || map->kind != json::Value::Obj) throw std::runtime_error("missing weight_map in base index");
+  std::vector<std::string> files;
+  for (const auto& kv : map->obj) {
+    if (kv.second.kind != json::Value::Str || kv.second.str.empty() || kv.second.str.find('/') != std::string::npos ||
+        kv.second.str.find("..") != std::string::npos)
+      throw std::runtime_error("invalid base shard name");
+    files.push_back(dir + "/base/" + kv.second.str);
+  }
+  std::sort(files.begin(), files.end());
+  files.erase(std::unique(files.begin(), files.end()), files.end());
+  return files;
+}
+
 // Model::load + Head::load (src/lib.rs:287-367): the base tensors without
 // their "model.language_model." prefix, the adapter tensors as stored, the
-// head tensors prefixed "head.".
-void load_checkpoint_tensors(Engine& e, const std::string& dir) {
+// head tensors prefixed "head.". Every file's selected tensors are charged
+// to one WeightBudget from their header shapes before any payload of that
+// file is read (read_tensors, src/weights.rs:316-325), in the reference's
+// order: adapter, head, base.
+// The checkpoint files' budget check alone (no engine, no payload read): run
+// before the engine takes device memory, so an over-budget checkpoint is
+// refused without any allocation.
+void ensure_checkpoint_budget(const std::string& dir, const LoadLimits& limits) {
   const std::string prefix = "model.language_model.";
-  {
-    Safetensors base(dir + "/base/model.safetensors");
-    for (const auto& t : base.entries)
-      if (t.name.compare(0, prefix.size(), prefix) == 0) e.set_tensor(t.name.substr(prefix.size()), t.dtype, t.shape, t.data);
-  }
+  WeightBudget budget(limits);
+  auto charge_all = [&](const Safetensors& f, const std::string* pfx) {
+    for (const auto& t : f.entries) {
+      if (pfx && t.name.compare(0, pfx->size(), *pfx) != 0) continue;
+      budget.charge(t.name, std::vector<size_t>(t.shape.begin(), t.shape.end()));
+    }
+  };
   {
     Safetensors adapter(dir + "/lora/adapter_model.safetensors");
+    charge_all(adapter, nullptr);
     if (adapter.entries.empty()) throw std::runtime_error("empty LoRA adapter");
-    for (const auto& t : adapter.entries) e.set_tensor(t.name, t.dtype, t.shape, t.data);
   }
   {
     Safetensors head(dir + "/head.safetensors");
-    for (const auto& t : head.entries) e.set_tensor("head." + t.name, t.dtype, t.shape, t.data);
+    charge_all(head, nullptr);
   }
+  for (const std::string& f : base_files(dir)) {
+    Safetensors b(f);
+    charge_all(b, &prefix);
+  }
+}
+
+void load_checkpoint_tensors(Engine& e, const std::string& dir, const LoadLimits& limits) {
+  const std::string prefix = "model.language_model.";
+  WeightBudget budget(limits);
+  auto charge_all = [&](const Safetensors& f, const std::string* pfx) {
+    for (const auto& t : f.entries) {
+      if (pfx && t.name.compare(0, pfx->size(), *pfx) != 0) continue;
+      std::vector<size_t> shape(t.shape.begin(), t.shape.end());
+      budget.charge(t.name, shape);
+    }
+  };
+  Safetensors adapter(dir + "/lora/adapter_model.safetensors");
+  charge_all(adapter, nullptr);
+  if (adapter.entries.empty()) throw std::runtime_error("empty LoRA adapter");
+  Safetensors head(dir + "/head.safetensors");
+  charge_all(head, nullptr);
+  std::vector<std::unique_ptr<Safetensors>> base;
+  for (const std::string& f : base_files(dir)) {
+    base.emplace_back(new Safetensors(f));
+    charge_all(*base.back(), &prefix);
+  }
+  for (const auto& b : base)
+    for (const auto& t : b->entries)
+      if (t.name.compare(0, prefix.size(), prefix) == 0) e.set_tensor(t.name.substr(prefix.size()), t.dtype, t.shape, t.data);
+  for (const auto& t : adapter.entries) e.set_tensor(t.name, t.dtype, t.shape, t.data);
+  for (const auto& t : head.entries) e.set_tensor("head." + t.name, t.dtype, t.shape, t.data);
 }
 
 }  // namespace dg

@@ -15,16 +15,17 @@ LIB_PATH = os.path.join(PKG_ROOT, "libdecider_gpu.so")
 SYMBOLS = [
     "dg_last_error", "dg_launch_count",
     "dg_engine_create", "dg_engine_set_tensor", "dg_engine_fill_synthetic", "dg_engine_finalize",
-    "dg_engine_load", "dg_read_checkpoint_config",
+    "dg_engine_load", "dg_engine_load_with_limits", "dg_load_limits_default", "dg_read_checkpoint_config",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
     "dg_engine_gemm_timing_layers", "dg_engine_gemm_time_all", "dg_measure_i8_peak",
     "dg_forward_hidden", "dg_prefill", "dg_prefix_len", "dg_prefix_free", "dg_logits",
-    "dg_logits_batch", "dg_debug_layer", "dg_debug_layer_codes",
+    "dg_logits_batch", "dg_debug_layer", "dg_debug_layer_codes", "dg_forward_segments_hidden",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
     "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
+    "dg_attention_workspace_bytes", "dg_attention_device",
 ]
 
 
@@ -43,6 +44,12 @@ class ModelConfig(C.Structure):
 _lib = None
 
 
+class LoadLimits(C.Structure):
+    """dg_load_limits: LoadLimits (src/loading.rs:8-24), bytes."""
+    _fields_ = [("max_tensor_bytes", C.c_uint64), ("max_weight_bytes", C.c_uint64),
+                ("max_workspace_bytes", C.c_uint64)]
+
+
 def load() -> C.CDLL:
     """Load libdecider_gpu.so; raises if it has not been built."""
     global _lib
@@ -56,6 +63,9 @@ def load() -> C.CDLL:
     L.dg_launch_count.restype = C.c_uint64
     L.dg_engine_create.argtypes = [C.POINTER(ModelConfig), i32, i32, i32, C.POINTER(vp)]
     L.dg_engine_load.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp)]
+    L.dg_engine_load_with_limits.argtypes = [C.c_char_p, i32, C.POINTER(LoadLimits), i32, i32, C.POINTER(vp)]
+    L.dg_load_limits_default.argtypes = [C.POINTER(LoadLimits)]
+    L.dg_load_limits_default.restype = None
     L.dg_read_checkpoint_config.argtypes = [C.c_char_p, C.POINTER(ModelConfig), C.POINTER(C.c_int32), i32]
     L.dg_engine_set_tensor.argtypes = [vp, C.c_char_p, i32, vp, i32, vp]
     L.dg_engine_fill_synthetic.argtypes = [vp, C.c_uint64, C.c_float]
@@ -84,6 +94,10 @@ def load() -> C.CDLL:
     L.dg_prefix_free.restype = None
     L.dg_logits.argtypes = [vp, vp, u32p, sz, vp, sz, f32p]
     L.dg_logits_batch.argtypes = [vp, vp, sz, f32p, vp, vp]
+    L.dg_forward_segments_hidden.argtypes = [vp, vp, u32p, sz, sz, f32p]
+    L.dg_attention_workspace_bytes.argtypes = [i32, i32, i32, i32]
+    L.dg_attention_workspace_bytes.restype = sz
+    L.dg_attention_device.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, i32, vp, sz, vp]
     L.dg_debug_layer.argtypes = [vp, i32, f32p, sz, f32p]
     L.dg_measure_i8_peak.argtypes = [i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_float)]
     L.dg_debug_layer_codes.argtypes = [vp, i32, f32p, sz, f32p, vp]

@@ -172,6 +172,18 @@ class GpuModel:
                                        out.ctypes.data))
         return out
 
+    def forward_segments(self, seqs, prefix: GpuPrefix | None = None) -> np.ndarray:
+        """Several equal-length sequences continuing `prefix`, as one forward
+        (dg_forward_segments_hidden): returns [len(seqs)][seg_len][hidden]."""
+        seqs = [np.asarray(q) for q in seqs]
+        n = len(seqs[0])
+        assert all(len(q) == n for q in seqs), "sequences must have one length"
+        ids, p = _u32(np.concatenate(seqs))
+        out = np.zeros((len(seqs) * n, self.hidden), np.float32)
+        check(load().dg_forward_segments_hidden(self.h, None if prefix is None else prefix.h, p, n, len(seqs),
+                                                out.ctypes.data))
+        return out.reshape(len(seqs), n, self.hidden)
+
     def prefill(self, ids) -> GpuPrefix:
         ids, p = _u32(ids)
         h = C.c_void_p()
@@ -265,17 +277,28 @@ class GpuModel:
         return res, status[:len(requests)].copy(), ms[:len(requests)].copy(), err
 
     @classmethod
-    def load_native(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096):
-        """`from_dir` through the library's own checkpoint loader (dg_engine_load):
-        the C ABI reads the configs and the safetensors files itself."""
+    def load_native(cls, d: str, precision: str = "checkpoint", device: int = 0, max_tokens: int = 4096,
+                    limits: dict | None = None):
+        """`from_dir` through the library's own checkpoint loader
+        (dg_engine_load_with_limits): the C ABI reads the configs and the
+        safetensors files itself. `limits` (NativeEngine::load_with_limits,
+        src/lib.rs:287-367) maps max_tensor_bytes / max_weight_bytes /
+        max_workspace_bytes to byte budgets; missing keys keep the defaults."""
+        from ._lib import LoadLimits
         from .host import read_decider_config, read_text_config
         m = cls.__new__(cls)
         m.config = dict(read_text_config(d))
         m.precision = precision
         m.pointer_dim = read_decider_config(d)["pointer_dim"]
         m.hidden = m.config["hidden_size"]
+        lim = LoadLimits()
+        load().dg_load_limits_default(C.byref(lim))
+        for k, v in (limits or {}).items():
+            setattr(lim, k, int(v))
         h = C.c_void_p()
-        check(load().dg_engine_load(d.encode(), PRECISIONS[precision], device, max_tokens, C.byref(h)))
+        m.h = None
+        check(load().dg_engine_load_with_limits(d.encode(), PRECISIONS[precision], C.byref(lim), device, max_tokens,
+                                                C.byref(h)))
         m.h = h.value
         return m
 

@@ -78,6 +78,29 @@ void dg_engine_free(dg_engine* e);
  * "head.") into a new engine and finalizes it. Equivalent to
  * dg_engine_create + dg_engine_set_tensor for every tensor + dg_engine_finalize. */
 int dg_engine_load(const char* dir, int precision, int device, int max_tokens, dg_engine** out);
+/* LoadLimits (src/loading.rs:8-24): allocation budgets, in bytes, checked at
+ * the checkpoint boundary before any payload is read or any device memory is
+ * taken. Defaults (dg_load_limits_default): 2 GiB per tensor, 12 GiB of
+ * weights and conversion scratch, 2 GiB of forward workspace. */
+typedef struct dg_load_limits {
+  uint64_t max_tensor_bytes;
+  uint64_t max_weight_bytes;
+  uint64_t max_workspace_bytes;
+} dg_load_limits;
+void dg_load_limits_default(dg_load_limits* out);
+/* NativeEngine::load_with_limits (src/lib.rs:287-367): dg_engine_load with
+ * explicit budgets (limits NULL: the defaults). Before the engine is created
+ * it runs the reference's checks in its order: Config::validate_layout
+ * (src/qwen.rs:37-135: the architecture's FP32 weight estimate, LoRA
+ * included, and the forward workspace for max_length tokens), then
+ * WeightBudget::charge (src/loading.rs:61-80) of every tensor in the adapter,
+ * head and base files (base: model.safetensors, or the shards of
+ * model.safetensors.index.json) from their headers. Over-budget checkpoints
+ * fail with the reference's messages ("{name}: allocation of {bytes} bytes
+ * exceeds budget {limit}", "{name}: dimension product overflow"), with no
+ * device memory taken. dg_engine_load is this call with the defaults. */
+int dg_engine_load_with_limits(const char* dir, int precision, const dg_load_limits* limits, int device,
+                               int max_tokens, dg_engine** out);
 /* The validated model config of a checkpoint directory (no device needed):
  * fills *cfg, with cfg->layer_types pointing at the caller's buffer of
  * max_layers entries (0 DeltaNet, 1 attention). */
@@ -134,6 +157,16 @@ int dg_debug_layer(dg_engine* e, int layer, const float* x_in, size_t n, float* 
  * normalised post-mixer rows (gate/up) and [n][intermediate] of the SwiGLU
  * rows (down_proj). int8-compute engines on the tcgen05 path only. */
 int dg_debug_layer_codes(dg_engine* e, int layer, const float* x_in, size_t n, float* x_out, int8_t* codes_out);
+/* Model::forward_after for `segs` sequences of seg_len tokens each, ids
+ * concatenated ([segs][seg_len]), every one continuing `past` (nullable: from
+ * position 0), run as ONE forward over segs * seg_len rows (the questions of
+ * one request; dg_logits_batch uses it for equal-length questions). Each
+ * sequence's hidden rows equal those of dg_forward_hidden(past, its ids) (bit
+ * for bit in reference order); hidden_out (nullable) receives
+ * [segs * seg_len][hidden_size]. Needs the 2B-shaped int8-compute path
+ * (head_dim 256, DeltaNet heads of 128) and segs * seg_len <= max_tokens. */
+int dg_forward_segments_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t seg_len, size_t segs,
+                               float* hidden_out);
 size_t dg_prefix_len(const dg_prefix* p);
 void dg_prefix_free(dg_prefix* p);
 
@@ -240,6 +273,21 @@ size_t dg_gated_delta_chunk_workspace_bytes(int batch, int t, int heads);
 int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const float* v, const float* g,
                                        const float* beta, int batch, int t, int heads, float* state, float* o,
                                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- isolated gated causal attention (causal_attention and the output
+ * gate of Full::forward, src/qwen.rs:581-643), a measurement and test entry
+ * with no counterpart in the reference's API. Device buffers: q [n][heads][d]
+ * (normalised, rotated), kc / vc [offset + n][kv_heads * d] (the prefix's
+ * keys then the rows' own), gate rows of ld_gate floats with head h's gate at
+ * column h * 2d + d; out [n][heads][d]. tensor_cores = 1: the fast-mode
+ * tensor-core path (3 x TF32 tcgen05 products, head_dim 256; workspace of
+ * dg_attention_workspace_bytes, owned by the caller); 0: the CUDA-core kernel
+ * of reference-order mode (workspace unused). Runs on `stream` (a
+ * cudaStream_t, NULL for the default stream) and synchronises it. */
+size_t dg_attention_workspace_bytes(int heads, int kv_heads, int d, int n);
+int dg_attention_device(const float* q, const float* kc, const float* vc, const float* gate, int ld_gate, int n,
+                        int offset, int heads, int kv_heads, int d, float* out, int tensor_cores, void* workspace,
+                        size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -120,6 +120,9 @@ def rel_err(a, b):
 # runs the CPU oracle once and commits its outputs) and the GPU tests.
 FULL_SEED = 20261202
 FULL_POINTER_DIM = 256
+# Relative size of the input perturbation that measures the oracle's own
+# sensitivity (far below FP32 rounding of the layers' arithmetic).
+NOISE_REL = 1e-7
 # temperature_by_kind of the reference's tiny fixture config (noul 0.8,
 # choice 0.7, score 1.2).
 TEMPERATURES = {"noul": 0.8, "choice": 0.7, "score": 1.2}
@@ -169,3 +172,16 @@ def probabilities(logits, kind):
     for x in e:
         total = np.float32(total + x)
     return (e / total).astype(np.float32)
+
+
+def perturbed_embedding(tensors, ids, seed, rel=None):
+    """The embedding tensor with the rows of `ids` scaled by (1 + rel N(0, 1))
+    (seeded): the oracle's sensitivity probe."""
+    code, shp, arr = tensors["embed_tokens.weight"]
+    rows = np.unique(np.asarray(ids, np.int64))
+    out = arr.copy()
+    rng = np.random.default_rng(seed)
+    out[rows] = (arr[rows] * (1 + (NOISE_REL if rel is None else rel) * rng.standard_normal(arr[rows].shape))
+                 ).astype(np.float32)
+    return code, shp, out
+

@@ -392,3 +392,97 @@ def test_cfg2_shape_unflipped_rows_within_north_star_bar(oracle_mod, exact, toke
               f"{rows[flipped].max() if flipped.any() else 0:.3e}")
         assert clean.size > tokens // 2, (i, int(flipped.sum()))
         assert clean.max() <= 1e-4, (i, float(clean.max()), int(np.argmax(rows * ~flipped)))
+
+
+@pytest.mark.parametrize("prefix_len,seg_len,segs", [(300, 64, 5), (0, 64, 3), (1000, 17, 4), (130, 100, 3)])
+def test_segmented_forward_equals_one_forward_per_sequence(prefix_len, seg_len, segs):
+    """Several equal-length sequences continuing one prefix run as one forward
+    (dg_forward_segments_hidden: the questions of a request). In reference
+    order each sequence's rows equal, bit for bit, its own forward after the
+    prefix (4-layer 2B-shaped model). Covers a shared prefix, no prefix,
+    sequences shorter than an attention block, and sequences longer than a
+    DeltaNet chunk."""
+    from decider_gpu import GpuModel
+    c = cfg2_config(4, vocab=1024)
+    t = random_tensors(c, rank=32, pointer_dim=64, seed=31)
+    m = GpuModel(c, "int8-compute", 32, 2.0, 64, 0, 1024)
+    m.set_tensors(t)
+    m = m.finalize()
+    m.set_exact(True)
+    rng = np.random.default_rng(prefix_len + seg_len)
+    prefix_ids = rng.integers(0, c["vocab_size"], prefix_len)
+    seqs = [rng.integers(0, c["vocab_size"], seg_len) for _ in range(segs)]
+    prefix = m.prefill(prefix_ids) if prefix_len else None
+    got = m.forward_segments(seqs, prefix)
+    for i, q in enumerate(seqs):
+        exp = m.forward(q, prefix)
+        assert np.array_equal(got[i], exp), (i, np.abs(got[i] - exp).max())
+    if prefix is not None:
+        assert np.array_equal(m.forward(seqs[0], prefix), got[0])  # the prefix is unchanged by its use
+
+
+@pytest.mark.parametrize("lt", ["linear_attention", "full_attention"])
+@pytest.mark.parametrize("prefix_len,seg_len,segs", [(300, 64, 5), (0, 64, 3), (130, 100, 3)])
+def test_segmented_forward_fma_mode_one_layer(lt, prefix_len, seg_len, segs):
+    """FMA mode (the benchmark mode) of the segmented forward, one layer of
+    each type at the 2B shapes: joining the rows changes how the projections
+    and LoRA-A split their K sums over the grid, a reordering of FP32 work
+    that flips an int8 code in a few rows (each such row moves by 1e-4 to
+    1e-2). The bar is the single-layer bar of FMA mode: median row within
+    1e-5, at least 75 % of rows within 1e-5, every row within 1e-2."""
+    from decider_gpu import GpuModel
+    c = cfg2_config(4, vocab=1024)
+    c["num_hidden_layers"], c["layer_types"] = 1, [lt]
+    t = random_tensors(c, rank=32, pointer_dim=64, seed=31)
+    m = GpuModel(c, "int8-compute", 32, 2.0, 64, 0, 1024)
+    m.set_tensors(t)
+    m = m.finalize()
+    m.set_exact(False)
+    rng = np.random.default_rng(prefix_len + seg_len + 7)
+    prefix = m.prefill(rng.integers(0, c["vocab_size"], prefix_len)) if prefix_len else None
+    seqs = [rng.integers(0, c["vocab_size"], seg_len) for _ in range(segs)]
+    got = m.forward_segments(seqs, prefix)
+    rows = np.concatenate([_row_errors(got[i], m.forward(q, prefix)) for i, q in enumerate(seqs)])
+    print(f"{lt} fma: median row {np.median(rows):.2e}, rows > 1e-5: {(rows > 1e-5).sum()} of {len(rows)}, "
+          f"max {rows.max():.2e}")
+    assert np.median(rows) < 1e-5 and (rows <= 1e-5).mean() >= 0.75 and rows.max() < 1e-2
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
+def test_logits_batch_runs_equal_length_questions_together(small, exact, monkeypatch):
+    """dg_logits_batch with a request whose questions share one length runs
+    them as one segmented forward: the logits equal one dg_logits call per
+    question (bit for bit in reference order; in FMA mode within 1e-2 of the
+    largest logit, the 4-layer bar of FMA mode, since joined rows reorder FP32
+    sums and int8 flips compound over the layers), with and without a state, and with the batching switched off
+    (DG_BATCH_QUESTIONS=0) the per-question path gives the same logits."""
+    from decider_gpu import GpuModel
+    cfg, tensors = small
+    rng = np.random.default_rng(41)
+    ids = lambda n: rng.integers(0, cfg["vocab_size"], n)
+    state = ids(250)
+    qs = [(ids(48), [40, 41]), (ids(48), [10, 20, 30, 44]), (ids(48), [1, 2, 3, 4, 46]), (ids(48), [0, 46])]
+    reqs = [{"state": state, "questions": qs}, {"questions": qs[:3]}]
+    results = {}
+    for batching in ("1", "0"):
+        monkeypatch.setenv("DG_BATCH_QUESTIONS", batching)
+        m = _gpu_small(cfg, tensors)
+        m.set_exact(exact)
+        got, status, ms, err = m.logits_batch(reqs)
+        assert not status.any(), err
+        results[batching] = got
+    m.set_exact(exact)
+    sp = m.prefill(state)
+    for i, (q, pos) in enumerate(qs):
+        single = m.logits(q, pos, sp)
+        for b in ("1", "0"):
+            if exact or b == "0":
+                assert np.array_equal(results[b][0][i], single), (b, i)
+            else:
+                assert np.abs(results[b][0][i] - single).max() <= 1e-2 * max(1.0, np.abs(single).max()), (b, i)
+    for i, (q, pos) in enumerate(qs[:3]):
+        single = m.logits(q, pos)
+        if exact:
+            assert np.array_equal(results["1"][1][i], single), i
+        else:
+            assert np.abs(results["1"][1][i] - single).max() <= 1e-2 * max(1.0, np.abs(single).max()), i

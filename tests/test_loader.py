@@ -105,3 +105,58 @@ def test_native_loader_rejects_a_truncated_safetensors_file(tmp_path):
         f.write(raw[:-4])
     with pytest.raises(GpuError, match="do not match|length does not match"):
         GpuModel.load_native(d, "checkpoint", max_tokens=64)
+
+
+# Budgets of the tiny checkpoint (vocab 32, hidden 8, max_length 256), charged
+# as WeightBudget::charge does (src/loading.rs:61-80): the embedding [32, 8] is
+# 32*8*4 bytes plus 32*ceil(8/64)*4 bytes of possible group scales = 1152; the
+# aggregate check counts it twice (2304); the forward workspace for 256 tokens
+# is (256*16*16 + 256*2*2 + 2*2*2) floats = 266272 bytes (widest projection
+# 16, rotary dim 2, recurrent state 2 x 2 x 2).
+@pytest.mark.parametrize("limits,message", [
+    ({"max_tensor_bytes": 1151}, "embedding: allocation of 1152 bytes exceeds budget 1151"),
+    ({"max_weight_bytes": 2303}, "checkpoint weights and conversion scratch: allocation of 2304 bytes exceeds budget 2303"),
+    ({"max_workspace_bytes": 266271}, "forward workspace: allocation of 266272 bytes exceeds budget 266271"),
+])
+def test_load_limits_refuse_before_any_device_memory(limits, message):
+    """NativeEngine::load_with_limits (src/lib.rs:287-367) at the C ABI: the
+    reference's budgets and messages, checked before the engine exists (so the
+    refusal needs no GPU)."""
+    from decider_gpu import GpuModel
+    with pytest.raises(GpuError) as e:
+        GpuModel.load_native(TINY, "int8-compute", max_tokens=64, limits=limits)
+    assert message in str(e.value), str(e.value)
+
+
+def test_default_load_limits_are_the_references():
+    import ctypes as C
+    from decider_gpu._lib import LoadLimits, load
+    lim = LoadLimits()
+    load().dg_load_limits_default(C.byref(lim))
+    assert (lim.max_tensor_bytes, lim.max_weight_bytes, lim.max_workspace_bytes) == (2 << 30, 12 << 30, 2 << 30)
+
+
+def test_load_limits_count_every_checkpoint_tensor(tmp_path):
+    """The files' tensors are charged from their headers before any payload is
+    read (read_tensors, src/weights.rs:316-325), unsupported extra tensors
+    included: an adapter file with one extra [300, 300] tensor passes the
+    architecture check but is refused by that tensor's own charge
+    (300*300*4 + 300*5*4 = 366000 bytes)."""
+    import struct
+    from decider_gpu import GpuModel
+    d = _copy(tmp_path)
+    p = os.path.join(d, "lora", "adapter_model.safetensors")
+    with open(p, "rb") as f:
+        raw = f.read()
+    n = struct.unpack("<Q", raw[:8])[0]
+    header = json.loads(raw[8:8 + n])
+    payload = raw[8 + n:]
+    end = max(v["data_offsets"][1] for k, v in header.items() if k != "__metadata__")
+    header["extra.weight"] = {"dtype": "F32", "shape": [300, 300], "data_offsets": [end, end + 300 * 300 * 4]}
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    with open(p, "wb") as f:
+        f.write(struct.pack("<Q", len(hb)) + hb + payload[:end] + bytes(300 * 300 * 4))
+    with pytest.raises(GpuError) as e:
+        GpuModel.load_native(d, "int8-compute", max_tokens=64, limits={"max_tensor_bytes": 100000})
+    assert "extra.weight: allocation of 366000 bytes exceeds budget 100000" in str(e.value), str(e.value)
