@@ -12,10 +12,14 @@
 // by all 256 threads (16-byte loads, the next chunk in flight while the
 // current one is stored), split into the TF32 part (low 13 mantissa bits
 // cleared) and the remainder, and stored in the 128-byte-swizzled K-major
-// layout; one thread issues hi·hi + hi·lo + lo·hi as tcgen05.mma kind::tf32
-// (M = N = 128, K = 8) into a TMEM accumulator, two chunk slots alternating
-// (each freed by the commit of its MMAs). The error of the split product is
-// about 2^-21 relative per term, far inside the 1e-5 per-row bar of fast mode.
+// layout; one thread issues the chunk's tcgen05.mma kind::tf32 (M = N = 128,
+// K = 8): hi·hi into one TMEM accumulator, the correction hi·lo + lo·hi into
+// a second. The tensor core's FP32 accumulation does not round to nearest, so
+// long chains of it drift: each chunk therefore starts fresh accumulators
+// (two buffers of the pair, alternating), and once its MMAs complete every
+// thread reads its rows' values and adds main + correction into its FP32
+// register sums, rounding to nearest. Error per product about 2^-21; per
+// output, a few TF32-chain steps plus the FP32 sum of the chunks.
 // Batches (grid.z) index heads and sequences through per-operand offsets.
 #include <algorithm>
 
@@ -53,7 +57,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
     fence_barrier_init();
   }
   if (warp == 0) {
-    tmem_alloc(holder, 128);
+    tmem_alloc(holder, 512);  // [2 buffers][main, correction] x 128 columns
     tmem_relinquish();
   }
   tc_fence_before();
@@ -76,7 +80,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
       }
     }
   };
+  // Warps w and w + 4 read TMEM lanes 32 (w % 4) ..: columns 0-63 and 64-127.
+  const int q = warp & 3, half = warp >> 2;
+  const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16) + uint32_t(half * 64);
+  float acc[64];
+#pragma unroll
+  for (int e = 0; e < 64; ++e) acc[e] = 0.0f;
   bool ok = true;
+  // Adds chunk c's products (buffer c & 1) into acc once its MMAs are complete.
+  auto take = [&](int c) {
+    const int b = c & 1;
+    ok = mbar_wait_bounded(&done[b], (c >> 1) & 1, g.status, 500 + b, nullptr) && ok;
+    tc_fence_after();
+    const uint32_t base = lane_base + uint32_t(b * 256);
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t dm[16], dc[16];
+      tmem_ld16x2_sync(base + uint32_t(16 * cc), base + 128u + uint32_t(16 * cc), dm, dc);
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        acc[16 * cc + e] = acc[16 * cc + e] + (__uint_as_float(dm[e]) + __uint_as_float(dc[e]));
+    }
+    tc_fence_before();
+  };
   float4 v[8];
   if (nch > 0) gather(v, 0);
   for (int c = 0; c < nch; ++c) {
@@ -84,8 +110,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
     uint8_t* s = sm + b * kTcSlot;
     float4 w[8];
     if (c + 1 < nch) gather(w, 32 * (c + 1));
-    // The slot was last read by the MMAs of chunk c - 2.
-    if (c >= 2) ok = mbar_wait_bounded(&done[b], ((c - 2) >> 1) & 1, g.status, 500 + b, nullptr) && ok;
+    // Slot and accumulator buffer b were last used by chunk c - 2: add its
+    // products, which also frees both.
+    if (c >= 2) take(c - 2);
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int i = tid + u * kTcThreads, r = i >> 3, j = i & 7;
@@ -104,12 +131,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
       if (ok) {
         tc_fence_after();
         const uint32_t aa = smem_addr(s), ba = aa + 32768;
+        const uint32_t dmain = tmem + uint32_t(b * 256), dcorr = dmain + 128u;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t ah = aa + kk * 32, al = ah + 16384, bh = ba + kk * 32, bl = bh + 16384;
-          mma_tf32(tmem, smem_desc_sw128(ah), smem_desc_sw128(bh), idesc, (c > 0 || kk > 0) ? 1u : 0u);
-          mma_tf32(tmem, smem_desc_sw128(ah), smem_desc_sw128(bl), idesc, 1u);
-          mma_tf32(tmem, smem_desc_sw128(al), smem_desc_sw128(bh), idesc, 1u);
+          mma_tf32(dmain, smem_desc_sw128(ah), smem_desc_sw128(bh), idesc, kk > 0 ? 1u : 0u);
+          mma_tf32(dcorr, smem_desc_sw128(ah), smem_desc_sw128(bl), idesc, kk > 0 ? 1u : 0u);
+          mma_tf32(dcorr, smem_desc_sw128(al), smem_desc_sw128(bh), idesc, 1u);
         }
       }
       mma_commit(&done[b]);  // also after a failed wait, so that every later wait ends
@@ -117,26 +145,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
 #pragma unroll
     for (int u = 0; u < 8; ++u) v[u] = w[u];
   }
-  // The last commit covers every MMA of the issuing thread.
-  if (nch > 0 && !mbar_wait_bounded(&done[(nch - 1) & 1], ((nch - 1) >> 1) & 1, g.status, 510, nullptr)) ok = false;
-  tc_fence_after();
+  if (nch >= 2) take(nch - 2);
+  if (nch >= 1) take(nch - 1);
   {
-    // Warps w and w + 4 read TMEM lanes 32 (w % 4) ..: columns 0-63 and 64-127.
-    const int q = warp & 3, half = warp >> 2, r = q * 32 + lane, m = m0 + r;
+    const int r = q * 32 + lane, m = m0 + r;
     float* C = g.C + outer * g.c_outer + inner * g.c_inner + size_t(m) * g.ldc;
     const float* G = g.gate ? g.gate + outer * g.g_outer + inner * g.g_inner + size_t(m) * g.ldg : nullptr;
     const bool has = nch > 0 && ok;  // no chunk: the product is zero
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      const int col0 = half * 64 + 16 * cc;
-      uint32_t d[16];
-      tmem_ld16_sync(tmem + (uint32_t(q * 32) << 16) + uint32_t(col0), d);
-      if (m < g.M) {
+    if (m < g.M) {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int n = n0 + col0 + e;
-          if (n >= g.N) break;
-          float val = has ? __uint_as_float(d[e]) * g.alpha : 0.0f;
+      for (int e = 0; e < 64; ++e) {
+        const int n = n0 + half * 64 + e;
+        if (n < g.N) {
+          float val = has ? acc[e] * g.alpha : 0.0f;
           if (g.accumulate) val = C[n] + val;
           if (G) val = val * sigmoid_f(G[n]);
           C[n] = val;
@@ -149,7 +170,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(TcGemmArgs g) {
   if (warp == 0) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 512);
   }
 }
 

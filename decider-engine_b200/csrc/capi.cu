@@ -43,6 +43,10 @@ struct dg_linear {
   // quantiser, before the projection kernel, after it.
   cudaEvent_t ev[3] = {};
   float last_total_ms = 0.0f, last_gemm_ms = 0.0f;
+  // dg_linear_test_wait_fault: 0, or the group whose completion the next
+  // projections leave out, plus one; and their wait budget (0: 2 s).
+  int test_skip_commit = 0;
+  unsigned long long test_wait_ns = 0;
 };
 
 namespace {
@@ -142,6 +146,8 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
     dump = dots;
   }
   a.dots = dump;
+  a.test_skip_commit = l->test_skip_commit;
+  a.wait_ns = l->test_wait_ns;
   DG_CUDA(cudaEventRecord(l->ev[1], l->stream));
   launch_gemm_i8(map_a, l->maps, a, l->rank, kEpiWrite, l->exact, l->stream);
   DG_CUDA(cudaEventRecord(l->ev[2], l->stream));
@@ -154,6 +160,9 @@ void linear_run(dg_linear* l, const float* x_dev, int m, float* y_dev, int32_t* 
   DG_CUDA(cudaEventElapsedTime(&l->last_total_ms, l->ev[0], l->ev[2]));
   DG_CUDA(cudaEventElapsedTime(&l->last_gemm_ms, l->ev[1], l->ev[2]));
   if (h.code == kNonFinite) throw std::runtime_error("non-finite projection input");
+  if (h.code == kWaitTimeout)
+    throw std::runtime_error("device pipeline wait timed out (device error code " + std::to_string(h.code) +
+                             " at location " + std::to_string(h.where) + ")");
   if (h.code) throw std::runtime_error("device error code " + std::to_string(h.code) + " at " + std::to_string(h.where));
 }
 }  // namespace
@@ -596,6 +605,16 @@ int dg_linear_last_times(const dg_linear* l, float* total_ms, float* gemm_ms) {
     if (!l) throw std::runtime_error("null argument");
     if (total_ms) *total_ms = l->last_total_ms;
     if (gemm_ms) *gemm_ms = l->last_gemm_ms;
+  });
+}
+
+int dg_linear_test_wait_fault(dg_linear* l, int skip_group, uint64_t wait_ns) {
+  return guarded([&] {
+    if (!l) throw std::runtime_error("null argument");
+    if (skip_group >= 0 && (l->k / 64 <= skip_group || wait_ns == 0 || wait_ns > 1000000000ull))
+      throw std::runtime_error("dg_linear_test_wait_fault: group out of range or wait budget not in (0, 1 s]");
+    l->test_skip_commit = skip_group >= 0 ? skip_group + 1 : 0;
+    l->test_wait_ns = skip_group >= 0 ? wait_ns : 0;
   });
 }
 

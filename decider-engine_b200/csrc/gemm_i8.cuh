@@ -60,6 +60,12 @@ struct GemmArgs {
   int* split_cnt;
   size_t split_ws_floats;  // capacity of split_ws
   int splits;              // set by launch_gemm_i8 (1: no split)
+  // Failure-path test aid (0 / 0 in normal launches): test_skip_commit = g + 1
+  // makes the MMA issuer leave out the completion signal of group g, so the
+  // promotion warps' wait for it runs out; wait_ns replaces the 2 s budget
+  // of the pipeline's bounded waits.
+  int test_skip_commit;
+  unsigned long long wait_ns;
 };
 
 template <int BN_>
@@ -190,6 +196,7 @@ __global__ void __launch_bounds__(576, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
+  const uint64_t budget = p.wait_ns ? p.wait_ns : 2000000000ull;  // every pipeline wait
   const int KS = p.K / BK / int(gridDim.z);  // this split's K stages
   const int ks0 = int(blockIdx.z) * KS;      // its first stage
 
@@ -245,7 +252,7 @@ __global__ void __launch_bounds__(576, 1)
       // ---------------- TMA producer
       for (int ks = 0; ks < KS; ++ks) {
         const int s = ks % STAGES, use = ks / STAGES;
-        if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 100 + s, abort_flag)) break;
+        if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 100 + s, abort_flag, budget)) break;
         uint8_t* st = smem + s * STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES + 2 * BN * 4 + 2 * BM * 4);
         tma_load_2d(st, &map_a, &full[s], (ks0 + ks) * BK, m0);
@@ -264,7 +271,7 @@ __global__ void __launch_bounds__(576, 1)
           if (p.late_dep) griddep_wait();  // lora_mid comes from the previous kernel
           for (int j = 0; j <= plan->nparts; ++j) {
             const int ls = KS + j, s = ls % STAGES, use = ls / STAGES;
-            if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 120 + s, abort_flag)) break;
+            if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, p.status, 120 + s, abort_flag, budget)) break;
             uint8_t* st = smem + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], LT);
             if (j == 0) {
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(576, 1)
       bool ready = issued == KS + 1 + plan->nparts;
       for (int j = 0; j <= plan->nparts && ready; ++j) {
         const int ls = KS + j, s = ls % STAGES;
-        ready = mbar_wait_bounded(&full[s], (ls / STAGES) & 1, p.status, 140 + s, abort_flag);
+        ready = mbar_wait_bounded(&full[s], (ls / STAGES) & 1, p.status, 140 + s, abort_flag, budget);
         if (!ready) break;
         float4* t = reinterpret_cast<float4*>(smem + s * STAGE_BYTES);
 #pragma unroll 4
@@ -318,13 +325,13 @@ __global__ void __launch_bounds__(576, 1)
       bool run = true;
       for (int ks = 0; ks < KS && run; ++ks) {
         const int s = ks % STAGES;
-        if (!mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag)) break;
+        if (!mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 200 + s, abort_flag, budget)) break;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           // Group g goes to accumulator g % NBUF once every promotion warp
           // has read that accumulator's previous group (phase g / NBUF).
           const int g = 2 * ks + j, b = g % NBUF;
-          if (!mbar_wait_bounded(&tempty[b], (g / NBUF) & 1, p.status, 210 + b, abort_flag)) {
+          if (!mbar_wait_bounded(&tempty[b], (g / NBUF) & 1, p.status, 210 + b, abort_flag, budget)) {
             run = false;
             break;
           }
@@ -336,7 +343,7 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
           for (int kk = 0; kk < 2; ++kk)
             mma_i8(d, smem_desc_sw128(a_addr + kk * 32), smem_desc_sw128(b_addr + kk * 32), idesc, kk);
-          mma_commit(&tfull[b]);
+          if (g + 1 != p.test_skip_commit) mma_commit(&tfull[b]);
         }
       }
       if constexpr (TCL) {
@@ -344,8 +351,8 @@ __global__ void __launch_bounds__(576, 1)
         // accumulator that the main loop's group 2 KS would have used.
         const int gd = 2 * KS, bd = gd % NBUF;
         if (run && !*abort_flag &&
-            mbar_wait_bounded(&tempty[bd], (gd / NBUF) & 1, p.status, 230, abort_flag) &&
-            mbar_wait_bounded(lora_ready, 0, p.status, 231, abort_flag)) {
+            mbar_wait_bounded(&tempty[bd], (gd / NBUF) & 1, p.status, 230, abort_flag, budget) &&
+            mbar_wait_bounded(lora_ready, 0, p.status, 231, abort_flag, budget)) {
           tc_fence_after();
           const LoraPlan& pl = *plan;
           const uint32_t d = tmem_base + uint32_t(bd * BN);
@@ -399,7 +406,7 @@ __global__ void __launch_bounds__(576, 1)
     bool ok = true;
     for (int ks = 0; ks < KS && ok; ++ks) {
       const int s = ks % STAGES;
-      ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 300 + s, abort_flag);
+      ok = mbar_wait_bounded(&full[s], (ks / STAGES) & 1, p.status, 300 + s, abort_flag, budget);
       if (!ok) break;
       const uint8_t* st = smem + s * STAGE_BYTES;
       const float* xsp = reinterpret_cast<const float*>(st + S::XS_OFF);
@@ -409,7 +416,7 @@ __global__ void __launch_bounds__(576, 1)
 #pragma unroll
         for (int jj = 0; jj < GB && ok; ++jj) {
           const int g = 2 * ks + j0 + jj, b = g % NBUF;
-          ok = mbar_wait_bounded(&tfull[b], (g / NBUF) & 1, p.status, 310 + b, abort_flag);
+          ok = mbar_wait_bounded(&tfull[b], (g / NBUF) & 1, p.status, 310 + b, abort_flag, budget);
         }
         if (!ok) break;
         tc_fence_after();
@@ -529,7 +536,7 @@ __global__ void __launch_bounds__(576, 1)
     const int et = threadIdx.x - S::EPI_WARP0 * 32;  // 0 .. 511
     if constexpr (TCL) {
       const LoraPlan& pl = *plan;
-      ok = ok && mbar_wait_bounded(lora_done, 0, p.status, 330, abort_flag);
+      ok = ok && mbar_wait_bounded(lora_done, 0, p.status, 330, abort_flag, budget);
       if (ok) {
         // This thread's 32 columns: two 16-column chunks, at their part-sorted
         // slots of the delta accumulator.

@@ -700,11 +700,100 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
   DG_CUDA(cudaGetLastError());
 }
 
+// The generic projection's FP32-dot precisions (checkpoint, int8 and int4
+// weights, FP32 activations) as a tiled kernel: CTA = 32 rows x 64 outputs,
+// 32-wide K chunks of x and of the (dequantised) weights in shared memory;
+// thread (tid / 16, tid % 16) owns rows 2 t, 2 t + 1 and outputs c, c + 16,
+// c + 32, c + 48, each with the eight dot_scores lanes of the reference
+// (src/tensor.rs:6-25): lane k % 8 adds x[k] * w[k] in order of k, the lanes
+// are summed in order from -0.0. Same arithmetic per output as
+// proj_generic_kernel, bit for bit; K % 32 == 0.
+constexpr int PGT_M = 32, PGT_N = 64, PGT_K = 32, PGT_LD = PGT_K + 1;
+__global__ void __launch_bounds__(256) proj_generic_tiled_kernel(GenericProj p, const float* __restrict__ x, int ldx,
+                                                                 const float* __restrict__ mid, int ldm, int M,
+                                                                 float* __restrict__ out, int ldo, int epi) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ float xs_t[PGT_M][PGT_LD];
+  __shared__ float ws_t[PGT_N][PGT_LD];
+  const int tid = threadIdx.x, tm = tid / 16, tn = tid % 16;
+  const int m0 = blockIdx.y * PGT_M, n0 = blockIdx.x * PGT_N, K = p.in;
+  float lanes[2][4][8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int l = 0; l < 8; ++l) lanes[i][j][l] = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += PGT_K) {
+    __syncthreads();
+    for (int i = tid; i < PGT_M * PGT_K; i += 256) {
+      const int r = i / PGT_K, k = i % PGT_K;
+      xs_t[r][k] = m0 + r < M ? x[size_t(m0 + r) * ldx + k0 + k] : 0.0f;
+    }
+    for (int i = tid; i < PGT_N * PGT_K; i += 256) {
+      const int r = i / PGT_K, k = i % PGT_K, n = n0 + r;
+      float w = 0.0f;
+      if (n < p.out) w = p.precision == 0 ? p.w[size_t(n) * K + k0 + k] : dequant(p.wq, p.wscale, p.precision, n, k0 + k, K);
+      ws_t[r][k] = w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < PGT_K; ++k) {
+      const float a0 = xs_t[2 * tm][k], a1 = xs_t[2 * tm + 1][k];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float w = ws_t[tn + 16 * j][k];
+        lanes[0][j][k & 7] = lanes[0][j][k & 7] + a0 * w;
+        lanes[1][j][k & 7] = lanes[1][j][k & 7] + a1 * w;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = m0 + 2 * tm + i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tn + 16 * j;
+      if (m >= M || n >= p.out) continue;
+      float sum = -0.0f;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) sum = sum + lanes[i][j][l];
+      const float base = sum + (p.bias ? p.bias[n] : 0.0f);
+      float v = base;
+      if (p.lora_b) {
+        const float* mr = mid + size_t(m) * ldm;
+        const float* br = p.lora_b + size_t(n) * p.rank;
+        float ln[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        const int rfull = (p.rank / 8) * 8;
+        for (int r = 0; r < rfull; ++r) ln[r & 7] = ln[r & 7] + mr[r] * br[r];
+        float d = -0.0f;
+        for (int l = 0; l < 8; ++l) d = d + ln[l];
+        for (int r = rfull; r < p.rank; ++r) d = d + mr[r] * br[r];
+        d = d + 0.0f;
+        v = base + p.lora_scale * d;
+      }
+      float* o = out + size_t(m) * ldo + n;
+      if (epi == kEpiWrite)
+        *o = v;
+      else if (epi == kEpiAdd)
+        *o = *o + v;
+      else
+        *o = silu_f(*o) * v;
+    }
+  }
+}
+
 void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const int8_t* xq, const float* xs, int ldxs,
                          const float* mid, int ldm, int M, float* out, int ldo, int epi, cudaStream_t s) {
   if (M <= 0) return;
-  dim3 grid((p.out + 127) / 128, M);
-  launch_pdl(proj_generic_kernel, dim3(grid), dim3(128), 0, s, p, x, ldx, xq, xs, ldxs, mid, ldm, M, out, ldo, epi);
+  if (p.precision != 2 && p.in % PGT_K == 0) {
+    dim3 grid((p.out + PGT_N - 1) / PGT_N, (M + PGT_M - 1) / PGT_M);
+    launch_pdl(proj_generic_tiled_kernel, dim3(grid), dim3(256), 0, s, p, x, ldx, mid, ldm, M, out, ldo, epi);
+  } else {
+    dim3 grid((p.out + 127) / 128, M);
+    launch_pdl(proj_generic_kernel, dim3(grid), dim3(128), 0, s, p, x, ldx, xq, xs, ldxs, mid, ldm, M, out, ldo, epi);
+  }
   DG_CUDA(cudaGetLastError());
 }
 

@@ -23,7 +23,7 @@ SYMBOLS = [
     "dg_logits_batch", "dg_debug_layer", "dg_debug_layer_codes", "dg_forward_segments_hidden",
     "dg_linear_create", "dg_linear_forward", "dg_linear_forward_device", "dg_linear_forward_device_noalloc",
     "dg_linear_last_quantized",
-    "dg_linear_set_exact", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
+    "dg_linear_set_exact", "dg_linear_test_wait_fault", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
     "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
     "dg_attention_workspace_bytes", "dg_attention_device",
 ]
@@ -105,6 +105,7 @@ def load() -> C.CDLL:
     L.dg_linear_forward.argtypes = [vp, f32p, i32, f32p]
     L.dg_linear_forward_device.argtypes = [vp, vp, i32, vp, vp]
     L.dg_linear_forward_device_noalloc.argtypes = [vp, vp, i32, vp]
+    L.dg_linear_test_wait_fault.argtypes = [vp, i32, C.c_uint64]
     L.dg_linear_last_quantized.argtypes = [vp, i32, vp, vp]
     L.dg_linear_set_exact.argtypes = [vp, i32]
     L.dg_linear_free.argtypes = [vp]

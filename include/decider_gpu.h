@@ -247,6 +247,15 @@ int dg_linear_forward_device_noalloc(dg_linear* l, const float* x_device, int m,
 /* Quantised activations of the last call: xq [m][k] int8 and scales [k/64][m] (host). */
 int dg_linear_last_quantized(dg_linear* l, int m, int8_t* xq, float* xs);
 int dg_linear_set_exact(dg_linear* l, int exact);
+/* Failure-path test aid with no counterpart in the reference: with
+ * skip_group >= 0 (0 .. k/64 - 1), the handle's next projection launches
+ * leave out the tensor cores' completion signal of that 64-wide K group and
+ * bound every pipeline wait by wait_ns (1 ns .. 1 s) instead of 2 s, so the
+ * wait for the group runs out: the kernel records the timeout in its status
+ * word, lets its copies in flight land, frees its tensor memory and returns,
+ * and the call fails with "device pipeline wait timed out" and the wait's
+ * location. skip_group < 0 restores normal launches. */
+int dg_linear_test_wait_fault(dg_linear* l, int skip_group, uint64_t wait_ns);
 /* The CUDA stream the projection runs on (cudaStream_t). */
 void* dg_linear_stream(const dg_linear* l);
 /* Device time of the last dg_linear_forward / dg_linear_forward_device call,
