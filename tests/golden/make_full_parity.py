@@ -20,6 +20,7 @@ probabilities. The file holds:
 Usage:
 
     python tests/golden/make_full_parity.py [--threads N] [--noise-cfg2 6] [--noise-cfg4 2]
+    python tests/golden/make_full_parity.py --add-noise cfg4 --count 4   # more samples
 """
 import argparse
 import json
@@ -73,10 +74,32 @@ def main():
     ap.add_argument("--threads", type=int, default=os.cpu_count())
     ap.add_argument("--noise-cfg2", type=int, default=6)
     ap.add_argument("--noise-cfg4", type=int, default=2)
+    ap.add_argument("--add-noise", choices=["cfg2", "cfg4"], default=None,
+                    help="append --count more perturbed int8-compute samples of one config to the existing file")
+    ap.add_argument("--count", type=int, default=4)
     args = ap.parse_args()
     O.build()
     O.set_threads(args.threads)
     c, tensors = full_model_tensors()
+    if args.add_noise:
+        with open(OUT) as f:
+            out = json.load(f)
+        which = args.add_noise
+        fn = run_cfg2 if which == "cfg2" else run_cfg4
+        samples = out["int8-compute"][which]["noise"]
+        for k in range(len(samples), len(samples) + args.count):
+            t0 = time.time()
+            t2 = dict(tensors)
+            t2["embed_tokens.weight"] = perturbed_embedding(tensors, ids_of(which, c), seed=100 + k)
+            m = O.OracleModel(c, t2, "int8-compute", 32, 2.0)
+            r = fn(m, c)
+            del m, t2
+            samples.append([q["probabilities"] for q in r["questions"]] if which == "cfg4" else [r["probabilities"]])
+            print(f"noise {which} {k} in {time.time() - t0:.0f} s", flush=True)
+            with open(OUT, "w") as f:
+                json.dump(out, f, indent=1)
+                f.write("\n")
+        return
     out = {"what": "CPU oracle outputs on the 2B decider (24 layers, vocab 248320, LoRA r32)",
            "weights": {"seed": FULL_SEED, "pointer_dim": FULL_POINTER_DIM, "checksums": tensor_checksums(tensors)},
            "noise_rel": NOISE_REL}
