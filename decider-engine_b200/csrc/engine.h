@@ -41,10 +41,10 @@ struct DevBuf {
   int device = -1;      // the pool's device (pooled buffers)
   DevBuf() = default;
   explicit DevBuf(size_t n);
-  // Stream-ordered allocation from a memory pool (the engine's prefix pool),
-  // for buffers made and dropped per request (prefix caches): no device-wide
+  // Stream-ordered allocation from the device's default memory pool, for
+  // buffers made and dropped per request (prefix caches): no device-wide
   // synchronisation on free, and the pool keeps released memory for reuse.
-  static DevBuf pooled_on(size_t n, cudaStream_t s, cudaMemPool_t pool);
+  static DevBuf pooled_on(size_t n, cudaStream_t s);
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
   DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes), pooled(o.pooled), device(o.device) {
@@ -209,7 +209,7 @@ class Engine {
   int precision_, device_, max_tokens_;
   bool fast_ = false, finalized_ = false;
   cudaStream_t stream_ = nullptr;
-  cudaMemPool_t prefix_pool_ = nullptr;  // prefix caches (pooled DevBufs)
+  bool pool_held_ = false;  // this engine counts as a user of the device's prefix pool settings
   std::map<std::string, HostTensor> staged_;
   std::vector<Layer> layers_;
   DevBuf embedding_, final_norm_, rope_;
@@ -256,6 +256,12 @@ class Engine {
   // Times the projections of layers [first_layer, first_layer + layers) only.
   void set_gemm_timing(bool on, int first_layer = 0, int layers = 1 << 30);
 };
+
+// While any engine lives on a device, that device's default stream-ordered
+// pool keeps up to 4 GiB of released prefix blocks; the last engine restores
+// the pool's release threshold and trims it.
+void prefix_pool_acquire(int device);
+void prefix_pool_release(int device);
 
 // LoadLimits (src/loading.rs:8-24): allocation budgets checked before any
 // payload is read or any memory taken. Defaults: 2 GiB per tensor, 12 GiB of

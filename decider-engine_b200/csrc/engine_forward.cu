@@ -169,11 +169,11 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
                           xq_.as<int8_t>(), xs_.as<float>(), ldxs_, q, status(), stream_);
   if (cap) {
     cap->full = false;
-    cap->state = DevBuf::pooled_on(sbytes, stream_, prefix_pool_);
+    cap->state = DevBuf::pooled_on(sbytes, stream_);
     DG_CUDA(cudaMemcpyAsync(cap->state.ptr, state_[i].ptr, sbytes, cudaMemcpyDeviceToDevice, stream_));
     const int keep = std::min(start + n, k - 1), from_tail = std::max(0, keep - n), from_raw = keep - from_tail;
     cap->tail_rows = keep;
-    cap->tail = DevBuf::pooled_on(size_t(std::max(keep, 1)) * W * 4, stream_, prefix_pool_);
+    cap->tail = DevBuf::pooled_on(size_t(std::max(keep, 1)) * W * 4, stream_);
     if (from_tail)
       DG_CUDA(cudaMemcpyAsync(cap->tail.ptr, tail + size_t(tail_rows - from_tail) * W, size_t(from_tail) * W * 4,
                               cudaMemcpyDeviceToDevice, stream_));
@@ -230,8 +230,8 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     dump_codes(n, c.qw());
     if (cap) {
       cap->full = true;
-      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
-      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
+      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
+      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
       DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
       DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
     }
@@ -287,8 +287,8 @@ void Engine::layer_generic(int i, int n, int start, const Prefix::LayerState* pa
     }
     if (cap) {
       cap->full = true;
-      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
-      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_, prefix_pool_);
+      cap->k = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
+      cap->v = DevBuf::pooled_on(size_t(start + n) * kw * 4, stream_);
       DG_CUDA(cudaMemcpyAsync(cap->k.ptr, kcache_[i].ptr, cap->k.bytes, cudaMemcpyDeviceToDevice, stream_));
       DG_CUDA(cudaMemcpyAsync(cap->v.ptr, vcache_[i].ptr, cap->v.bytes, cudaMemcpyDeviceToDevice, stream_));
     }

@@ -16,13 +16,50 @@ namespace dg {
 DevBuf::DevBuf(size_t n) : bytes(n) {
   if (n) DG_CUDA(cudaMalloc(&ptr, n));
 }
-DevBuf DevBuf::pooled_on(size_t n, cudaStream_t s, cudaMemPool_t pool) {
+DevBuf DevBuf::pooled_on(size_t n, cudaStream_t s) {
   DevBuf b;
   b.bytes = n;
   b.pooled = true;
   DG_CUDA(cudaGetDevice(&b.device));
-  if (n) DG_CUDA(cudaMallocFromPoolAsync(&b.ptr, n, pool, s));
+  if (n) DG_CUDA(cudaMallocAsync(&b.ptr, n, s));
   return b;
+}
+
+// The device's default stream-ordered pool keeps up to 4 GiB of released
+// prefix blocks while any engine lives on the device (instead of returning
+// them to the driver at every synchronisation). The first engine on a device
+// saves the pool's release threshold and raises it; the last one trims the
+// pool and restores the threshold, so the retained memory does not outlive
+// the engines. (The prefixes use the default pool rather than a pool of
+// their own: profilers track allocations from the default pool.)
+namespace {
+std::mutex g_pool_mu;
+int g_pool_users[64] = {};
+uint64_t g_pool_saved[64] = {};
+}  // namespace
+
+void prefix_pool_acquire(int device) {
+  if (device < 0 || device >= 64) return;
+  std::lock_guard<std::mutex> lk(g_pool_mu);
+  if (g_pool_users[device]++ == 0) {
+    cudaMemPool_t pool = nullptr;
+    DG_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+    DG_CUDA(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &g_pool_saved[device]));
+    uint64_t keep = uint64_t(4) << 30;
+    DG_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep));
+  }
+}
+
+void prefix_pool_release(int device) {
+  if (device < 0 || device >= 64) return;
+  std::lock_guard<std::mutex> lk(g_pool_mu);
+  if (g_pool_users[device] > 0 && --g_pool_users[device] == 0) {
+    cudaMemPool_t pool = nullptr;
+    if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &g_pool_saved[device]);
+      cudaMemPoolTrimTo(pool, 0);
+    }
+  }
 }
 // A pooled buffer goes back on the legacy stream: every use of a prefix
 // buffer is a forward on the engine stream that the host has synchronised
@@ -128,21 +165,6 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   DG_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
   if (major != 10) throw std::runtime_error("decider GPU kernels need an sm_100 (B200) device");
   DG_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
-  {
-    // Prefix caches come from this engine's own stream-ordered pool (not the
-    // device's default pool, whose settings other code in the process shares),
-    // which keeps up to 4 GiB of released blocks for the next requests instead
-    // of returning them to the driver at every synchronisation. The engine
-    // trims and destroys it when it is freed.
-    cudaMemPoolProps props{};
-    props.allocType = cudaMemAllocationTypePinned;
-    props.handleTypes = cudaMemHandleTypeNone;
-    props.location.type = cudaMemLocationTypeDevice;
-    props.location.id = device_;
-    DG_CUDA(cudaMemPoolCreate(&prefix_pool_, &props));
-    uint64_t keep = uint64_t(4) << 30;
-    DG_CUDA(cudaMemPoolSetAttribute(prefix_pool_, cudaMemPoolAttrReleaseThreshold, &keep));
-  }
   DG_CUDA(cudaEventCreate(&ev0_));
   DG_CUDA(cudaEventCreate(&ev1_));
   // DG_CUDA_GRAPHS=0 launches every forward kernel by kernel (A/B timing).
@@ -150,6 +172,8 @@ Engine::Engine(const Config& c, int precision, int device, int max_tokens)
   if (const char* o = std::getenv("DG_LORA_OVERLAP")) lora_overlap_ = std::atoi(o) != 0;
   if (const char* b = std::getenv("DG_BATCH_QUESTIONS")) batch_questions = std::atoi(b) != 0;
   if (const char* a = std::getenv("DG_ATTN_TC")) attn_tc_ = std::atoi(a) != 0;
+  prefix_pool_acquire(device_);  // last: nothing after it can throw
+  pool_held_ = true;
 }
 
 Engine::~Engine() {
@@ -162,13 +186,10 @@ Engine::~Engine() {
   if (ev0_) cudaEventDestroy(ev0_);
   if (ev1_) cudaEventDestroy(ev1_);
   for (cudaEvent_t ev : gemm_ev_) cudaEventDestroy(ev);
-  if (prefix_pool_) {
-    // Released blocks go back to the driver now; prefixes that outlive the
-    // engine keep their memory, and the pool itself goes with the last of them.
+  if (pool_held_) {
     cudaSetDevice(device_);
     cudaDeviceSynchronize();
-    cudaMemPoolTrimTo(prefix_pool_, 0);
-    cudaMemPoolDestroy(prefix_pool_);
+    prefix_pool_release(device_);
   }
 }
 
