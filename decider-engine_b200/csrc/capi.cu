@@ -430,6 +430,16 @@ int dg_attention_device(const float* q, const float* kc, const float* vc, const 
   });
 }
 
+int dg_quantize_weights_device(const float* w, size_t rows, size_t width, int bits, uint8_t* values, float* scales,
+                               void* stream) {
+  return guarded([&] {
+    if (!w || !values || !scales) throw std::runtime_error("null argument");
+    auto s = static_cast<cudaStream_t>(stream);
+    dg::quantize_weights_device(w, rows, width, bits, values, scales, nullptr, s);
+    DG_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
 int dg_forward_segments_hidden(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t seg_len, size_t segs,
                                float* hidden_out) {
   return guarded([&] {
@@ -536,22 +546,26 @@ int dg_linear_create(const float* w, int n, int k, const float* lora_a, const fl
     l->scale = lora_scale;
     l->n_pad = (n + 255) / 256 * 256;
     const int G = k / 64, N = l->n_pad;
-    std::vector<float> wf(w, w + size_t(n) * k);
-    std::vector<uint8_t> q;
-    std::vector<float> sc;
-    quantize_host(wf, size_t(n), size_t(k), 8, q, sc);
-    std::vector<uint8_t> wq(size_t(N) * k, 0);
-    std::memcpy(wq.data(), q.data(), q.size());
-    std::vector<float> ws(size_t(G) * N, 1.0f);
-    for (int r = 0; r < n; ++r)
-      for (int g = 0; g < G; ++g) ws[size_t(g) * N + r] = sc[size_t(r) * G + g];
     auto up = [](const void* src, size_t bytes) {
       DevBuf b(bytes);
       DG_CUDA(cudaMemcpy(b.ptr, src, bytes, cudaMemcpyHostToDevice));
       return b;
     };
-    l->wq = up(wq.data(), wq.size());
-    l->ws_t = up(ws.data(), ws.size() * 4);
+    // Data::quantize on the device into the kernel's layout: rows padded
+    // to N with zero weights and unit scales, scales transposed to [G][N].
+    l->wq = DevBuf(size_t(N) * k);
+    DG_CUDA(cudaMemset(l->wq.ptr, 0, l->wq.bytes));
+    std::vector<float> ones(size_t(G) * N, 1.0f);
+    l->ws_t = up(ones.data(), ones.size() * 4);
+    {
+      DevBuf wf = up(w, size_t(n) * k * 4);
+      QuantLayout L = quant_plain_layout(size_t(n), size_t(k));
+      L.s_row = 1;
+      L.s_group = size_t(N);
+      quantize_weights_device(wf.as<float>(), size_t(n), size_t(k), 8, l->wq.as<uint8_t>(), l->ws_t.as<float>(), &L,
+                              0);
+      DG_CUDA(cudaStreamSynchronize(0));
+    }
     std::vector<int> pid(N / 16, 0);
     l->chunk_pid = up(pid.data(), pid.size() * 4);
     if (rank) {

@@ -58,19 +58,16 @@ struct DevBuf {
 };
 
 // Host-side staged tensor (FP32, or already quantized projection weights).
+// A staged checkpoint tensor, F32 on the host. `quantized` marks a
+// projection that read_tensors quantises (src/weights.rs:346-355): it is
+// quantised on the device (quantize_weights_device, Data::quantize) when
+// its projection is built, straight into the projection's layout.
 struct HostTensor {
   std::vector<int64_t> shape;
   std::vector<float> f32;
   bool quantized = false;
-  int bits = 0;
-  std::vector<uint8_t> q;      // bits 8: [rows][width]; bits 4: packed as the reference
-  std::vector<float> scales;   // [rows][ceil(width/64)]
+  int bits = 0;  // 8 or 4 when quantized
 };
-
-// Data::quantize (src/weights.rs:98-146) of an F32 [rows][width] tensor:
-// bits 8 -> one byte per value, bits 4 -> nibbles packed as the reference.
-void quantize_host(const std::vector<float>& w, size_t rows, size_t width, int bits, std::vector<uint8_t>& q,
-                   std::vector<float>& scales);
 
 // One (possibly fused) projection on the device.
 struct DevProj {

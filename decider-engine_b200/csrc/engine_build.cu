@@ -43,8 +43,11 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
   d.out_pad = N;
   d.part_off = off;
   d.lora_rows = P * R;
-  std::vector<uint8_t> wq(size_t(N) * in, 0);
-  std::vector<float> ws(size_t(G) * N, 1.0f), lb(size_t(N) * R, 0.0f), la(size_t(P) * R * in);
+  // Padding columns: zero weights, unit scales.
+  d.wq = DevBuf(size_t(N) * in);
+  DG_CUDA(cudaMemset(d.wq.ptr, 0, d.wq.bytes));
+  d.ws_t = upload(std::vector<float>(size_t(G) * N, 1.0f));
+  std::vector<float> lb(size_t(N) * R, 0.0f), la(size_t(P) * R * in);
   std::vector<int> pid(N / 16, 0);
   for (int p = 0; p < P; ++p) {
     HostTensor w = take(keys[p] + ".weight");
@@ -52,23 +55,31 @@ DevProj Engine::build_fused(const std::vector<std::string>& keys, const std::vec
     HostTensor A = take("base_model.model." + keys[p] + ".lora_A.weight");
     HostTensor B = take("base_model.model." + keys[p] + ".lora_B.weight");
     std::copy(A.f32.begin(), A.f32.end(), la.begin() + size_t(p) * R * in);
+    // Every 32 fused columns of the MLP hold 16 gate columns then the 16
+    // matching up columns, so any tile of 128 or 256 columns splits into
+    // whole pairs; other parts are contiguous from their offset.
+    auto fused_row = [&](int j) { return interleave_mlp ? (j / 16) * 32 + p * 16 + (j % 16) : off[p] + j; };
+    // Data::quantize on the device, straight into the fused layout (rows
+    // of the weights at their fused rows, scales transposed to [G][N]).
+    QuantLayout L;
+    L.q_row = size_t(in);
+    L.s_row = 1;
+    L.s_group = size_t(N);
+    L.rb = interleave_mlp ? 16 : std::max(outs[p], 1);
+    L.rs = interleave_mlp ? 32 : 0;
+    L.ro = interleave_mlp ? p * 16 : off[p];
+    {
+      DevBuf wf = upload(w.f32);
+      quantize_weights_device(wf.as<float>(), size_t(outs[p]), size_t(in), 8, d.wq.as<uint8_t>(), d.ws_t.as<float>(),
+                              &L, 0);
+      DG_CUDA(cudaStreamSynchronize(0));
+    }
     for (int j = 0; j < outs[p]; ++j) {
-      int r;
-      if (interleave_mlp) {
-        // Every 32 fused columns hold 16 gate columns then the 16 matching up
-        // columns, so any tile of 128 or 256 columns splits into whole pairs.
-        r = (j / 16) * 32 + p * 16 + (j % 16);
-      } else {
-        r = off[p] + j;
-      }
-      std::memcpy(&wq[size_t(r) * in], &w.q[size_t(j) * in], in);
-      for (int g = 0; g < G; ++g) ws[size_t(g) * N + r] = w.scales[size_t(j) * G + g];
+      const int r = fused_row(j);
       std::copy(B.f32.begin() + size_t(j) * R, B.f32.begin() + size_t(j + 1) * R, lb.begin() + size_t(r) * R);
       pid[r / 16] = p;
     }
   }
-  d.wq = upload(wq);
-  d.ws_t = upload(ws);
   d.lora_a = upload(la);
   d.lora_b = upload(lb);
   d.chunk_pid = upload(pid);
@@ -86,9 +97,17 @@ DevProj Engine::build_generic_proj(const std::string& key, int in, int out, bool
   g.in = in;
   g.out = out;
   if (w.quantized) {
+    // Data::quantize on the device, in the reference's own layout.
     g.precision = precision_;
-    d.wq = upload(w.q);
-    d.scale_rows = upload(w.scales);
+    const size_t rows = size_t(w.shape[0]), width = size_t(w.shape[1]);
+    d.wq = DevBuf(w.bits == 8 ? rows * width : (rows * width + 1) / 2);
+    d.scale_rows = DevBuf(rows * ((width + 63) / 64) * 4);
+    {
+      DevBuf wf = upload(w.f32);
+      quantize_weights_device(wf.as<float>(), rows, width, w.bits, d.wq.as<uint8_t>(), d.scale_rows.as<float>(),
+                              nullptr, 0);
+      DG_CUDA(cudaStreamSynchronize(0));
+    }
     g.wq = d.wq.as<uint8_t>();
     g.wscale = d.scale_rows.as<float>();
   } else {

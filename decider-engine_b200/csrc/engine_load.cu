@@ -123,37 +123,6 @@ void Config::validate() const {
   if (rank < 0 || (rank > 0 && !(lora_scale > 0.0f))) throw std::runtime_error("invalid LoRA rank or scale");
 }
 
-// Data::quantize for one F32 [rows][width] tensor (bits 8 or 4).
-void quantize_host(const std::vector<float>& w, size_t rows, size_t width, int bits, std::vector<uint8_t>& q,
-                          std::vector<float>& scales) {
-  const size_t groups = (width + 63) / 64, el = rows * width;
-  const float bound = bits == 8 ? 127.0f : 7.0f;
-  q.assign(bits == 8 ? el : (el + 1) / 2, 0);
-  scales.assign(rows * groups, 0.0f);
-  std::vector<int8_t> qv(el);
-  host_parallel(rows, [&](size_t r0, size_t r1) {
-    for (size_t r = r0; r < r1; ++r)
-      for (size_t g = 0; g < groups; ++g) {
-        const size_t lo = g * 64, n = std::min<size_t>(64, width - lo);
-        const float* v = w.data() + r * width + lo;
-        float mx = 0.0f;
-        for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, std::fabs(v[i]));
-        const float scale = mx == 0.0f ? 1.0f : std::fmax(mx / bound, FLT_MIN);
-        scales[r * groups + g] = scale;
-        for (size_t i = 0; i < n; ++i) {
-          float x = std::round(v[i] / scale);
-          x = std::fmin(std::fmax(x, -bound), bound);
-          qv[r * width + lo + i] = int8_t(x);
-        }
-      }
-  });
-  if (bits == 8) {
-    std::memcpy(q.data(), qv.data(), el);
-  } else {
-    for (size_t i = 0; i < el; ++i) q[i / 2] |= uint8_t(uint8_t(qv[i] + 8) << (4 * (i % 2)));
-  }
-}
-
 // ---------------------------------------------------------------- Engine
 Engine::Engine(const Config& c, int precision, int device, int max_tokens)
     : c_(c), precision_(precision), device_(device), max_tokens_(max_tokens) {
@@ -322,14 +291,13 @@ void Engine::stage(const std::string& name, std::vector<int64_t> shape, std::vec
   if (staged_.count(name)) throw std::runtime_error("duplicate tensor " + name);
   HostTensor t;
   t.shape = shape;
-  // read_tensors' quantisation selection, src/weights.rs:346-355.
+  // read_tensors' quantisation selection, src/weights.rs:346-355; the
+  // quantisation itself runs on the device when the projection is built.
   if (it->second.projection && precision_ != kCheckpoint) {
     t.quantized = true;
     t.bits = precision_ == kInt4 ? 4 : 8;
-    quantize_host(f32, size_t(shape[0]), size_t(shape[1]), t.bits, t.q, t.scales);
-  } else {
-    t.f32 = std::move(f32);
   }
+  t.f32 = std::move(f32);
   staged_[name] = std::move(t);
 }
 

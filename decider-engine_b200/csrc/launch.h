@@ -199,4 +199,18 @@ void launch_head_norm(const float* hidden, int K, const int* rows, int n_rows, c
 void launch_head_dot(const float* q, const float* k, int n_keys, int dim, float scale, const float* bq,
                      const float* bk, float* logits, cudaStream_t s);
 
+// Data::quantize of an F32 [rows][width] device tensor (bits 8 or 4), group
+// 64 along the width. Plain layout (layout null): q [rows][width] bytes for
+// 8 bits, ceil(rows * width / 2) packed bytes for 4 bits; scales
+// [rows][ceil(width / 64)]. An 8-bit layout may map row j to output row
+// (j / rb) * rs + ro + j % rb (q_row bytes per output row) and its scales to
+// scales[out_row * s_row + group * s_group].
+struct QuantLayout {
+  size_t q_row, s_row, s_group;
+  int rb, rs, ro;
+};
+QuantLayout quant_plain_layout(size_t rows, size_t width);
+void quantize_weights_device(const float* w, size_t rows, size_t width, int bits, uint8_t* q, float* scales,
+                             const QuantLayout* layout, cudaStream_t s);
+
 }  // namespace dg

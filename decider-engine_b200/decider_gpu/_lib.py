@@ -25,7 +25,7 @@ SYMBOLS = [
     "dg_linear_last_quantized",
     "dg_linear_set_exact", "dg_linear_test_wait_fault", "dg_linear_stream", "dg_linear_last_times", "dg_linear_free",
     "dg_gated_delta_rule_device", "dg_gated_delta_chunk_workspace_bytes", "dg_gated_delta_rule_chunked_device",
-    "dg_attention_workspace_bytes", "dg_attention_device",
+    "dg_attention_workspace_bytes", "dg_attention_device", "dg_quantize_weights_device",
 ]
 
 
@@ -99,6 +99,7 @@ def load() -> C.CDLL:
     L.dg_attention_workspace_bytes.restype = sz
     L.dg_attention_device.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, i32, vp, sz, vp]
     L.dg_debug_layer.argtypes = [vp, i32, f32p, sz, f32p]
+    L.dg_quantize_weights_device.argtypes = [vp, sz, sz, i32, vp, vp, vp]
     L.dg_measure_i8_peak.argtypes = [i32, i32, C.POINTER(C.c_double), C.POINTER(C.c_float)]
     L.dg_debug_layer_codes.argtypes = [vp, i32, f32p, sz, f32p, vp]
     L.dg_linear_create.argtypes = [f32p, i32, i32, f32p, f32p, i32, C.c_float, i32, C.POINTER(vp)]

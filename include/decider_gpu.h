@@ -283,6 +283,20 @@ int dg_gated_delta_rule_chunked_device(const float* q, const float* k, const flo
                                        const float* beta, int batch, int t, int heads, float* state, float* o,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- weight quantisation on the device: Data::quantize
+ * (src/weights.rs:98-146), which the reference runs on the host while
+ * read_tensors loads a projection (src/weights.rs:346-355); the engine runs
+ * it on the device as it builds each projection. Device buffers: w [rows]
+ * [width] F32; bits 8: values [rows][width] (one int8 code per byte), bits 4:
+ * ceil(rows * width / 2) bytes (value i in the low nibble of byte i / 2 when
+ * i is even, the high nibble when odd, as code + 8); scales [rows]
+ * [ceil(width / 64)]. Per group of 64: scale = max |w| / bound (127 or 7),
+ * at least FLT_MIN, 1 for an all-zero group; code = clamp(round(w / scale)).
+ * Bit for bit the reference's values. Runs on `stream` and synchronises it;
+ * bits other than 4 / 8 or width 0 is an error. */
+int dg_quantize_weights_device(const float* w, size_t rows, size_t width, int bits, uint8_t* values, float* scales,
+                               void* stream);
+
 /* ---- isolated gated causal attention (causal_attention and the output
  * gate of Full::forward, src/qwen.rs:581-643), a measurement and test entry
  * with no counterpart in the reference's API. Device buffers: q [n][heads][d]

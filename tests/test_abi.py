@@ -38,3 +38,14 @@ def test_no_device_call_needed_for_errors():
     h = ctypes.c_void_p()
     assert L.dg_engine_create(None, 2, 0, 16, ctypes.byref(h)) != 0
     assert b"null" in L.dg_last_error()
+
+
+def test_quantize_rejects_bad_arguments_before_any_device_call():
+    import decider_gpu
+    L = decider_gpu.load()
+    fake = 0x1000  # never dereferenced: the checks run first
+    for rows, width, bits, msg in [(1, 64, 5, b"bits must be 8 or 4"), (1, 0, 8, b"bad width")]:
+        assert L.dg_quantize_weights_device(fake, rows, width, bits, fake, fake, None) != 0
+        assert msg in L.dg_last_error()
+    assert L.dg_quantize_weights_device(None, 1, 64, 8, fake, fake, None) != 0
+    assert b"null" in L.dg_last_error()
