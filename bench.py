@@ -13,8 +13,13 @@ scaling, no collective on the data path, time = max over ranks.
 `--workload cfg2` measures config 2 (one 512-token prompt + one noul
 question per step); cfg1, cfg3 and cfg4 the other configs.
 
-value  : prefill tokens/s from the device time of the forward kernels (CUDA
-         events on the engine stream), ids already resident;
+value  : prefill tokens/s from device time, ids already resident: config 5
+         (and 4) the span of each dg_logits_batch call on the device (CUDA
+         events from before its first kernel to the end of its last lane;
+         host gaps between requests included), config 2 the forward kernels;
+lanes  : config 5 deals each rank's requests to --lanes engines sharing one
+         copy of the weights (dg_engine_set_lanes), each driven from its own
+         host thread, so their latency-bound kernels overlap on the GPU;
 e2e    : the same through the public C ABI call (dg_logits_batch / dg_logits:
          host ids in, host logits out, copies inside the timed region);
 roofline: the dominant kernel, the tcgen05 INT8 projection: its launches in
@@ -701,6 +706,8 @@ def run_batch(args, world, rank, local, dist, which):
         # Every rank derives the same plan: the share of each rank, for the report.
         shard = {"tokens_per_rank": [int(sum(toks[i] for i in p)) for p in plan],
                  "requests_per_rank": [len(p) for p in plan]}
+    lanes = args.lanes if which == "cfg5" else 1
+    model.set_lanes(lanes)
     model.gemm_timing_layers(0, min(4, args.layers))
     for _ in range(args.warmup):
         _, st, _, err = model.logits_batch(mine)
@@ -715,12 +722,22 @@ def run_batch(args, world, rank, local, dist, which):
             _, st, ms, err = model.logits_batch(mine)
             wall.append((time.perf_counter() - t0) * 1000.0)
             assert not st.any(), err
-            dev.append(float(ms.sum()))
+            dev.append(model.last_batch_ms())
             per_req += [float(x) for x in ms]
     launches = decider_gpu.launch_count() - n0
     barrier(dist, local)
     g_ms, g_ops, g_n = model.gemm_time()
     g_ms, g_ops, g_n = g_ms - g0_ms, g_ops - g0_ops, g_n - g0_n
+    alone = None
+    if lanes > 1:
+        # The projection with no other lane beside it: one untimed one-lane
+        # pass over up to 32 of this rank's requests, after the timed region.
+        model.set_lanes(1)
+        a0 = model.gemm_time()
+        _, st, _, err = model.logits_batch(mine[:32])
+        assert not st.any(), err
+        a1 = model.gemm_time()
+        alone = ((a1[0] - a0[0]), (a1[1] - a0[1]), (a1[2] - a0[2]))
     model.gemm_timing(False)
     my_ms = sum(dev) / len(dev)
     rank_ms = [my_ms]
@@ -750,9 +767,11 @@ def run_batch(args, world, rank, local, dist, which):
                  roofline={"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
                            "frac": achieved / peak, "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH,
                            "kernel": "gemm_i8_g64_kernel, the projection launches of layers 0-3 in every forward "
-                                     "of the timed steps (achieved = sum 2*M*N*K / sum event time)",
+                                     "the engine's own lane ran in the timed steps (achieved = sum 2*M*N*K / sum "
+                                     "event time)",
                            "launches": int(g_n), "ms_per_launch": g_ms / max(g_n, 1),
                            "peak_source": f"2 x {src} bf16 dense ({bf16} TF/s): int8 dense is twice bf16",
+                           "lanes": lanes,
                            "i8_loop_peak": i8_loop, "frac_of_i8_loop": achieved / i8_loop if i8_loop else None,
                            "i8_loop": "dg_measure_i8_peak: one CTA per SM issuing back-to-back "
                                       f"tcgen05.mma.kind::i8 128x256x32 ({i8_loop_ms:.1f} ms launch), after the "
@@ -761,6 +780,14 @@ def run_batch(args, world, rank, local, dist, which):
                           "what": "device time of one request's forwards, max over ranks"},
                  gpu_launches=int(launches), clocks=clocks.summary(), scaling=scaling)
     line["config"]["tokens_rank0"] = tokens_mine
+    line["config"]["lanes"] = lanes
+    if alone is not None and alone[0] > 0:
+        a_ach = alone[1] / (alone[0] / 1000.0) / 1e12
+        line["roofline"]["alone"] = {
+            "achieved": a_ach, "frac": a_ach / peak, "launches": int(alone[2]),
+            "what": f"the same projection launches timed with no other lane running (one untimed one-lane pass "
+                    f"over up to 32 requests after the timed region); with {lanes} lanes a projection shares "
+                    "the SMs with the other lanes' kernels, so its live launch time is longer"}
     if which == "cfg5":
         tot = sum(shard["tokens_per_rank"])
         line["sharding"] = dict(shard, device_ms_per_rank=rank_ms,
@@ -837,6 +864,8 @@ def main():
                     help="BASELINE config to measure; the default line is cfg5 (256 requests, LPT-sharded over the "
                          "ranks)")
     ap.add_argument("--requests", type=int, default=256, help="cfg5: requests taken from the seeded draw")
+    ap.add_argument("--lanes", type=int, default=2,
+                    help="cfg5: engines per GPU sharing one copy of the weights (dg_engine_set_lanes)")
     args = ap.parse_args()
     args.default_line = args.workload is None
     if args.workload is None:

@@ -3,6 +3,8 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <algorithm>
+#include <thread>
 
 #include "../../include/decider_gpu.h"
 #include "engine.h"
@@ -22,7 +24,15 @@ void note_launches(uint64_t n) { g_launches.fetch_add(n); }
 }  // namespace dg
 
 struct dg_engine {
-  std::unique_ptr<dg::Engine> e;
+  // The engine whose weights this one reads (dg_engine_create_sibling),
+  // held so that the weights outlive every engine sharing them; declared
+  // first, so it is released after `e`.
+  std::shared_ptr<dg::Engine> weights_owner;
+  std::shared_ptr<dg::Engine> e;
+  // dg_engine_set_lanes: engines sharing e's weights that serve a batch's
+  // requests alongside e, each from its own host thread.
+  std::vector<std::unique_ptr<dg::Engine>> lanes;
+  float last_batch_ms = 0.0f;
 };
 struct dg_prefix {
   std::unique_ptr<dg::Prefix> p;
@@ -186,6 +196,24 @@ int dg_engine_create(const dg_model_config* cfg, int precision, int device, int 
   });
 }
 
+int dg_engine_create_sibling(dg_engine* base, dg_engine** out) {
+  return guarded([&] {
+    check_engine(base);
+    if (!out) throw std::runtime_error("null argument");
+    std::unique_ptr<dg_engine> e(new dg_engine());
+    {
+      std::lock_guard<std::mutex> lk(base->e->mu);
+      const dg::Engine& b = *base->e;
+      e->e = std::make_shared<dg::Engine>(b.config(), b.precision(), b.device(), b.max_tokens());
+      e->e->share_weights(b);
+      e->e->exact = b.exact;  // the base's arithmetic mode
+      e->e->batch_questions = b.batch_questions;
+    }
+    e->weights_owner = base->weights_owner ? base->weights_owner : base->e;
+    *out = e.release();
+  });
+}
+
 int dg_engine_set_tensor(dg_engine* e, const char* name, int dtype, const int64_t* shape, int ndim, const void* data) {
   return guarded([&] {
     check_engine(e);
@@ -287,8 +315,30 @@ int dg_engine_set_exact(dg_engine* e, int exact) {
   return guarded([&] {
     check_engine(e);
     e->e->exact = exact != 0;
+    for (auto& l : e->lanes) l->exact = exact != 0;
   });
 }
+
+int dg_engine_set_lanes(dg_engine* e, int lanes) {
+  return guarded([&] {
+    check_engine(e);
+    if (lanes < 1 || lanes > 8) throw std::runtime_error("lanes must be 1 to 8");
+    std::lock_guard<std::mutex> lk(e->e->mu);
+    const dg::Engine& b = *e->e;
+    while (int(e->lanes.size()) > lanes - 1) e->lanes.pop_back();
+    while (int(e->lanes.size()) < lanes - 1) {
+      std::unique_ptr<dg::Engine> l(new dg::Engine(b.config(), b.precision(), b.device(), b.max_tokens()));
+      l->share_weights(b);
+      l->exact = b.exact;
+      l->batch_questions = b.batch_questions;
+      e->lanes.push_back(std::move(l));
+    }
+  });
+}
+
+int dg_engine_lanes(const dg_engine* e) { return e && e->e ? 1 + int(e->lanes.size()) : 0; }
+
+float dg_engine_last_batch_ms(const dg_engine* e) { return e && e->e ? e->last_batch_ms : -1.0f; }
 
 void dg_engine_free(dg_engine* e) { delete e; }
 
@@ -452,6 +502,86 @@ int dg_forward_segments_hidden(dg_engine* e, const dg_prefix* past, const uint32
   });
 }
 
+}  // extern "C"
+
+namespace {
+
+// One request of dg_logits_batch on engine g (NativeEngine::evaluate,
+// src/lib.rs:477-559): the state prefilled once, then its questions, the
+// logits written from `logits_out` on. Returns the status; the device time
+// of its forwards goes to ms.
+int run_request(const dg_engine* e, dg::Engine& g, const dg_request& q, float* logits_out, float& ms) {
+  return guarded([&] {
+    if (!q.questions || q.n_questions == 0) throw std::runtime_error("request has no questions");
+    if (q.past && q.past->owner != e) throw std::runtime_error("prefix belongs to another engine");
+    if (q.past && q.n_state) throw std::runtime_error("a request continues either a prefix or its own state ids");
+    if (q.n_state && !q.state_ids) throw std::runtime_error("null state ids");
+    for (size_t i = 0; i < q.n_questions; ++i) {
+      const dg_question& u = q.questions[i];
+      if (!u.ids || !u.opt_pos || u.n == 0 || u.n_opt == 0)
+        throw std::runtime_error("invalid encoding positions or window");
+      for (size_t j = 0; j < u.n_opt; ++j)
+        if (u.opt_pos[j] + 1 >= u.n) throw std::runtime_error("invalid encoding positions or window");
+    }
+    std::lock_guard<std::mutex> lk(g.mu);
+    std::unique_ptr<dg::Prefix> state;
+    const dg::Prefix* past = q.past ? q.past->p.get() : nullptr;
+    if (q.n_state) {
+      g.forward(q.state_ids, int(std::min<size_t>(q.n_state, 1u << 30)), nullptr, true, nullptr, &state);
+      ms += g.last_forward_ms;
+      past = state.get();
+    }
+    size_t o = 0;
+    // Questions of one length continue the state together: one segmented
+    // forward per group of as many as the workspace holds, each question's
+    // rows the same as its own forward's (bit for bit in reference order).
+    const size_t nq = q.n_questions, len0 = q.questions[0].n;
+    bool together = nq >= 2 && g.batch_questions && g.segments_supported() && len0 <= size_t(g.max_tokens());
+    for (size_t i = 1; together && i < nq; ++i) together = q.questions[i].n == len0;
+    if (together) {
+      const size_t per = std::min(nq, std::max<size_t>(1, size_t(g.max_tokens()) / len0));
+      std::vector<uint32_t> ids;
+      for (size_t i0 = 0; i0 < nq; i0 += per) {
+        const size_t cnt = std::min(per, nq - i0);
+        ids.clear();
+        for (size_t i = i0; i < i0 + cnt; ++i) ids.insert(ids.end(), q.questions[i].ids, q.questions[i].ids + len0);
+        g.forward_segments(ids.data(), int(len0), int(cnt), past, nullptr);
+        ms += g.last_forward_ms;
+        for (size_t j = 0; j < cnt; ++j) {
+          const dg_question& u = q.questions[i0 + j];
+          g.head_logits(int(len0), u.opt_pos, int(u.n_opt), logits_out + o, int(j * len0));
+          o += u.n_opt;
+        }
+      }
+    } else {
+      for (size_t i = 0; i < nq; ++i) {
+        const dg_question& u = q.questions[i];
+        g.forward(u.ids, int(std::min<size_t>(u.n, 1u << 30)), past, false, nullptr, nullptr);
+        ms += g.last_forward_ms;
+        g.head_logits(int(u.n), u.opt_pos, int(u.n_opt), logits_out + o);
+        o += u.n_opt;
+      }
+    }
+  });
+}
+
+// Cost of a request in token-equivalents, as the request sharding across
+// GPUs weighs it: computed tokens, the attention term of the longest
+// window, and a fixed cost per forward pass.
+double request_cost(const dg_request& q) {
+  double tokens = double(q.n_state), window = 0.0, forwards = q.n_state ? 1.0 : 0.0;
+  for (size_t i = 0; q.questions && i < q.n_questions; ++i) {
+    tokens += double(q.questions[i].n);
+    window = std::max(window, double(q.n_state + q.questions[i].n));
+    forwards += 1.0;
+  }
+  return tokens + window * window / 4096.0 + 300.0 * forwards;
+}
+
+}  // namespace
+
+extern "C" {
+
 int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests, float* logits_out, int* status_out,
                     float* request_ms) {
   const int rc = guarded([&] {
@@ -459,70 +589,82 @@ int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests,
     if (n_requests && (!requests || !logits_out)) throw std::runtime_error("null argument");
   });
   if (rc) return rc;
-  std::string first_error;
-  size_t out = 0;
+  // Where each request's logits start (request order).
+  std::vector<size_t> off(n_requests + 1, 0);
   for (size_t r = 0; r < n_requests; ++r) {
-    const dg_request& q = requests[r];
     size_t n_logits = 0;
+    const dg_request& q = requests[r];
     for (size_t i = 0; q.questions && i < q.n_questions; ++i) n_logits += q.questions[i].n_opt;
-    float ms = 0.0f;
-    const int st = guarded([&] {
-      if (!q.questions || q.n_questions == 0) throw std::runtime_error("request has no questions");
-      if (q.past && q.past->owner != e) throw std::runtime_error("prefix belongs to another engine");
-      if (q.past && q.n_state) throw std::runtime_error("a request continues either a prefix or its own state ids");
-      if (q.n_state && !q.state_ids) throw std::runtime_error("null state ids");
-      for (size_t i = 0; i < q.n_questions; ++i) {
-        const dg_question& u = q.questions[i];
-        if (!u.ids || !u.opt_pos || u.n == 0 || u.n_opt == 0)
-          throw std::runtime_error("invalid encoding positions or window");
-        for (size_t j = 0; j < u.n_opt; ++j)
-          if (u.opt_pos[j] + 1 >= u.n) throw std::runtime_error("invalid encoding positions or window");
-      }
-      dg::Engine& g = *e->e;
-      std::lock_guard<std::mutex> lk(g.mu);
-      std::unique_ptr<dg::Prefix> state;
-      const dg::Prefix* past = q.past ? q.past->p.get() : nullptr;
-      if (q.n_state) {
-        g.forward(q.state_ids, int(std::min<size_t>(q.n_state, 1u << 30)), nullptr, true, nullptr, &state);
-        ms += g.last_forward_ms;
-        past = state.get();
-      }
-      size_t o = out;
-      // Questions of one length continue the state together: one segmented
-      // forward per group of as many as the workspace holds, each question's
-      // rows the same as its own forward's (bit for bit in reference order).
-      const size_t nq = q.n_questions, len0 = q.questions[0].n;
-      bool together = nq >= 2 && g.batch_questions && g.segments_supported() && len0 <= size_t(g.max_tokens());
-      for (size_t i = 1; together && i < nq; ++i) together = q.questions[i].n == len0;
-      if (together) {
-        const size_t per = std::min(nq, std::max<size_t>(1, size_t(g.max_tokens()) / len0));
-        std::vector<uint32_t> ids;
-        for (size_t i0 = 0; i0 < nq; i0 += per) {
-          const size_t cnt = std::min(per, nq - i0);
-          ids.clear();
-          for (size_t i = i0; i < i0 + cnt; ++i) ids.insert(ids.end(), q.questions[i].ids, q.questions[i].ids + len0);
-          g.forward_segments(ids.data(), int(len0), int(cnt), past, nullptr);
-          ms += g.last_forward_ms;
-          for (size_t j = 0; j < cnt; ++j) {
-            const dg_question& u = q.questions[i0 + j];
-            g.head_logits(int(len0), u.opt_pos, int(u.n_opt), logits_out + o, int(j * len0));
-            o += u.n_opt;
-          }
-        }
-      } else {
-        for (size_t i = 0; i < nq; ++i) {
-          const dg_question& u = q.questions[i];
-          g.forward(u.ids, int(std::min<size_t>(u.n, 1u << 30)), past, false, nullptr, nullptr);
-          ms += g.last_forward_ms;
-          g.head_logits(int(u.n), u.opt_pos, int(u.n_opt), logits_out + o);
-          o += u.n_opt;
-        }
-      }
-    });
-    if (st && first_error.empty()) first_error = dg_last_error();
-    if (status_out) status_out[r] = st;
-    if (request_ms) request_ms[r] = ms;
-    out += n_logits;
+    off[r + 1] = off[r] + n_logits;
+  }
+  // Requests over the lanes, longest processing time first (a request that
+  // continues a prefix stays on the engine that made it); each lane runs
+  // its share in request order.
+  const size_t lanes = 1 + e->lanes.size();
+  std::vector<std::vector<size_t>> plan(lanes);
+  {
+    std::vector<size_t> order(n_requests);
+    for (size_t r = 0; r < n_requests; ++r) order[r] = r;
+    std::vector<double> cost(n_requests);
+    for (size_t r = 0; r < n_requests; ++r) cost[r] = request_cost(requests[r]);
+    std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return cost[a] > cost[b]; });
+    std::vector<double> load(lanes, 0.0);
+    for (size_t r : order) {
+      size_t best = 0;
+      if (!requests[r].past)
+        for (size_t k = 1; k < lanes; ++k)
+          if (load[k] < load[best]) best = k;
+      plan[best].push_back(r);
+      load[best] += cost[r];
+    }
+    for (auto& p : plan) std::sort(p.begin(), p.end());
+  }
+  std::vector<int> status(n_requests, 0);
+  std::vector<float> ms(n_requests, 0.0f);
+  std::vector<std::string> errors(n_requests);
+  // The batch's device span: every lane's stream waits for an event of the
+  // engine's stream recorded before the first request; each lane records
+  // its end after its last request.
+  dg::Engine& g0 = *e->e;
+  std::vector<cudaEvent_t> ev(lanes + 1, nullptr);
+  bool timed = true;
+  for (auto& x : ev) timed = timed && cudaEventCreate(&x) == cudaSuccess;
+  if (timed) {
+    cudaSetDevice(g0.device());
+    timed = cudaEventRecord(ev[0], g0.stream()) == cudaSuccess;
+  }
+  auto run_lane = [&](size_t k) {
+    dg::Engine& g = k == 0 ? g0 : *e->lanes[k - 1];
+    cudaSetDevice(g.device());
+    if (timed) cudaStreamWaitEvent(g.stream(), ev[0], 0);
+    for (size_t r : plan[k]) {
+      float t = 0.0f;
+      status[r] = run_request(e, g, requests[r], logits_out + off[r], t);
+      ms[r] = t;
+      if (status[r]) errors[r] = dg_last_error();
+    }
+    if (timed) cudaEventRecord(ev[k + 1], g.stream());
+  };
+  std::vector<std::thread> threads;
+  for (size_t k = 1; k < lanes; ++k)
+    if (!plan[k].empty()) threads.emplace_back(run_lane, k);
+  run_lane(0);
+  for (auto& t : threads) t.join();
+  float span = 0.0f;
+  for (size_t k = 0; timed && k < lanes; ++k) {
+    if (k > 0 && plan[k].empty()) continue;
+    float t = 0.0f;
+    if (cudaEventSynchronize(ev[k + 1]) == cudaSuccess && cudaEventElapsedTime(&t, ev[0], ev[k + 1]) == cudaSuccess)
+      span = std::max(span, t);
+  }
+  for (auto& x : ev)
+    if (x) cudaEventDestroy(x);
+  e->last_batch_ms = span;
+  std::string first_error;
+  for (size_t r = 0; r < n_requests; ++r) {
+    if (status_out) status_out[r] = status[r];
+    if (request_ms) request_ms[r] = ms[r];
+    if (status[r] && first_error.empty()) first_error = errors[r];
   }
   if (first_error.empty()) return 0;
   g_error = first_error;

@@ -39,7 +39,16 @@ struct DevBuf {
   size_t bytes = 0;
   bool pooled = false;  // from the device's stream-ordered pool (cudaMallocAsync)
   int device = -1;      // the pool's device (pooled buffers)
+  bool borrowed = false;  // a view of another buffer's memory: never freed through this one
   DevBuf() = default;
+  // A non-owning view of o's memory (weights shared between engines).
+  static DevBuf view_of(const DevBuf& o) {
+    DevBuf b;
+    b.ptr = o.ptr;
+    b.bytes = o.bytes;
+    b.borrowed = o.ptr != nullptr;
+    return b;
+  }
   explicit DevBuf(size_t n);
   // Stream-ordered allocation from the device's default memory pool, for
   // buffers made and dropped per request (prefix caches): no device-wide
@@ -47,10 +56,12 @@ struct DevBuf {
   static DevBuf pooled_on(size_t n, cudaStream_t s);
   DevBuf(const DevBuf&) = delete;
   DevBuf& operator=(const DevBuf&) = delete;
-  DevBuf(DevBuf&& o) noexcept : ptr(o.ptr), bytes(o.bytes), pooled(o.pooled), device(o.device) {
+  DevBuf(DevBuf&& o) noexcept
+      : ptr(o.ptr), bytes(o.bytes), pooled(o.pooled), device(o.device), borrowed(o.borrowed) {
     o.ptr = nullptr;
     o.bytes = 0;
     o.pooled = false;
+    o.borrowed = false;
   }
   DevBuf& operator=(DevBuf&& o) noexcept;
   ~DevBuf();
@@ -111,6 +122,13 @@ class Engine {
   void set_tensor(const std::string& name, int dtype, const std::vector<int64_t>& shape, const void* data);
   void fill_synthetic(uint64_t seed, float stddev);
   void finalize();
+  // Instead of staging and finalize: use the weights of `base` (a finalized
+  // engine on the same device, same model, precision and token budget) as
+  // read-only views. Stream, workspaces, CUDA graphs and prefixes stay this
+  // engine's own, so engines that share weights can run forwards
+  // concurrently from different host threads. The caller keeps `base`
+  // alive while this engine lives.
+  void share_weights(const Engine& base);
   // Model::run: hidden [n][hidden] to host (nullable); capture -> new prefix.
   void forward(const uint32_t* ids, int n, const Prefix* past, bool capture, float* hidden_out,
                std::unique_ptr<Prefix>* captured);
@@ -146,6 +164,7 @@ class Engine {
   bool batch_questions = true;
   bool fast_path() const { return fast_; }
   int device() const { return device_; }
+  int precision() const { return precision_; }
   cudaStream_t stream() const { return stream_; }
   std::mutex mu;
   // Exact FP32 promotion order in the tcgen05 projections (reference order).
@@ -176,6 +195,9 @@ class Engine {
   void mixer_tail(int i, int n, int start, const Prefix::LayerState* past, Prefix::LayerState* cap,
                   const float* raw, int ldr);
   void check_status();
+  // The forward's device buffers, sized for max_tokens_ rows (ld_proj: the
+  // widest fused input projection).
+  void alloc_workspaces(int ld_proj);
   // Debug copy of the quantised activations (xq_) after each quantisation of
   // a debug_layer_codes call; a no-op otherwise.
   int8_t* dbg_codes_ = nullptr;

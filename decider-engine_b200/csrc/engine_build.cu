@@ -225,7 +225,76 @@ void Engine::finalize() {
       }
     rope_ = upload(tab);
   }
-  // Workspaces.
+  alloc_workspaces(ld_proj);
+  finalized_ = true;
+}
+
+// Read-only views of a projection / layer of another engine's weights.
+static DevProj proj_view(const DevProj& p) {
+  DevProj d;
+  d.in = p.in;
+  d.out = p.out;
+  d.out_pad = p.out_pad;
+  d.wq = DevBuf::view_of(p.wq);
+  d.ws_t = DevBuf::view_of(p.ws_t);
+  d.lora_a = DevBuf::view_of(p.lora_a);
+  d.lora_b = DevBuf::view_of(p.lora_b);
+  d.chunk_pid = DevBuf::view_of(p.chunk_pid);
+  d.maps = p.maps;
+  d.lora_rows = p.lora_rows;
+  d.part_off = p.part_off;
+  d.g = p.g;
+  d.w_f32 = DevBuf::view_of(p.w_f32);
+  d.scale_rows = DevBuf::view_of(p.scale_rows);
+  d.bias = DevBuf::view_of(p.bias);
+  return d;
+}
+
+static Layer layer_view(const Layer& L) {
+  Layer v;
+  v.full = L.full;
+  v.input_norm = DevBuf::view_of(L.input_norm);
+  v.post_norm = DevBuf::view_of(L.post_norm);
+  v.in_proj = proj_view(L.in_proj);
+  v.out_proj = proj_view(L.out_proj);
+  v.mlp_in = proj_view(L.mlp_in);
+  v.down = proj_view(L.down);
+  for (const DevProj& p : L.parts) v.parts.push_back(proj_view(p));
+  v.q_norm = DevBuf::view_of(L.q_norm);
+  v.k_norm = DevBuf::view_of(L.k_norm);
+  v.conv = DevBuf::view_of(L.conv);
+  v.dt = DevBuf::view_of(L.dt);
+  v.decay_rate = DevBuf::view_of(L.decay_rate);
+  v.norm = DevBuf::view_of(L.norm);
+  return v;
+}
+
+void Engine::share_weights(const Engine& base) {
+  if (finalized_ || !staged_.empty()) throw std::runtime_error("share_weights: this engine already has weights");
+  if (!base.finalized_) throw std::runtime_error("share_weights: the base engine is not finalized");
+  if (base.device_ != device_ || base.precision_ != precision_ || base.max_tokens_ != max_tokens_ ||
+      base.c_.layers != c_.layers || base.c_.hidden != c_.hidden || base.c_.vocab != c_.vocab ||
+      base.c_.pointer_dim != c_.pointer_dim || base.c_.rank != c_.rank)
+    throw std::runtime_error("share_weights: the engines differ in device, precision, model or token budget");
+  DG_CUDA(cudaSetDevice(device_));
+  fast_ = base.fast_;
+  layers_.clear();
+  for (const Layer& L : base.layers_) layers_.push_back(layer_view(L));
+  embedding_ = DevBuf::view_of(base.embedding_);
+  final_norm_ = DevBuf::view_of(base.final_norm_);
+  rope_ = DevBuf::view_of(base.rope_);
+  rope_half_ = base.rope_half_;
+  head_norm_w_ = DevBuf::view_of(base.head_norm_w_);
+  head_norm_b_ = DevBuf::view_of(base.head_norm_b_);
+  head_q_ = proj_view(base.head_q_);
+  head_k_ = proj_view(base.head_k_);
+  alloc_workspaces(base.ld_proj_);
+  finalized_ = true;
+}
+
+void Engine::alloc_workspaces(int ld_proj) {
+  const Config& c = c_;
+  const int H = c.hidden, I = c.intermediate;
   const int M = max_tokens_;
   const int kmax = std::max(std::max(H, I), std::max(c.qw(), c.vd()));
   ldxs_ = round_up(M, 128);
@@ -282,7 +351,6 @@ void Engine::finalize() {
   status_ = DevBuf(sizeof(DeviceStatus));
   DG_CUDA(cudaMemset(status_.ptr, 0, sizeof(DeviceStatus)));
   DG_CUDA(cudaDeviceSynchronize());
-  finalized_ = true;
 }
 
 }  // namespace dg

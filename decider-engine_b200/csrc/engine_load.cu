@@ -78,18 +78,22 @@ static void release(void* p, bool pooled, int device) {
 }
 DevBuf& DevBuf::operator=(DevBuf&& o) noexcept {
   if (this != &o) {
-    release(ptr, pooled, device);
+    if (!borrowed) release(ptr, pooled, device);
     ptr = o.ptr;
     bytes = o.bytes;
     pooled = o.pooled;
     device = o.device;
+    borrowed = o.borrowed;
     o.ptr = nullptr;
     o.bytes = 0;
     o.pooled = false;
+    o.borrowed = false;
   }
   return *this;
 }
-DevBuf::~DevBuf() { release(ptr, pooled, device); }
+DevBuf::~DevBuf() {
+  if (!borrowed) release(ptr, pooled, device);
+}
 
 static void host_parallel(size_t n, const std::function<void(size_t, size_t)>& f) {
   size_t t = std::min<size_t>(std::max(1u, std::thread::hardware_concurrency()), 32);

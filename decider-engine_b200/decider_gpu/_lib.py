@@ -14,7 +14,8 @@ LIB_PATH = os.path.join(PKG_ROOT, "libdecider_gpu.so")
 # Every entry point declared in include/decider_gpu.h.
 SYMBOLS = [
     "dg_last_error", "dg_launch_count",
-    "dg_engine_create", "dg_engine_set_tensor", "dg_engine_fill_synthetic", "dg_engine_finalize",
+    "dg_engine_create", "dg_engine_create_sibling", "dg_engine_set_lanes", "dg_engine_lanes",
+    "dg_engine_last_batch_ms", "dg_engine_set_tensor", "dg_engine_fill_synthetic", "dg_engine_finalize",
     "dg_engine_load", "dg_engine_load_with_limits", "dg_load_limits_default", "dg_read_checkpoint_config",
     "dg_engine_fast_path", "dg_engine_set_exact", "dg_engine_free", "dg_engine_stream",
     "dg_engine_last_forward_ms", "dg_engine_last_launches", "dg_engine_gemm_timing", "dg_engine_gemm_time",
@@ -62,6 +63,11 @@ def load() -> C.CDLL:
     L.dg_last_error.restype = C.c_char_p
     L.dg_launch_count.restype = C.c_uint64
     L.dg_engine_create.argtypes = [C.POINTER(ModelConfig), i32, i32, i32, C.POINTER(vp)]
+    L.dg_engine_create_sibling.argtypes = [vp, C.POINTER(vp)]
+    L.dg_engine_set_lanes.argtypes = [vp, i32]
+    L.dg_engine_lanes.argtypes = [vp]
+    L.dg_engine_last_batch_ms.argtypes = [vp]
+    L.dg_engine_last_batch_ms.restype = C.c_float
     L.dg_engine_load.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp)]
     L.dg_engine_load_with_limits.argtypes = [C.c_char_p, i32, C.POINTER(LoadLimits), i32, i32, C.POINTER(vp)]
     L.dg_load_limits_default.argtypes = [C.POINTER(LoadLimits)]

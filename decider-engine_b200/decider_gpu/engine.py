@@ -132,6 +132,32 @@ class GpuModel:
         check(load().dg_engine_finalize(self.h))
         return self
 
+    def sibling(self) -> "GpuModel":
+        """A second engine on this one's device that reads this one's weights
+        (dg_engine_create_sibling): its own stream and buffers, so the two
+        can serve requests concurrently from different host threads."""
+        h = C.c_void_p()
+        check(load().dg_engine_create_sibling(self.h, C.byref(h)))
+        m = GpuModel.__new__(GpuModel)
+        m.config, m.precision, m.pointer_dim, m._lt = self.config, self.precision, self.pointer_dim, self._lt
+        m.hidden = self.hidden
+        m.h = h.value
+        return m
+
+    def set_lanes(self, lanes: int) -> None:
+        """Concurrent lanes of logits_batch (dg_engine_set_lanes): the batch's
+        requests are dealt to `lanes` engines sharing these weights, each run
+        from its own host thread."""
+        check(load().dg_engine_set_lanes(self.h, int(lanes)))
+
+    @property
+    def lanes(self) -> int:
+        return int(load().dg_engine_lanes(self.h))
+
+    def last_batch_ms(self) -> float:
+        """Device time of the last logits_batch call, first kernel to the end of its last lane."""
+        return float(load().dg_engine_last_batch_ms(self.h))
+
     @property
     def fast_path(self) -> bool:
         return bool(load().dg_engine_fast_path(self.h))

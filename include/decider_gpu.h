@@ -54,9 +54,9 @@ uint64_t dg_launch_count(void);
  * (src/qwen.rs:291-406, src/lib.rs:94-105). Tensors use the checkpoint names
  * without the "model.language_model." prefix; adapter tensors keep
  * "base_model.model."; pointer-head tensors are "head.<name>". Projection
- * weights ("layers.*_proj.weight") are quantised at staging per `precision`
- * exactly as Data::quantize (src/weights.rs:98-146). max_tokens bounds the
- * rows of one forward call (1..4096). */
+ * weights ("layers.*_proj.weight") are quantised per `precision` exactly as
+ * Data::quantize (src/weights.rs:98-146), on the device when the engine is
+ * finalized. max_tokens bounds the rows of one forward call (1..4096). */
 int dg_engine_create(const dg_model_config* cfg, int precision, int device, int max_tokens, dg_engine** out);
 int dg_engine_set_tensor(dg_engine* e, const char* name, int dtype, const int64_t* shape, int ndim,
                          const void* data);
@@ -64,6 +64,16 @@ int dg_engine_set_tensor(dg_engine* e, const char* name, int dtype, const int64_
  * weights 1, biases 0): synthetic checkpoints of a given architecture. */
 int dg_engine_fill_synthetic(dg_engine* e, uint64_t seed, float stddev);
 int dg_engine_finalize(dg_engine* e);
+/* A second engine on the base's device that reads the base's weights
+ * (finalized, read-only; no copy) and has its own stream, forward buffers,
+ * CUDA graphs and prefixes; it starts in the base's arithmetic mode. Engines that share weights may run forward,
+ * logits and batch calls concurrently from different host threads (one call
+ * at a time per engine): on one GPU, two or three request streams overlap
+ * each other's latency-bound kernels. A prefix belongs to the engine that
+ * made it. The weights stay alive until the base and every sibling have
+ * been freed, in any order. No counterpart in the reference, whose engine
+ * serves one forward at a time. */
+int dg_engine_create_sibling(dg_engine* base, dg_engine** out);
 /* 1 when the tcgen05 INT8 path serves the projections, 0 for the generic kernels. */
 int dg_engine_fast_path(const dg_engine* e);
 /* 1: tcgen05 promotion in the reference's FP32 order (default); 0: fused multiply-add. */
@@ -192,10 +202,26 @@ int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n
  * request, concatenated in order. status_out (nullable, [n_requests]) gets
  * 0 or 1 per request and request_ms (nullable) the device time of that
  * request's forwards; a failed request's logits are unspecified and the
- * batch continues with the next request. Returns 0 when every request succeeded, otherwise 1 with
- * dg_last_error() holding the first failure's message. Requests run in order
- * on the engine's device and stream; to spread a batch over several GPUs,
+ * batch continues with the next request. Returns 0 when every request
+ * succeeded, otherwise 1 with dg_last_error() holding the first failure's
+ * message (in request order). With one lane (the default) the requests run
+ * in order on the engine's stream; with dg_engine_set_lanes(e, k) they are
+ * dealt to k lanes (the engine and k - 1 engines sharing its weights,
+ * longest processing time first; a request that continues a prefix stays on
+ * the engine that made it), each lane running its share in order from its
+ * own host thread, so their kernels overlap on the device. Results do not
+ * depend on the lane a request ran on. To spread a batch over several GPUs,
  * give each device's engine its share (one host thread or process per GPU). */
+/* Lanes of dg_logits_batch (1 to 8; 1 = the engine alone). Each extra lane
+ * is an engine on the same device reading this engine's weights (see
+ * dg_engine_create_sibling) with its own stream and forward buffers (about
+ * 1.2 GB at max_tokens 4096 for the 2B model). dg_engine_set_exact applies
+ * to every lane. */
+int dg_engine_set_lanes(dg_engine* e, int lanes);
+int dg_engine_lanes(const dg_engine* e);
+/* Device time of the last dg_logits_batch call from its first kernel to the
+ * end of its last lane (CUDA events; host gaps between requests included). */
+float dg_engine_last_batch_ms(const dg_engine* e);
 typedef struct dg_question {
   const uint32_t* ids;
   size_t n;

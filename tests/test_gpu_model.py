@@ -503,3 +503,52 @@ def test_logits_batch_runs_equal_length_questions_together(small, exact, monkeyp
             assert np.array_equal(results["1"][1][i], single), i
         else:
             assert np.abs(results["1"][1][i] - single).max() <= 1e-2 * max(1.0, np.abs(single).max()), i
+
+
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
+def test_logits_batch_lanes_and_siblings_give_the_same_logits(small, exact):
+    """dg_logits_batch over three lanes (engines sharing the weights, each
+    from its own host thread) returns, request for request, the logits,
+    statuses and first error of the one-lane call, bit for bit: a request's
+    result does not depend on the lane it ran on or on what ran beside it.
+    A request that continues a prefix stays on the engine that made it. A
+    sibling engine (dg_engine_create_sibling) gives the base engine's logits
+    and keeps working after the base has been freed."""
+    import gc
+    cfg, tensors = small
+    m = _gpu_small(cfg, tensors)
+    m.set_exact(exact)
+    rng = np.random.default_rng(77)
+    ids = lambda n: rng.integers(0, cfg["vocab_size"], n)
+    past = m.prefill(ids(90))
+    reqs = []
+    for k in range(9):
+        n = int(rng.integers(20, 400))
+        if k % 3 == 0:
+            reqs.append({"state": ids(n), "questions": [(ids(32), [5, 30]), (ids(32), [1, 2, 29])]})
+        else:
+            reqs.append({"questions": [(ids(n), [n - 3, n - 2])]})
+    reqs.insert(4, {"past": past, "questions": [(ids(21), [4, 19])]})
+    reqs.insert(7, {"questions": [(ids(10), [10])]})  # option position outside the question
+    one, st1, ms1, err1 = m.logits_batch(reqs)
+    assert list(st1) == [int(i == 7) for i in range(len(reqs))], (st1, err1)
+    assert "invalid encoding positions" in err1
+    assert m.lanes == 1 and m.last_batch_ms() > 0
+    m.set_lanes(3)
+    assert m.lanes == 3
+    for _ in range(2):
+        three, st3, ms3, err3 = m.logits_batch(reqs)
+        assert list(st3) == list(st1) and st1[7] == 1 and err3 == err1
+        for a, b in zip(one, three):
+            for x, y in zip(a, b):
+                assert np.array_equal(x, y)
+        assert m.last_batch_ms() > 0
+        assert all(ms3[i] > 0 for i in range(len(reqs)) if i != 7), (ms1, ms3)
+    m.set_lanes(1)
+    s = m.sibling()
+    q, pos = ids(150), [140, 141]
+    ref = m.logits(q, pos)
+    assert np.array_equal(s.logits(q, pos), ref)
+    del m, past
+    gc.collect()
+    assert np.array_equal(s.logits(q, pos), ref)
