@@ -13,7 +13,7 @@
 //
 // delta_chunk_prep_kernel (one CTA per sequence x head x chunk, all chunks in
 // parallel) builds T, U, W, the masked Q K^T and the decay vectors;
-// delta_chunk_scan_kernel (one CTA per sequence x head x 16 value columns)
+// delta_chunk_scan_kernel (one CTA per sequence x head x 32 value columns)
 // carries the state slice through the chunks. FP32 throughout.
 #include "launch.h"
 
@@ -21,9 +21,13 @@ namespace dg {
 
 namespace {
 
-constexpr int CK = 64, DK = 128, SC = 16;
-// Scan threads per CTA (measured in the 2B forward: 128 beats 64 and 256).
-constexpr int SCAN_NT = 128;
+constexpr int CK = 64, DK = 128;
+// Scan CTAs: SC value columns on 8 * SC threads (each thread the same tile).
+// 16 columns (128 threads) keep one sequence's scan on 8 CTAs per head, the
+// shorter latency per chunk; 32 columns (256 threads) halve the CTAs and the
+// W / K staging traffic per column, which pays when many sequences fill the
+// GPU anyway (measured: 64 sequences x 4096 tokens 38.9 -> 34.0 ms; one
+// 512-token sequence 8.45 -> 8.72 ms per 24-layer forward).
 
 // Per-chunk products written by the prep kernel.
 struct ChunkOut {
@@ -253,12 +257,13 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
   }
 }
 
-// Sequential pass over the chunks for one sequence, head and 16 value
+// Sequential pass over the chunks for one sequence, head and SC value
 // columns: D = U - W S0 and S_C = G_C S0 + K^T diag(G_C / G) D. The state
-// slice S[128][16] stays in shared memory; chunk c + 1's W, K, U slice and
+// slice S[128][SC] stays in shared memory; chunk c + 1's W, K, U slice and
 // decay are copied in (cp.async) while chunk c is computed. Each chunk's
 // starting state and D go to `states` for the output pass.
 constexpr int SCAN_LD = DK + 4;  // padded row stride, keeps 16-byte alignment
+template <int SC>
 struct ScanStage {
   float W[CK][SCAN_LD];
   float K[CK][SCAN_LD];
@@ -271,24 +276,25 @@ __device__ __forceinline__ void cp16(void* smem, const void* gmem, int src_bytes
                : "memory");
 }
 
-// NT threads, register tiles: with NG = NT / 4 row groups, thread (g, q)
-// (g = tid / 4, q = tid % 4) owns in D = U - W S0 the rows g + NG r
-// (r < 64 / NG) and in the state update the rows 4g + (r % 4) + 64 (r / 4)
-// (r < 128 / NG), each at columns 4q .. 4q + 3. Every output keeps the single
+// NT threads, register tiles: with CQ = SC / 4 column quads and
+// NG = NT / CQ row groups, thread (g, q) (g = tid / CQ, q = tid % CQ) owns
+// in D = U - W S0 the rows g + NG r (r < 64 / NG) and in the state update the
+// rows 4g + (r % 4) + 64 (r / 4) (r < 128 / NG), each at columns
+// 4q .. 4q + 3. Every output keeps the single
 // FMA chain, in the same order, of a one-output-per-thread formulation, so
 // the results do not depend on the tiling; the tiles cut the shared-memory
 // operand traffic per FMA.
-template <int NT>
+template <int NT, int SC>
 __global__ void __launch_bounds__(NT) delta_chunk_scan_kernel(DeltaArgs a, const ChunkOut* __restrict__ outs,
                                                               ChunkState* __restrict__ states, int chunks) {
-  constexpr int SCAN_THREADS = NT, NG = NT / 4, RD = CK / NG, RS = DK / NG;
+  constexpr int CQ = SC / 4, SCAN_THREADS = NT, NG = NT / CQ, RD = CK / NG, RS = DK / NG;
   static_assert(RD >= 1 && RS % 4 == 0 && (RS == 4 || NG == 16), "tile shape");
   griddep_wait();
   griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* S = sm;                                            // [DK][SC]
   float* D = S + DK * SC;                                   // [CK][SC]
-  ScanStage* stg = reinterpret_cast<ScanStage*>(D + CK * SC);  // [2]
+  ScanStage<SC>* stg = reinterpret_cast<ScanStage<SC>*>(D + CK * SC);  // [2]
   const int tid = threadIdx.x;
   const int groups = a.dv / SC;
   const int slice = blockIdx.x % groups, h = (blockIdx.x / groups) % a.value_heads;
@@ -297,7 +303,7 @@ __global__ void __launch_bounds__(NT) delta_chunk_scan_kernel(DeltaArgs a, const
   const float* kb = a.k + bi * a.bs_qkv + kh * DK;
   float* Sg = a.state + bi * a.bs_state + size_t(h) * DK * a.dv;
   const size_t head = bi * a.value_heads + h;
-  auto stage = [&](int c, ScanStage& st) {
+  auto stage = [&](int c, ScanStage<SC>& st) {
     const ChunkOut& co = outs[head * chunks + c];
     const int t0 = c * CK, tn = min(CK, a.n - t0);
     for (int i = tid; i < CK * (DK / 4); i += SCAN_THREADS) {
@@ -315,9 +321,9 @@ __global__ void __launch_bounds__(NT) delta_chunk_scan_kernel(DeltaArgs a, const
   };
   for (int e = tid; e < DK * SC; e += SCAN_THREADS) S[e] = Sg[size_t(e / SC) * a.dv + j0 + e % SC];
   stage(0, stg[0]);
-  const int g = tid >> 2, jc = (tid & 3) * 4;
+  const int g = tid / CQ, jc = (tid % CQ) * 4;
   for (int c = 0; c < chunks; ++c) {
-    const ScanStage& st = stg[c & 1];
+    const ScanStage<SC>& st = stg[c & 1];
     ChunkState& cs = states[head * chunks + c];
     const int t0 = c * CK, tn = min(CK, a.n - t0);
     if (c + 1 < chunks) {
@@ -526,19 +532,27 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   ChunkOut* outs = static_cast<ChunkOut*>(workspace);
   ChunkState* states = reinterpret_cast<ChunkState*>(outs + units);
   const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK + (CK / 16 - 1) * 256) * sizeof(float);
-  const int scan_smem = (DK * SC + CK * SC) * sizeof(float) + 2 * sizeof(ScanStage);
+  auto scan_smem = [](int sc, int stage_bytes) { return (DK * sc + CK * sc) * int(sizeof(float)) + 2 * stage_bytes; };
+  const int scan16_smem = scan_smem(16, sizeof(ScanStage<16>)), scan32_smem = scan_smem(32, sizeof(ScanStage<32>));
   const int out_smem = (CK * OQ_LD + DK * OS_LD + CK * OK_LD + CK * OS_LD) * sizeof(float);
   static std::atomic<uint64_t> configured{0};
   once_per_device(configured, [&] {
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, prep_smem));
-    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel<SCAN_NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 scan_smem));
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel<128, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 scan16_smem));
+    DG_CUDA(cudaFuncSetAttribute(delta_chunk_scan_kernel<256, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 scan32_smem));
     DG_CUDA(cudaFuncSetAttribute(delta_chunk_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, out_smem));
   });
   launch_pdl(delta_chunk_prep_kernel, dim3(int(units)), dim3(256), prep_smem, s, a, outs, chunks);
   DG_CUDA(cudaGetLastError());
-  launch_pdl(delta_chunk_scan_kernel<SCAN_NT>, dim3(batch * a.value_heads * (a.dv / SC)), dim3(SCAN_NT), scan_smem,
-             s, a, outs, states, chunks);
+  // Wide slices once they make at least two waves of scan CTAs.
+  if (size_t(batch) * a.value_heads * (a.dv / 32) >= 2 * 148)
+    launch_pdl(delta_chunk_scan_kernel<256, 32>, dim3(batch * a.value_heads * (a.dv / 32)), dim3(256), scan32_smem, s,
+               a, outs, states, chunks);
+  else
+    launch_pdl(delta_chunk_scan_kernel<128, 16>, dim3(batch * a.value_heads * (a.dv / 16)), dim3(128), scan16_smem, s,
+               a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());
   launch_pdl(delta_chunk_out_kernel, dim3(int(units) * (a.dv / OUT_COLS)), dim3(256), out_smem, s, a, outs, states, chunks);
   DG_CUDA(cudaGetLastError());

@@ -192,10 +192,15 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
   float* nb = n_.as<float>();
   float* mid = mid_.as<float>();
   float* proj = proj_.as<float>();
+  // mid = x · Aᵀ of a projection's fused LoRA parts (x: k-wide rows).
+  auto lora_a = [&](const float* xin, int k, const DevProj& p) {
+    launch_lora_a(xin, k, n, k, p.lora_a.as<float>(), p.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(),
+                  lora_part_.bytes / 4, status(), lora_overlap_);
+  };
   launch_norm_quant(x, H, n, H, L.input_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
   dump_codes(n, H);
-  launch_lora_a(nb, H, n, H, L.in_proj.lora_a.as<float>(), L.in_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
+  lora_a(nb, H, L.in_proj);
   run_proj_fast(L.in_proj, n, mid, proj, ld_proj_, kEpiWrite);
   const float* mixed_in;
   int kin;
@@ -243,17 +248,17 @@ void Engine::layer_fast(int i, int n, int start, const Prefix::LayerState* past,
     mixed_in = ofin_.as<float>();
     kin = c.vd();
   }
-  launch_lora_a(mixed_in, kin, n, kin, L.out_proj.lora_a.as<float>(), L.out_proj.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
+  lora_a(mixed_in, kin, L.out_proj);
   run_proj_fast(L.out_proj, n, mid, x, H, kEpiAdd);  // x += mixed (residual_norm's add)
   launch_norm_quant(x, H, n, H, L.post_norm.as<float>(), c.eps, nb, H, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
   dump_codes(n, H);
-  launch_lora_a(nb, H, n, H, L.mlp_in.lora_a.as<float>(), L.mlp_in.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
+  lora_a(nb, H, L.mlp_in);
   run_proj_fast(L.mlp_in, n, mid, h_.as<float>(), I, kEpiSwiGlu);
   launch_norm_quant(h_.as<float>(), I, n, I, nullptr, c.eps, nullptr, 0, xq_.as<int8_t>(), xs_.as<float>(), ldxs_,
                     status(), stream_);
   dump_codes(n, I);
-  launch_lora_a(h_.as<float>(), I, n, I, L.down.lora_a.as<float>(), L.down.lora_rows, mid, 128, exact, stream_, lora_part_.as<float>(), lora_part_.bytes / 4, status(), lora_overlap_);
+  lora_a(h_.as<float>(), I, L.down);
   run_proj_fast(L.down, n, mid, x, H, kEpiAdd);
 }
 

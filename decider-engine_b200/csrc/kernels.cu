@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(256) lora_a_kernel(const float* __restrict__ x
 #pragma unroll
     for (int b = 0; b < TR; ++b) acc[a][b] = 0.0f;
   if (m0 < M) {
-#pragma unroll(TM == 1 ? 4 : 2)
+#pragma unroll(TM == 1 ? 16 : 2)
     for (int k = lane8; k < kfull; k += 8) {
       float xv[TM], av[TR];
 #pragma unroll
@@ -677,9 +677,11 @@ void launch_lora_a(const float* x, int ldx, int M, int K, const float* A, int R,
   const int blocks = int((threads + 255) / 256);
   if (exact && M <= 16) {
     // One row x one output per group of eight lanes: the head's few rows
-    // still spread over R * M * 8 threads.
+    // still spread over R * M * 8 threads, in blocks of 64 so that they
+    // reach many SMs, each lane with 16 steps of loads in flight (the chain
+    // of one output lane is K / 8 dependent adds; its loads are not).
     const long t1 = long(M) * R * 8;
-    launch_pdl(lora_a_kernel<true, 1, 1>, dim3(int((t1 + 255) / 256)), dim3(256), 0, s, x, ldx, M, K, A, R, mid, ldm);
+    launch_pdl(lora_a_kernel<true, 1, 1>, dim3(int((t1 + 63) / 64)), dim3(64), 0, s, x, ldx, M, K, A, R, mid, ldm);
   } else if (exact) {
     launch_k(overlap || pdl_enabled(), lora_a_kernel<true>, dim3(blocks), dim3(256), 0, s, x, ldx, M, K, A, R, mid,
              ldm);
