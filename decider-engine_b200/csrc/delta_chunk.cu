@@ -46,15 +46,18 @@ struct ChunkState {
   float D[CK][DK];  // U - W S0
 };
 
-__global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, ChunkOut* __restrict__ outs,
+// Shared memory holds K and Q, and V once Q is no longer needed (V is loaded
+// by the warps the triangular solve leaves idle), so two CTAs fit on an SM
+// and one CTA's solve overlaps the other's products.
+__global__ void __launch_bounds__(256, 2) delta_chunk_prep_kernel(DeltaArgs a, ChunkOut* __restrict__ outs,
                                                                int chunks) {
   griddep_wait();
   griddep_launch();
   extern __shared__ __align__(16) float sm[];
   float* Ks = sm;                   // [CK][DK + 1]
   float* Qs = Ks + CK * (DK + 1);   // [CK][DK + 1]
-  float* Vs = Qs + CK * (DK + 1);   // [CK][DK + 1]  (later reused)
-  float* L = Vs + CK * (DK + 1);    // [CK][CK + 1]
+  float* Vs = Qs;                   // [CK][DK + 1]: V after the Q K^T products
+  float* L = Qs + CK * (DK + 1);    // [CK][CK + 1]
   float* T = L + CK * (CK + 1);     // [CK][CK + 1]
   float* lg = T + CK * (CK + 1);    // [CK] cumulative log decay
   float* bt = lg + CK;              // [CK]
@@ -71,18 +74,15 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
   const float* vb = a.v + bi * a.bs_qkv + h * a.dv;
   for (int i = tid; i < CK * (DK / 4); i += 256) {
     const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
-    float4 q4 = make_float4(0, 0, 0, 0), k4 = q4, v4 = q4;
+    float4 q4 = make_float4(0, 0, 0, 0), k4 = q4;
     if (t < tn) {
       q4 = *reinterpret_cast<const float4*>(qb + size_t(t0 + t) * a.ld_qk + d);
       k4 = *reinterpret_cast<const float4*>(kb + size_t(t0 + t) * a.ld_qk + d);
-      v4 = *reinterpret_cast<const float4*>(vb + size_t(t0 + t) * a.ld_v + d);
     }
     float* qd = Qs + t * (DK + 1) + d;
     float* kd = Ks + t * (DK + 1) + d;
-    float* vd = Vs + t * (DK + 1) + d;
     qd[0] = q4.x; qd[1] = q4.y; qd[2] = q4.z; qd[3] = q4.w;
     kd[0] = k4.x; kd[1] = k4.y; kd[2] = k4.z; kd[3] = k4.w;
-    vd[0] = v4.x; vd[1] = v4.y; vd[2] = v4.z; vd[3] = v4.w;
   }
   if (tid < 32) {
     // Cumulative log decay over the chunk (two tokens per lane, then a scan).
@@ -188,6 +188,15 @@ __global__ void __launch_bounds__(256) delta_chunk_prep_kernel(DeltaArgs a, Chun
         float acc = 0.0f;
         for (int u = s; u < t; ++u) acc = __fmaf_rn(L[t * (CK + 1) + u], T[u * (CK + 1) + s], acc);
         T[t * (CK + 1) + s] = s < t ? -acc : (s == t ? 1.0f : 0.0f);
+      }
+    } else if (warp >= NB) {
+      // The other warps bring V into Q's buffer (Q K^T is done).
+      for (int i = tid - NB * 32; i < CK * (DK / 4); i += 256 - NB * 32) {
+        const int t = i / (DK / 4), d = (i % (DK / 4)) * 4;
+        float4 v4 = make_float4(0, 0, 0, 0);
+        if (t < tn) v4 = *reinterpret_cast<const float4*>(vb + size_t(t0 + t) * a.ld_v + d);
+        float* vd = Vs + t * (DK + 1) + d;
+        vd[0] = v4.x; vd[1] = v4.y; vd[2] = v4.z; vd[3] = v4.w;
       }
     }
     __syncthreads();
@@ -531,7 +540,7 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   const size_t units = size_t(batch) * a.value_heads * chunks;
   ChunkOut* outs = static_cast<ChunkOut*>(workspace);
   ChunkState* states = reinterpret_cast<ChunkState*>(outs + units);
-  const int prep_smem = (3 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK + (CK / 16 - 1) * 256) * sizeof(float);
+  const int prep_smem = (2 * CK * (DK + 1) + 2 * CK * (CK + 1) + 3 * CK + (CK / 16 - 1) * 256) * sizeof(float);
   auto scan_smem = [](int sc, int stage_bytes) { return (DK * sc + CK * sc) * int(sizeof(float)) + 2 * stage_bytes; };
   const int scan16_smem = scan_smem(16, sizeof(ScanStage<16>)), scan32_smem = scan_smem(32, sizeof(ScanStage<32>));
   const int out_smem = (CK * OQ_LD + DK * OS_LD + CK * OK_LD + CK * OS_LD) * sizeof(float);
