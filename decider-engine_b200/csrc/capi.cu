@@ -627,23 +627,23 @@ int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests,
   // its end after its last request.
   dg::Engine& g0 = *e->e;
   std::vector<cudaEvent_t> ev(lanes + 1, nullptr);
-  bool timed = true;
+  // The events belong to the engine's device (the calling thread may have
+  // another one current).
+  bool timed = cudaSetDevice(g0.device()) == cudaSuccess;
   for (auto& x : ev) timed = timed && cudaEventCreate(&x) == cudaSuccess;
-  if (timed) {
-    cudaSetDevice(g0.device());
-    timed = cudaEventRecord(ev[0], g0.stream()) == cudaSuccess;
-  }
+  if (timed) timed = cudaEventRecord(ev[0], g0.stream()) == cudaSuccess;
+  if (!timed) cudaGetLastError();  // a failed timing call must not fail the first launch
   auto run_lane = [&](size_t k) {
     dg::Engine& g = k == 0 ? g0 : *e->lanes[k - 1];
     cudaSetDevice(g.device());
-    if (timed) cudaStreamWaitEvent(g.stream(), ev[0], 0);
+    if (timed && cudaStreamWaitEvent(g.stream(), ev[0], 0) != cudaSuccess) cudaGetLastError();
     for (size_t r : plan[k]) {
       float t = 0.0f;
       status[r] = run_request(e, g, requests[r], logits_out + off[r], t);
       ms[r] = t;
       if (status[r]) errors[r] = dg_last_error();
     }
-    if (timed) cudaEventRecord(ev[k + 1], g.stream());
+    if (timed && cudaEventRecord(ev[k + 1], g.stream()) != cudaSuccess) cudaGetLastError();
   };
   std::vector<std::thread> threads;
   for (size_t k = 1; k < lanes; ++k)
@@ -659,6 +659,7 @@ int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests,
   }
   for (auto& x : ev)
     if (x) cudaEventDestroy(x);
+  cudaGetLastError();  // the timing calls' own failures are not the batch's
   e->last_batch_ms = span;
   std::string first_error;
   for (size_t r = 0; r < n_requests; ++r) {

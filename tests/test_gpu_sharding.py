@@ -2,7 +2,8 @@
 data path): the same seeded request set, split over two engines by
 decider_gpu.sharding.shard_requests (longest processing time first), gives
 every request the logits, bit for bit in reference order, that one engine on
-one device gives the whole set. Needs two GPUs; skipped on fewer."""
+one device gives the whole set; the second device's engine runs two lanes.
+Needs two GPUs; skipped on fewer."""
 import numpy as np
 import pytest
 
@@ -41,6 +42,7 @@ def test_sharded_requests_on_two_devices_match_one_device():
     one, st, _, err = engine(0).logits_batch(reqs)
     assert not st.any(), err
     engines = [engine(0), engine(1)]
+    engines[1].set_lanes(2)  # lanes on a device other than the current one
     for rank, idx in enumerate(plan):
         got, st, _, err = engines[rank].logits_batch([reqs[i] for i in idx])
         assert not st.any(), err
