@@ -6,8 +6,8 @@
 // Split K over the grid so the skinny [M x R] product still fills the GPU:
 // CTA (t, z) owns rows 128 t .. 128 t + 127 and the K slice z. Per 32-wide K
 // chunk its 256 threads gather the x rows and A rows into registers
-// (coalesced 16-byte loads; the next chunk's loads are in flight while the
-// current chunk is stored), split every value into its TF32 part (low 13
+// (coalesced 16-byte loads; the next one or two chunks' loads are in flight
+// while the current chunk is stored), split every value into its TF32 part (low 13
 // mantissa bits cleared) and the remainder, and store both in the
 // 128-byte-swizzled K-major layout the tensor cores read; one thread issues
 // hi·hi + hi·lo + lo·hi as tcgen05.mma kind::tf32 (M = 128, N = R rounded up
@@ -47,6 +47,10 @@ __device__ __forceinline__ void lora_tc_gather(float4 (&v)[8], const float* __re
   }
 }
 
+// DEPTH: chunks of loads in flight ahead of the one being stored (2 for
+// CTAs of at most four chunks, where the first loads dominate; 1 otherwise,
+// measured slightly faster for longer slices).
+template <int DEPTH>
 __global__ void __launch_bounds__(kLaThreads, 1)
     lora_a_tc_kernel(const float* __restrict__ x, int ldx, int M, int K, const float* __restrict__ A, int R, int NP,
                      float* __restrict__ partial, int kslice, DeviceStatus* st) {
@@ -78,13 +82,14 @@ __global__ void __launch_bounds__(kLaThreads, 1)
   const uint32_t idesc = idesc_tf32(128, uint32_t(NP));
   const int items = (128 + NP) * 8;  // 16-byte pieces per chunk: x rows, then A rows
   bool ok = true;
-  float4 v[8];
+  float4 v[8], w[8];
   if (nch > 0) lora_tc_gather(v, x, ldx, M, m0, A, R, K, k0, items, tid);
+  if (DEPTH == 2 && nch > 1) lora_tc_gather(w, x, ldx, M, m0, A, R, K, k0 + 32, items, tid);
   for (int c = 0; c < nch; ++c) {
     const int b = c & 1;
     uint8_t* s = sm + b * slot;
-    float4 w[8];
-    if (c + 1 < nch) lora_tc_gather(w, x, ldx, M, m0, A, R, K, k0 + 32 * (c + 1), items, tid);
+    float4 nxt[8];
+    if (c + DEPTH < nch) lora_tc_gather(nxt, x, ldx, M, m0, A, R, K, k0 + 32 * (c + DEPTH), items, tid);
     // The slot was last read by the MMAs of chunk c - 2.
     if (c >= 2) ok = mbar_wait_bounded(&done[b], ((c - 2) >> 1) & 1, st, 400 + b, nullptr) && ok;
 #pragma unroll
@@ -120,7 +125,14 @@ __global__ void __launch_bounds__(kLaThreads, 1)
       mma_commit(&done[b]);  // also after a failed wait, so that every later wait ends
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = w[u];
+    for (int u = 0; u < 8; ++u) {
+      if (DEPTH == 2) {
+        v[u] = w[u];
+        w[u] = nxt[u];
+      } else {
+        v[u] = nxt[u];
+      }
+    }
   }
   // The last commit covers every MMA of the issuing thread.
   if (nch > 0 && !mbar_wait_bounded(&done[(nch - 1) & 1], ((nch - 1) >> 1) & 1, st, 410, nullptr)) ok = false;
@@ -169,7 +181,9 @@ void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int
                       float* partial, size_t partial_floats, DeviceStatus* st, cudaStream_t s, bool overlap) {
   static std::atomic<uint64_t> configured{0};
   once_per_device(configured, [] {
-    DG_CUDA(cudaFuncSetAttribute(lora_a_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    DG_CUDA(cudaFuncSetAttribute(lora_a_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 lora_tc_smem_bytes(128)));
+    DG_CUDA(cudaFuncSetAttribute(lora_a_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  lora_tc_smem_bytes(128)));
   });
   const int NP = (R + 15) / 16 * 16;
@@ -182,8 +196,8 @@ void launch_lora_a_tc(const float* x, int ldx, int M, int K, const float* A, int
   const int kslice = ((K + splits - 1) / splits + 31) / 32 * 32;
   const int used = (K + kslice - 1) / kslice;
   if (size_t(used) * M * R > partial_floats) throw CudaError("lora_a: split-K workspace too small");
-  launch_k(overlap || pdl_enabled(), lora_a_tc_kernel, dim3(mt, used), dim3(kLaThreads), lora_tc_smem_bytes(NP), s, x,
-           ldx, M, K, A, R, NP, partial, kslice, st);
+  launch_k(overlap || pdl_enabled(), kslice / 32 <= 4 ? lora_a_tc_kernel<2> : lora_a_tc_kernel<1>, dim3(mt, used),
+           dim3(kLaThreads), lora_tc_smem_bytes(NP), s, x, ldx, M, K, A, R, NP, partial, kslice, st);
   DG_CUDA(cudaGetLastError());
   launch_lora_a_reduce(partial, used, M, R, mid, ldm, s, overlap);
 }
