@@ -216,7 +216,8 @@ int dg_logits(dg_engine* e, const dg_prefix* past, const uint32_t* ids, size_t n
  * is an engine on the same device reading this engine's weights (see
  * dg_engine_create_sibling) with its own stream and forward buffers (about
  * 1.2 GB at max_tokens 4096 for the 2B model). dg_engine_set_exact applies
- * to every lane. */
+ * to every lane. Set the lanes between calls: not while another thread runs
+ * a call on this engine. */
 int dg_engine_set_lanes(dg_engine* e, int lanes);
 int dg_engine_lanes(const dg_engine* e);
 /* Device time of the last dg_logits_batch call from its first kernel to the
