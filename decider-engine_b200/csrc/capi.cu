@@ -333,6 +333,8 @@ int dg_engine_set_lanes(dg_engine* e, int lanes) {
       l->batch_questions = b.batch_questions;
       e->lanes.push_back(std::move(l));
     }
+    e->e->wide_scan = lanes > 1;
+    for (auto& l : e->lanes) l->wide_scan = lanes > 1;
   });
 }
 

@@ -26,8 +26,9 @@ constexpr int CK = 64, DK = 128;
 // 16 columns (128 threads) keep one sequence's scan on 8 CTAs per head, the
 // shorter latency per chunk; 32 columns (256 threads) halve the CTAs and the
 // W / K staging traffic per column, which pays when many sequences fill the
-// GPU anyway (measured: 64 sequences x 4096 tokens 38.9 -> 34.0 ms; one
-// 512-token sequence 8.45 -> 8.72 ms per 24-layer forward).
+// GPU anyway, or when other work runs beside the scan (measured: 64
+// sequences x 4096 tokens 38.9 -> 34.0 ms; one 512-token sequence 8.45 ->
+// 8.72 ms per 24-layer forward; config 5 on two lanes +1 %).
 
 // Per-chunk products written by the prep kernel.
 struct ChunkOut {
@@ -527,7 +528,8 @@ size_t delta_chunk_workspace_bytes(int batch, int heads, int n) {
   return size_t(batch) * heads * chunks * (sizeof(ChunkOut) + sizeof(ChunkState));
 }
 
-void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s,
+                          bool wide) {
   if (a.n <= 0 || batch <= 0) return;
   if (a.dv != DK || a.value_heads % a.key_heads)
     throw CudaError("delta_chunked: needs dk = dv = 128");
@@ -555,8 +557,9 @@ void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t
   });
   launch_pdl(delta_chunk_prep_kernel, dim3(int(units)), dim3(256), prep_smem, s, a, outs, chunks);
   DG_CUDA(cudaGetLastError());
-  // Wide slices once they make at least two waves of scan CTAs.
-  if (size_t(batch) * a.value_heads * (a.dv / 32) >= 2 * 148)
+  // Wide slices once they make at least two waves of scan CTAs, or when
+  // asked for (other lanes' kernels fill the SMs the scan leaves free).
+  if (wide || size_t(batch) * a.value_heads * (a.dv / 32) >= 2 * 148)
     launch_pdl(delta_chunk_scan_kernel<256, 32>, dim3(batch * a.value_heads * (a.dv / 32)), dim3(256), scan32_smem, s,
                a, outs, states, chunks);
   else

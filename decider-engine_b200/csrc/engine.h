@@ -169,6 +169,9 @@ class Engine {
   std::mutex mu;
   // Exact FP32 promotion order in the tcgen05 projections (reference order).
   bool exact = true;
+  // The chunked DeltaNet scan in 32-column slices (half the CTAs): set for
+  // engines that serve batch lanes, where other lanes use the free SMs.
+  bool wide_scan = false;
   // Device launches issued by the last forward (kernels only).
   int last_launches = 0;
   // Device time of the last forward's kernels (after the id upload, before

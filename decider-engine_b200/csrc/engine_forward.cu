@@ -122,7 +122,7 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
     // token recurrence.
     if (!exact && delta_ws_.ptr && sl > kDeltaChunk &&
         delta_chunk_workspace_bytes(ns, H, sl) <= delta_ws_.bytes)
-      launch_delta_chunked(da, ns, delta_ws_.ptr, delta_ws_.bytes, stream_);
+      launch_delta_chunked(da, ns, delta_ws_.ptr, delta_ws_.bytes, stream_, wide_scan);
     else
       launch_delta_rec128(da, ns, stream_);
     const bool q = precision_ == kInt8Compute;
@@ -159,7 +159,7 @@ void Engine::mixer_tail(int i, int n, int start, const Prefix::LayerState* past,
     da.state = state_[i].as<float>();
     da.o = o_.as<float>();
     da.ldo = H * c.dv;
-    launch_delta_chunked(da, 1, delta_ws_.ptr, delta_ws_.bytes, stream_);
+    launch_delta_chunked(da, 1, delta_ws_.ptr, delta_ws_.bytes, stream_, wide_scan);
   } else {
     launch_delta_recurrence(conv_.as<float>(), n, c.key_heads, c.dk, H, c.dv, decay_.as<float>(),
                             beta_.as<float>(), state_[i].as<float>(), o_.as<float>(), stream_);

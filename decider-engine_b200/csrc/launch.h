@@ -129,7 +129,11 @@ void launch_delta_rec128(const DeltaArgs& a, int batch, cudaStream_t s);
 // device workspace of delta_chunk_workspace_bytes(batch, heads, n).
 size_t delta_chunk_workspace_bytes(int batch, int heads, int n);
 constexpr int kDeltaChunk = 64;  // tokens per chunk of the chunked form
-void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s);
+// wide: 32-column scan slices (half the scan CTAs, the same work per thread)
+// even when the batch alone would not fill two waves of them; an engine that
+// shares the GPU with other lanes asks for them.
+void launch_delta_chunked(const DeltaArgs& a, int batch, void* workspace, size_t workspace_bytes, cudaStream_t s,
+                          bool wide = false);
 void launch_exp(const float* g, float* out, size_t n, cudaStream_t s);
 // Split q|gate per head, centred RMSNorm of q and k, partial RoPE from the
 // precomputed table, append k/v to the cache at `start`. seg_len > 0: the n
