@@ -648,9 +648,17 @@ int dg_logits_batch(dg_engine* e, const dg_request* requests, size_t n_requests,
     if (timed && cudaEventRecord(ev[k + 1], g.stream()) != cudaSuccess) cudaGetLastError();
   };
   std::vector<std::thread> threads;
-  for (size_t k = 1; k < lanes; ++k)
-    if (!plan[k].empty()) threads.emplace_back(run_lane, k);
+  std::vector<size_t> inline_lanes;  // lanes whose thread could not be started run here
+  for (size_t k = 1; k < lanes; ++k) {
+    if (plan[k].empty()) continue;
+    try {
+      threads.emplace_back(run_lane, k);
+    } catch (...) {
+      inline_lanes.push_back(k);
+    }
+  }
   run_lane(0);
+  for (size_t k : inline_lanes) run_lane(k);
   for (auto& t : threads) t.join();
   float span = 0.0f;
   for (size_t k = 0; timed && k < lanes; ++k) {
