@@ -255,6 +255,7 @@ class Engine {
   DevBuf attn_ws_;
   bool attn_tc_ = true;
   DevBuf lora_part_; // split-K LoRA-A partial sums (fast mode)
+  DevBuf tc_prod_;   // FP32-weight projections on the tensor cores: the product before the SwiGLU
   DevBuf gemm_split_ws_, gemm_split_cnt_;  // split-K projection partials and tile counters (fast mode)
   DevBuf status_;
   cudaEvent_t ev0_ = nullptr, ev1_ = nullptr;

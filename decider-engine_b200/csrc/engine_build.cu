@@ -336,6 +336,7 @@ void Engine::alloc_workspaces(int ld_proj) {
     vseg_ = DevBuf(size_t(M) * c.kw() * 4);
   }
   if (fast_) lora_part_ = DevBuf(lora_a_partial_floats(M) * 4);
+  if (!fast_ && precision_ == kCheckpoint) tc_prod_ = DevBuf(size_t(M) * I * 4);
   if (fast_) {
     gemm_split_ws_ = DevBuf(kGemmSplitFloats * 4);
     gemm_split_cnt_ = DevBuf(kGemmSplitTiles * sizeof(int));

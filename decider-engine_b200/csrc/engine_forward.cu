@@ -66,6 +66,50 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
 }
 
 void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi) {
+  // Fast mode with FP32 weights (checkpoint precision): the product on the
+  // tensor cores (3 x TF32, FP32 sums per 32-wide K chunk), then LoRA-B as a
+  // second product added into the output, then the bias and the SwiGLU.
+  const bool lora_tc = p.lora_rows == 0 || (p.lora_rows % 32 == 0 && p.lora_rows <= 128 && p.g.rank == p.lora_rows);
+  if (!exact && p.g.precision == 0 && p.w_f32.ptr && p.in % 32 == 0 && ldx % 4 == 0 &&
+      reinterpret_cast<uintptr_t>(x) % 16 == 0 && lora_tc &&
+      (epi != kEpiSwiGlu || (tc_prod_.ptr && size_t(M) * p.out * 4 <= tc_prod_.bytes))) {
+    float* dst = epi == kEpiSwiGlu ? tc_prod_.as<float>() : out;
+    const int ldd = epi == kEpiSwiGlu ? p.out : ldo;
+    TcGemmArgs g;
+    g.A = x;
+    g.lda = ldx;
+    g.B = p.w_f32.as<float>();
+    g.ldb = p.in;
+    g.C = dst;
+    g.ldc = ldd;
+    g.M = M;
+    g.N = p.out;
+    g.K = p.in;
+    g.accumulate = epi == kEpiAdd ? 1 : 0;
+    g.status = status();
+    launch_tc_gemm(g, 1, stream_);
+    if (p.lora_rows) {
+      launch_lora_a(x, ldx, M, p.in, p.lora_a.as<float>(), p.lora_rows, mid_.as<float>(), 128, false, stream_);
+      TcGemmArgs l;
+      l.A = mid_.as<float>();
+      l.lda = 128;
+      l.B = p.lora_b.as<float>();
+      l.ldb = p.lora_rows;
+      l.C = dst;
+      l.ldc = ldd;
+      l.M = M;
+      l.N = p.out;
+      l.K = p.lora_rows;
+      l.alpha = p.g.lora_scale;
+      l.accumulate = 1;
+      l.status = status();
+      launch_tc_gemm(l, 1, stream_);
+    }
+    if (epi == kEpiSwiGlu || p.g.bias)
+      launch_proj_finish(dst, ldd, p.g.bias, out, ldo, M, p.out, epi == kEpiSwiGlu ? kEpiSwiGlu : kEpiWrite,
+                         stream_);
+    return;
+  }
   if (p.lora_rows) {
     launch_lora_a(x, ldx, M, p.in, p.lora_a.as<float>(), p.lora_rows, mid_.as<float>(), 128, true, stream_);
   }

@@ -799,6 +799,31 @@ void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const in
   DG_CUDA(cudaGetLastError());
 }
 
+namespace {
+__global__ void __launch_bounds__(256) proj_finish_kernel(const float* __restrict__ prod, int ldp,
+                                                          const float* __restrict__ bias, float* out, int ldo,
+                                                          int M, int N, int epi) {
+  griddep_wait();
+  griddep_launch();
+  const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= long(M) * N) return;
+  const int m = int(i / N), n = int(i % N);
+  float v = prod[size_t(m) * ldp + n];
+  if (bias) v = v + bias[n];
+  float* o = out + size_t(m) * ldo + n;
+  *o = epi == kEpiSwiGlu ? silu_f(*o) * v : v;
+}
+}  // namespace
+
+void launch_proj_finish(const float* prod, int ldp, const float* bias, float* out, int ldo, int M, int N, int epi,
+                        cudaStream_t s) {
+  if (M <= 0 || N <= 0) return;
+  const long total = long(M) * N;
+  launch_pdl(proj_finish_kernel, dim3(unsigned((total + 255) / 256)), dim3(256), 0, s, prod, ldp, bias, out, ldo, M,
+             N, epi);
+  DG_CUDA(cudaGetLastError());
+}
+
 void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids, int n, float* x, cudaStream_t s) {
   if (n <= 0) return;
   launch_pdl(embed_kernel, dim3(n), dim3(256), 0, s, table, dtype, hidden, ids, x);

@@ -88,6 +88,11 @@ struct GenericProj {
 void launch_proj_generic(const GenericProj& p, const float* x, int ldx, const int8_t* xq, const float* xs,
                          int ldxs, const float* mid, int ldm, int M, float* out, int ldo, int epi,
                          cudaStream_t s);
+// Finishes a projection whose product v (+ bias) is in `prod` (row stride
+// ldp): out = silu(out) * (v + bias) for kEpiSwiGlu, out = v + bias
+// otherwise (in place when prod == out). Bias nullable.
+void launch_proj_finish(const float* prod, int ldp, const float* bias, float* out, int ldo, int M, int N, int epi,
+                        cudaStream_t s);
 void launch_embed(const void* table, int dtype, int hidden, const uint32_t* ids, int n, float* x,
                   cudaStream_t s);
 // Causal depthwise conv (tap-major weights [k][W]) + SiLU, continuing from a

@@ -95,13 +95,18 @@ def _noise_band(golden, which):
     return band
 
 
+@pytest.mark.parametrize("exact", [True, False], ids=["reference-order", "fma"])
 @pytest.mark.parametrize("which", ["cfg2", "cfg4"])
-def test_checkpoint_precision_probabilities_within_1e3(full, which):
+def test_checkpoint_precision_probabilities_within_1e3(full, which, exact):
+    """FMA mode puts the FP32-weight projections on the tensor cores (3 x TF32)."""
     models, golden = full
-    got = _run(models["checkpoint"], which)
+    m = models["checkpoint"]
+    m.set_exact(exact)
+    got = _run(m, which)
     ref = _reference(golden, "checkpoint", which)
     errs = [float(np.abs(p - r).max()) for (p, _), r in zip(got, ref)]
-    print(f"checkpoint {which}: max probability error per question {['%.2e' % e for e in errs]}")
+    print(f"checkpoint {which} ({'reference order' if exact else 'fma'}): max probability error per question "
+          f"{['%.2e' % e for e in errs]}")
     assert max(errs) <= PROB_TOL, errs
 
 
