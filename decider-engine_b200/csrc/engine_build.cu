@@ -106,6 +106,13 @@ DevProj Engine::build_generic_proj(const std::string& key, int in, int out, bool
       DevBuf wf = upload(w.f32);
       quantize_weights_device(wf.as<float>(), rows, width, w.bits, d.wq.as<uint8_t>(), d.scale_rows.as<float>(),
                               nullptr, 0);
+      if (precision_ != kInt8Compute) {
+        // Weight-only precisions: the dequantised FP32 weights too, for the
+        // tensor-core projections of the fast mode.
+        d.w_f32 = DevBuf(rows * width * 4);
+        dequantize_weights_device(d.wq.as<uint8_t>(), d.scale_rows.as<float>(), rows, width, w.bits,
+                                  d.w_f32.as<float>(), 0);
+      }
       DG_CUDA(cudaStreamSynchronize(0));
     }
     g.wq = d.wq.as<uint8_t>();
@@ -336,7 +343,7 @@ void Engine::alloc_workspaces(int ld_proj) {
     vseg_ = DevBuf(size_t(M) * c.kw() * 4);
   }
   if (fast_) lora_part_ = DevBuf(lora_a_partial_floats(M) * 4);
-  if (!fast_ && precision_ == kCheckpoint) tc_prod_ = DevBuf(size_t(M) * I * 4);
+  if (!fast_ && precision_ != kInt8Compute) tc_prod_ = DevBuf(size_t(M) * I * 4);
   if (fast_) {
     gemm_split_ws_ = DevBuf(kGemmSplitFloats * 4);
     gemm_split_cnt_ = DevBuf(kGemmSplitTiles * sizeof(int));

@@ -66,11 +66,13 @@ void Engine::run_proj_fast(const DevProj& p, int M, const float* mid, float* out
 }
 
 void Engine::run_proj_generic(const DevProj& p, const float* x, int ldx, int M, float* out, int ldo, int epi) {
-  // Fast mode with FP32 weights (checkpoint precision): the product on the
+  // Fast mode with FP32 weights (checkpoint precision, or the dequantised
+  // weights of the int8 and int4 weight-only precisions): the product on the
   // tensor cores (3 x TF32, FP32 sums per 32-wide K chunk), then LoRA-B as a
   // second product added into the output, then the bias and the SwiGLU.
+  // int8-compute quantises its activations and keeps its own kernel.
   const bool lora_tc = p.lora_rows == 0 || (p.lora_rows % 32 == 0 && p.lora_rows <= 128 && p.g.rank == p.lora_rows);
-  if (!exact && p.g.precision == 0 && p.w_f32.ptr && p.in % 32 == 0 && ldx % 4 == 0 &&
+  if (!exact && p.g.precision != kInt8Compute && p.w_f32.ptr && p.in % 32 == 0 && ldx % 4 == 0 &&
       reinterpret_cast<uintptr_t>(x) % 16 == 0 && lora_tc &&
       (epi != kEpiSwiGlu || (tc_prod_.ptr && size_t(M) * p.out * 4 <= tc_prod_.bytes))) {
     float* dst = epi == kEpiSwiGlu ? tc_prod_.as<float>() : out;

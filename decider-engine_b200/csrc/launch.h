@@ -221,5 +221,9 @@ struct QuantLayout {
 QuantLayout quant_plain_layout(size_t rows, size_t width);
 void quantize_weights_device(const float* w, size_t rows, size_t width, int bits, uint8_t* q, float* scales,
                              const QuantLayout* layout, cudaStream_t s);
+// The FP32 values the reference reads from plain-layout quantised weights
+// (Data::row: code times its group's scale), out [rows][width].
+void dequantize_weights_device(const uint8_t* q, const float* scales, size_t rows, size_t width, int bits,
+                               float* out, cudaStream_t s);
 
 }  // namespace dg

@@ -88,7 +88,31 @@ __global__ void __launch_bounds__(256) weight_codes_i4_kernel(const float* __res
   q[b] = uint8_t(out);
 }
 
+// The reference's reading of a quantised row (Data::row): q as f32 times its
+// group's scale, one IEEE multiply (8 bits: the signed byte; 4 bits: the
+// nibble minus 8).
+__global__ void __launch_bounds__(256) weight_dequant_kernel(const uint8_t* __restrict__ q,
+                                                             const float* __restrict__ scales, long el, int width,
+                                                             int bits, float* __restrict__ out) {
+  const long i = long(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= el) return;
+  const long r = i / width;
+  const int c = int(i % width), groups = (width + 63) / 64;
+  const float code = bits == 8 ? float(int8_t(q[i])) : float(int((q[i / 2] >> (4 * (i % 2))) & 15)) - 8.0f;
+  out[i] = __fmul_rn(code, scales[size_t(r) * groups + c / 64]);
+}
+
 }  // namespace
+
+void dequantize_weights_device(const uint8_t* q, const float* scales, size_t rows, size_t width, int bits,
+                               float* out, cudaStream_t s) {
+  if (width == 0 || width > size_t(INT32_MAX) || rows > size_t(INT32_MAX)) throw CudaError("dequantize: bad width");
+  if (bits != 8 && bits != 4) throw CudaError("dequantize: bits must be 8 or 4");
+  const long el = long(rows) * long(width);
+  if (el == 0) return;
+  weight_dequant_kernel<<<unsigned((el + 255) / 256), 256, 0, s>>>(q, scales, el, int(width), bits, out);
+  DG_CUDA(cudaGetLastError());
+}
 
 QuantLayout quant_plain_layout(size_t rows, size_t width) {
   QuantLayout L;

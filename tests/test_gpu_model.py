@@ -71,25 +71,27 @@ def test_small_model_fp32_dot_precisions_match_oracle(oracle_mod, precision):
     assert rel_err(got, exp) < 1e-5, rel_err(got, exp)
 
 
-def test_checkpoint_precision_fma_mode_on_tensor_cores(oracle_mod):
-    """Checkpoint precision (FP32 weights) in FMA mode runs its projections
-    on the tensor cores (3 x TF32 tcgen05, FP32 sums per 32-wide K chunk;
-    LoRA-B a second product into the output; the SwiGLU after both): a
-    4-layer forward stays within 1e-4 relative of the oracle, the
-    north_star's per-layer bar, with prefix continuation and several token
-    counts."""
+@pytest.mark.parametrize("precision", ["checkpoint", "int8", "int4"])
+def test_weight_only_precisions_fma_mode_on_tensor_cores(oracle_mod, precision):
+    """The FP32-dot precisions in FMA mode run their projections on the
+    tensor cores (3 x TF32 tcgen05, FP32 sums per 32-wide K chunk; LoRA-B a
+    second product into the output; the SwiGLU after both), over the FP32
+    weights, or for int8 / int4 over the weights as the reference reads them
+    back (code times scale, dequantised on the device at load): a 4-layer
+    forward stays within 1e-4 relative of the oracle, the north_star's
+    per-layer bar, with prefix continuation and several token counts."""
     cfg = small_config()
     tensors = random_tensors(cfg, rank=32, pointer_dim=64, seed=13)
-    m = _gpu_small(cfg, tensors, "checkpoint")
+    m = _gpu_small(cfg, tensors, precision)
     assert not m.fast_path
-    o = oracle_mod.OracleModel(cfg, tensors, "checkpoint", 32, 2.0)
+    o = oracle_mod.OracleModel(cfg, tensors, precision, 32, 2.0)
     m.set_exact(False)
     for n in (200, 64, 129):
         ids = np.random.default_rng(n).integers(0, cfg["vocab_size"], n)
         got = m.forward(ids)
         exp = o.forward(ids)
         err = rel_err(got, exp)
-        print(f"checkpoint, FMA mode, {n} tokens: relative error {err:.2e}")
+        print(f"{precision}, FMA mode, {n} tokens: relative error {err:.2e}")
         assert err < 1e-4, (n, err)
     ids = np.random.default_rng(5).integers(0, cfg["vocab_size"], 300)
     pre = m.prefill(ids[:170])
