@@ -76,7 +76,12 @@ int dg_engine_finalize(dg_engine* e);
 int dg_engine_create_sibling(dg_engine* base, dg_engine** out);
 /* 1 when the tcgen05 INT8 path serves the projections, 0 for the generic kernels. */
 int dg_engine_fast_path(const dg_engine* e);
-/* 1: tcgen05 promotion in the reference's FP32 order (default); 0: fused multiply-add. */
+/* 1 (default): every FP32 sum in the reference's order (the tcgen05 INT8
+ * promotion in group order, the other precisions' projections in dot_scores
+ * lane order, the token recurrence, the CUDA-core attention). 0: the fast
+ * mode: fused multiply-adds in the promotion, the chunked delta rule,
+ * attention and LoRA products on the tensor cores (3 x TF32), and the
+ * weight-only precisions' projections on the tensor cores. */
 int dg_engine_set_exact(dg_engine* e, int exact);
 void dg_engine_free(dg_engine* e);
 /* Model::load + Head::load from a checkpoint directory in the reference's
