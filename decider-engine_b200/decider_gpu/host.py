@@ -214,6 +214,81 @@ class NativeEngine:
                 return self.model.logits(enc.input_ids[n:], [p - n for p in enc.option_positions], prefix)
         return self.model.logits(enc.input_ids, enc.option_positions)
 
+    def set_lanes(self, lanes: int) -> None:
+        """Requests of evaluate_batch served `lanes` at a time on this GPU
+        (dg_engine_set_lanes)."""
+        self.model.set_lanes(lanes)
+
+    def _readout(self, items, logits) -> dict:
+        """Temperature, softmax and typed answers of one request
+        (src/lib.rs:525-548)."""
+        answers, used = {}, 0
+        for (name, q), lg in zip(items, logits):
+            kind, labels, enc = q[0], q[1], q[2]
+            legend = q[3] if len(q) > 3 else None
+            t = np.float32(self.config["temperature_by_kind"].get(kind, self.config["temperature"]))
+            p = softmax((np.asarray(lg, np.float32) / t).astype(np.float32))
+            if not np.all(np.isfinite(p)):
+                raise DecideError(ErrorKind.ENGINE, "non-finite decision probabilities")
+            answers[name] = answer(kind, labels, p, self.config["ordinal_smoothing"], legend)
+            used += len(enc.input_ids)
+        return {"model": self.model_id(), "answers": answers, "usage": {"input_tokens": used, "output_tokens": 0}}
+
+    def evaluate_batch(self, requests, limits: InferenceLimits | None = None) -> list:
+        """`evaluate_encoded` for many requests in one device call
+        (dg_logits_batch): requests is a list of (questions, state_tokens).
+        Each request keeps evaluate's semantics: its questions in name order,
+        one shared state when it has two or more questions (a question that
+        does not continue the state runs as its own forward, as
+        NativeEngine::logits does), the token limit checked first. Returns,
+        per request, the response dict or the DecideError it raised; one bad
+        request does not stop the others."""
+        limits = limits or InferenceLimits()
+        out = [None] * len(requests)
+        dev, where = [], []  # device requests; (request index, [question slots]) for each
+        plans = []
+        for r, (questions, state_tokens) in enumerate(requests):
+            total = sum(len(q[2].input_ids) for q in questions.values())
+            if total > limits.max_total_tokens:
+                out[r] = DecideError(ErrorKind.RESOURCE_LIMIT,
+                                     f"request binds {total} total tokens; limit is {limits.max_total_tokens}")
+                continue
+            items = sorted(questions.items())
+            plans.append((r, items))
+            shared, alone = [], []
+            sids = list(items[0][1][2].input_ids[:state_tokens]) if len(items) >= 2 else None
+            for k, (_, q) in enumerate(items):
+                enc, n = q[2], len(sids) if sids is not None else 0
+                if (sids is not None and len(enc.input_ids) > n and list(enc.input_ids[:n]) == sids
+                        and all(p >= n for p in enc.option_positions)):
+                    shared.append((k, (list(enc.input_ids[n:]), [p - n for p in enc.option_positions])))
+                else:
+                    alone.append((k, (list(enc.input_ids), list(enc.option_positions))))
+            if shared:
+                dev.append({"state": sids, "questions": [x for _, x in shared]})
+                where.append((r, [k for k, _ in shared]))
+            for k, x in alone:
+                dev.append({"questions": [x]})
+                where.append((r, [k]))
+        logits, status, _, err = self.model.logits_batch(dev) if dev else ([], [], [], None)
+        per = {r: [None] * len(items) for r, items in plans}
+        failed = {}
+        for d, (r, slots) in enumerate(where):
+            if status[d]:
+                failed.setdefault(r, err or "device request failed")
+                continue
+            for k, lg in zip(slots, logits[d]):
+                per[r][k] = lg
+        for r, items in plans:
+            if r in failed:
+                out[r] = DecideError(ErrorKind.ENGINE, failed[r])
+                continue
+            try:
+                out[r] = self._readout(items, per[r])
+            except DecideError as e:
+                out[r] = e
+        return out
+
     def evaluate_encoded(self, questions: dict, state_tokens: int, limits: InferenceLimits | None = None):
         """`evaluate` after prompt binding (src/lib.rs:494-559): questions maps
         name -> (kind, labels, Encoding[, legend]); BTreeMap order; one shared
