@@ -580,3 +580,35 @@ def test_logits_batch_lanes_and_siblings_give_the_same_logits(small, exact):
     del m, past
     gc.collect()
     assert np.array_equal(s.logits(q, pos), ref)
+
+
+def test_native_engine_batch_equals_one_request_at_a_time(small):
+    """NativeEngine.evaluate_batch (one dg_logits_batch call over two lanes)
+    answers every request exactly as evaluate_encoded does one request at a
+    time (reference order: the same probabilities bit for bit), and reports
+    the refused and the failing requests in their own slots."""
+    from decider_gpu import DecideError, Encoding, ErrorKind, NativeEngine, Precision
+    cfg, tensors = small
+    m = _gpu_small(cfg, tensors)
+    dcfg = json.load(open(os.path.join(TINY, "strands_decider_config.json")))
+    eng = NativeEngine(m, dcfg, Precision.INT8_COMPUTE)
+    rng = np.random.default_rng(8)
+    ids = lambda n: [int(x) for x in rng.integers(0, cfg["vocab_size"], n)]
+
+    def q(kind, state, n, k):
+        full = list(state) + ids(n)
+        pos = list(range(len(full) - 1 - k, len(full) - 1))
+        labels = ["false", "true"] if kind == "noul" else [str(i) for i in range(k)]
+        return (kind, labels, Encoding(full, pos, len(full) - 1))
+
+    state = ids(120)
+    reqs = [({"a": q("noul", state, 20, 2), "b": q("choice", state, 33, 4), "c": q("noul", state, 20, 2)}, 120),
+            ({"x": q("noul", [], 77, 2)}, 0),
+            ({"big": q("noul", [], 9000, 2)}, 0),
+            ({"bad": ("noul", ["false", "true"], Encoding(ids(10), [8, 9], 9))}, 0)]
+    eng.set_lanes(2)
+    got = eng.evaluate_batch(reqs)
+    for (questions, st), g in zip(reqs[:2], got[:2]):
+        assert g == eng.evaluate_encoded(questions, st)
+    assert isinstance(got[2], DecideError) and got[2].kind == ErrorKind.RESOURCE_LIMIT
+    assert isinstance(got[3], DecideError) and got[3].kind == ErrorKind.ENGINE
